@@ -1,0 +1,145 @@
+"""Step-numbered, crash-safe checkpoints in the reference's on-disk format.
+
+One checkpoint is three files in ``save_dir`` (reference
+``utils/checkpoint.py:11-110``):
+
+* ``model_step_N.safetensors`` - the state dict, one key per *storage*
+  (tied tensors are written once: the first key in iteration order wins);
+* ``optim_step_N.pt`` - ``torch.save`` of the optimizer state dict;
+* ``meta_step_N.json`` - ``{"step": N, ...}``; the file name's step wins over
+  a caller-supplied ``step``.
+
+Each file is written to a temporary file in the same directory and moved into
+place with ``os.replace``, so a crash leaves either the old file or none.  A
+step counts as present only when all three files exist.
+"""
+from __future__ import annotations
+
+import contextlib
+import json
+import logging
+import os
+import tempfile
+from pathlib import Path
+from typing import Dict, Optional
+
+import torch
+from safetensors.torch import load_file, save_file
+
+log = logging.getLogger(__name__)
+
+_FILES = ("model_step_{}.safetensors", "optim_step_{}.pt", "meta_step_{}.json")
+
+
+class CheckpointManager:
+    """Save and restore model / optimizer / metadata triples by step."""
+
+    def __init__(self, save_dir: str):
+        self.save_dir = Path(save_dir)
+        self.save_dir.mkdir(parents=True, exist_ok=True)
+
+    # ------------------------------------------------------------------ paths
+    def _path(self, kind: int, step: int) -> Path:
+        return self.save_dir / _FILES[kind].format(step)
+
+    def _list_steps(self) -> list:
+        steps = []
+        for p in self.save_dir.glob("model_step_*.safetensors"):
+            tail = p.stem.rsplit("_", 1)[-1]
+            if tail.isdigit():
+                steps.append(int(tail))
+        return steps
+
+    def _checkpoint_complete(self, step: int) -> bool:
+        return all(self._path(i, step).exists() for i in range(3))
+
+    def latest_step(self) -> Optional[int]:
+        """Newest step whose three files all exist, or ``None``."""
+        complete = [s for s in self._list_steps() if self._checkpoint_complete(s)]
+        return max(complete) if complete else None
+
+    # ------------------------------------------------------------------- save
+    @contextlib.contextmanager
+    def _atomic_write(self, path: Path, suffix: str):
+        fd, tmp = tempfile.mkstemp(dir=self.save_dir, suffix=suffix)
+        os.close(fd)
+        try:
+            yield tmp
+            os.replace(tmp, path)
+        except BaseException:
+            with contextlib.suppress(OSError):
+                os.unlink(tmp)
+            raise
+
+    @staticmethod
+    def _unique_storage(state: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
+        seen, out = set(), {}
+        for key, t in state.items():
+            ptr = t.data_ptr()
+            if ptr in seen:
+                continue
+            seen.add(ptr)
+            out[key] = t.detach().contiguous()
+        return out
+
+    def _atomic_save_safetensors(self, state: dict, path: Path) -> None:
+        tensors = self._unique_storage(state)
+        with self._atomic_write(path, ".safetensors.tmp") as tmp:
+            save_file(tensors, tmp)
+
+    def _atomic_save_torch(self, obj, path: Path) -> None:
+        with self._atomic_write(path, ".pt.tmp") as tmp:
+            torch.save(obj, tmp)
+
+    def _atomic_save_json(self, obj: dict, path: Path) -> None:
+        with self._atomic_write(path, ".json.tmp") as tmp:
+            with open(tmp, "w") as f:
+                json.dump(obj, f, indent=2, default=str)
+
+    def save(self, model: torch.nn.Module, optimizer, step: int, extra_meta: Optional[dict] = None,
+             state_dict: Optional[dict] = None, optimizer_state: Optional[dict] = None) -> None:
+        """Write the three files for ``step``.
+
+        ``state_dict`` overrides ``model.state_dict()``; ``optimizer_state``
+        overrides ``optimizer.state_dict()`` (used by sharded optimizers that
+        gather to the reference layout first).
+        """
+        state = state_dict if state_dict is not None else model.state_dict()
+        self._atomic_save_safetensors(state, self._path(0, step))
+        opt_state = optimizer_state if optimizer_state is not None else optimizer.state_dict()
+        self._atomic_save_torch(opt_state, self._path(1, step))
+        meta = {k: v for k, v in (extra_meta or {}).items() if k != "step"}
+        self._atomic_save_json({"step": step, **meta}, self._path(2, step))
+        log.info("[checkpoint] saved step %d -> %s", step, self.save_dir)
+
+    # ------------------------------------------------------------------- load
+    def load(self, model: torch.nn.Module, step: int, device: str = "cuda", optimizer=None,
+             strict: bool = True) -> dict:
+        """Restore ``step`` into ``model`` (and ``optimizer``); return the metadata.
+
+        With ``strict`` a missing or unexpected key raises ``RuntimeError``;
+        otherwise it is logged.
+        """
+        wpath = self._path(0, step)
+        if not wpath.exists():
+            raise FileNotFoundError(f"Checkpoint not found: {wpath}\nAvailable steps: {sorted(self._list_steps())}")
+        weights = load_file(str(wpath), device=str(device))
+        missing, unexpected = model.load_state_dict(weights, strict=False)
+        for what, keys in (("missing", missing), ("unexpected", unexpected)):
+            if not keys:
+                continue
+            msg = f"[checkpoint] {len(keys)} {what} key(s): {list(keys)[:5]}{'...' if len(keys) > 5 else ''}"
+            if strict:
+                raise RuntimeError(msg)
+            log.warning(msg)
+        if optimizer is not None:
+            opath = self._path(1, step)
+            if opath.exists():
+                optimizer.load_state_dict(torch.load(opath, map_location=device, weights_only=True))
+            else:
+                log.warning("[checkpoint] no optimizer state at %s; optimizer starts fresh", opath)
+        mpath = self._path(2, step)
+        if mpath.exists():
+            with open(mpath) as f:
+                return json.load(f)
+        return {"step": step}

@@ -1,0 +1,306 @@
+"""CPU tests of model semantics (shapes, caches, routing, MTP, sampling)."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from models.moe import AuxLossFreeGate, DeepSeekMoE, Expert
+from models.mla import MultiHeadLatentAttention
+from models.mtp import MTPBlock, MTPModule, MultiTokenPrediction
+from models.transformer import SwiGLUFFN, Transformer, TransformerBlock, count_parameters
+from models._native_dispatch import normalize_backend_keys
+
+
+def _tokens(cfg, b=2, s=16, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg["vocab_size"], (b, s), generator=g)
+
+
+class TestTransformer:
+    def test_tied_head_shares_storage(self, small_cfg):
+        m = Transformer(small_cfg)
+        assert m.head.weight.data_ptr() == m.embed.weight.data_ptr()
+
+    def test_untied_head(self, small_cfg):
+        m = Transformer({**small_cfg, "weight_tying": False})
+        assert m.head.weight.data_ptr() != m.embed.weight.data_ptr()
+
+    def test_nested_config(self, small_cfg):
+        m = Transformer({"model": dict(small_cfg)})
+        assert len(m.layers) == small_cfg["n_layers"]
+
+    def test_shapes(self, small_cfg):
+        m = Transformer(small_cfg)
+        t = _tokens(small_cfg)
+        logits = m(t, use_cache=False)
+        assert logits.shape == (2, 16, small_cfg["vocab_size"])
+        lg, h = m.forward_with_hidden(t)
+        assert h.shape == (2, 16, small_cfg["dim"])
+        assert torch.allclose(lg, logits, atol=1e-6)
+
+    def test_dense_then_moe(self, small_cfg):
+        m = Transformer(small_cfg)
+        assert isinstance(m.layers[0].ffn, SwiGLUFFN)
+        assert isinstance(m.layers[1].ffn, DeepSeekMoE)
+        assert len(list(m.moe_layers())) == small_cfg["n_layers"] - small_cfg["n_dense_layers"]
+
+    @pytest.mark.parametrize("impl", ["sdpa", "manual"])
+    def test_chunked_prefill_equals_full(self, small_cfg, impl):
+        torch.manual_seed(0)
+        m = Transformer({**small_cfg, "attn_impl": impl}).eval()
+        t = _tokens(small_cfg, s=24)
+        full = m(t, use_cache=False)
+        m.reset_cache()
+        a = m(t[:, :10], start_pos=0, use_cache=True)
+        b = m(t[:, 10:], start_pos=10, use_cache=True)
+        assert torch.allclose(torch.cat([a, b], 1), full, atol=1e-5)
+
+    def test_single_token_decode_matches(self, small_cfg):
+        torch.manual_seed(1)
+        m = Transformer(small_cfg).eval()
+        t = _tokens(small_cfg, s=12)
+        full = m(t, use_cache=False)
+        m.reset_cache()
+        m(t[:, :11], start_pos=0, use_cache=True)
+        last = m(t[:, 11:], start_pos=11, use_cache=True)
+        assert torch.allclose(last[:, 0], full[:, 11], atol=1e-5)
+
+    def test_backward_reaches_all_params(self, small_cfg):
+        torch.manual_seed(0)
+        m = Transformer(small_cfg)
+        t = _tokens(small_cfg, s=32)
+        loss = F.cross_entropy(m(t, use_cache=False).flatten(0, 1), t.flatten())
+        loss.backward()
+        for name, p in m.named_parameters():
+            if ".experts." in name:
+                continue  # an expert may receive no tokens
+            assert p.grad is not None and torch.isfinite(p.grad).all(), name
+
+    def test_reset_cache(self, small_cfg):
+        m = Transformer(small_cfg)
+        m(_tokens(small_cfg), use_cache=True)
+        assert all(l.attn.kv_cache is not None for l in m.layers)
+        m.reset_cache()
+        assert all(l.attn.kv_cache is None and l.attn._cache_batch == 0 for l in m.layers)
+
+    def test_causal(self, small_cfg):
+        torch.manual_seed(0)
+        m = Transformer(small_cfg).eval()
+        t = _tokens(small_cfg, s=16)
+        a = m(t, use_cache=False)
+        t2 = t.clone()
+        t2[:, 10:] = (t2[:, 10:] + 7) % small_cfg["vocab_size"]
+        b = m(t2, use_cache=False)
+        assert torch.allclose(a[:, :10], b[:, :10], atol=1e-5)
+        assert not torch.allclose(a[:, 10:], b[:, 10:])
+
+
+class TestMLA:
+    def test_sdpa_and_absorbed_agree(self, small_cfg):
+        torch.manual_seed(0)
+        a = MultiHeadLatentAttention(small_cfg)
+        b = MultiHeadLatentAttention({**small_cfg, "attn_impl": "manual"})
+        b.load_state_dict(a.state_dict())
+        x = torch.randn(2, 16, small_cfg["dim"])
+        mask = Transformer(small_cfg)._build_causal_mask(16, 16, 0, "cpu")
+        assert torch.allclose(a(x, 0, mask, False), b(x, 0, mask, False), atol=1e-5)
+
+    def test_cache_growth_and_reset(self, small_cfg):
+        a = MultiHeadLatentAttention(small_cfg)
+        a._ensure_cache(3, "cpu", torch.float32)
+        assert a._cache_batch == 16
+        a._ensure_cache(20, "cpu", torch.float32)
+        assert a._cache_batch == 32
+        assert a.kv_cache.shape == (32, small_cfg["max_seq_len"], small_cfg["kv_lora_rank"])
+        a.reset_cache()
+        assert a.kv_cache is None
+
+    def test_rope_table_growth(self, small_cfg):
+        a = MultiHeadLatentAttention({**small_cfg, "max_seq_len": 512})
+        a._extend_rope(10, "cpu")
+        assert a._rope_seq_len == 64
+        a._extend_rope(100, "cpu")
+        assert a._rope_seq_len == 128
+        a._extend_rope(500, "cpu")
+        assert a._rope_seq_len == 500
+
+    def test_overflow_raises(self, small_cfg):
+        a = MultiHeadLatentAttention(small_cfg)
+        with pytest.raises(RuntimeError, match="exceeds max_seq_len"):
+            a(torch.randn(1, 4, small_cfg["dim"]), start_pos=small_cfg["max_seq_len"] - 2)
+
+    def test_softmax_scale_rules(self, small_cfg):
+        base = MultiHeadLatentAttention(small_cfg)
+        assert math.isclose(base.softmax_scale, (8 + 4) ** -0.5)
+        yarn = MultiHeadLatentAttention({**small_cfg, "rope_factor": 4.0, "mscale": 1.0, "max_seq_len": 8192})
+        ms = 0.1 * math.log(4.0) + 1.0
+        assert math.isclose(yarn.mscale, ms)
+        assert math.isclose(yarn.softmax_scale, (12 ** -0.5) * ms ** 2)
+        short = MultiHeadLatentAttention({**small_cfg, "rope_factor": 4.0})
+        assert math.isclose(short.softmax_scale, 12 ** -0.5)
+
+    def test_q_lora(self, small_cfg):
+        a = MultiHeadLatentAttention({**small_cfg, "q_lora_rank": 32})
+        assert hasattr(a, "wq_a") and hasattr(a, "wq_b") and not hasattr(a, "wq")
+        assert a(torch.randn(1, 4, small_cfg["dim"]), use_cache=False).shape == (1, 4, small_cfg["dim"])
+
+
+class TestMoE:
+    def test_gate_shapes_and_normalisation(self, small_cfg):
+        g = AuxLossFreeGate(small_cfg)
+        w, idx = g(torch.randn(50, small_cfg["dim"]))
+        assert w.shape == idx.shape == (50, small_cfg["n_activated_experts"])
+        assert torch.allclose(w.sum(-1), torch.ones(50), atol=1e-5)
+
+    def test_bias_selects_but_does_not_weight(self, small_cfg):
+        g = AuxLossFreeGate(small_cfg)
+        x = torch.randn(64, small_cfg["dim"])
+        g.bias[2] = 10.0
+        w, idx = g(x)
+        assert (idx == 2).any(dim=-1).all()
+        scores = torch.sigmoid(x @ g.weight.t())
+        picked = scores.gather(1, idx)
+        assert torch.allclose(w, picked / picked.sum(-1, keepdim=True), atol=1e-6)
+
+    def test_bias_is_buffer(self, small_cfg):
+        g = AuxLossFreeGate(small_cfg)
+        assert all(p is not g.bias for p in g.parameters())
+        assert "bias" in g.state_dict() and g.state_dict()["bias"].dtype == torch.float32
+
+    def test_update_bias_deadband(self):
+        g = AuxLossFreeGate({"dim": 8, "n_activated_experts": 2, "n_routed_experts": 4})
+        g.update_bias(torch.tensor([10.0, 5.0, 5.0, 0.0]), speed=0.01)
+        assert g.bias[0] < 0 and g.bias[3] > 0 and g.bias[1] == 0 and g.bias[2] == 0
+
+    def test_matches_dense_oracle(self, small_cfg):
+        torch.manual_seed(0)
+        moe = DeepSeekMoE(small_cfg)
+        x = torch.randn(2, 8, small_cfg["dim"])
+        out = moe(x)
+        flat = x.view(-1, small_cfg["dim"])
+        w, idx = moe.gate(flat)
+        ref = torch.zeros_like(flat)
+        for t in range(flat.size(0)):
+            for j in range(idx.size(1)):
+                ref[t] += w[t, j] * moe.experts[int(idx[t, j])](flat[t:t + 1])[0]
+            ref[t] += moe.shared_experts[0](flat[t:t + 1])[0]
+        assert torch.allclose(out.view(-1, small_cfg["dim"]), ref, atol=1e-5)
+
+    def test_balance_metric(self, small_cfg):
+        moe = DeepSeekMoE(small_cfg)
+        assert moe.get_load_balance_loss().item() == 0.0
+        moe(torch.randn(2, 8, small_cfg["dim"]))
+        v = moe.get_load_balance_loss()
+        assert v.ndim == 0 and v > 0
+
+    def test_update_gate_bias_from_last_forward(self, small_cfg):
+        moe = DeepSeekMoE(small_cfg)
+        moe(torch.randn(1, 4, small_cfg["dim"]))
+        moe._last_indices = torch.zeros(128, 2, dtype=torch.long)
+        before = moe.gate.bias.clone()
+        moe.update_gate_bias(speed=0.1)
+        assert moe.gate.bias[0] < before[0] and (moe.gate.bias[1:] > before[1:]).any()
+
+    def test_stacked_views_track_weights(self, small_cfg):
+        moe = DeepSeekMoE(small_cfg)
+        with torch.no_grad():
+            moe.experts[1].w1.weight.add_(1.0)
+        assert torch.equal(moe._stacked_w1[1], moe.experts[1].w1.weight)
+        assert torch.equal(moe._shared_w1[0], moe.shared_experts[0].w1.weight)
+
+    def test_legacy_dispatch_values(self, small_cfg):
+        cfg = {**small_cfg, "moe_dispatch": "triton_grouped", "attn_impl": "triton"}
+        normalize_backend_keys(cfg, log=lambda s: None)
+        assert cfg["moe_dispatch"] == "grouped" and cfg["attn_impl"] == "native"
+        with pytest.raises(ValueError):
+            normalize_backend_keys({**small_cfg, "attn_impl": "flash"}, log=lambda s: None)
+
+
+class TestMTP:
+    def test_block_and_module(self, small_cfg):
+        blk = MTPBlock(small_cfg)
+        h = torch.randn(2, 6, small_cfg["dim"])
+        assert blk(h, torch.randn_like(h)).shape == h.shape
+        mod = MTPModule(small_cfg)
+        with pytest.raises(RuntimeError):
+            mod(h, h)
+        mod.set_output_head(torch.nn.Linear(small_cfg["dim"], small_cfg["vocab_size"], bias=False))
+        lg, hn = mod(h, h)
+        assert lg.shape == (2, 6, small_cfg["vocab_size"])
+        with pytest.raises(ValueError):
+            mod(h, h[:, :3])
+
+    def test_wrapper_alignment_and_loss(self, small_cfg):
+        torch.manual_seed(0)
+        m = Transformer(small_cfg)
+        mt = MultiTokenPrediction(small_cfg, m)
+        t = _tokens(small_cfg, s=16)
+        main, pairs = mt(t)
+        assert len(pairs) == 1
+        lg, tgt = pairs[0]
+        assert lg.shape[1] == 16 - 2 and torch.equal(tgt, t[:, 2:])
+        total, ml, mtp = mt.compute_loss(main, t, pairs)
+        assert torch.allclose(total, ml + 0.3 * mtp)
+        total.backward()
+        assert m.embed.weight.grad is not None
+        assert m.layers[0].attn.wkv_a.weight.grad.abs().sum() > 0
+
+    def test_depth_two_chain(self, small_cfg):
+        cfg = {**small_cfg, "mtp_depth": 2}
+        mt = MultiTokenPrediction(cfg, Transformer(cfg))
+        _, pairs = mt(_tokens(cfg, s=12))
+        assert [p[0].shape[1] for p in pairs] == [10, 9]
+
+    def test_short_sequence(self, small_cfg):
+        mt = MultiTokenPrediction(small_cfg, Transformer(small_cfg))
+        main, pairs = mt(_tokens(small_cfg, s=2))
+        assert pairs == []
+        total, ml, mtp = mt.compute_loss(main, _tokens(small_cfg, s=2), pairs)
+        assert mtp.item() == 0.0
+
+    def test_nested_mtp_config(self, small_cfg):
+        cfg = {k: v for k, v in small_cfg.items() if k not in ("mtp_depth", "mtp_loss_weight")}
+        mt = MultiTokenPrediction({"model": cfg, "mtp": {"depth": 2, "weight": 0.5}}, Transformer(cfg))
+        assert mt.depth == 2 and mt.mtp_weight == 0.5
+
+
+class TestGenerate:
+    def test_lengths_and_train_mode(self, small_cfg):
+        m = Transformer(small_cfg)
+        m.train()
+        out = m.generate(_tokens(small_cfg, b=1, s=5), max_new_tokens=7, temperature=0)
+        assert out.shape == (1, 12) and m.training
+
+    def test_greedy_is_deterministic(self, small_cfg):
+        m = Transformer(small_cfg)
+        p = _tokens(small_cfg, b=2, s=4)
+        assert torch.equal(m.generate(p, 6, temperature=0), m.generate(p, 6, temperature=0))
+
+    def test_eos_and_max_len(self, small_cfg):
+        m = Transformer(small_cfg)
+        p = _tokens(small_cfg, b=1, s=4)
+        first = m.generate(p, 1, temperature=0)[0, -1].item()
+        assert m.generate(p, 10, temperature=0, eos_token_id=first).shape[1] == 5
+        long = m.generate(_tokens(small_cfg, b=1, s=60), 50, temperature=0)
+        assert long.shape[1] == small_cfg["max_seq_len"]
+
+    def test_negative_temperature(self, small_cfg):
+        with pytest.raises(ValueError):
+            Transformer(small_cfg).generate(_tokens(small_cfg, b=1, s=3), 2, temperature=-1.0)
+
+    def test_sample_rules(self):
+        logits = torch.tensor([[0.0, 5.0, 1.0, -2.0]])
+        assert Transformer._sample(logits, 0.0, 1.0, 0).item() == 1
+        torch.manual_seed(0)
+        assert all(Transformer._sample(logits, 1.0, 1.0, 1).item() == 1 for _ in range(20))
+        # top_p smaller than the top token's mass keeps only that token.
+        assert all(Transformer._sample(logits, 1.0, 0.5, 0).item() == 1 for _ in range(20))
+
+
+def test_count_parameters_dedups(small_cfg):
+    m = Transformer(small_cfg)
+    total, trainable = count_parameters(m)
+    assert total == trainable == sum(p.numel() for p in set(m.parameters()))
+    untied, _ = count_parameters(Transformer({**small_cfg, "weight_tying": False}))
+    assert untied - total == small_cfg["vocab_size"] * small_cfg["dim"]

@@ -1,0 +1,162 @@
+"""CPU tests of the trainer, dataset, schedule, checkpoint round trips and NaN guard."""
+import json
+from dataclasses import asdict
+from unittest.mock import patch
+
+import pytest
+import torch
+import yaml
+
+from models.transformer import count_parameters
+from training.pretrain import (Pretrainer, PretrainDataset, TrainingConfig, config_from_yaml,
+                               make_warmup_cosine_lambda)
+
+
+def _cfg(small_cfg, ckpt, **kw):
+    base = dict(model_config=small_cfg, data_path="/nonexistent", checkpoint_dir=str(ckpt),
+                max_seq_len=small_cfg["max_seq_len"], vocab_size=small_cfg["vocab_size"], batch_size=2,
+                gradient_accumulation_steps=2, max_steps=4, warmup_steps=1, lr=1e-3, weight_decay=0.0,
+                grad_checkpoint=False, compile_model=False, nan_guard=False, save_every=10, log_every=10)
+    base.update(kw)
+    return TrainingConfig(**base)
+
+
+def test_config_defaults_and_serialisable():
+    c = TrainingConfig()
+    assert (c.lr, c.weight_decay, c.beta1, c.beta2, c.max_grad_norm) == (2.2e-4, 0.1, 0.9, 0.95, 1.0)
+    assert c.bias_update_every == 10 and c.mtp_weight == 0.0 and c.seed == 42
+    json.dumps(asdict(c))
+
+
+def test_schedule_points():
+    f = make_warmup_cosine_lambda(10, 110, 0.1)
+    assert f(0) == 0.0 and f(5) == 0.5 and f(10) == 1.0
+    assert abs(f(60) - (0.1 + 0.9 * 0.5)) < 1e-9
+    assert f(110) == 0.1 and f(500) == 0.1
+    assert make_warmup_cosine_lambda(0, 10, 0.2)(0) == 1.0
+
+
+class TestDataset:
+    def test_single_file_windows(self, token_file):
+        ds = PretrainDataset(token_file, 32, 1024)
+        assert len(ds) == (512 - 1) // 32
+        x, y = ds[3]
+        assert x.shape == (32,) and torch.equal(x[1:], y[:-1])
+
+    def test_shards_cross_boundaries(self, shard_dir):
+        ds = PretrainDataset(shard_dir, 50, 1024)
+        assert len(ds) == (384 - 1) // 50
+        x, y = ds[2]   # tokens 100..150 span shard 0 and 1
+        assert torch.equal(x, torch.arange(100, 150)) and torch.equal(y, torch.arange(101, 151))
+
+    def test_locate(self, shard_dir):
+        ds = PretrainDataset(shard_dir, 50, 1024)
+        assert ds._locate(0) == (0, 0) and ds._locate(128) == (1, 0) and ds._locate(383) == (2, 127)
+        for bad in (-1, 384):
+            with pytest.raises(IndexError):
+                ds._locate(bad)
+
+    def test_missing(self):
+        with pytest.raises(FileNotFoundError):
+            PretrainDataset("/no/such/file.bin", 8, 10)
+
+
+class TestPretrainer:
+    def test_construct_and_groups(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir))
+        assert tr.mtp_wrapper is None and tr.device.type == "cpu"
+        n_opt = sum(p.numel() for g in tr.optimizer.param_groups for p in g["params"])
+        assert n_opt == sum(p.numel() for p in set(tr.model.parameters()))
+        assert all(p.dim() >= 2 for p in tr.optimizer.param_groups[0]["params"])
+        assert all(p.dim() < 2 for p in tr.optimizer.param_groups[1]["params"])
+
+    def test_mtp_enabled_only_with_weight(self, small_cfg, tmp_dir):
+        assert Pretrainer(_cfg(small_cfg, tmp_dir, mtp_weight=0.3)).mtp_wrapper is not None
+
+    def test_mup(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir, mup_lr=True))
+        total, _ = count_parameters(tr.raw_model)
+        assert abs(tr.config.lr - 6e-4 * (757226496 / total) ** 0.5) < 1e-12
+
+    def test_scheduler_horizon(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir, max_steps=8, warmup_steps=0, min_lr_ratio=0.1))
+        t = torch.randint(0, small_cfg["vocab_size"], (2, small_cfg["max_seq_len"]))
+        for i in range(8):
+            tr.train_step(t, t, i)
+        assert tr._opt_steps == 4
+        assert abs(tr.scheduler.get_last_lr()[0] - 1e-3 * 0.1) < 1e-12
+
+    def test_step_updates_and_bias(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir, gradient_accumulation_steps=1, bias_update_every=1, warmup_steps=0,
+                             mtp_weight=0.3))
+        before = {n: p.detach().clone() for n, p in tr.raw_model.named_parameters()}
+        bias0 = [m.gate.bias.clone() for m in tr.raw_model.moe_layers()]
+        t = torch.randint(0, small_cfg["vocab_size"], (2, 32))
+        out = tr.train_step(t, t, 0)
+        assert torch.isfinite(out["loss"]) and out["mtp_loss"] is not None
+        changed = [n for n, p in tr.raw_model.named_parameters() if not torch.equal(p, before[n])]
+        assert "layers.0.attn.wkv_a.weight" in changed
+        assert any(not torch.equal(b, m.gate.bias) for b, m in zip(bias0, tr.raw_model.moe_layers()))
+
+    def test_nan_guard(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir, nan_guard=True, gradient_accumulation_steps=1))
+        t = torch.randint(0, small_cfg["vocab_size"], (1, 4))
+        bad = lambda *a, **k: torch.full((1, 4, small_cfg["vocab_size"]), float("nan"))
+        with patch.object(tr.model, "forward", side_effect=bad):
+            assert tr.train_step(t, t, 0) is None
+
+    def test_nan_streak_rolls_back(self, small_cfg, tmp_dir, token_file):
+        cfg = _cfg(small_cfg, tmp_dir, nan_guard=True, nan_guard_max_consecutive=2, gradient_accumulation_steps=1,
+                   data_path=token_file, max_seq_len=16, max_steps=3)
+        tr = Pretrainer(cfg)
+        tr.save_checkpoint(1)
+        calls = []
+        real = tr.load_checkpoint
+        bad = lambda *a, **k: torch.full((2, 16, small_cfg["vocab_size"]), float("nan"))
+
+        def spy(step):
+            calls.append(step)
+            tr.model.forward = tr.model.__class__.forward.__get__(tr.model)
+            return real(step)
+
+        with patch.object(tr, "load_checkpoint", side_effect=spy):
+            tr.model.forward = bad
+            tr.train()
+        assert calls and calls[0] == 1
+
+    def test_nan_without_checkpoint_raises(self, small_cfg, tmp_dir, token_file):
+        cfg = _cfg(small_cfg, tmp_dir, nan_guard=True, nan_guard_max_consecutive=1, gradient_accumulation_steps=1,
+                   data_path=token_file, max_seq_len=16, max_steps=3)
+        tr = Pretrainer(cfg)
+        tr.model.forward = lambda *a, **k: torch.full((2, 16, small_cfg["vocab_size"]), float("nan"))
+        with pytest.raises(RuntimeError, match="no checkpoint"):
+            tr.train()
+
+
+class TestCheckpointRoundTrip:
+    def test_weights_optimizer_meta(self, small_cfg, tmp_dir):
+        tr = Pretrainer(_cfg(small_cfg, tmp_dir, mtp_weight=0.3, gradient_accumulation_steps=1))
+        t = torch.randint(0, small_cfg["vocab_size"], (2, 32))
+        tr.train_step(t, t, 0)
+        tr.save_checkpoint(7)
+        meta = json.load(open(tmp_dir / "meta_step_7.json"))
+        assert meta["step"] == 7 and meta["opt_steps"] == 1 and meta["has_mtp"] is True
+        from safetensors.torch import load_file
+        keys = load_file(str(tmp_dir / "model_step_7.safetensors")).keys()
+        assert "head.weight" not in keys and any(k.startswith("mtp.mtp_modules.0.block.") for k in keys)
+        assert all(v.dtype == torch.float32 for v in load_file(str(tmp_dir / "model_step_7.safetensors")).values())
+        tr2 = Pretrainer(_cfg(small_cfg, tmp_dir, mtp_weight=0.3, gradient_accumulation_steps=1))
+        assert tr2.load_checkpoint(7) == 7 and tr2._opt_steps == 1
+        for (n, a), (_, b) in zip(tr.mtp_wrapper.named_parameters(), tr2.mtp_wrapper.named_parameters()):
+            assert torch.equal(a, b), n
+        assert tr2.raw_model.head.weight.data_ptr() == tr2.raw_model.embed.weight.data_ptr()
+
+
+def test_yaml_mapping(small_cfg, tmp_dir):
+    y = {"model": small_cfg, "training": {"micro_batch_size": 3, "total_steps": 9, "grad_clip": 0.5,
+                                          "mtp_loss_weight": 0.3, "log_interval": 7, "save_interval": 11},
+         "data": {"train_data_path": "/d"}}
+    c = config_from_yaml(y)
+    assert (c.batch_size, c.max_steps, c.max_grad_norm, c.mtp_weight, c.log_every, c.save_every) == (3, 9, 0.5, 0.3, 7, 11)
+    assert c.data_path == "/d" and c.max_seq_len == small_cfg["max_seq_len"]
+    assert config_from_yaml(y, no_checkpoint=True).grad_checkpoint is False

@@ -1,0 +1,109 @@
+"""CPU tests of the checkpoint manager and memory estimator."""
+import os
+from unittest.mock import patch
+
+import pytest
+import torch
+
+from models.transformer import Transformer
+from utils.checkpoint import CheckpointManager
+from utils import memory
+
+
+def _opt(m):
+    return torch.optim.AdamW(m.parameters(), lr=1e-3)
+
+
+class TestCheckpointManager:
+    def test_save_load_and_latest(self, small_cfg, tmp_dir):
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        mgr.save(m, _opt(m), 3, extra_meta={"step": 99, "x": 1})
+        mgr.save(m, _opt(m), 5)
+        assert mgr.latest_step() == 5
+        m2 = Transformer(small_cfg)
+        meta = mgr.load(m2, 3, device="cpu", optimizer=_opt(m2), strict=False)
+        assert meta == {"step": 3, "x": 1}
+        for a, b in zip(m.state_dict().values(), m2.state_dict().values()):
+            assert torch.equal(a, b)
+
+    def test_incomplete_ignored(self, small_cfg, tmp_dir):
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        mgr.save(m, _opt(m), 2)
+        mgr.save(m, _opt(m), 4)
+        os.remove(tmp_dir / "optim_step_4.pt")
+        assert mgr.latest_step() == 2
+
+    def test_missing_raises(self, small_cfg, tmp_dir):
+        with pytest.raises(FileNotFoundError):
+            CheckpointManager(str(tmp_dir)).load(Transformer(small_cfg), 1, device="cpu")
+
+    def test_tied_saved_once(self, small_cfg, tmp_dir):
+        from safetensors.torch import load_file
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        mgr.save(m, _opt(m), 1)
+        keys = load_file(str(tmp_dir / "model_step_1.safetensors")).keys()
+        assert ("embed.weight" in keys) != ("head.weight" in keys)
+        m2 = Transformer(small_cfg)
+        mgr.load(m2, 1, device="cpu", strict=False)
+        assert m2.head.weight.data_ptr() == m2.embed.weight.data_ptr()
+        assert torch.equal(m2.head.weight, m.head.weight)
+
+    def test_crash_leaves_no_temp(self, small_cfg, tmp_dir):
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        with patch("utils.checkpoint.save_file", side_effect=OSError("disk full")):
+            with pytest.raises(OSError):
+                mgr.save(m, _opt(m), 1)
+        assert list(tmp_dir.iterdir()) == []
+        assert mgr.latest_step() is None
+
+    def test_strict(self, small_cfg, tmp_dir):
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        state = dict(m.state_dict())
+        state["bogus"] = torch.zeros(1)
+        mgr.save(m, _opt(m), 1, state_dict=state)
+        with pytest.raises(RuntimeError, match="missing|unexpected"):
+            mgr.load(Transformer(small_cfg), 1, device="cpu", strict=True)
+        mgr.load(Transformer(small_cfg), 1, device="cpu", strict=False)
+        untied = {**small_cfg, "weight_tying": False}
+        mu = Transformer(untied)
+        mgr.save(mu, _opt(mu), 2)
+        mgr.load(Transformer(untied), 2, device="cpu", strict=True)
+
+
+class TestMemory:
+    def test_components(self, small_cfg):
+        m = Transformer(small_cfg)
+        n = sum(p.numel() for p in set(m.parameters()))
+        assert memory._parameter_bytes(m) == 2 * n and memory._optimiser_bytes(m) == 12 * n
+        assert memory._kv_cache_bytes(m, 10, 2) == 2 * 10 * (16 + 4) * 2 * small_cfg["n_layers"]
+        assert memory._activation_bytes(10, 2, 64, 2, True) == 24 * 10 * 2 * 64 * 2 * 2
+        assert memory._activation_bytes(10, 2, 64, 2, False) == 36 * 10 * 2 * 64 * 2 * 2
+        assert memory._infer_dim_n_layers(m) == (64, 2)
+        assert memory._infer_dim_n_layers(torch.nn.Linear(2, 2)) == (0, 0)
+
+    def test_estimates(self, small_cfg):
+        m = Transformer(small_cfg)
+        a = memory.estimate_model_memory_gb(m, 64, 1, overhead_gb=0.0)
+        b = memory.estimate_model_memory_gb(m, 64, 8, overhead_gb=0.0)
+        inf = memory.estimate_model_memory_gb(m, 64, 8, overhead_gb=0.0, inference=True)
+        assert 0 < a < b and inf < b
+        assert memory._detect_overhead_gb() == 2.0
+
+    def test_fit_assertion(self, monkeypatch):
+        memory.assert_fits_in_available_gpu(1e9)  # no CUDA: no-op
+        class Props:
+            total_memory = 8 * 1024 ** 3
+        monkeypatch.setattr(memory.torch.cuda, "is_available", lambda: True)
+        monkeypatch.setattr(memory.torch.cuda, "get_device_properties", lambda i: Props())
+        with pytest.raises(RuntimeError):
+            memory.assert_fits_in_available_gpu(7.5, safety_margin_gb=1.0)
+        memory.assert_fits_in_available_gpu(6.0, safety_margin_gb=1.0)
+
+    def test_sharded_estimate_shrinks(self, small_cfg):
+        m = Transformer(small_cfg)
+        assert memory.estimate_sharded_training_gb(m, 64, 2, 4, 4) < memory.estimate_sharded_training_gb(m, 64, 2)
