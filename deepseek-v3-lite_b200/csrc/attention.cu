@@ -1,0 +1,595 @@
+// MLA attention kernels.
+//
+// fa_fwd / fa_bwd: causal (global-position) flash attention over the
+// materialised formulation: Q, K [BH, S, DQK] (DQK = dn + dr rounded up to a
+// multiple of 16, zero padded), V [BH, S, DV].  Online softmax in the log2
+// domain; the forward stores L = m + log2(l) per query row, the backward
+// recomputes P from it (FlashAttention-2 schedule: one CTA per 64-key block,
+// dK/dV in registers, dQ accumulated with fp32 atomics).  These use the
+// warp-level mma.sync bf16 tensor-core path.
+//
+// latent_decode: absorbed-formulation decode over the latent cache with a
+// per-row cache length, split over the sequence (split-K) with a second
+// combine pass -- the decode step reads each cached latent row once per head
+// group instead of materialising K/V.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dsv3 {
+
+namespace {
+
+typedef __nv_bfloat16 bf16;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const int n = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, bf16 in, fp32 accumulate.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int BM = 64;
+constexpr int BN = 64;
+
+// Copy a [rows x D] bf16 tile (row stride D in global) into smem with row
+// stride SD, zero-filling rows >= valid_rows.
+template <int D, int SD>
+__device__ __forceinline__ void load_tile_async(bf16* s, const bf16* g, int rows, int valid_rows, int tid, int nthr) {
+  constexpr int CH = D / 8;
+  for (int c = tid; c < rows * CH; c += nthr) {
+    const int r = c / CH, cc = (c % CH) * 8;
+    const bool ok = r < valid_rows;
+    cp_async16(s + r * SD + cc, g + (size_t)(ok ? r : 0) * D + cc, ok);
+  }
+}
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(128) fa_fwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                     const bf16* __restrict__ V, bf16* __restrict__ O,
+                                                     float* __restrict__ L, int Sq, int Sk, int q_off,
+                                                     float scale_log2, int causal) {
+  constexpr int QS = DQK + 8, VS = DV + 8;
+  extern __shared__ __align__(16) uint8_t fa_smem[];
+  bf16* sQ = reinterpret_cast<bf16*>(fa_smem);
+  bf16* sK = sQ + BM * QS;
+  bf16* sV = sK + 2 * BN * QS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bh = blockIdx.y, m0 = blockIdx.x * BM;
+  const bf16* Qb = Q + (size_t)bh * Sq * DQK;
+  const bf16* Kb = K + (size_t)bh * Sk * DQK;
+  const bf16* Vb = V + (size_t)bh * Sk * DV;
+
+  load_tile_async<DQK, QS>(sQ, Qb + (size_t)m0 * DQK, BM, Sq - m0, tid, 128);
+  const int n_end = causal ? min(Sk, q_off + m0 + BM) : Sk;
+  const int nblocks = (n_end + BN - 1) / BN;
+  if (nblocks > 0) {
+    load_tile_async<DQK, QS>(sK, Kb, BN, Sk, tid, 128);
+    load_tile_async<DV, VS>(sV, Vb, BN, Sk, tid, 128);
+  }
+  cp_async_commit();
+
+  float o[DV / 8][4];
+#pragma unroll
+  for (int i = 0; i < DV / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  const int g = lane >> 2, tig = lane & 3;
+  const int qrow0 = m0 + warp * 16 + g;  // rows qrow0 and qrow0 + 8
+
+  for (int nb = 0; nb < nblocks; ++nb) {
+    const int st = nb & 1;
+    if (nb + 1 < nblocks) {
+      const int n1 = (nb + 1) * BN;
+      load_tile_async<DQK, QS>(sK + (st ^ 1) * BN * QS, Kb + (size_t)n1 * DQK, BN, Sk - n1, tid, 128);
+      load_tile_async<DV, VS>(sV + (st ^ 1) * BN * VS, Vb + (size_t)n1 * DV, BN, Sk - n1, tid, 128);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const bf16* k_s = sK + st * BN * QS;
+    const bf16* v_s = sV + st * BN * VS;
+
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DQK / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, sQ + (warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * QS + kk * 16 + 8 * (lane >> 4));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b[4];
+        ldsm_x4(b, k_s + (np * 16 + (lane & 7) + 8 * (lane >> 4)) * QS + kk * 16 + 8 * ((lane >> 3) & 1));
+        mma16816(s[2 * np], a, b[0], b[1]);
+        mma16816(s[2 * np + 1], a, b[2], b[3]);
+      }
+    }
+    // scale + mask, then online softmax per row (rows g and g + 8 of the warp)
+    const int n0 = nb * BN;
+    float mx[2] = {mrow[0], mrow[1]};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = n0 + j * 8 + 2 * tig + (e & 1);
+        const int qr = qrow0 + (e >> 1) * 8;
+        float v = s[j][e] * scale_log2;
+        if (col >= Sk || (causal && col > q_off + qr)) v = -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float corr[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) corr[r] = mx[r] == -INFINITY ? 1.f : exp2f(mrow[r] - mx[r]);
+    uint32_t pa[4][4];  // P as A fragments, 4 k16 chunks over the 64 keys
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float m = mx[e >> 1];
+        p[e] = m == -INFINITY ? 0.f : exp2f(s[j][e] - m);
+        rs[e >> 1] += p[e];
+      }
+      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(p[0], p[1]);
+      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(p[2], p[3]);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+      lrow[r] = lrow[r] * corr[r] + rs[r];
+      mrow[r] = mx[r];
+    }
+#pragma unroll
+    for (int i = 0; i < DV / 8; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[0];
+      o[i][2] *= corr[1];
+      o[i][3] *= corr[1];
+    }
+    // O += P V   (A fragment order: a0 = rows g / k lo, a1 = rows g+8 / k lo, a2, a3 = k hi)
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t a[4] = {pa[kc][0], pa[kc][1], pa[kc][2], pa[kc][3]};
+#pragma unroll
+      for (int dp = 0; dp < DV / 16; ++dp) {
+        uint32_t b[4];
+        ldsm_x4_t(b, v_s + (kc * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * VS + dp * 16 + 8 * (lane >> 4));
+        mma16816(o[2 * dp], a, b[0], b[1]);
+        mma16816(o[2 * dp + 1], a, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  bf16* Ob = O + (size_t)bh * Sq * DV;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qr = qrow0 + r * 8;
+    if (qr >= Sq) continue;
+    const float inv = lrow[r] > 0.f ? 1.f / lrow[r] : 0.f;
+#pragma unroll
+    for (int i = 0; i < DV / 8; ++i) {
+      const int col = i * 8 + 2 * tig;
+      *reinterpret_cast<uint32_t*>(Ob + (size_t)qr * DV + col) = pack_bf16x2(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
+    }
+    if (tig == 0) L[(size_t)bh * Sq + qr] = lrow[r] > 0.f ? mrow[r] + log2f(lrow[r]) : -INFINITY;
+  }
+}
+
+// delta[row] = sum_d dO[row, d] * O[row, d]
+template <int DV>
+__global__ void fa_bwd_pre_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, float* __restrict__ delta,
+                                  long rows) {
+  const long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float acc = 0.f;
+  for (int c = lane; c < DV; c += 32) acc += __bfloat162float(O[r * DV + c]) * __bfloat162float(dO[r * DV + c]);
+  acc = warp_sum(acc);
+  if (lane == 0) delta[r] = acc;
+}
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(128) fa_bwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                     const bf16* __restrict__ V, const bf16* __restrict__ dO,
+                                                     const float* __restrict__ L, const float* __restrict__ delta,
+                                                     float* __restrict__ dQ, float* __restrict__ dK,
+                                                     float* __restrict__ dV, int Sq, int Sk, int q_off,
+                                                     float scale_log2, float scale, int causal) {
+  constexpr int QS = DQK + 8, VS = DV + 8, PS = BM + 8;
+  extern __shared__ __align__(16) uint8_t fa_smem[];
+  bf16* sK = reinterpret_cast<bf16*>(fa_smem);
+  bf16* sV = sK + BN * QS;
+  bf16* sQ = sV + BN * VS;
+  bf16* sdO = sQ + BM * QS;
+  bf16* sdS = sdO + BM * VS;  // dS^T [keys][queries]
+  float* sL = reinterpret_cast<float*>(sdS + BN * PS);
+  float* sD = sL + BM;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int bh = blockIdx.y, n0 = blockIdx.x * BN;
+  const bf16* Qb = Q + (size_t)bh * Sq * DQK;
+  const bf16* Kb = K + (size_t)bh * Sk * DQK;
+  const bf16* Vb = V + (size_t)bh * Sk * DV;
+  const bf16* dOb = dO + (size_t)bh * Sq * DV;
+
+  load_tile_async<DQK, QS>(sK, Kb + (size_t)n0 * DQK, BN, Sk - n0, tid, 128);
+  load_tile_async<DV, VS>(sV, Vb + (size_t)n0 * DV, BN, Sk - n0, tid, 128);
+  cp_async_commit();
+
+  float dk[DQK / 8][4], dv[DV / 8][4];
+#pragma unroll
+  for (int i = 0; i < DQK / 8; ++i) dk[i][0] = dk[i][1] = dk[i][2] = dk[i][3] = 0.f;
+#pragma unroll
+  for (int i = 0; i < DV / 8; ++i) dv[i][0] = dv[i][1] = dv[i][2] = dv[i][3] = 0.f;
+
+  // first query block that can see key n0: q_off + q >= n0
+  const int qstart = causal ? max(0, (n0 - q_off) / BM * BM) : 0;
+  const int key0 = n0 + warp * 16 + g;  // this thread's keys: key0, key0 + 8
+  for (int m0 = qstart; m0 < Sq; m0 += BM) {
+    load_tile_async<DQK, QS>(sQ, Qb + (size_t)m0 * DQK, BM, Sq - m0, tid, 128);
+    load_tile_async<DV, VS>(sdO, dOb + (size_t)m0 * DV, BM, Sq - m0, tid, 128);
+    cp_async_commit();
+    for (int i = tid; i < BM; i += 128) {
+      const bool ok = m0 + i < Sq;
+      sL[i] = ok ? L[(size_t)bh * Sq + m0 + i] : 0.f;
+      sD[i] = ok ? delta[(size_t)bh * Sq + m0 + i] : 0.f;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // S^T = K Q^T  (16 keys x 64 queries per warp)
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DQK / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, sK + (warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * QS + kk * 16 + 8 * (lane >> 4));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b[4];
+        ldsm_x4(b, sQ + (np * 16 + (lane & 7) + 8 * (lane >> 4)) * QS + kk * 16 + 8 * ((lane >> 3) & 1));
+        mma16816(s[2 * np], a, b[0], b[1]);
+        mma16816(s[2 * np + 1], a, b[2], b[3]);
+      }
+    }
+    // dP^T = V dO^T
+    float dp[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dp[j][0] = dp[j][1] = dp[j][2] = dp[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < DV / 16; ++kk) {
+      uint32_t a[4];
+      ldsm_x4(a, sV + (warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * VS + kk * 16 + 8 * (lane >> 4));
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t b[4];
+        ldsm_x4(b, sdO + (np * 16 + (lane & 7) + 8 * (lane >> 4)) * VS + kk * 16 + 8 * ((lane >> 3) & 1));
+        mma16816(dp[2 * np], a, b[0], b[1]);
+        mma16816(dp[2 * np + 1], a, b[2], b[3]);
+      }
+    }
+    // P^T, dS^T (register fragments reused as A operands)
+    uint32_t pa[4][4], dsa[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p[4], ds[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = m0 + j * 8 + 2 * tig + (e & 1);
+        const int key = key0 + (e >> 1) * 8;
+        const int qi = j * 8 + 2 * tig + (e & 1);
+        const bool valid = q < Sq && key < Sk && !(causal && key > q_off + q);
+        p[e] = valid ? exp2f(s[j][e] * scale_log2 - sL[qi]) : 0.f;
+        ds[e] = p[e] * (dp[j][e] - sD[qi]);
+      }
+      pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(p[0], p[1]);
+      pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(p[2], p[3]);
+      dsa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(ds[0], ds[1]);
+      dsa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
+      // stash dS^T for the dQ product
+      bf16* row0 = sdS + (warp * 16 + g) * PS + j * 8 + 2 * tig;
+      bf16* row1 = row0 + 8 * PS;
+      *reinterpret_cast<uint32_t*>(row0) = pack_bf16x2(ds[0], ds[1]);
+      *reinterpret_cast<uint32_t*>(row1) = pack_bf16x2(ds[2], ds[3]);
+    }
+    // dV += P^T dO ; dK += dS^T Q
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {
+      uint32_t a[4] = {pa[kc][0], pa[kc][1], pa[kc][2], pa[kc][3]};
+#pragma unroll
+      for (int d2 = 0; d2 < DV / 16; ++d2) {
+        uint32_t b[4];
+        ldsm_x4_t(b, sdO + (kc * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * VS + d2 * 16 + 8 * (lane >> 4));
+        mma16816(dv[2 * d2], a, b[0], b[1]);
+        mma16816(dv[2 * d2 + 1], a, b[2], b[3]);
+      }
+      uint32_t a2[4] = {dsa[kc][0], dsa[kc][1], dsa[kc][2], dsa[kc][3]};
+#pragma unroll
+      for (int d2 = 0; d2 < DQK / 16; ++d2) {
+        uint32_t b[4];
+        ldsm_x4_t(b, sQ + (kc * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * QS + d2 * 16 + 8 * (lane >> 4));
+        mma16816(dk[2 * d2], a2, b[0], b[1]);
+        mma16816(dk[2 * d2 + 1], a2, b[2], b[3]);
+      }
+    }
+    __syncthreads();
+    // dQ[q, :] += sum_keys dS[q, key] K[key, :]   (warp: 16 queries)
+    {
+      float dq[DQK / 8][4];
+#pragma unroll
+      for (int i = 0; i < DQK / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+#pragma unroll
+      for (int kc = 0; kc < 4; ++kc) {
+        uint32_t a[4];
+        ldsm_x4_t(a, sdS + (kc * 16 + (lane & 7) + 8 * (lane >> 4)) * PS + warp * 16 + 8 * ((lane >> 3) & 1));
+#pragma unroll
+        for (int d2 = 0; d2 < DQK / 16; ++d2) {
+          uint32_t b[4];
+          ldsm_x4_t(b, sK + (kc * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * QS + d2 * 16 + 8 * (lane >> 4));
+          mma16816(dq[2 * d2], a, b[0], b[1]);
+          mma16816(dq[2 * d2 + 1], a, b[2], b[3]);
+        }
+      }
+      float* dQb = dQ + (size_t)bh * Sq * DQK;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int q = m0 + warp * 16 + g + r * 8;
+        if (q >= Sq) continue;
+#pragma unroll
+        for (int i = 0; i < DQK / 8; ++i) {
+          atomicAdd(dQb + (size_t)q * DQK + i * 8 + 2 * tig, dq[i][2 * r] * scale);
+          atomicAdd(dQb + (size_t)q * DQK + i * 8 + 2 * tig + 1, dq[i][2 * r + 1] * scale);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  float* dKb = dK + (size_t)bh * Sk * DQK;
+  float* dVb = dV + (size_t)bh * Sk * DV;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int key = key0 + r * 8;
+    if (key >= Sk) continue;
+#pragma unroll
+    for (int i = 0; i < DQK / 8; ++i) {
+      dKb[(size_t)key * DQK + i * 8 + 2 * tig] = dk[i][2 * r] * scale;
+      dKb[(size_t)key * DQK + i * 8 + 2 * tig + 1] = dk[i][2 * r + 1] * scale;
+    }
+#pragma unroll
+    for (int i = 0; i < DV / 8; ++i) {
+      dVb[(size_t)key * DV + i * 8 + 2 * tig] = dv[i][2 * r];
+      dVb[(size_t)key * DV + i * 8 + 2 * tig + 1] = dv[i][2 * r + 1];
+    }
+  }
+}
+
+// ------------------------------------------------------------ latent decode
+// Absorbed decode: per (batch row b, head h): scores over cache rows
+// [0, len_b) = q_lat . kv + q_pe . pe, softmax, out = sum p * kv (latent R).
+// Split-K over the sequence: split s handles rows [s*chunk, (s+1)*chunk) and
+// writes (max, sum, partial out); a second kernel merges the splits.
+// One warp per (b, h, split); R <= 1024.
+__global__ void latent_decode_split_kernel(const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe,
+                                           const bf16* __restrict__ kv, const bf16* __restrict__ pe,
+                                           const int* __restrict__ lens, int H, int R, int dr, long kv_bs, long pe_bs,
+                                           int chunk, int nsplit, int BH, float scale, float* __restrict__ part_m,
+                                           float* __restrict__ part_l, float* __restrict__ part_o) {
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int split = warp_global % nsplit;
+  const int bh = warp_global / nsplit;
+  const int b = bh / H, h = bh % H;
+  if (bh >= BH) return;
+  const int len = lens[b];
+  const int r0 = split * chunk, r1 = min(len, r0 + chunk);
+  float ql[32], qp[4];  // R <= 1024 (32 per lane), dr <= 128
+  for (int i = 0; i < 32; ++i) ql[i] = (lane + 32 * i < R) ? __bfloat162float(q_lat[((size_t)b * H + h) * R + lane + 32 * i]) : 0.f;
+  for (int i = 0; i < 4; ++i) qp[i] = (lane + 32 * i < dr) ? __bfloat162float(q_pe[((size_t)b * H + h) * dr + lane + 32 * i]) : 0.f;
+  float m = -INFINITY, l = 0.f;
+  float acc[32];
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const bf16* kr = kv + (size_t)b * kv_bs + (size_t)r * R;
+    const bf16* pr = pe + (size_t)b * pe_bs + (size_t)r * dr;
+    float kvv[32];
+    float dot = 0.f;
+    for (int i = 0; i < 32; ++i) {
+      kvv[i] = (lane + 32 * i < R) ? __bfloat162float(kr[lane + 32 * i]) : 0.f;
+      dot += ql[i] * kvv[i];
+    }
+    for (int i = 0; i < 4; ++i) dot += (lane + 32 * i < dr) ? qp[i] * __bfloat162float(pr[lane + 32 * i]) : 0.f;
+    dot = warp_sum(dot) * scale;
+    const float nm = fmaxf(m, dot);
+    const float c = __expf(m - nm), p = __expf(dot - nm);
+    l = l * c + p;
+    for (int i = 0; i < 32; ++i) acc[i] = acc[i] * c + p * kvv[i];
+    m = nm;
+  }
+  const size_t pi = (size_t)bh * nsplit + split;
+  if (lane == 0) {
+    part_m[pi] = m;
+    part_l[pi] = l;
+  }
+  for (int i = 0; i < 32; ++i)
+    if (lane + 32 * i < R) part_o[pi * R + lane + 32 * i] = acc[i];
+}
+
+__global__ void latent_decode_merge_kernel(const float* __restrict__ part_m, const float* __restrict__ part_l,
+                                           const float* __restrict__ part_o, int nsplit, int R, int BH,
+                                           bf16* __restrict__ out) {
+  const int bh = blockIdx.x;
+  if (bh >= BH) return;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_m[(size_t)bh * nsplit + s]);
+  float Lsum = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float ms = part_m[(size_t)bh * nsplit + s];
+    if (ms != -INFINITY) Lsum += part_l[(size_t)bh * nsplit + s] * __expf(ms - M);
+  }
+  for (int c = threadIdx.x; c < R; c += blockDim.x) {
+    float v = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = part_m[(size_t)bh * nsplit + s];
+      if (ms != -INFINITY) v += part_o[((size_t)bh * nsplit + s) * R + c] * __expf(ms - M);
+    }
+    out[(size_t)bh * R + c] = __float2bfloat16(Lsum > 0.f ? v / Lsum : 0.f);
+  }
+}
+
+template <int DQK, int DV>
+size_t fwd_smem() {
+  return (size_t)(BM * (DQK + 8) + 2 * BN * (DQK + 8) + 2 * BN * (DV + 8)) * 2;
+}
+template <int DQK, int DV>
+size_t bwd_smem() {
+  return (size_t)(BN * (DQK + 8) + BN * (DV + 8) + BM * (DQK + 8) + BM * (DV + 8) + BN * (BM + 8)) * 2 +
+         2 * BM * sizeof(float);
+}
+
+template <int DQK, int DV>
+void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse, int q_off,
+             double scale, bool causal) {
+  const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1);
+  auto kern = fa_fwd_kernel<DQK, DV>;
+  const size_t smem = fwd_smem<DQK, DV>();
+  static bool cfg = false;
+  if (!cfg) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cfg = true;
+  }
+  dim3 grid((Sq + BM - 1) / BM, BH);
+  kern<<<grid, 128, smem, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+      reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq,
+      Sk, q_off, (float)(scale * 1.4426950408889634), causal ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int DQK, int DV>
+void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+             const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+             at::Tensor& dv, int q_off, double scale, bool causal) {
+  const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1);
+  auto st = at::cuda::getCurrentCUDAStream();
+  const long rows = (long)BH * Sq;
+  fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
+      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto kern = fa_bwd_kernel<DQK, DV>;
+  const size_t smem = bwd_smem<DQK, DV>();
+  static bool cfg = false;
+  if (!cfg) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cfg = true;
+  }
+  dim3 grid((Sk + BN - 1) / BN, BH);
+  kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+      reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+      lse.data_ptr<float>(), delta.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(),
+      dv.data_ptr<float>(), Sq, Sk, q_off, (float)(scale * 1.4426950408889634), (float)scale, causal ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+#define DSV3_FA_DISPATCH(DQK_, DV_, CALL)                                                          \
+  if (dqk == DQK_ && dvv == DV_) {                                                                 \
+    CALL;                                                                                          \
+    return;                                                                                        \
+  }
+
+}  // namespace
+
+// q, k: [BH, S, DQK] bf16; v: [BH, Sk, DV]; o: [BH, Sq, DV] bf16; lse: [BH, Sq] fp32 (log2 domain).
+void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+               int64_t q_off, double scale, bool causal) {
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(), "flash_fwd: contiguous");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dqk = q.size(2), dvv = v.size(2);
+  DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(32, 16, (run_fwd<32, 16>(q, k, v, o, lse, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(192, 128, (run_fwd<192, 128>(q, k, v, o, lse, q_off, scale, causal)))
+  TORCH_CHECK(false, "flash_fwd: unsupported head dims ", dqk, "/", dvv);
+}
+
+void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+               at::Tensor& dv, int64_t q_off, double scale, bool causal) {
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dqk = q.size(2), dvv = v.size(2);
+  DSV3_FA_DISPATCH(80, 64, (run_bwd<80, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(32, 16, (run_bwd<32, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(64, 64, (run_bwd<64, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(128, 128, (run_bwd<128, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(192, 128, (run_bwd<192, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  TORCH_CHECK(false, "flash_bwd: unsupported head dims ", dqk, "/", dvv);
+}
+
+// q_lat [B, H, R], q_pe [B, H, dr], kv [B, S, R] (batch stride kv.stride(0)),
+// pe [B, S, dr], lens [B] int32 -> out [B, H, R] bf16.
+void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv, const at::Tensor& pe,
+                   const at::Tensor& lens, double scale, int64_t max_len, at::Tensor& scratch, at::Tensor& out) {
+  const int B = q_lat.size(0), H = q_lat.size(1), R = q_lat.size(2), dr = q_pe.size(2);
+  TORCH_CHECK(R <= 1024 && dr <= 128, "latent_decode: R <= 1024, dr <= 128");
+  const at::cuda::CUDAGuard guard(q_lat.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int chunk = 256;
+  const int nsplit = std::max<int>(1, (max_len + chunk - 1) / chunk);
+  const long need = (long)B * H * nsplit * (2 + R);
+  TORCH_CHECK(scratch.numel() >= need && scratch.scalar_type() == at::kFloat, "latent_decode: scratch too small (need ",
+              need, " floats)");
+  float* pm = scratch.data_ptr<float>();
+  float* pl = pm + (long)B * H * nsplit;
+  float* po = pl + (long)B * H * nsplit;
+  const int warps = B * H * nsplit;
+  latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, st>>>(
+      reinterpret_cast<const bf16*>(q_lat.data_ptr()), reinterpret_cast<const bf16*>(q_pe.data_ptr()),
+      reinterpret_cast<const bf16*>(kv.data_ptr()), reinterpret_cast<const bf16*>(pe.data_ptr()),
+      lens.data_ptr<int>(), H, R, dr, kv.stride(0), pe.stride(0), chunk, nsplit, B * H, (float)scale, pm, pl, po);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  latent_decode_merge_kernel<<<B * H, 128, 0, st>>>(pm, pl, po, nsplit, R, B * H,
+                                                    reinterpret_cast<bf16*>(out.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void register_attention(pybind11::module_& m) {
+  m.def("flash_fwd", &flash_fwd, "causal flash attention forward (stores log2-domain LSE)");
+  m.def("flash_bwd", &flash_bwd, "flash attention backward (dQ fp32 accumulated, dK/dV fp32)");
+  m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)");
+}
+
+}  // namespace dsv3

@@ -1,0 +1,459 @@
+// Memory-bound kernels of the training step: RMSNorm forward/backward (fp32
+// residual stream in, bf16 GEMM operand out), decoupled RoPE, MLA Q/K/V
+// packing for the attention kernels, token embedding, dtype casts and the
+// cross-entropy finalisation.  One warp per row throughout; rows are
+// processed with 16-byte vector accesses where the width allows.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dsv3 {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p);
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+constexpr int kMaxPerLane = 64;  // supports rows up to 2048 wide
+
+// ------------------------------------------------------------------ RMSNorm
+template <typename TIn>
+__global__ void rmsnorm_fwd_kernel(const TIn* __restrict__ x, long ldx, const float* __restrict__ w, float eps,
+                                   __nv_bfloat16* __restrict__ y, long ldy, float* __restrict__ rstd, int T, int D) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const TIn* xr = x + (size_t)row * ldx;
+  float v[kMaxPerLane];
+  float ss = 0.f;
+  int n = 0;
+  for (int c = lane; c < D; c += 32, ++n) {
+    v[n] = ld_f(xr + c);
+    ss += v[n] * v[n];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+  __nv_bfloat16* yr = y + (size_t)row * ldy;
+  n = 0;
+  for (int c = lane; c < D; c += 32, ++n) yr[c] = __float2bfloat16(v[n] * r * w[c]);
+  if (lane == 0 && rstd) rstd[row] = r;
+}
+
+// dx = r * (w*dy - xhat * mean(xhat * w * dy)),  xhat = x * r;  dw += sum_rows dy * xhat.
+// dx is either accumulated into an fp32 buffer (residual stream gradient;
+// then `dx_copy` optionally receives a bf16 copy of the updated sum) or
+// stored as bf16.
+template <typename TIn, typename TDy>
+__global__ void rmsnorm_bwd_kernel(const TDy* __restrict__ dy, long lddy, const TIn* __restrict__ x, long ldx,
+                                   const float* __restrict__ w, const float* __restrict__ rstd,
+                                   float* __restrict__ dx_acc, long ldacc, __nv_bfloat16* __restrict__ dx_out,
+                                   long ldout, __nv_bfloat16* __restrict__ dx_copy, long ldcopy,
+                                   float* __restrict__ dw, int T, int D, int rows_per_block) {
+  extern __shared__ float dw_s[];
+  const int warps = blockDim.x >> 5;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) dw_s[c] = 0.f;
+  __syncthreads();
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(T, r0 + rows_per_block);
+  float dwl[kMaxPerLane];
+  for (int i = 0; i < kMaxPerLane; ++i) dwl[i] = 0.f;
+  for (int row = r0 + wid; row < r1; row += warps) {
+    const float r = rstd[row];
+    float xh[kMaxPerLane], g[kMaxPerLane];
+    float dot = 0.f;
+    int n = 0;
+    for (int c = lane; c < D; c += 32, ++n) {
+      xh[n] = ld_f(x + (size_t)row * ldx + c) * r;
+      const float gy = ld_f(dy + (size_t)row * lddy + c);
+      g[n] = gy * w[c];
+      dot += xh[n] * g[n];
+      dwl[n] += gy * xh[n];
+    }
+    dot = warp_sum(dot) / D;
+    n = 0;
+    for (int c = lane; c < D; c += 32, ++n) {
+      const float d = r * (g[n] - xh[n] * dot);
+      if (dx_acc) {
+        float* p = dx_acc + (size_t)row * ldacc + c;
+        const float s = *p + d;
+        *p = s;
+        if (dx_copy) dx_copy[(size_t)row * ldcopy + c] = __float2bfloat16(s);
+      } else {
+        dx_out[(size_t)row * ldout + c] = __float2bfloat16(d);
+      }
+    }
+  }
+  int n = 0;
+  for (int c = lane; c < D; c += 32, ++n) atomicAdd(&dw_s[c], dwl[n]);
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], dw_s[c]);
+}
+
+// --------------------------------------------------------------------- RoPE
+// Rotate pairs (x[2i], x[2i+1]) of a [T, H, ...] bf16 tensor in place, at
+// column offset `off` of each head.  Position of token t is pos[t] when given,
+// else (t % seqlen) + start.  `inverse` rotates by -theta (backward pass).
+__global__ void rope_kernel(__nv_bfloat16* __restrict__ x, long ld_tok, long ld_head, int off, int T, int H,
+                            int half, const float* __restrict__ cosv, const float* __restrict__ sinv,
+                            const int* __restrict__ pos, int seqlen, int start, int inverse) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long total = (long)T * H * half;
+  if (idx >= total) return;
+  const int i = idx % half;
+  const int h = (idx / half) % H;
+  const int t = idx / ((long)half * H);
+  const int p = pos ? pos[t] : (t % seqlen) + start;
+  const float c = cosv[(size_t)p * half + i];
+  const float s = inverse ? -sinv[(size_t)p * half + i] : sinv[(size_t)p * half + i];
+  __nv_bfloat16* e = x + (size_t)t * ld_tok + (size_t)h * ld_head + off + 2 * i;
+  const float a = __bfloat162float(e[0]), b = __bfloat162float(e[1]);
+  e[0] = __float2bfloat16(a * c - b * s);
+  e[1] = __float2bfloat16(a * s + b * c);
+}
+
+// ------------------------------------------------------------ MLA packing
+// Build the attention operands of the materialised formulation from the
+// projection outputs of T = B*S tokens:
+//   q   [T, H, dn + dr]      (q_nope | q_pe, q_pe not yet rotated)
+//   kvb [T, H, dn + dv]      (k_nope | v)
+//   kpe [T, dr] (stride ldk) (shared RoPE key, not yet rotated)
+// into Q, K [B, H, S, DP] (DP >= dn + dr, zero padded) and V [B, H, S, dv],
+// rotating q_pe / k_pe on the way (RoPE in fp32, rounded to bf16 once).
+__global__ void mla_pack_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kvb,
+                                const __nv_bfloat16* __restrict__ kpe, long ldk, __nv_bfloat16* __restrict__ Q,
+                                __nv_bfloat16* __restrict__ K, __nv_bfloat16* __restrict__ V, int B, int S, int H,
+                                int dn, int dr, int dv, int DP, const float* __restrict__ cosv,
+                                const float* __restrict__ sinv, int start) {
+  const int t = blockIdx.x;       // token
+  const int h = blockIdx.y;       // head
+  const int b = t / S, s = t % S;
+  const int p = s + start;
+  const size_t o_qk = (((size_t)b * H + h) * S + s) * DP;
+  const size_t o_v = (((size_t)b * H + h) * S + s) * dv;
+  const __nv_bfloat16* qs = q + ((size_t)t * H + h) * (dn + dr);
+  const __nv_bfloat16* ks = kvb + ((size_t)t * H + h) * (dn + dv);
+  for (int c = threadIdx.x; c < DP; c += blockDim.x) {
+    __nv_bfloat16 qv, kv;
+    if (c < dn) {
+      qv = qs[c];
+      kv = ks[c];
+    } else if (c < dn + dr) {
+      const int j = c - dn, i = j >> 1;
+      const float cs = cosv[(size_t)p * (dr / 2) + i], sn = sinv[(size_t)p * (dr / 2) + i];
+      const float qa = __bfloat162float(qs[dn + 2 * i]), qb = __bfloat162float(qs[dn + 2 * i + 1]);
+      const float ka = __bfloat162float(kpe[(size_t)t * ldk + 2 * i]), kb = __bfloat162float(kpe[(size_t)t * ldk + 2 * i + 1]);
+      qv = __float2bfloat16((j & 1) ? qa * sn + qb * cs : qa * cs - qb * sn);
+      kv = __float2bfloat16((j & 1) ? ka * sn + kb * cs : ka * cs - kb * sn);
+    } else {
+      qv = __float2bfloat16(0.f);
+      kv = qv;
+    }
+    Q[o_qk + c] = qv;
+    K[o_qk + c] = kv;
+  }
+  for (int c = threadIdx.x; c < dv; c += blockDim.x) V[o_v + c] = ks[dn + c];
+}
+
+// Inverse of the packing for the gradients.  dQ, dK are fp32 [B,H,S,DP]; dV
+// bf16 or fp32 [B,H,S,dv].  Writes dq [T,H,dn+dr] and dkvb [T,H,dn+dv] (bf16)
+// and dkpe [T, dr] (bf16, summed over heads) with the RoPE rotation undone.
+template <typename TV>
+__global__ void mla_unpack_kernel(const float* __restrict__ dQ, const float* __restrict__ dK,
+                                  const TV* __restrict__ dV, __nv_bfloat16* __restrict__ dq,
+                                  __nv_bfloat16* __restrict__ dkvb, __nv_bfloat16* __restrict__ dkpe, long ldk, int B,
+                                  int S, int H, int dn, int dr, int dv, int DP, const float* __restrict__ cosv,
+                                  const float* __restrict__ sinv, int start) {
+  const int t = blockIdx.x;
+  const int b = t / S, s = t % S;
+  const int p = s + start;
+  extern __shared__ float kpe_acc[];  // [dr]
+  for (int c = threadIdx.x; c < dr; c += blockDim.x) kpe_acc[c] = 0.f;
+  __syncthreads();
+  for (int h = 0; h < H; ++h) {
+    const size_t o_qk = (((size_t)b * H + h) * S + s) * DP;
+    const size_t o_v = (((size_t)b * H + h) * S + s) * dv;
+    __nv_bfloat16* dqs = dq + ((size_t)t * H + h) * (dn + dr);
+    __nv_bfloat16* dks = dkvb + ((size_t)t * H + h) * (dn + dv);
+    for (int c = threadIdx.x; c < dn; c += blockDim.x) {
+      dqs[c] = __float2bfloat16(dQ[o_qk + c]);
+      dks[c] = __float2bfloat16(dK[o_qk + c]);
+    }
+    for (int i = threadIdx.x; i < dr / 2; i += blockDim.x) {
+      const float cs = cosv[(size_t)p * (dr / 2) + i], sn = sinv[(size_t)p * (dr / 2) + i];
+      const float qa = dQ[o_qk + dn + 2 * i], qb = dQ[o_qk + dn + 2 * i + 1];
+      dqs[dn + 2 * i] = __float2bfloat16(qa * cs + qb * sn);
+      dqs[dn + 2 * i + 1] = __float2bfloat16(-qa * sn + qb * cs);
+      const float ka = dK[o_qk + dn + 2 * i], kb = dK[o_qk + dn + 2 * i + 1];
+      kpe_acc[2 * i] += ka * cs + kb * sn;
+      kpe_acc[2 * i + 1] += -ka * sn + kb * cs;
+    }
+    for (int c = threadIdx.x; c < dv; c += blockDim.x) dks[dn + c] = __float2bfloat16(ld_f(dV + o_v + c));
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dr; c += blockDim.x) dkpe[(size_t)t * ldk + c] = __float2bfloat16(kpe_acc[c]);
+}
+
+// ---------------------------------------------------------------- embedding
+__global__ void embedding_fwd_kernel(const long* __restrict__ tok, const float* __restrict__ w,
+                                     float* __restrict__ out, int T, int D) {
+  const int row = blockIdx.x;
+  const float4* src = reinterpret_cast<const float4*>(w + (size_t)tok[row] * D);
+  float4* dst = reinterpret_cast<float4*>(out + (size_t)row * D);
+  for (int c = threadIdx.x; c < D / 4; c += blockDim.x) dst[c] = src[c];
+}
+
+__global__ void embedding_bwd_kernel(const long* __restrict__ tok, const float* __restrict__ g,
+                                     float* __restrict__ dw, int T, int D) {
+  const int row = blockIdx.x;
+  float* dst = dw + (size_t)tok[row] * D;
+  const float* src = g + (size_t)row * D;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(dst + c, src[c]);
+}
+
+__global__ void cast_f32_bf16_kernel(const float* __restrict__ a, __nv_bfloat16* __restrict__ b, long n) {
+  const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(a + i);
+    uint2 o;
+    o.x = pack_bf16x2(v.x, v.y);
+    o.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(b + i) = o;
+  } else {
+    for (long j = i; j < n; ++j) b[j] = __float2bfloat16(a[j]);
+  }
+}
+
+// ---------------------------------------------------------- cross-entropy
+// Combine the per-tile (max, sum-exp) partials into lse and per-row loss.
+__global__ void ce_rows_kernel(const float* __restrict__ pmax, const float* __restrict__ psum,
+                               const float* __restrict__ tgt_logit, const long* __restrict__ tgt, int T, int nt,
+                               float* __restrict__ lse, float* __restrict__ loss) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  float m = -INFINITY;
+  for (int i = lane; i < nt; i += 32) m = fmaxf(m, pmax[(size_t)row * nt + i]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = lane; i < nt; i += 32) {
+    const float pm = pmax[(size_t)row * nt + i];
+    if (pm != -INFINITY) s += psum[(size_t)row * nt + i] * __expf(pm - m);
+  }
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float l = m + logf(s);
+    lse[row] = l;
+    loss[row] = tgt[row] >= 0 ? l - tgt_logit[row] : 0.f;
+  }
+}
+
+// Deterministic per-segment mean of the row losses (rows [seg_start[i],
+// seg_start[i+1]) with targets != -100).  Writes loss[i] = mean and the
+// backward row scale  weight[i] * grad_scale / count_i  (0 for ignored rows).
+__global__ void ce_reduce_kernel(const float* __restrict__ loss_rows, const long* __restrict__ tgt,
+                                 const int* __restrict__ seg_start, const float* __restrict__ seg_weight, int nseg,
+                                 float grad_scale, float* __restrict__ loss_out, float* __restrict__ row_scale) {
+  __shared__ float ssum[32];
+  __shared__ float scnt[32];
+  for (int sgi = 0; sgi < nseg; ++sgi) {
+    const int a = seg_start[sgi], b = seg_start[sgi + 1];
+    float sum = 0.f, cnt = 0.f;
+    for (int r = a + threadIdx.x; r < b; r += blockDim.x) {
+      if (tgt[r] >= 0) {
+        sum += loss_rows[r];
+        cnt += 1.f;
+      }
+    }
+    sum = warp_sum(sum);
+    cnt = warp_sum(cnt);
+    if ((threadIdx.x & 31) == 0) {
+      ssum[threadIdx.x >> 5] = sum;
+      scnt[threadIdx.x >> 5] = cnt;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float s2 = threadIdx.x < (blockDim.x >> 5) ? ssum[threadIdx.x] : 0.f;
+      float c2 = threadIdx.x < (blockDim.x >> 5) ? scnt[threadIdx.x] : 0.f;
+      s2 = warp_sum(s2);
+      c2 = warp_sum(c2);
+      if (threadIdx.x == 0) {
+        loss_out[sgi] = c2 > 0 ? s2 / c2 : 0.f;
+        scnt[0] = c2;
+      }
+    }
+    __syncthreads();
+    const float c = scnt[0];
+    const float sc = c > 0 ? seg_weight[sgi] * grad_scale / c : 0.f;
+    for (int r = a + threadIdx.x; r < b; r += blockDim.x) row_scale[r] = tgt[r] >= 0 ? sc : 0.f;
+    __syncthreads();
+  }
+}
+
+int blocks_for(long n, int per) { return (int)((n + per - 1) / per); }
+
+}  // namespace
+
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, at::Tensor& y, at::Tensor& rstd) {
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.stride(1) == 1, "rmsnorm_fwd: 2-D row-major views");
+  const int T = x.size(0), D = x.size(1);
+  TORCH_CHECK(D <= 32 * kMaxPerLane, "rmsnorm_fwd: row too wide");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  float* r = rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr;
+  if (x.scalar_type() == at::kFloat)
+    rmsnorm_fwd_kernel<float><<<blocks_for(T, 8), 256, 0, st>>>(x.data_ptr<float>(), x.stride(0), w.data_ptr<float>(),
+        (float)eps, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), r, T, D);
+  else
+    rmsnorm_fwd_kernel<__nv_bfloat16><<<blocks_for(T, 8), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), (float)eps,
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), r, T, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                 c10::optional<at::Tensor> dx_acc, c10::optional<at::Tensor> dx_out, c10::optional<at::Tensor> dx_copy,
+                 at::Tensor& dw) {
+  const int T = x.size(0), D = x.size(1);
+  TORCH_CHECK(D <= 32 * kMaxPerLane, "rmsnorm_bwd: row too wide");
+  TORCH_CHECK(dx_acc.has_value() != dx_out.has_value(), "rmsnorm_bwd: exactly one of dx_acc / dx_out");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int rows_per_block = 64;
+  float* acc = dx_acc ? dx_acc->data_ptr<float>() : nullptr;
+  long ldacc = dx_acc ? dx_acc->stride(0) : 0;
+  auto* out = dx_out ? reinterpret_cast<__nv_bfloat16*>(dx_out->data_ptr()) : nullptr;
+  long ldout = dx_out ? dx_out->stride(0) : 0;
+  auto* cp = dx_copy ? reinterpret_cast<__nv_bfloat16*>(dx_copy->data_ptr()) : nullptr;
+  long ldcp = dx_copy ? dx_copy->stride(0) : 0;
+  const int grid = blocks_for(T, rows_per_block);
+  const size_t smem = D * sizeof(float);
+#define DSV3_NORM_BWD(TIN, TDY)                                                                                   \
+  rmsnorm_bwd_kernel<TIN, TDY><<<grid, 256, smem, st>>>(                                                          \
+      reinterpret_cast<const TDY*>(dy.data_ptr()), dy.stride(0), reinterpret_cast<const TIN*>(x.data_ptr()),      \
+      x.stride(0), w.data_ptr<float>(), rstd.data_ptr<float>(), acc, ldacc, out, ldout, cp, ldcp,                 \
+      dw.data_ptr<float>(), T, D, rows_per_block)
+  const bool xf = x.scalar_type() == at::kFloat, df = dy.scalar_type() == at::kFloat;
+  if (xf && df) DSV3_NORM_BWD(float, float);
+  else if (xf) DSV3_NORM_BWD(float, __nv_bfloat16);
+  else if (df) DSV3_NORM_BWD(__nv_bfloat16, float);
+  else DSV3_NORM_BWD(__nv_bfloat16, __nv_bfloat16);
+#undef DSV3_NORM_BWD
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_inplace(at::Tensor& x, int64_t off, int64_t half, const at::Tensor& cosv, const at::Tensor& sinv,
+                  c10::optional<at::Tensor> pos, int64_t seqlen, int64_t start, bool inverse) {
+  // x: [T, H, W] bf16 view (any strides on T / H, unit on W)
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.scalar_type() == at::kBFloat16, "rope_inplace: [T,H,W] bf16");
+  const int T = x.size(0), H = x.size(1);
+  const at::cuda::CUDAGuard guard(x.device());
+  const long total = (long)T * H * half;
+  rope_kernel<<<blocks_for(total, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), x.stride(1), off, T, H, half,
+      cosv.data_ptr<float>(), sinv.data_ptr<float>(), pos ? pos->data_ptr<int>() : nullptr, seqlen, start,
+      inverse ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mla_pack(const at::Tensor& q, const at::Tensor& kvb, const at::Tensor& kpe, at::Tensor& Q, at::Tensor& K,
+              at::Tensor& V, int64_t B, int64_t S, int64_t H, int64_t dn, int64_t dr, int64_t dv,
+              const at::Tensor& cosv, const at::Tensor& sinv, int64_t start) {
+  const int DP = Q.size(-1);
+  const at::cuda::CUDAGuard guard(q.device());
+  dim3 grid(B * S, H);
+  mla_pack_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(kpe.data_ptr()), kpe.stride(0),
+      reinterpret_cast<__nv_bfloat16*>(Q.data_ptr()), reinterpret_cast<__nv_bfloat16*>(K.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(V.data_ptr()), B, S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
+      sinv.data_ptr<float>(), start);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mla_unpack(const at::Tensor& dQ, const at::Tensor& dK, const at::Tensor& dV, at::Tensor& dq, at::Tensor& dkvb,
+                at::Tensor& dkpe, int64_t B, int64_t S, int64_t H, int64_t dn, int64_t dr, int64_t dv,
+                const at::Tensor& cosv, const at::Tensor& sinv, int64_t start) {
+  const int DP = dQ.size(-1);
+  const at::cuda::CUDAGuard guard(dQ.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto* dqp = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  auto* dkp = reinterpret_cast<__nv_bfloat16*>(dkvb.data_ptr());
+  auto* dpe = reinterpret_cast<__nv_bfloat16*>(dkpe.data_ptr());
+  if (dV.scalar_type() == at::kFloat)
+    mla_unpack_kernel<float><<<B * S, 64, dr * sizeof(float), st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
+        dV.data_ptr<float>(), dqp, dkp, dpe, dkpe.stride(0), B, S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
+        sinv.data_ptr<float>(), start);
+  else
+    mla_unpack_kernel<__nv_bfloat16><<<B * S, 64, dr * sizeof(float), st>>>(dQ.data_ptr<float>(),
+        dK.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(dV.data_ptr()), dqp, dkp, dpe, dkpe.stride(0),
+        B, S, H, dn, dr, dv, DP, cosv.data_ptr<float>(), sinv.data_ptr<float>(), start);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embedding_fwd(const at::Tensor& tok, const at::Tensor& w, at::Tensor& out) {
+  const int T = tok.numel(), D = w.size(1);
+  TORCH_CHECK(D % 4 == 0 && tok.scalar_type() == at::kLong, "embedding_fwd: D % 4 == 0, int64 ids");
+  const at::cuda::CUDAGuard guard(w.device());
+  embedding_fwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
+      w.data_ptr<float>(), out.data_ptr<float>(), T, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embedding_bwd(const at::Tensor& tok, const at::Tensor& g, at::Tensor& dw) {
+  const int T = tok.numel(), D = dw.size(1);
+  const at::cuda::CUDAGuard guard(dw.device());
+  embedding_bwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
+      g.data_ptr<float>(), dw.data_ptr<float>(), T, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void cast_f32_bf16(const at::Tensor& a, at::Tensor& b) {
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && a.numel() == b.numel(), "cast: contiguous, same size");
+  const long n = a.numel();
+  if (n == 0) return;
+  const at::cuda::CUDAGuard guard(a.device());
+  cast_f32_bf16_kernel<<<blocks_for(n, 1024), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      a.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(b.data_ptr()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_rows(const at::Tensor& pmax, const at::Tensor& psum, const at::Tensor& tl, const at::Tensor& tgt,
+             at::Tensor& lse, at::Tensor& loss) {
+  const int T = pmax.size(0), nt = pmax.size(1);
+  const at::cuda::CUDAGuard guard(pmax.device());
+  ce_rows_kernel<<<blocks_for(T, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(pmax.data_ptr<float>(),
+      psum.data_ptr<float>(), tl.data_ptr<float>(), tgt.data_ptr<int64_t>(), T, nt, lse.data_ptr<float>(),
+      loss.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_reduce(const at::Tensor& loss_rows, const at::Tensor& tgt, const at::Tensor& seg_start,
+               const at::Tensor& seg_weight, double grad_scale, at::Tensor& loss_out, at::Tensor& row_scale) {
+  const at::cuda::CUDAGuard guard(loss_rows.device());
+  ce_reduce_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(loss_rows.data_ptr<float>(),
+      tgt.data_ptr<int64_t>(), seg_start.data_ptr<int>(), seg_weight.data_ptr<float>(), seg_start.numel() - 1,
+      (float)grad_scale, loss_out.data_ptr<float>(), row_scale.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void register_elementwise(pybind11::module_& m) {
+  m.def("rmsnorm_fwd", &rmsnorm_fwd, "y(bf16) = rmsnorm(x) * w; stores 1/rms per row");
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, "RMSNorm backward (dx accumulate or store, dw +=)");
+  m.def("rope_inplace", &rope_inplace, "rotate interleaved pairs in place (optionally inverse)");
+  m.def("mla_pack", &mla_pack, "MLA Q/K/V packing with RoPE for the attention kernels");
+  m.def("mla_unpack", &mla_unpack, "gradient of mla_pack");
+  m.def("embedding_fwd", &embedding_fwd, "fp32 row gather");
+  m.def("embedding_bwd", &embedding_bwd, "fp32 scatter-add into the embedding gradient");
+  m.def("cast_f32_bf16", &cast_f32_bf16, "fp32 -> bf16");
+  m.def("ce_rows", &ce_rows, "log-sum-exp and per-row loss from the fused head partials");
+  m.def("ce_reduce", &ce_reduce, "per-segment mean loss and backward row scales");
+}
+
+}  // namespace dsv3

@@ -1,0 +1,400 @@
+// Host side of the tcgen05 GEMM engine: TMA tensor-map construction and the
+// typed entry points used by ops/*.py (dense forward / data-gradient /
+// weight-gradient, expert-grouped variants, fused SwiGLU and LM-head
+// cross-entropy).  Every entry point runs on the current CUDA stream.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+
+#include "gemm_sm100.cuh"
+#include "status.h"
+
+namespace dsv3 {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
+                "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map, 128-byte swizzle, zero fill out of bounds.  dims[0] is the
+// contiguous dimension; strides are in bytes for dims[1..rank-1].
+CUtensorMap make_map(const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                     const uint32_t* box) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base address must be 16-byte aligned");
+  for (int i = 0; i + 1 < rank; ++i)
+    TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), d, s, b, e,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
+  return m;
+}
+
+// A operand, K-major: logical [rows, K] with row stride ld (elements).
+CUtensorMap map_a_kmajor(const at::Tensor& t, int64_t rows, int64_t K, int64_t ld) {
+  uint64_t dims[2] = {(uint64_t)K, (uint64_t)rows};
+  uint64_t st[1] = {(uint64_t)ld * 2};
+  uint32_t box[2] = {64, 128};
+  return make_map(t.data_ptr(), 2, dims, st, box);
+}
+
+// A operand, MN-major: logical [Ktot, rows] with the output-row dim contiguous.
+CUtensorMap map_a_mnmajor(const at::Tensor& t, int64_t rows, int64_t Ktot, int64_t ld) {
+  uint64_t dims[2] = {(uint64_t)rows, (uint64_t)Ktot};
+  uint64_t st[1] = {(uint64_t)ld * 2};
+  uint32_t box[2] = {64, 64};
+  return make_map(t.data_ptr(), 2, dims, st, box);
+}
+
+// B operand, K-major, grouped: [G][N][K], rows of length K (stride ld), group stride gs.
+CUtensorMap map_b_kmajor(const at::Tensor& t, int64_t G, int64_t N, int64_t K, int64_t ld, int64_t gs) {
+  uint64_t dims[3] = {(uint64_t)K, (uint64_t)N, (uint64_t)G};
+  uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)gs * 2};
+  uint32_t box[3] = {64, 128, 1};
+  return make_map(t.data_ptr(), 3, dims, st, box);
+}
+
+// B operand, MN-major, grouped: [G][Kred][N] with N contiguous.
+CUtensorMap map_b_mnmajor(const at::Tensor& t, int64_t G, int64_t Kred, int64_t N, int64_t ld, int64_t gs) {
+  uint64_t dims[3] = {(uint64_t)N, (uint64_t)Kred, (uint64_t)G};
+  uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)gs * 2};
+  uint32_t box[3] = {64, 64, 1};
+  return make_map(t.data_ptr(), 3, dims, st, box);
+}
+
+// SwiGLU weights [G][2][I][K] (gate rows, then up rows, per group).
+CUtensorMap map_b_swiglu(const at::Tensor& t, int64_t G, int64_t I, int64_t K) {
+  uint64_t dims[4] = {(uint64_t)K, (uint64_t)I, 2, (uint64_t)G};
+  uint64_t st[3] = {(uint64_t)K * 2, (uint64_t)I * K * 2, (uint64_t)2 * I * K * 2};
+  uint32_t box[4] = {64, 128, 1, 1};
+  return make_map(t.data_ptr(), 4, dims, st, box);
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
+  using C = GemmCfg<BN>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    configured = true;
+  }
+  if (a.num_tiles <= 0) return;
+  a.status = status_ptr();
+  const int grid = std::min(a.num_tiles, num_sms());
+  kern<<<grid, 192, C::SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(ta, tb, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+GemmArgs blank_args() {
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.k_splits = 1;
+  a.groups = 1;
+  return a;
+}
+
+void check_bf16_rows(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be a CUDA bf16 tensor");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+  TORCH_CHECK(t.stride(0) % 8 == 0, name, " row stride must be a multiple of 8 elements");
+}
+
+int cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+}  // namespace
+
+// out (bf16, store) or out (fp32, accumulate) = a[M,K] @ w[N,K]^T
+void linear_fwd(const at::Tensor& a, const at::Tensor& w, at::Tensor& out) {
+  check_bf16_rows(a, "a");
+  check_bf16_rows(w, "w");
+  const int64_t M = a.size(0), K = a.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "linear_fwd: K mismatch");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "linear_fwd: out shape");
+  const at::cuda::CUDAGuard guard(a.device());
+  GemmArgs g = blank_args();
+  g.M = M; g.N = N; g.K = K;
+  g.out = out.data_ptr(); g.ldo = out.stride(0);
+  CUtensorMap ta = map_a_kmajor(a, M, K, a.stride(0));
+  CUtensorMap tb = map_b_kmajor(w, 1, N, K, w.stride(0), N * w.stride(0));
+  const bool f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || out.scalar_type() == at::kBFloat16, "linear_fwd: out must be bf16 or fp32");
+  TORCH_CHECK(out.stride(0) % 8 == 0, "linear_fwd: out row stride must be a multiple of 8");
+  if (N <= 128) {
+    g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, 128); g.kb_per_split = cdiv(K, 64);
+    g.num_tiles = g.m_tiles * g.n_tiles;
+    if (f32) launch<128, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+    else launch<128, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+  } else {
+    g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
+    g.num_tiles = g.m_tiles * g.n_tiles;
+    if (f32) launch<256, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+    else launch<256, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+  }
+}
+
+// out [M,K] (bf16 store or fp32 accumulate) = dy[M,N] @ w[N,K]
+void linear_dgrad(const at::Tensor& dy, const at::Tensor& w, at::Tensor& out) {
+  check_bf16_rows(dy, "dy");
+  check_bf16_rows(w, "w");
+  const int64_t M = dy.size(0), N = dy.size(1), K = w.size(1);
+  TORCH_CHECK(w.size(0) == N, "linear_dgrad: N mismatch");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == K && out.stride(1) == 1, "linear_dgrad: out shape");
+  TORCH_CHECK(out.stride(0) % 8 == 0, "linear_dgrad: out row stride must be a multiple of 8");
+  const at::cuda::CUDAGuard guard(dy.device());
+  GemmArgs g = blank_args();
+  g.M = M; g.N = K; g.K = N;
+  g.out = out.data_ptr(); g.ldo = out.stride(0);
+  CUtensorMap ta = map_a_kmajor(dy, M, N, dy.stride(0));
+  CUtensorMap tb = map_b_mnmajor(w, 1, N, K, w.stride(0), N * w.stride(0));
+  const bool f32 = out.scalar_type() == at::kFloat;
+  g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(K, 256); g.kb_per_split = cdiv(N, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  if (f32) launch<256, 0, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+  else launch<256, 0, 1, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+}
+
+// dw [N,K] fp32 += dy[M,N]^T @ x[M,K]   (reduction over the M token rows)
+void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw) {
+  check_bf16_rows(dy, "dy");
+  check_bf16_rows(x, "x");
+  const int64_t M = dy.size(0), N = dy.size(1), K = x.size(1);
+  TORCH_CHECK(x.size(0) == M, "linear_wgrad: M mismatch");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.size(0) == N && dw.size(1) == K,
+              "linear_wgrad: dw must be contiguous fp32 [N, K]");
+  const at::cuda::CUDAGuard guard(dy.device());
+  GemmArgs g = blank_args();
+  g.M = N; g.N = K; g.K = M;
+  g.out = dw.data_ptr(); g.ldo = K;
+  CUtensorMap ta = map_a_mnmajor(dy, N, M, dy.stride(0));
+  CUtensorMap tb = map_b_mnmajor(x, 1, M, K, x.stride(0), M * x.stride(0));
+  g.m_tiles = cdiv(N, 128); g.n_tiles = cdiv(K, 256);
+  const int total_kb = cdiv(M, 64);
+  const int base_tiles = g.m_tiles * g.n_tiles;
+  int splits = std::max(1, std::min(total_kb / 8, (2 * num_sms() + base_tiles - 1) / base_tiles));
+  g.kb_per_split = cdiv(total_kb, splits);
+  splits = cdiv(total_kb, g.kb_per_split);
+  g.k_splits = splits;
+  g.num_tiles = base_tiles * splits;
+  if (splits > 1) launch<256, 1, 1, Sched::Dense, Epi::AtomicAddF32, false>(ta, tb, g);
+  else launch<256, 1, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+}
+
+// SwiGLU up-projection: x[P,D] against w13 [G,2,I,D] (dense when G == 1 and
+// tile_group is empty).  Writes h = silu(g) * u [P, I] and gu = [g | u] [P, 2I].
+void swiglu_fwd(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& tile_group, at::Tensor& h,
+                at::Tensor& gu) {
+  check_bf16_rows(x, "x");
+  TORCH_CHECK(w13.scalar_type() == at::kBFloat16 && w13.is_contiguous() && w13.dim() == 4 && w13.size(1) == 2,
+              "w13 must be contiguous bf16 [G, 2, I, D]");
+  const int64_t P = x.size(0), D = x.size(1), G = w13.size(0), I = w13.size(2);
+  TORCH_CHECK(w13.size(3) == D, "swiglu_fwd: D mismatch");
+  TORCH_CHECK(I % 8 == 0 && D % 8 == 0, "swiglu_fwd: I and D must be multiples of 8");
+  check_bf16_rows(h, "h");
+  check_bf16_rows(gu, "gu");
+  TORCH_CHECK(h.size(0) == P && h.size(1) == I && gu.size(0) == P && gu.size(1) == 2 * I, "swiglu_fwd: outputs");
+  const at::cuda::CUDAGuard guard(x.device());
+  GemmArgs g = blank_args();
+  g.M = P; g.N = I; g.K = D; g.inter = I;
+  g.out = h.data_ptr(); g.ldo = h.stride(0);
+  g.out2 = gu.data_ptr(); g.ldo2 = gu.stride(0);
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(I, 128); g.kb_per_split = cdiv(D, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(x, P, D, x.stride(0));
+  CUtensorMap tb = map_b_swiglu(w13, G, I, D);
+  if (tile_group.numel() > 0) {
+    TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.numel() >= g.m_tiles, "tile_group: int32 [tiles]");
+    g.tile_group = tile_group.data_ptr<int>();
+    launch<256, 0, 0, Sched::GroupedM, Epi::SwigluFwd, true>(ta, tb, g);
+  } else {
+    TORCH_CHECK(G == 1, "dense SwiGLU expects one weight group");
+    launch<256, 0, 0, Sched::Dense, Epi::SwigluFwd, true>(ta, tb, g);
+  }
+}
+
+// SwiGLU backward through the down projection: dh = dy[P,D] @ w2[G](D x I),
+// then dgu = [dh * u * silu'(g) | dh * silu(g)] using the saved pre-activations.
+void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& tile_group, const at::Tensor& gu,
+                  at::Tensor& dgu) {
+  check_bf16_rows(dy, "dy");
+  check_bf16_rows(gu, "gu");
+  check_bf16_rows(dgu, "dgu");
+  TORCH_CHECK(w2.scalar_type() == at::kBFloat16 && w2.is_contiguous() && w2.dim() == 3, "w2: bf16 [G, D, I]");
+  const int64_t P = dy.size(0), D = dy.size(1), G = w2.size(0), I = w2.size(2);
+  TORCH_CHECK(w2.size(1) == D && gu.size(1) == 2 * I && dgu.size(1) == 2 * I, "swiglu_dgrad: shapes");
+  const at::cuda::CUDAGuard guard(dy.device());
+  GemmArgs g = blank_args();
+  g.M = P; g.N = I; g.K = D; g.inter = I;
+  g.out = dgu.data_ptr(); g.ldo = dgu.stride(0);
+  g.aux = gu.data_ptr(); g.ld_aux = gu.stride(0);
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(I, 256); g.kb_per_split = cdiv(D, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(dy, P, D, dy.stride(0));
+  CUtensorMap tb = map_b_mnmajor(w2, G, D, I, I, D * I);
+  if (tile_group.numel() > 0) {
+    g.tile_group = tile_group.data_ptr<int>();
+    launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+  } else {
+    launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+  }
+}
+
+// Grouped forward: out[P,N] = a[P,K] @ w[g(tile)] ^T, w: [G, N, K].
+void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out) {
+  check_bf16_rows(a, "a");
+  check_bf16_rows(out, "out");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
+  const int64_t P = a.size(0), K = a.size(1), G = w.size(0), N = w.size(1);
+  TORCH_CHECK(w.size(2) == K && out.size(0) == P && out.size(1) == N, "grouped_fwd: shapes");
+  const at::cuda::CUDAGuard guard(a.device());
+  GemmArgs g = blank_args();
+  g.M = P; g.N = N; g.K = K;
+  g.out = out.data_ptr(); g.ldo = out.stride(0);
+  g.tile_group = tile_group.data_ptr<int>();
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(a, P, K, a.stride(0));
+  CUtensorMap tb = map_b_kmajor(w, G, N, K, K, N * K);
+  launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
+}
+
+// Grouped data gradient: out[P,K] = dy[P,N] @ w[g(tile)], w: [G, N, K].
+void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out) {
+  check_bf16_rows(dy, "dy");
+  check_bf16_rows(out, "out");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
+  const int64_t P = dy.size(0), N = dy.size(1), G = w.size(0), K = w.size(2);
+  TORCH_CHECK(w.size(1) == N && out.size(0) == P && out.size(1) == K, "grouped_dgrad: shapes");
+  const at::cuda::CUDAGuard guard(dy.device());
+  GemmArgs g = blank_args();
+  g.M = P; g.N = K; g.K = N;
+  g.out = out.data_ptr(); g.ldo = out.stride(0);
+  g.tile_group = tile_group.data_ptr<int>();
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(K, 256); g.kb_per_split = cdiv(N, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(dy, P, N, dy.stride(0));
+  CUtensorMap tb = map_b_mnmajor(w, G, N, K, K, N * K);
+  launch<256, 0, 1, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
+}
+
+// Grouped weight gradient: out[g] [Ma, Nb] fp32 += a[rows_g, Ma]^T @ b[rows_g, Nb]
+// where rows_g = [off[g], off[g+1]) (128-aligned padded expert ranges).
+void grouped_wgrad(const at::Tensor& a, const at::Tensor& b, const at::Tensor& row_off, at::Tensor& out) {
+  check_bf16_rows(a, "a");
+  check_bf16_rows(b, "b");
+  const int64_t P = a.size(0), Ma = a.size(1), Nb = b.size(1);
+  const int64_t G = row_off.numel() - 1;
+  TORCH_CHECK(b.size(0) == P, "grouped_wgrad: row mismatch");
+  TORCH_CHECK(row_off.scalar_type() == at::kInt, "row_off must be int32 [G+1]");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == G * Ma * Nb,
+              "grouped_wgrad: out must be contiguous fp32 [G, Ma, Nb]");
+  const at::cuda::CUDAGuard guard(a.device());
+  GemmArgs g = blank_args();
+  g.M = Ma; g.N = Nb; g.K = P; g.groups = G;
+  g.out = out.data_ptr(); g.ldo = Nb; g.out_group_stride = Ma * Nb;
+  g.group_row_off = row_off.data_ptr<int>();
+  g.m_tiles = cdiv(Ma, 128); g.n_tiles = cdiv(Nb, 256);
+  g.num_tiles = g.m_tiles * g.n_tiles * G;
+  CUtensorMap ta = map_a_mnmajor(a, Ma, P, a.stride(0));
+  CUtensorMap tb = map_b_mnmajor(b, 1, P, Nb, b.stride(0), P * b.stride(0));
+  launch<256, 1, 1, Sched::GroupedK, Epi::AddF32, false>(ta, tb, g);
+}
+
+// Fused LM head + cross-entropy, forward half: per (row, 256-column tile)
+// online max / sum-exp partials and the target logit.  No logits are stored.
+void ce_fwd_partials(const at::Tensor& x, const at::Tensor& w, const at::Tensor& targets, at::Tensor& part_max,
+                     at::Tensor& part_sum, at::Tensor& tgt_logit) {
+  check_bf16_rows(x, "x");
+  check_bf16_rows(w, "w");
+  const int64_t T = x.size(0), D = x.size(1), V = w.size(0);
+  const int nt = cdiv(V, 256);
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == T, "targets: int64 [T]");
+  TORCH_CHECK(part_max.numel() == T * nt && part_sum.numel() == T * nt && tgt_logit.numel() == T, "ce partial shapes");
+  const at::cuda::CUDAGuard guard(x.device());
+  GemmArgs g = blank_args();
+  g.M = T; g.N = V; g.K = D;
+  g.targets = targets.data_ptr<int64_t>();
+  g.part_max = part_max.data_ptr<float>();
+  g.part_sum = part_sum.data_ptr<float>();
+  g.tgt_logit = tgt_logit.data_ptr<float>();
+  g.m_tiles = cdiv(T, 128); g.n_tiles = nt; g.kb_per_split = cdiv(D, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(x, T, D, x.stride(0));
+  CUtensorMap tb = map_b_kmajor(w, 1, V, D, w.stride(0), V * w.stride(0));
+  launch<256, 0, 0, Sched::Dense, Epi::CeFwd, false>(ta, tb, g);
+}
+
+// Backward half: dlogits[T, :V] = (softmax(x w^T) - onehot(target)) * row_scale.
+void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& targets, const at::Tensor& lse,
+                   const at::Tensor& row_scale, at::Tensor& dlogits) {
+  check_bf16_rows(x, "x");
+  check_bf16_rows(w, "w");
+  check_bf16_rows(dlogits, "dlogits");
+  const int64_t T = x.size(0), D = x.size(1), V = w.size(0);
+  TORCH_CHECK(dlogits.size(0) == T && dlogits.size(1) >= V, "dlogits shape");
+  const at::cuda::CUDAGuard guard(x.device());
+  GemmArgs g = blank_args();
+  g.M = T; g.N = V; g.K = D;
+  g.targets = targets.data_ptr<int64_t>();
+  g.lse = lse.data_ptr<float>();
+  g.row_scale = row_scale.data_ptr<float>();
+  g.out = dlogits.data_ptr(); g.ldo = dlogits.stride(0);
+  g.m_tiles = cdiv(T, 128); g.n_tiles = cdiv(V, 256); g.kb_per_split = cdiv(D, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(x, T, D, x.stride(0));
+  CUtensorMap tb = map_b_kmajor(w, 1, V, D, w.stride(0), V * w.stride(0));
+  launch<256, 0, 0, Sched::Dense, Epi::CeBwd, false>(ta, tb, g);
+}
+
+}  // namespace dsv3
+
+namespace dsv3 {
+void register_gemm(pybind11::module_& m) {
+  m.def("linear_fwd", &linear_fwd, "out = a @ w^T (bf16 store, or fp32 accumulate when out is fp32)");
+  m.def("linear_dgrad", &linear_dgrad, "out = dy @ w (bf16 store, or fp32 accumulate)");
+  m.def("linear_wgrad", &linear_wgrad, "dw (fp32) += dy^T @ x");
+  m.def("swiglu_fwd", &swiglu_fwd, "h, gu from x @ [w1|w3]^T (dense or expert-grouped)");
+  m.def("swiglu_dgrad", &swiglu_dgrad, "dgu from (dy @ w2) and the saved gate/up");
+  m.def("grouped_fwd", &grouped_fwd, "expert-grouped out = a @ w[e]^T");
+  m.def("grouped_dgrad", &grouped_dgrad, "expert-grouped out = dy @ w[e]");
+  m.def("grouped_wgrad", &grouped_wgrad, "per-expert dw[e] (fp32) += a_e^T @ b_e");
+  m.def("ce_fwd_partials", &ce_fwd_partials, "fused LM head + log-sum-exp partials");
+  m.def("ce_bwd_logits", &ce_bwd_logits, "fused LM head + softmax-minus-onehot gradient");
+}
+}  // namespace dsv3

@@ -1,0 +1,494 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]        (bf16 in, fp32 accumulate in TMEM)
+//
+// One CTA per SM loops over output tiles of 128 x BN.  Warp 0 is the TMA
+// producer, warp 1 issues tcgen05.mma from one elected thread and owns the
+// TMEM allocation, warps 2-5 run the epilogue (TMEM -> registers -> global).
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the MMAs of tile i+1.  Shared memory holds a ring of
+// STAGES (A, B) K-blocks of 64 elements, 128-byte swizzled.
+//
+// Operands may be K-major (reduction dimension contiguous) or MN-major
+// (output dimension contiguous); together that covers the forward (x W^T),
+// data-gradient (dY W) and weight-gradient (dY^T X) products without any
+// transpose copies.  Three schedules:
+//   Dense     - one problem, optional split-K (weight gradients);
+//   GroupedM  - rows are expert-sorted and padded to 128 per expert; a device
+//               array maps each 128-row tile to its expert (B is per expert);
+//   GroupedK  - per-expert weight gradients: the reduction runs over the
+//               expert's padded row range, read from a device offset array.
+// Epilogues are fused: bf16 store, fp32 accumulate (residual stream, weight
+// gradients), SwiGLU forward/backward, and the two halves of the LM-head
+// cross-entropy (online log-sum-exp partials; softmax-minus-one-hot grads).
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv3 {
+
+enum class Sched : int { Dense = 0, GroupedM = 1, GroupedK = 2 };
+enum class Epi : int { StoreBF16 = 0, AddF32 = 1, AtomicAddF32 = 2, SwigluFwd = 3, SwigluBwd = 4, CeFwd = 5, CeBwd = 6 };
+
+struct GemmArgs {
+  int M;                 // valid output rows (per group for GroupedK)
+  int N;                 // valid output columns
+  int K;                 // reduction length (Dense / GroupedM)
+  int m_tiles, n_tiles, k_splits, groups;
+  int num_tiles;
+  int kb_per_split;      // Dense: K-blocks per split
+  const int* tile_group;     // GroupedM: expert of each 128-row tile (< 0: unused tile)
+  const int* group_row_off;  // GroupedK: [groups + 1] padded row offsets (multiples of 128)
+  void* out;             // primary output
+  long ldo;
+  long out_group_stride; // GroupedK: elements between consecutive experts' outputs
+  void* out2;            // SwigluFwd: pre-activations [M, 2I]
+  long ldo2;
+  const void* aux;       // SwigluBwd: pre-activations [M, 2I]
+  long ld_aux;
+  int inter;             // SwiGLU: I (the up half starts at column I of out2 / aux)
+  const long* targets;   // CE: target id per row (-100 = ignored)
+  float* part_max;       // CeFwd: [M, n_tiles]
+  float* part_sum;       // CeFwd: [M, n_tiles]
+  float* tgt_logit;      // CeFwd: [M]
+  const float* lse;      // CeBwd: [M]
+  const float* row_scale;// CeBwd: [M]
+  unsigned int* status;  // device status word (bounded-wait failures)
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
+};
+
+struct TileInfo {
+  int m0, n0, g, kb0, kb1, n_tile;
+  bool run;
+};
+
+template <Sched S>
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN_) {
+  TileInfo ti;
+  int n = t % a.n_tiles;
+  int rest = t / a.n_tiles;
+  int m = rest % a.m_tiles;
+  int outer = rest / a.m_tiles;
+  ti.n_tile = n;
+  ti.n0 = n * BN_;
+  ti.m0 = m * 128;
+  ti.g = 0;
+  ti.run = true;
+  if constexpr (S == Sched::Dense) {
+    int total = (a.K + 63) / 64;
+    ti.kb0 = outer * a.kb_per_split;
+    ti.kb1 = min(total, ti.kb0 + a.kb_per_split);
+  } else if constexpr (S == Sched::GroupedM) {
+    ti.g = a.tile_group[m];
+    ti.kb0 = 0;
+    ti.kb1 = (a.K + 63) / 64;
+    ti.run = ti.g >= 0;
+  } else {
+    ti.g = outer;
+    ti.kb0 = a.group_row_off[outer] / 64;
+    ti.kb1 = a.group_row_off[outer + 1] / 64;
+  }
+  ti.run = ti.run && (ti.kb1 > ti.kb0);
+  return ti;
+}
+
+// B_SWIGLU: B is read as two 128-row halves (gate rows, up rows) of a 4-D
+// tensor map [G][2][I][K]; BN must be 256 and the epilogue pairs column c of
+// the gate half with column c of the up half.
+template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU>
+__global__ void __launch_bounds__(192, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  using C = GemmCfg<BN>;
+  static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, last_phase = 0;
+      for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+        if (!ti.run) continue;
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status, DSV3_ERR_WAIT_EMPTY)) break;
+          uint8_t* sA = smem + stage * C::STAGE_BYTES;
+          uint8_t* sB = sA + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          const int k0 = kb * 64;
+          // GroupedK walks global rows of A and B; their maps have no group axis.
+          const int bg = (S == Sched::GroupedK) ? 0 : ti.g;
+          if constexpr (A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], ti.m0, k0);
+            tma_load_2d(sA + 8192, &tmA, &full[stage], ti.m0 + 64, k0);
+          } else {
+            tma_load_2d(sA, &tmA, &full[stage], k0, ti.m0);
+          }
+          if constexpr (B_SWIGLU) {
+            tma_load_4d(sB, &tmB, &full[stage], k0, ti.n0, 0, bg);
+            tma_load_4d(sB + 16384, &tmB, &full[stage], k0, ti.n0, 1, bg);
+          } else if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sB + j * 8192, &tmB, &full[stage], ti.n0 + 64 * j, k0, bg);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) tma_load_3d(sB + j * 16384, &tmB, &full[stage], k0, ti.n0 + 128 * j, bg);
+          }
+          issued_mask |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Every issued copy must land before the CTA may exit.
+      for (int s = 0; s < C::STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_wait_bounded(&full[s], (last_phase >> s) & 1u, nullptr, args.status, DSV3_ERR_WAIT_FULL);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(128, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+        if (!ti.run) continue;
+        const int buf = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty[buf], aphase ^ 1u, abort_flag, args.status, DSV3_ERR_WAIT_TMEM)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        bool ok = true;
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.status, DSV3_ERR_WAIT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_base = a_base + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, IDESC, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+        ++local;
+      }
+      // Drain: make sure no MMA still writes TMEM when it is freed.
+      if (issued_any) {
+        umma_commit(drain);
+        mbar_wait_bounded(drain, 0, nullptr, args.status, DSV3_ERR_WAIT_TMEM);
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int r_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+      TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+      if (!ti.run) continue;
+      const int buf = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      if (!mbar_wait_bounded(&tfull[buf], aphase, abort_flag, args.status, DSV3_ERR_WAIT_TMEM)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+      const int row = ti.m0 + r_in_tile;
+      const bool row_ok = row < args.M;
+      uint32_t r[16];
+
+      if constexpr (E == Epi::StoreBF16 || E == Epi::AddF32 || E == Epi::AtomicAddF32) {
+        char* base = reinterpret_cast<char*>(args.out);
+        if constexpr (S == Sched::GroupedK)
+          base += (size_t)ti.g * args.out_group_stride * (E == Epi::StoreBF16 ? 2 : 4);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          __syncwarp();
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col = ti.n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          const bool full16 = col + 16 <= args.N;
+          if constexpr (E == Epi::StoreBF16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + (size_t)row * args.ldo + col;
+            if (full16) {
+              uint4 v0, v1;
+              v0.x = pack_bf16x2(__uint_as_float(r[0]), __uint_as_float(r[1]));
+              v0.y = pack_bf16x2(__uint_as_float(r[2]), __uint_as_float(r[3]));
+              v0.z = pack_bf16x2(__uint_as_float(r[4]), __uint_as_float(r[5]));
+              v0.w = pack_bf16x2(__uint_as_float(r[6]), __uint_as_float(r[7]));
+              v1.x = pack_bf16x2(__uint_as_float(r[8]), __uint_as_float(r[9]));
+              v1.y = pack_bf16x2(__uint_as_float(r[10]), __uint_as_float(r[11]));
+              v1.z = pack_bf16x2(__uint_as_float(r[12]), __uint_as_float(r[13]));
+              v1.w = pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15]));
+              reinterpret_cast<uint4*>(o)[0] = v0;
+              reinterpret_cast<uint4*>(o)[1] = v1;
+            } else {
+              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] = __float2bfloat16(__uint_as_float(r[j]));
+            }
+          } else if constexpr (E == Epi::AddF32) {
+            float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
+            if (full16) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                float4 v = *reinterpret_cast<float4*>(o + j);
+                v.x += __uint_as_float(r[j]);
+                v.y += __uint_as_float(r[j + 1]);
+                v.z += __uint_as_float(r[j + 2]);
+                v.w += __uint_as_float(r[j + 3]);
+                *reinterpret_cast<float4*>(o + j) = v;
+              }
+            } else {
+              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] += __uint_as_float(r[j]);
+            }
+          } else {
+            float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
+            for (int j = 0; j < 16; ++j)
+              if (col + j < args.N) atomicAdd(o + j, __uint_as_float(r[j]));
+          }
+        }
+      } else if constexpr (E == Epi::SwigluFwd) {
+        // TMEM columns [0,128): gate, [128,256): up, for I-columns n0 .. n0+127.
+        __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(args.out);
+        __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out2);
+        uint32_t u[16];
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 16) {
+          __syncwarp();
+          tmem_ld16(tbase + c, r);
+          tmem_ld16(tbase + 128 + c, u);
+          tmem_ld_wait();
+          const int col = ti.n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          const int nv = min(16, args.N - col);
+          uint32_t hp[8], gp[8], up[8];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            // Round the pre-activations to bf16 first so forward and backward
+            // see identical gate/up values.
+            const float g0 = __bfloat162float(__float2bfloat16(__uint_as_float(r[j])));
+            const float g1 = __bfloat162float(__float2bfloat16(__uint_as_float(r[j + 1])));
+            const float u0 = __bfloat162float(__float2bfloat16(__uint_as_float(u[j])));
+            const float u1 = __bfloat162float(__float2bfloat16(__uint_as_float(u[j + 1])));
+            hp[j / 2] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+            gp[j / 2] = pack_bf16x2(g0, g1);
+            up[j / 2] = pack_bf16x2(u0, u1);
+          }
+          __nv_bfloat16* ho = h + (size_t)row * args.ldo + col;
+          __nv_bfloat16* go = gu + (size_t)row * args.ldo2 + col;
+          __nv_bfloat16* uo = gu + (size_t)row * args.ldo2 + args.inter + col;
+          if (nv == 16) {
+            reinterpret_cast<uint4*>(ho)[0] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+            reinterpret_cast<uint4*>(ho)[1] = make_uint4(hp[4], hp[5], hp[6], hp[7]);
+            reinterpret_cast<uint4*>(go)[0] = make_uint4(gp[0], gp[1], gp[2], gp[3]);
+            reinterpret_cast<uint4*>(go)[1] = make_uint4(gp[4], gp[5], gp[6], gp[7]);
+            reinterpret_cast<uint4*>(uo)[0] = make_uint4(up[0], up[1], up[2], up[3]);
+            reinterpret_cast<uint4*>(uo)[1] = make_uint4(up[4], up[5], up[6], up[7]);
+          } else {
+            const uint16_t* hs = reinterpret_cast<const uint16_t*>(hp);
+            const uint16_t* gs = reinterpret_cast<const uint16_t*>(gp);
+            const uint16_t* us = reinterpret_cast<const uint16_t*>(up);
+            for (int j = 0; j < nv; ++j) {
+              reinterpret_cast<uint16_t*>(ho)[j] = hs[j];
+              reinterpret_cast<uint16_t*>(go)[j] = gs[j];
+              reinterpret_cast<uint16_t*>(uo)[j] = us[j];
+            }
+          }
+        }
+      } else if constexpr (E == Epi::SwigluBwd) {
+        // Accumulator = dh for I-columns n0 .. n0+BN-1.  out = dgu [M, 2I].
+        const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(args.aux);
+        __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          __syncwarp();
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col = ti.n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          const int nv = min(16, args.N - col);
+          const uint16_t* gsrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + col);
+          const uint16_t* usrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + args.inter + col);
+          uint16_t gv[16], uv[16];
+          if (nv == 16) {
+            *reinterpret_cast<uint4*>(gv) = reinterpret_cast<const uint4*>(gsrc)[0];
+            *reinterpret_cast<uint4*>(gv + 8) = reinterpret_cast<const uint4*>(gsrc)[1];
+            *reinterpret_cast<uint4*>(uv) = reinterpret_cast<const uint4*>(usrc)[0];
+            *reinterpret_cast<uint4*>(uv + 8) = reinterpret_cast<const uint4*>(usrc)[1];
+          } else {
+            for (int j = 0; j < 16; ++j) {
+              gv[j] = j < nv ? gsrc[j] : 0;
+              uv[j] = j < nv ? usrc[j] : 0;
+            }
+          }
+          uint32_t dg[8], du[8];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            float o[2][2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const float g = bf16_bits_to_float(gv[j + q]);
+              const float u = bf16_bits_to_float(uv[j + q]);
+              const float dh = __uint_as_float(r[j + q]);
+              const float s = 1.0f / (1.0f + __expf(-g));
+              o[0][q] = dh * u * s * (1.0f + g * (1.0f - s));
+              o[1][q] = dh * g * s;
+            }
+            dg[j / 2] = pack_bf16x2(o[0][0], o[0][1]);
+            du[j / 2] = pack_bf16x2(o[1][0], o[1][1]);
+          }
+          __nv_bfloat16* go = dgu + (size_t)row * args.ldo + col;
+          __nv_bfloat16* uo = dgu + (size_t)row * args.ldo + args.inter + col;
+          if (nv == 16) {
+            reinterpret_cast<uint4*>(go)[0] = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+            reinterpret_cast<uint4*>(go)[1] = make_uint4(dg[4], dg[5], dg[6], dg[7]);
+            reinterpret_cast<uint4*>(uo)[0] = make_uint4(du[0], du[1], du[2], du[3]);
+            reinterpret_cast<uint4*>(uo)[1] = make_uint4(du[4], du[5], du[6], du[7]);
+          } else {
+            const uint16_t* gs = reinterpret_cast<const uint16_t*>(dg);
+            const uint16_t* us = reinterpret_cast<const uint16_t*>(du);
+            for (int j = 0; j < nv; ++j) {
+              reinterpret_cast<uint16_t*>(go)[j] = gs[j];
+              reinterpret_cast<uint16_t*>(uo)[j] = us[j];
+            }
+          }
+        }
+      } else if constexpr (E == Epi::CeFwd) {
+        const long tgt = row_ok ? args.targets[row] : -1;
+        float run_max = -INFINITY, run_sum = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          __syncwarp();
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col = ti.n0 + c;
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (col + j < args.N) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+          if (cmax == -INFINITY) continue;
+          const float nm = fmaxf(run_max, cmax);
+          float s = run_sum * __expf(run_max - nm);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (col + j < args.N) s += __expf(__uint_as_float(r[j]) - nm);
+          run_sum = s;
+          run_max = nm;
+          if (tgt >= col && tgt < col + 16 && tgt < args.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j == tgt && row_ok) args.tgt_logit[row] = __uint_as_float(r[j]);
+          }
+        }
+        if (row_ok) {
+          args.part_max[(size_t)row * args.n_tiles + ti.n_tile] = run_max;
+          args.part_sum[(size_t)row * args.n_tiles + ti.n_tile] = run_sum;
+        }
+      } else if constexpr (E == Epi::CeBwd) {
+        const long tgt = row_ok ? args.targets[row] : -1;
+        const float l = row_ok ? args.lse[row] : 0.0f;
+        const float sc = row_ok ? args.row_scale[row] : 0.0f;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          __syncwarp();
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col = ti.n0 + c;
+          if (!row_ok || col >= args.N) continue;
+          uint32_t pk[8];
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            const float p0 = (__expf(__uint_as_float(r[j]) - l) - (col + j == tgt ? 1.0f : 0.0f)) * sc;
+            const float p1 = (__expf(__uint_as_float(r[j + 1]) - l) - (col + j + 1 == tgt ? 1.0f : 0.0f)) * sc;
+            pk[j / 2] = pack_bf16x2(p0, p1);
+          }
+          if (col + 16 <= args.N) {
+            reinterpret_cast<uint4*>(o + col)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4*>(o + col)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else {
+            const uint16_t* ps = reinterpret_cast<const uint16_t*>(pk);
+            for (int j = 0; col + j < args.N; ++j) reinterpret_cast<uint16_t*>(o + col)[j] = ps[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+      ++local;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace dsv3
