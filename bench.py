@@ -1,0 +1,335 @@
+"""Headline benchmark: DeepSeek-V3-Lite 412M (MLA + MoE + MTP) pretraining throughput.
+
+``python bench.py --gpus N --steps K --warmup W`` (under torchrun for N > 1)
+runs the flagship training step on N GPUs of one node: the 412M config with
+the yaml's dims, bf16 compute, synthetic uniform-random tokens over the vocab,
+random-init weights, global batch 256 x 2048 = 524,288 tokens per optimizer
+step split over the ranks (data parallel; strong scaling), AdamW + grad
+clipping + router bias update every step.
+
+Two timed phases, both on the same trainer:
+
+* device: K optimizer steps on inputs already resident on the device,
+  bracketed by barrier + ``cuda.synchronize`` and CUDA events; the max over
+  ranks is reported as ``value`` (total tokens/s of the whole job);
+* e2e: K steps through the public API (``Pretrainer.train_step``) where every
+  micro-batch is copied host->device from pinned memory and every step's loss
+  is read back to the host -> ``e2e``.
+
+``--impl reference`` runs the unmodified reference (installed in
+``baseline/_ref``) through its own ``Pretrainer.train_step`` on the same
+config, batch and timing (``torch.nn.parallel.DistributedDataParallel`` around
+its model for N > 1, since the reference has no multi-GPU code).
+
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+BASELINE_TOKENS_PER_S = None  # the reference publishes no measured number
+METRIC = "train tokens/sec (device, max over ranks)"
+GLOBAL_SEQS = 256
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--micro-batch", type=int, default=0, help="sequences per micro-step per rank (0 = auto)")
+    ap.add_argument("--global-seqs", type=int, default=GLOBAL_SEQS)
+    ap.add_argument("--config", type=str, default="")
+    return ap.parse_args()
+
+
+def init_dist(n):
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        mhz.sort()
+        return {"sm_mhz": mhz[len(mhz) // 2] if mhz else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def load_yaml(path):
+    import yaml
+    with open(path) as f:
+        return yaml.safe_load(f)
+
+
+def timed_steps(run_step, steps, world, local):
+    """Barrier + sync, CUDA events around `steps` calls, sync; returns ms/step (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    wall0 = time.perf_counter()
+    t0.record()
+    for i in range(steps):
+        run_step(i)
+    t1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t0.elapsed_time(t1) / steps
+    return max_over_ranks(ms, world), max_over_ranks(wall * 1000.0 / steps, world), clocks
+
+
+def make_inputs(vocab, seqs, seq_len, seed, device):
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    data = torch.randint(0, vocab, (seqs, seq_len + 1), generator=g, dtype=torch.long)
+    return data.pin_memory() if device == "pinned" else data.to(device)
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    sys.path.insert(0, str(ROOT / "deepseek-v3-lite_b200"))
+    from ops import _ext
+    from training.pretrain import Pretrainer, config_from_yaml
+    cfg_path = args.config or str(ROOT / "deepseek-v3-lite_b200" / "configs" / "pretrain_412m.yaml")
+    y = load_yaml(cfg_path)
+    S = y["model"]["max_seq_len"]
+    per_rank = args.global_seqs // world
+    micro = args.micro_batch or min(per_rank, 16)
+    accum = per_rank // micro
+    cfg = config_from_yaml(y)
+    cfg.batch_size, cfg.gradient_accumulation_steps = micro, accum
+    cfg.max_steps = 10 ** 9
+    cfg.warmup_steps = 10
+    cfg.log_per_component_params = False
+    cfg.checkpoint_dir = "/tmp/dsv3_bench_ckpt"
+    trainer = Pretrainer(cfg)
+    vocab = y["model"]["vocab_size"]
+    dev = torch.device("cuda", local)
+    dev_data = [make_inputs(vocab, micro, S, 1000 + 97 * rank + i, dev) for i in range(accum)]
+    host_data = [make_inputs(vocab, micro, S, 5000 + 97 * rank + i, "pinned") for i in range(accum)]
+    micro_step = [0]
+
+    def step_device(_):
+        last = None
+        for i in range(accum):
+            d = dev_data[i]
+            last = trainer.train_step(d[:, :-1], d[:, 1:], micro_step[0])
+            micro_step[0] += 1
+        return last
+
+    loss_box = []
+
+    def step_e2e(_):
+        last = None
+        for i in range(accum):
+            d = host_data[i].to(dev, non_blocking=True)
+            last = trainer.train_step(d[:, :-1], d[:, 1:], micro_step[0])
+            micro_step[0] += 1
+        loss_box.append(float(last["loss"]))   # device -> host read of the step's loss
+        return last
+
+    for i in range(args.warmup):
+        step_device(i)
+    torch.cuda.synchronize()
+    _ext.count_launches(True)
+    ms, wall_ms, clocks = timed_steps(step_device, args.steps, world, local)
+    launches = _ext.count_launches(False) // max(1, args.steps)
+    e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, args.steps, world, local)
+    trainer.engine.check()
+    tokens_per_step = args.global_seqs * S
+    value = tokens_per_step / (ms / 1000.0)
+    e2e = tokens_per_step / (max(e2e_ms, e2e_wall_ms) / 1000.0)
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
+        "dtype": "bf16", "data": "synthetic uniform tokens, random-init weights",
+        "config": {"model": "deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 V100018)",
+                   "global_batch": args.global_seqs * S, "seq_len": S, "parallelism": f"dp{world}",
+                   "micro_batch_seqs": micro, "grad_accum": accum,
+                   "l2": "working set (weights+activations, GBs) far exceeds the 126 MB L2"},
+        "clocks": clocks,
+        "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(accum * micro * (S + 1) * 8),
+                "d2h_bytes_per_step": 4, "last_loss": loss_box[-1] if loss_box else None},
+        "gpu_launches": int(launches),
+        "impl": "ours",
+    }
+
+
+def run_reference(args, rank, world, local):
+    import torch
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "training" / "pretrain.py").exists():
+        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, str(ref_root))
+    from training.pretrain import Pretrainer, TrainingConfig  # the reference's own modules
+    y = load_yaml(str(ref_root / "configs" / "pretrain_a100_422m.yaml"))
+    t, m = y["training"], y["model"]
+    S = m["max_seq_len"]
+    per_rank = args.global_seqs // world
+    micro = args.micro_batch or min(per_rank, t.get("micro_batch_size", 8))
+    accum = per_rank // micro
+    cfg = TrainingConfig(model_config=y, data_path="/nonexistent", checkpoint_dir="/tmp/dsv3_ref_ckpt",
+                         max_seq_len=S, vocab_size=m["vocab_size"], batch_size=micro,
+                         gradient_accumulation_steps=accum, max_steps=10 ** 9, warmup_steps=10, lr=t["lr"],
+                         min_lr_ratio=t["min_lr_ratio"], weight_decay=t["weight_decay"], max_grad_norm=t["grad_clip"],
+                         grad_checkpoint=t["grad_checkpoint"], compile_model=t["compile"],
+                         mtp_weight=t["mtp_loss_weight"], bias_update_speed=t["bias_update_speed"],
+                         bias_update_every=t["bias_update_every"], nan_guard=t["nan_guard"], mup_lr=t["mup_lr"],
+                         log_per_component_params=False)
+    trainer = Pretrainer(cfg)
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        trainer.model = DDP(trainer.model, device_ids=[local], find_unused_parameters=True)
+    dev = torch.device("cuda", local)
+    dev_data = [make_inputs(m["vocab_size"], micro, S, 1000 + 97 * rank + i, dev) for i in range(accum)]
+    host_data = [make_inputs(m["vocab_size"], micro, S, 5000 + 97 * rank + i, "pinned") for i in range(accum)]
+    micro_step = [0]
+
+    def one(d):
+        boundary = (micro_step[0] + 1) % accum == 0
+        if world > 1 and not boundary:
+            with trainer.model.no_sync():
+                out = trainer.train_step(d[:, :-1], d[:, 1:], micro_step[0])
+        else:
+            out = trainer.train_step(d[:, :-1], d[:, 1:], micro_step[0])
+        micro_step[0] += 1
+        return out
+
+    def step_device(_):
+        for i in range(accum):
+            one(dev_data[i])
+
+    loss_box = []
+
+    def step_e2e(_):
+        last = None
+        for i in range(accum):
+            last = one(host_data[i].to(dev, non_blocking=True))
+        if last is not None:
+            loss_box.append(float(last["loss"]))
+
+    for i in range(args.warmup):
+        step_device(i)
+    torch.cuda.synchronize()
+    ms, wall_ms, clocks = timed_steps(step_device, args.steps, world, local)
+    e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, args.steps, world, local)
+    tokens_per_step = args.global_seqs * S
+    value = tokens_per_step / (ms / 1000.0)
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 autocast (fp32 master)",
+        "data": "synthetic uniform tokens, random-init weights",
+        "config": {"model": "reference 412m yaml", "global_batch": tokens_per_step, "seq_len": S,
+                   "parallelism": f"ddp{world}", "micro_batch_seqs": micro, "grad_accum": accum,
+                   "torch_compile_mode": os.environ.get("TORCH_COMPILE_MODE", "max-autotune")},
+        "clocks": clocks,
+        "e2e": {"value": round(tokens_per_step / (max(e2e_ms, e2e_wall_ms) / 1000.0), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(accum * micro * (S + 1) * 8), "d2h_bytes_per_step": 4},
+        "impl": "reference",
+    }
+
+
+def main():
+    args = parse()
+    import torch
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": args.impl, "unavailable": "no CUDA device"}))
+        return
+    rank, world, local = init_dist(args.gpus)
+    try:
+        res = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    finally:
+        pass
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

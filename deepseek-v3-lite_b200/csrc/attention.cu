@@ -67,11 +67,23 @@ __device__ __forceinline__ void load_tile_async(bf16* s, const bf16* g, int rows
   }
 }
 
+// Same as load_tile_async with an explicit global row stride (elements).
+template <int D, int SD>
+__device__ __forceinline__ void load_tile_strided(bf16* s, const bf16* g, long ld, int rows, int valid_rows, int tid,
+                                                  int nthr) {
+  constexpr int CH = D / 8;
+  for (int c = tid; c < rows * CH; c += nthr) {
+    const int r = c / CH, cc = (c % CH) * 8;
+    const bool ok = r < valid_rows;
+    cp_async16(s + r * SD + cc, g + (size_t)(ok ? r : 0) * ld + cc, ok);
+  }
+}
+
 template <int DQK, int DV>
 __global__ void __launch_bounds__(128) fa_fwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                      const bf16* __restrict__ V, bf16* __restrict__ O,
                                                      float* __restrict__ L, int Sq, int Sk, int q_off,
-                                                     float scale_log2, int causal) {
+                                                     float scale_log2, int causal, int H) {
   constexpr int QS = DQK + 8, VS = DV + 8;
   extern __shared__ __align__(16) uint8_t fa_smem[];
   bf16* sQ = reinterpret_cast<bf16*>(fa_smem);
@@ -193,7 +205,8 @@ __global__ void __launch_bounds__(128) fa_fwd_kernel(const bf16* __restrict__ Q,
   }
   cp_async_wait<0>();
 
-  bf16* Ob = O + (size_t)bh * Sq * DV;
+  // O is token-major: [B, Sq, H, DV]
+  bf16* Ob = O + ((size_t)(bh / H) * Sq * H + (bh % H)) * DV;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int qr = qrow0 + r * 8;
@@ -202,23 +215,25 @@ __global__ void __launch_bounds__(128) fa_fwd_kernel(const bf16* __restrict__ Q,
 #pragma unroll
     for (int i = 0; i < DV / 8; ++i) {
       const int col = i * 8 + 2 * tig;
-      *reinterpret_cast<uint32_t*>(Ob + (size_t)qr * DV + col) = pack_bf16x2(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
+      *reinterpret_cast<uint32_t*>(Ob + (size_t)qr * H * DV + col) = pack_bf16x2(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
     }
     if (tig == 0) L[(size_t)bh * Sq + qr] = lrow[r] > 0.f ? mrow[r] + log2f(lrow[r]) : -INFINITY;
   }
 }
 
 // delta[row] = sum_d dO[row, d] * O[row, d]
+// O / dO token-major [B, S, H, DV]; row r = (b*S + s)*H + h; delta is [B*H, S].
 template <int DV>
 __global__ void fa_bwd_pre_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, float* __restrict__ delta,
-                                  long rows) {
+                                  long rows, int S, int H) {
   const long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
   float acc = 0.f;
   for (int c = lane; c < DV; c += 32) acc += __bfloat162float(O[r * DV + c]) * __bfloat162float(dO[r * DV + c]);
   acc = warp_sum(acc);
-  if (lane == 0) delta[r] = acc;
+  const long h = r % H, bs = r / H, b = bs / S, s = bs % S;
+  if (lane == 0) delta[(b * H + h) * S + s] = acc;
 }
 
 template <int DQK, int DV>
@@ -227,7 +242,7 @@ __global__ void __launch_bounds__(128) fa_bwd_kernel(const bf16* __restrict__ Q,
                                                      const float* __restrict__ L, const float* __restrict__ delta,
                                                      float* __restrict__ dQ, float* __restrict__ dK,
                                                      float* __restrict__ dV, int Sq, int Sk, int q_off,
-                                                     float scale_log2, float scale, int causal) {
+                                                     float scale_log2, float scale, int causal, int H) {
   constexpr int QS = DQK + 8, VS = DV + 8, PS = BM + 8;
   extern __shared__ __align__(16) uint8_t fa_smem[];
   bf16* sK = reinterpret_cast<bf16*>(fa_smem);
@@ -243,7 +258,7 @@ __global__ void __launch_bounds__(128) fa_bwd_kernel(const bf16* __restrict__ Q,
   const bf16* Qb = Q + (size_t)bh * Sq * DQK;
   const bf16* Kb = K + (size_t)bh * Sk * DQK;
   const bf16* Vb = V + (size_t)bh * Sk * DV;
-  const bf16* dOb = dO + (size_t)bh * Sq * DV;
+  const bf16* dOb = dO + ((size_t)(bh / H) * Sq * H + (bh % H)) * DV;  // token-major, row stride H*DV
 
   load_tile_async<DQK, QS>(sK, Kb + (size_t)n0 * DQK, BN, Sk - n0, tid, 128);
   load_tile_async<DV, VS>(sV, Vb + (size_t)n0 * DV, BN, Sk - n0, tid, 128);
@@ -260,7 +275,7 @@ __global__ void __launch_bounds__(128) fa_bwd_kernel(const bf16* __restrict__ Q,
   const int key0 = n0 + warp * 16 + g;  // this thread's keys: key0, key0 + 8
   for (int m0 = qstart; m0 < Sq; m0 += BM) {
     load_tile_async<DQK, QS>(sQ, Qb + (size_t)m0 * DQK, BM, Sq - m0, tid, 128);
-    load_tile_async<DV, VS>(sdO, dOb + (size_t)m0 * DV, BM, Sq - m0, tid, 128);
+    load_tile_strided<DV, VS>(sdO, dOb + (size_t)m0 * H * DV, (long)H * DV, BM, Sq - m0, tid, 128);
     cp_async_commit();
     for (int i = tid; i < BM; i += 128) {
       const bool ok = m0 + i < Sq;
@@ -482,7 +497,7 @@ size_t bwd_smem() {
 
 template <int DQK, int DV>
 void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse, int q_off,
-             double scale, bool causal) {
+             double scale, bool causal, int H) {
   const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1);
   auto kern = fa_fwd_kernel<DQK, DV>;
   const size_t smem = fwd_smem<DQK, DV>();
@@ -495,19 +510,19 @@ void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::
   kern<<<grid, 128, smem, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
       reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq,
-      Sk, q_off, (float)(scale * 1.4426950408889634), causal ? 1 : 0);
+      Sk, q_off, (float)(scale * 1.4426950408889634), causal ? 1 : 0, H);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 template <int DQK, int DV>
 void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
-             at::Tensor& dv, int q_off, double scale, bool causal) {
+             at::Tensor& dv, int q_off, double scale, bool causal, int H) {
   const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1);
   auto st = at::cuda::getCurrentCUDAStream();
   const long rows = (long)BH * Sq;
   fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
-      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows);
+      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto kern = fa_bwd_kernel<DQK, DV>;
   const size_t smem = bwd_smem<DQK, DV>();
@@ -520,7 +535,7 @@ void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, cons
   kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
       reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
       lse.data_ptr<float>(), delta.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(),
-      dv.data_ptr<float>(), Sq, Sk, q_off, (float)(scale * 1.4426950408889634), (float)scale, causal ? 1 : 0);
+      dv.data_ptr<float>(), Sq, Sk, q_off, (float)(scale * 1.4426950408889634), (float)scale, causal ? 1 : 0, H);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -532,30 +547,35 @@ void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, cons
 
 }  // namespace
 
-// q, k: [BH, S, DQK] bf16; v: [BH, Sk, DV]; o: [BH, Sq, DV] bf16; lse: [BH, Sq] fp32 (log2 domain).
+// q, k: [B*H, S, DQK] bf16; v: [B*H, Sk, DV]; o: token-major [B, Sq, H, DV] bf16;
+// lse: [B*H, Sq] fp32 (log2 domain).
 void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-               int64_t q_off, double scale, bool causal) {
+               int64_t q_off, double scale, bool causal, int64_t H) {
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(), "flash_fwd: contiguous");
   const at::cuda::CUDAGuard guard(q.device());
   const int dqk = q.size(2), dvv = v.size(2);
-  DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(32, 16, (run_fwd<32, 16>(q, k, v, o, lse, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(192, 128, (run_fwd<192, 128>(q, k, v, o, lse, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(32, 16, (run_fwd<32, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(16, 16, (run_fwd<16, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(32, 32, (run_fwd<32, 32>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(192, 128, (run_fwd<192, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   TORCH_CHECK(false, "flash_fwd: unsupported head dims ", dqk, "/", dvv);
 }
 
 void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
                const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
-               at::Tensor& dv, int64_t q_off, double scale, bool causal) {
+               at::Tensor& dv, int64_t q_off, double scale, bool causal, int64_t H) {
   const at::cuda::CUDAGuard guard(q.device());
   const int dqk = q.size(2), dvv = v.size(2);
-  DSV3_FA_DISPATCH(80, 64, (run_bwd<80, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(32, 16, (run_bwd<32, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(64, 64, (run_bwd<64, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(128, 128, (run_bwd<128, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
-  DSV3_FA_DISPATCH(192, 128, (run_bwd<192, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal)))
+  DSV3_FA_DISPATCH(80, 64, (run_bwd<80, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(32, 16, (run_bwd<32, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(16, 16, (run_bwd<16, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(32, 32, (run_bwd<32, 32>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_bwd<64, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(128, 128, (run_bwd<128, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(192, 128, (run_bwd<192, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   TORCH_CHECK(false, "flash_bwd: unsupported head dims ", dqk, "/", dvv);
 }
 

@@ -296,6 +296,27 @@ __global__ void ce_reduce_kernel(const float* __restrict__ loss_rows, const long
   }
 }
 
+// ---------------------------------------------------- generic head packing
+// dst[b*H + h, s, 0:hd] = src[(b*S + s), col0 + h*hd + (0:hd)], zero-padded to DP.
+__global__ void heads_pack_kernel(const __nv_bfloat16* __restrict__ src, long ld, int col0, int H, int hd, int S,
+                                  int DP, __nv_bfloat16* __restrict__ dst) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  const int b = t / S, s = t % S;
+  __nv_bfloat16* d = dst + (((size_t)b * H + h) * S + s) * DP;
+  const __nv_bfloat16* r = src + (size_t)t * ld + col0 + (size_t)h * hd;
+  for (int c = threadIdx.x; c < DP; c += blockDim.x) d[c] = c < hd ? r[c] : __float2bfloat16(0.f);
+}
+
+// Inverse for gradients: dst[(b*S + s), col0 + h*hd + c] = bf16(src[b*H + h, s, c]) (c < hd).
+__global__ void heads_unpack_kernel(const float* __restrict__ src, int H, int hd, int S, int DP,
+                                    __nv_bfloat16* __restrict__ dst, long ld, int col0) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  const int b = t / S, s = t % S;
+  const float* r = src + (((size_t)b * H + h) * S + s) * DP;
+  __nv_bfloat16* d = dst + (size_t)t * ld + col0 + (size_t)h * hd;
+  for (int c = threadIdx.x; c < hd; c += blockDim.x) d[c] = __float2bfloat16(r[c]);
+}
+
 int blocks_for(long n, int per) { return (int)((n + per - 1) / per); }
 
 }  // namespace
@@ -443,7 +464,26 @@ void ce_reduce(const at::Tensor& loss_rows, const at::Tensor& tgt, const at::Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void heads_pack(const at::Tensor& src, int64_t col0, int64_t H, int64_t hd, int64_t S, at::Tensor& dst) {
+  const int T = src.size(0), DP = dst.size(-1);
+  const at::cuda::CUDAGuard guard(src.device());
+  heads_pack_kernel<<<dim3(T, H), 64, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), col0, H, hd, S, DP,
+      reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void heads_unpack(const at::Tensor& src, int64_t H, int64_t hd, int64_t S, at::Tensor& dst, int64_t col0) {
+  const int T = dst.size(0), DP = src.size(-1);
+  const at::cuda::CUDAGuard guard(src.device());
+  heads_unpack_kernel<<<dim3(T, H), 64, 0, at::cuda::getCurrentCUDAStream()>>>(src.data_ptr<float>(), H, hd, S, DP,
+      reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), dst.stride(0), col0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void register_elementwise(pybind11::module_& m) {
+  m.def("heads_pack", &heads_pack, "[T, ld] head slices -> [B*H, S, DP] (zero padded)");
+  m.def("heads_unpack", &heads_unpack, "gradient of heads_pack (fp32 -> bf16 strided)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd, "y(bf16) = rmsnorm(x) * w; stores 1/rms per row");
   m.def("rmsnorm_bwd", &rmsnorm_bwd, "RMSNorm backward (dx accumulate or store, dw +=)");
   m.def("rope_inplace", &rope_inplace, "rotate interleaved pairs in place (optionally inverse)");

@@ -13,6 +13,42 @@ import torch  # noqa: F401  (loads libc10 / libtorch before the extension)
 _mod = None
 _err = None
 
+# Kernels launched per entry point (entries not listed launch one kernel).
+_LAUNCHES_PER_CALL = {"flash_bwd": 2, "latent_decode": 2, "grad_sqsum": 3, "status_read": 0, "status_reset": 0}
+_counting = [False, 0]
+
+
+class _CountingModule:
+    """Forwards to the extension; while counting is on, tallies kernel launches."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        w = self._cache.get(name)
+        if w is None:
+            n = _LAUNCHES_PER_CALL.get(name, 1)
+
+            def w(*a, **k):
+                if _counting[0]:
+                    _counting[1] += n
+                return fn(*a, **k)
+            self._cache[name] = w
+        return w
+
+
+def count_launches(enable: bool) -> int:
+    """Start (``True``) or stop (``False``) counting; returns the count so far."""
+    n = _counting[1]
+    _counting[0] = enable
+    if enable:
+        _counting[1] = 0
+    return n
+
 
 def native():
     """The compiled kernel module; raises ``RuntimeError`` if it is not built."""
@@ -20,7 +56,7 @@ def native():
     if _mod is not None:
         return _mod
     try:
-        _mod = importlib.import_module("ops._dsv3_C")
+        _mod = _CountingModule(importlib.import_module("ops._dsv3_C"))
     except ImportError as exc:  # not built, or built for another interpreter
         _err = exc
         raise RuntimeError(

@@ -1,0 +1,561 @@
+"""The B200 training engine: explicit forward and backward of the whole model
+(Transformer + MTP + fused LM-head cross-entropy) on the sm_100a kernels.
+
+There is no autograd and no tracing compiler in the step.  Each layer's
+forward saves exactly what its backward needs; the backward walks the layers
+in reverse, accumulating weight gradients straight into the fp32 flat gradient
+buffers (``ops.flat``) with the weight-gradient GEMM epilogues.  The residual
+stream and its gradient are fp32 (as the reference's autocast run keeps them:
+embedding output and residual adds are fp32 there too); every GEMM operand is
+bf16 with fp32 accumulation in TMEM.
+
+Per micro-batch the kernel sequence is (``L`` layers, ``T = B * S`` tokens):
+
+forward, per layer
+  RMSNorm -> q / kv_a projections (tcgen05 GEMM) -> latent RMSNorm -> kv_b
+  projection -> Q/K/V packing with RoPE -> flash attention -> o-projection
+  accumulated into the fp32 residual (GEMM epilogue) -> RMSNorm ->
+  dense SwiGLU (fused gate/up GEMM + SwiGLU epilogue, down GEMM into the
+  residual) or MoE (router GEMM -> top-k kernel -> padded expert permutation
+  -> gather -> grouped SwiGLU GEMM -> grouped down GEMM -> weighted combine
+  into the residual, plus the shared expert)
+head
+  final RMSNorm, MTP block (same kernels), one fused LM-head + CE pass over
+  main and MTP rows (no logits in memory), log-sum-exp combine, per-segment
+  mean.
+backward
+  CE gradient GEMM (chunked dlogits) -> MTP backward -> final-norm backward ->
+  layers in reverse -> embedding scatter-add.
+
+Semantics follow the reference model exactly (see ``models/``); the loss and
+gradients are checked against the eager PyTorch model in the GPU tests.
+"""
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+
+from ._ext import native, check_status
+from .flat import FlatAdamW, FlatParams
+from .rope import rope_cos_sin
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+
+
+def _pad(n: int, m: int) -> int:
+    return (n + m - 1) // m * m
+
+
+class _Ctx(dict):
+    """Saved tensors of one layer for its backward."""
+    __getattr__ = dict.__getitem__
+    __setattr__ = dict.__setitem__
+
+
+class TrainEngine:
+    """Fused forward/backward + optimizer for ``Transformer`` (+ MTP) on one GPU
+    (one rank of a data-parallel job when ``torch.distributed`` is up)."""
+
+    def __init__(self, model, mtp_wrapper, config, groups, dp_group=None):
+        self.model = model
+        self.mtp = mtp_wrapper
+        self.config = config
+        self.cfg = model.config
+        self.device = next(model.parameters()).device
+        self.C = native()
+        c = self.cfg
+        self.D = c["dim"]
+        self.H = c["n_heads"]
+        self.dn, self.dr, self.dv = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+        self.R = c["kv_lora_rank"]
+        self.DP = max(32, _pad(self.dn + self.dr, 16))
+        self.V = c["vocab_size"]
+        self.Vp = _pad(self.V, 64)
+        self.q_lora = c["q_lora_rank"]
+        if self.q_lora > 0:
+            raise NotImplementedError("q_lora_rank > 0 is not wired into the fused engine yet")
+        self.max_seq_len = c["max_seq_len"]
+        self.ce_chunk = int(os.environ.get("DSV3_CE_CHUNK_ROWS", "16384"))
+        self._build_flat(groups)
+        self.optimizer = FlatAdamW(groups, self.flats, lr=config.lr, betas=(config.beta1, config.beta2))
+        cos, sin = rope_cos_sin(self.max_seq_len, self.dr, float(c["rope_theta"]), self.device)
+        self.cos, self.sin = cos, sin
+        self.world_size = 1
+        self.rank = 0
+        self.dp = None
+        if torch.distributed.is_available() and torch.distributed.is_initialized():
+            from parallel.dp import DataParallel
+            self.dp = DataParallel(self, group=dp_group)
+            self.world_size = self.dp.world_size
+            self.rank = self.dp.rank
+        self._last_losses: Optional[torch.Tensor] = None
+        self._finite = torch.ones(1, dtype=torch.bool, device=self.device)
+
+    # ---------------------------------------------------------------- layout
+    def _build_flat(self, groups) -> None:
+        """Pack parameters into contiguous blocks the kernels can address.
+
+        SwiGLU weights get dedicated blocks ([w1, w3] per expert, then all
+        w2) so the grouped GEMMs see ``[E, 2, I, D]`` and ``[E, D, I]``
+        operands; every other decayed tensor is its own block.  Undecayed
+        (1-D) parameters live in a second buffer.
+        """
+        m = self.model
+        blocks: List[List[torch.nn.Parameter]] = []
+        placed = set()
+
+        def add(block):
+            block = [p for p in block if id(p) not in placed]
+            for p in block:
+                placed.add(id(p))
+            if block:
+                blocks.append(block)
+
+        for layer in m.layers:
+            ffn = layer.ffn
+            if hasattr(ffn, "experts"):
+                add([w for e in ffn.experts for w in (e.w1.weight, e.w3.weight)])
+                add([e.w2.weight for e in ffn.experts])
+                for e in ffn.shared_experts:
+                    add([e.w1.weight, e.w3.weight])
+                    add([e.w2.weight])
+            else:
+                add([ffn.w1.weight, ffn.w3.weight])
+                add([ffn.w2.weight])
+        if self.mtp is not None:
+            for mod in self.mtp.mtp_modules:
+                add([mod.block.w1.weight, mod.block.w3.weight])
+                add([mod.block.w2.weight])
+        for p in groups[0]["params"]:
+            add([p])
+        decay_ids = {id(p) for p in groups[0]["params"]}
+        if any(id(p) not in decay_ids for b in blocks for p in b):
+            raise RuntimeError("a packed block contains an undecayed parameter")
+        self.flat_decay = FlatParams(blocks, self.device)
+        self.flat_nodecay = FlatParams([[p] for p in groups[1]["params"]], self.device)
+        self.flats = [self.flat_decay, self.flat_nodecay]
+
+    def _fl(self, p) -> FlatParams:
+        return self.flat_decay if id(p) in self.flat_decay.offsets else self.flat_nodecay
+
+    def w(self, p) -> torch.Tensor:
+        """bf16 shadow of parameter ``p``."""
+        return self._fl(p).view(self._fl(p).shadow, p)
+
+    def g(self, p) -> torch.Tensor:
+        """fp32 gradient buffer of parameter ``p``."""
+        return self._fl(p).view(self._fl(p).grad, p)
+
+    def f32(self, p) -> torch.Tensor:
+        return self._fl(p).view(self._fl(p).master, p)
+
+    def swiglu_w13(self, w1, n_groups: int) -> torch.Tensor:
+        I, D = w1.shape
+        fl = self._fl(w1)
+        return fl.block_view(fl.shadow, w1, (n_groups, 2, I, D))
+
+    def swiglu_g13(self, w1, n_groups: int) -> torch.Tensor:
+        I, D = w1.shape
+        fl = self._fl(w1)
+        return fl.block_view(fl.grad, w1, (n_groups, 2 * I, D))
+
+    def stacked(self, w, n_groups: int, grad: bool = False) -> torch.Tensor:
+        fl = self._fl(w)
+        return fl.block_view(fl.grad if grad else fl.shadow, w, (n_groups,) + tuple(w.shape))
+
+    # --------------------------------------------------------------- helpers
+    def _norm(self, x, weight_param, eps=1e-6):
+        T = x.shape[0]
+        y = torch.empty(T, x.shape[1], dtype=BF16, device=self.device)
+        r = torch.empty(T, dtype=F32, device=self.device)
+        self.C.rmsnorm_fwd(x, self.f32(weight_param), eps, y, r)
+        return y, r
+
+    def _linear(self, x, p, out_dtype=BF16):
+        y = torch.empty(x.shape[0], p.shape[0], dtype=out_dtype, device=self.device)
+        if out_dtype == F32:
+            y.zero_()
+        self.C.linear_fwd(x, self.w(p), y)
+        return y
+
+    def _linear_bwd(self, dy, x, p, dx_acc=None):
+        """dW += dy^T x; returns dx (bf16) unless ``dx_acc`` (fp32) is given."""
+        self.C.linear_wgrad(dy, x, self.g(p))
+        if dx_acc is not None:
+            self.C.linear_dgrad(dy, self.w(p), dx_acc)
+            return dx_acc
+        dx = torch.empty(dy.shape[0], p.shape[1], dtype=BF16, device=self.device)
+        self.C.linear_dgrad(dy, self.w(p), dx)
+        return dx
+
+    # ------------------------------------------------------------ attention
+    def _mla_fwd(self, attn, xn, B, S):
+        C, H, dn, dr, dv, R = self.C, self.H, self.dn, self.dr, self.dv, self.R
+        T = B * S
+        ctx = _Ctx(xn=xn)
+        q = self._linear(xn, attn.wq.weight)                          # [T, H*(dn+dr)]
+        kv_a = self._linear(xn, attn.wkv_a.weight)                    # [T, R+dr]
+        lat = torch.empty(T, R, dtype=BF16, device=self.device)
+        rkv = torch.empty(T, dtype=F32, device=self.device)
+        C.rmsnorm_fwd(kv_a[:, :R], self.f32(attn.kv_norm.weight), 1e-6, lat, rkv)
+        kvb = self._linear(lat, attn.wkv_b.weight)                    # [T, H*(dn+dv)]
+        Q = torch.empty(B * H, S, self.DP, dtype=BF16, device=self.device)
+        K = torch.empty_like(Q)
+        Vt = torch.empty(B * H, S, dv, dtype=BF16, device=self.device)
+        C.mla_pack(q, kvb, kv_a[:, R:], Q, K, Vt, B, S, H, dn, dr, dv, self.cos, self.sin, 0)
+        O = torch.empty(T, H * dv, dtype=BF16, device=self.device)
+        L = torch.empty(B * H, S, dtype=F32, device=self.device)
+        C.flash_fwd(Q, K, Vt, O, L, 0, attn.softmax_scale, True, H)
+        ctx.update(kv_a=kv_a, lat=lat, rkv=rkv, Q=Q, K=K, V=Vt, O=O, L=L)
+        return ctx
+
+    def _mla_bwd(self, attn, ctx, dres_bf16, dxn_acc, B, S):
+        """dres_bf16: gradient of the o-projection output.  Accumulates into dxn_acc (fp32)."""
+        C, H, dn, dr, dv, R = self.C, self.H, self.dn, self.dr, self.dv, self.R
+        T = B * S
+        dO = self._linear_bwd(dres_bf16, ctx.O, attn.wo.weight)       # [T, H*dv]
+        dQ = torch.zeros(B * H, S, self.DP, dtype=F32, device=self.device)
+        dK = torch.empty_like(dQ)
+        dV = torch.empty(B * H, S, dv, dtype=F32, device=self.device)
+        delta = torch.empty(B * H, S, dtype=F32, device=self.device)
+        C.flash_bwd(ctx.Q, ctx.K, ctx.V, ctx.O, dO, ctx.L, delta, dQ, dK, dV, 0, attn.softmax_scale, True, H)
+        dq = torch.empty(T, H * (dn + dr), dtype=BF16, device=self.device)
+        dkvb = torch.empty(T, H * (dn + dv), dtype=BF16, device=self.device)
+        dkv_a = torch.empty(T, R + dr, dtype=BF16, device=self.device)
+        C.mla_unpack(dQ, dK, dV, dq, dkvb, dkv_a[:, R:], B, S, H, dn, dr, dv, self.cos, self.sin, 0)
+        dlat = self._linear_bwd(dkvb, ctx.lat, attn.wkv_b.weight)
+        C.rmsnorm_bwd(dlat, ctx.kv_a[:, :R], self.f32(attn.kv_norm.weight), ctx.rkv, None, dkv_a[:, :R], None,
+                      self.g(attn.kv_norm.weight))
+        self._linear_bwd(dkv_a, ctx.xn, attn.wkv_a.weight, dx_acc=dxn_acc)
+        self._linear_bwd(dq, ctx.xn, attn.wq.weight, dx_acc=dxn_acc)
+
+    # ------------------------------------------------------------------ FFN
+    def _swiglu_dense_fwd(self, w1, w2, xn, resid):
+        """resid += w2(silu(w1 x) * w3 x) with one fused gate/up GEMM."""
+        T = xn.shape[0]
+        I = w1.shape[0]
+        h = torch.empty(T, I, dtype=BF16, device=self.device)
+        gu = torch.empty(T, 2 * I, dtype=BF16, device=self.device)
+        self.C.swiglu_fwd(xn, self.swiglu_w13(w1, 1), self._empty_i32, h, gu)
+        self.C.linear_fwd(h, self.w(w2), resid)
+        return _Ctx(h=h, gu=gu)
+
+    def _swiglu_dense_bwd(self, w1, w2, ctx, xn, dres_bf16, dxn_acc):
+        I = w1.shape[0]
+        T = xn.shape[0]
+        dgu = torch.empty(T, 2 * I, dtype=BF16, device=self.device)
+        self.C.swiglu_dgrad(dres_bf16, self.stacked(w2, 1), self._empty_i32, ctx.gu, dgu)
+        self.C.linear_wgrad(dres_bf16, ctx.h, self.g(w2))
+        w13 = self.swiglu_w13(w1, 1).view(2 * I, -1)
+        self.C.linear_dgrad(dgu, w13, dxn_acc)
+        self.C.linear_wgrad(dgu, xn, self.swiglu_g13(w1, 1).view(2 * I, -1))
+
+    def _moe_fwd(self, moe, xn, resid):
+        C = self.C
+        T = xn.shape[0]
+        E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
+        Ep = _pad(E, 8)
+        logits = torch.zeros(T, Ep, dtype=F32, device=self.device)
+        C.linear_fwd(xn, self.w(moe.gate.weight), logits[:, :E])
+        idx = torch.empty(T, k, dtype=torch.int32, device=self.device)
+        wts = torch.empty(T, k, dtype=F32, device=self.device)
+        ssel = torch.empty(T, k, dtype=F32, device=self.device)
+        counts = torch.zeros(E, dtype=torch.int32, device=self.device)
+        C.router_topk(logits, moe.gate.bias, E, k, float(moe.gate.route_scale), idx, wts, ssel, counts)
+        P = _pad(T * k + E * 127, 128)
+        row_off = torch.empty(E + 1, dtype=torch.int32, device=self.device)
+        tile_group = torch.empty(P // 128, dtype=torch.int32, device=self.device)
+        cursor = torch.empty(E, dtype=torch.int32, device=self.device)
+        src = torch.empty(P, dtype=torch.int32, device=self.device)
+        dst = torch.empty(T, k, dtype=torch.int32, device=self.device)
+        C.permute_plan(counts, row_off, tile_group, cursor, src)
+        C.permute_scatter(idx, row_off, cursor, src, dst)
+        xs = torch.empty(P, self.D, dtype=BF16, device=self.device)
+        C.gather_rows(xn, src, k, xs)
+        w1 = moe.experts[0].w1.weight
+        h = torch.empty(P, I, dtype=BF16, device=self.device)
+        gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
+        C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu)
+        ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
+        C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys)
+        C.combine_fwd(ys, dst, wts, resid)
+        shared = [self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, resid) for e in moe.shared_experts]
+        moe._last_indices = idx
+        moe._last_weights = wts
+        moe._last_counts = counts
+        return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
+                    h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts)
+
+    def _moe_bwd(self, moe, ctx, xn, dres_bf16, dxn_acc):
+        C = self.C
+        T = xn.shape[0]
+        E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
+        for e, sctx in zip(moe.shared_experts, ctx.shared):
+            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc)
+        P = ctx.xs.shape[0]
+        dys = torch.empty(P, self.D, dtype=BF16, device=self.device)
+        dw = torch.empty(T, k, dtype=F32, device=self.device)
+        C.combine_bwd(dres_bf16, ctx.ys, ctx.src, ctx.wts, k, dys, dw)
+        w1 = moe.experts[0].w1.weight
+        w2 = moe.experts[0].w2.weight
+        dgu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
+        C.swiglu_dgrad(dys, self.stacked(w2, E), ctx.tile_group, ctx.gu, dgu)
+        C.grouped_wgrad(dys, ctx.h, ctx.row_off, self.stacked(w2, E, grad=True))
+        dxs = torch.empty(P, self.D, dtype=BF16, device=self.device)
+        C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs)
+        C.grouped_wgrad(dgu, ctx.xs, ctx.row_off, self.swiglu_g13(w1, E))
+        C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
+        dlog = torch.empty(T, ctx.Ep, dtype=BF16, device=self.device)
+        C.router_bwd(dw, ctx.ssel, ctx.idx, float(moe.gate.route_scale), dlog)
+        gw = moe.gate.weight
+        C.linear_wgrad(dlog[:, :E], xn, self.g(gw))
+        C.linear_dgrad(dlog[:, :E], self.w(gw), dxn_acc)
+
+    # ------------------------------------------------------------------ MTP
+    def _mtp_fwd(self, mod, h_prev, emb, Bm, Sm):
+        """One MTP depth on [Bm*Sm] rows: returns (ctx, normalised hidden bf16, pre-norm fp32 hidden)."""
+        C, D = self.C, self.D
+        blk = mod.block
+        T = h_prev.shape[0]
+        cat = torch.empty(T, 2 * D, dtype=BF16, device=self.device)
+        rh = torch.empty(T, dtype=F32, device=self.device)
+        re = torch.empty(T, dtype=F32, device=self.device)
+        C.rmsnorm_fwd(h_prev, self.f32(blk.norm_h.weight), 1e-6, cat[:, :D], rh)
+        C.rmsnorm_fwd(emb, self.f32(blk.norm_e.weight), 1e-6, cat[:, D:], re)
+        f = self._linear(cat, blk.proj.weight, out_dtype=F32)           # fp32 residual of the block
+        a_in, ra = self._norm(f, blk.norm_attn.weight)
+        qkv = self._linear(a_in, blk.attn.in_proj_weight)               # [T, 3D]
+        H = blk.n_heads
+        hd = D // H
+        Q = torch.empty(Bm * H, Sm, hd, dtype=BF16, device=self.device)
+        K = torch.empty_like(Q)
+        Vt = torch.empty_like(Q)
+        C.heads_pack(qkv, 0, H, hd, Sm, Q)
+        C.heads_pack(qkv, D, H, hd, Sm, K)
+        C.heads_pack(qkv, 2 * D, H, hd, Sm, Vt)
+        O = torch.empty(T, D, dtype=BF16, device=self.device)
+        L = torch.empty(Bm * H, Sm, dtype=F32, device=self.device)
+        C.flash_fwd(Q, K, Vt, O, L, 0, hd ** -0.5, True, H)
+        f2 = f.clone()
+        C.linear_fwd(O, self.w(blk.attn.out_proj.weight), f2)
+        x_ffn, rf = self._norm(f2, blk.norm_ffn.weight)
+        f3 = f2.clone()
+        ffn = self._swiglu_dense_fwd(blk.w1.weight, blk.w2.weight, x_ffn, f3)
+        hn, rn = self._norm(f3, mod.norm.weight)
+        ctx = _Ctx(h_prev=h_prev, emb=emb, cat=cat, rh=rh, re=re, f=f, a_in=a_in, ra=ra, qkv=qkv, Q=Q, K=K, V=Vt,
+                   O=O, L=L, f2=f2, x_ffn=x_ffn, rf=rf, ffn=ffn, f3=f3, rn=rn, hn=hn, Bm=Bm, Sm=Sm)
+        return ctx, hn, f3
+
+    def _mtp_bwd(self, mod, ctx, dhn, dprev_acc, demb):
+        """dhn: fp32 grad of the normalised MTP hidden.  Adds d(h_prev) into
+        ``dprev_acc`` (fp32) and writes d(emb) (fp32) into ``demb``."""
+        C, D = self.C, self.D
+        blk = mod.block
+        T = ctx.h_prev.shape[0]
+        H = blk.n_heads
+        hd = D // H
+        Bm, Sm = ctx.Bm, ctx.Sm
+        df = torch.zeros(T, D, dtype=F32, device=self.device)
+        dfb = torch.empty(T, D, dtype=BF16, device=self.device)
+        C.rmsnorm_bwd(dhn, ctx.f3, self.f32(mod.norm.weight), ctx.rn, df, None, dfb, self.g(mod.norm.weight))
+        dx_ffn = torch.zeros(T, D, dtype=F32, device=self.device)
+        self._swiglu_dense_bwd(blk.w1.weight, blk.w2.weight, ctx.ffn, ctx.x_ffn, dfb, dx_ffn)
+        C.rmsnorm_bwd(dx_ffn, ctx.f2, self.f32(blk.norm_ffn.weight), ctx.rf, df, None, dfb, self.g(blk.norm_ffn.weight))
+        dO = self._linear_bwd(dfb, ctx.O, blk.attn.out_proj.weight)
+        dQ = torch.zeros(Bm * H, Sm, hd, dtype=F32, device=self.device)
+        dK = torch.empty_like(dQ)
+        dV = torch.empty_like(dQ)
+        delta = torch.empty(Bm * H, Sm, dtype=F32, device=self.device)
+        C.flash_bwd(ctx.Q, ctx.K, ctx.V, ctx.O, dO, ctx.L, delta, dQ, dK, dV, 0, hd ** -0.5, True, H)
+        dqkv = torch.empty(T, 3 * D, dtype=BF16, device=self.device)
+        C.heads_unpack(dQ, H, hd, Sm, dqkv, 0)
+        C.heads_unpack(dK, H, hd, Sm, dqkv, D)
+        C.heads_unpack(dV, H, hd, Sm, dqkv, 2 * D)
+        da = torch.zeros(T, D, dtype=F32, device=self.device)
+        self._linear_bwd(dqkv, ctx.a_in, blk.attn.in_proj_weight, dx_acc=da)
+        C.rmsnorm_bwd(da, ctx.f, self.f32(blk.norm_attn.weight), ctx.ra, df, None, dfb, self.g(blk.norm_attn.weight))
+        dcat = self._linear_bwd(dfb, ctx.cat, blk.proj.weight)
+        C.rmsnorm_bwd(dcat[:, :D], ctx.h_prev, self.f32(blk.norm_h.weight), ctx.rh, dprev_acc, None, None,
+                      self.g(blk.norm_h.weight))
+        C.rmsnorm_bwd(dcat[:, D:], ctx.emb, self.f32(blk.norm_e.weight), ctx.re, demb, None, None,
+                      self.g(blk.norm_e.weight))
+
+    # ------------------------------------------------------------ full step
+    @property
+    def _empty_i32(self):
+        if not hasattr(self, "_e_i32"):
+            self._e_i32 = torch.empty(0, dtype=torch.int32, device=self.device)
+        return self._e_i32
+
+    def forward_backward(self, tokens: torch.Tensor, targets: torch.Tensor, loss_scale: float = 1.0) -> Dict:
+        """One micro-batch: forward, loss, backward (gradients accumulate).
+
+        Returns device tensors ``loss`` (main CE), ``mtp_loss`` (or None) and
+        ``balance_loss``; nothing here synchronises with the host.
+        """
+        C, m, D = self.C, self.model, self.D
+        B, S = tokens.shape
+        T = B * S
+        tok = tokens.reshape(-1).long()
+        tgt = targets.reshape(-1).long()
+        x = torch.empty(T, D, dtype=F32, device=self.device)
+        C.embedding_fwd(tok, self.f32(m.embed.weight), x)
+        saved = []
+        for layer in m.layers:
+            xn1, r1 = self._norm(x, layer.attn_norm.weight)
+            actx = self._mla_fwd(layer.attn, xn1, B, S)
+            x_mid = x.clone()
+            C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid)
+            xn2, r2 = self._norm(x_mid, layer.ffn_norm.weight)
+            x_next = x_mid.clone()
+            if hasattr(layer.ffn, "experts"):
+                fctx = self._moe_fwd(layer.ffn, xn2, x_next)
+            else:
+                fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next)
+            saved.append((x, r1, actx, x_mid, xn2, r2, fctx))
+            x = x_next
+        hL = x
+        xf, rf = self._norm(hL, m.norm.weight)
+
+        # MTP depths (h_prev = pre-final-norm hidden, emb = embed(tokens[:, d+1:]))
+        mtp_ctx = []
+        rows = [xf]
+        tgts = [tgt]
+        seg = [0, T]
+        if self.mtp is not None:
+            prev = hL.view(B, S, D)
+            for d, mod in enumerate(self.mtp.mtp_modules):
+                Sm = S - d - 2
+                if Sm <= 0:
+                    break
+                h_prev = prev[:, :Sm].reshape(B * Sm, D).contiguous()
+                etok = tokens[:, d + 1:d + 1 + Sm].reshape(-1).long().contiguous()
+                emb = torch.empty(B * Sm, D, dtype=F32, device=self.device)
+                C.embedding_fwd(etok, self.f32(m.embed.weight), emb)
+                ctx, hn, f3 = self._mtp_fwd(mod, h_prev, emb, B, Sm)
+                ctx.etok = etok
+                mtp_ctx.append(ctx)
+                rows.append(hn)
+                tgts.append(tokens[:, d + 2:d + 2 + Sm].reshape(-1).long())
+                seg.append(seg[-1] + B * Sm)
+                prev = hn.float().view(B, Sm, D)  # next depth chains on the normalised hidden
+        allx = torch.cat(rows, 0) if len(rows) > 1 else xf
+        allt = torch.cat(tgts, 0) if len(tgts) > 1 else tgt
+        Tt = allx.shape[0]
+
+        # fused LM head + cross-entropy over every row
+        head_w = self.w(m.head.weight)
+        nt = (self.V + 255) // 256
+        pmax = torch.empty(Tt, nt, dtype=F32, device=self.device)
+        psum = torch.empty(Tt, nt, dtype=F32, device=self.device)
+        tl = torch.zeros(Tt, dtype=F32, device=self.device)
+        C.ce_fwd_partials(allx, head_w, allt, pmax, psum, tl)
+        lse = torch.empty(Tt, dtype=F32, device=self.device)
+        lrows = torch.empty(Tt, dtype=F32, device=self.device)
+        C.ce_rows(pmax, psum, tl, allt, lse, lrows)
+        nseg = len(seg) - 1
+        segw = [1.0] + [self.mtp.mtp_weight / max(1, nseg - 1)] * (nseg - 1) if self.mtp is not None else [1.0]
+        seg_t = torch.tensor(seg, dtype=torch.int32, device=self.device)
+        segw_t = torch.tensor(segw, dtype=F32, device=self.device)
+        losses = torch.empty(nseg, dtype=F32, device=self.device)
+        rscale = torch.empty(Tt, dtype=F32, device=self.device)
+        C.ce_reduce(lrows, allt, seg_t, segw_t, float(loss_scale), losses, rscale)
+        self._last_losses = losses
+
+        # ---------------- backward
+        dall = torch.zeros(Tt, D, dtype=F32, device=self.device)
+        dlog = torch.empty(min(self.ce_chunk, Tt), self.Vp, dtype=BF16, device=self.device)
+        for a in range(0, Tt, self.ce_chunk):
+            b = min(Tt, a + self.ce_chunk)
+            dl = dlog[:b - a]
+            C.ce_bwd_logits(allx[a:b], head_w, allt[a:b], lse[a:b], rscale[a:b], dl)
+            C.linear_wgrad(dl[:, :self.V], allx[a:b], self.g(m.head.weight))
+            C.linear_dgrad(dl[:, :self.V], head_w, dall[a:b])
+        del dlog
+        dres = torch.zeros(T, D, dtype=F32, device=self.device)
+        if mtp_ctx:
+            # Depth d+1 consumed the first rows of depth d's normalised hidden,
+            # so its input gradient is carried back into depth d's output grad.
+            carry, carry_rows = None, 0
+            for d in range(len(mtp_ctx) - 1, -1, -1):
+                ctx = mtp_ctx[d]
+                mod = self.mtp.mtp_modules[d]
+                dhn = dall[seg[d + 1]:seg[d + 2]]
+                if carry is not None:
+                    dhn = dhn.clone()
+                    dhn.view(B, ctx.Sm, D)[:, :carry_rows].add_(carry.view(B, carry_rows, D))
+                dprev = torch.zeros(ctx.h_prev.shape, dtype=F32, device=self.device)
+                demb = torch.zeros(ctx.emb.shape, dtype=F32, device=self.device)
+                self._mtp_bwd(mod, ctx, dhn.contiguous(), dprev, demb)
+                C.embedding_bwd(ctx.etok, demb, self.g(m.embed.weight))
+                if d == 0:
+                    dres.view(B, S, D)[:, :ctx.Sm].add_(dprev.view(B, ctx.Sm, D))
+                else:
+                    carry, carry_rows = dprev, ctx.Sm
+        dres_b = torch.empty(T, D, dtype=BF16, device=self.device)
+        C.rmsnorm_bwd(dall[:T], hL, self.f32(m.norm.weight), rf, dres, None, dres_b, self.g(m.norm.weight))
+        for layer, (x_in, r1, actx, x_mid, xn2, r2, fctx) in zip(reversed(m.layers), reversed(saved)):
+            dxn2 = torch.zeros(T, D, dtype=F32, device=self.device)
+            if hasattr(layer.ffn, "experts"):
+                self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)
+            else:
+                self._swiglu_dense_bwd(layer.ffn.w1.weight, layer.ffn.w2.weight, fctx, xn2, dres_b, dxn2)
+            C.rmsnorm_bwd(dxn2, x_mid, self.f32(layer.ffn_norm.weight), r2, dres, None, dres_b,
+                          self.g(layer.ffn_norm.weight))
+            dxn1 = torch.zeros(T, D, dtype=F32, device=self.device)
+            self._mla_bwd(layer.attn, actx, dres_b, dxn1, B, S)
+            C.rmsnorm_bwd(dxn1, x_in, self.f32(layer.attn_norm.weight), r1, dres, None, dres_b,
+                          self.g(layer.attn_norm.weight))
+        C.embedding_bwd(tok, dres, self.g(m.embed.weight))
+
+        balance = torch.zeros((), device=self.device)
+        out = {"loss": losses[0], "mtp_loss": losses[1:].mean() if nseg > 1 else None, "balance_loss": balance}
+        self._finite = torch.isfinite(losses).all()
+        return out
+
+    # ------------------------------------------------------------ optimizer
+    def last_loss_finite(self) -> bool:
+        return bool(self._finite)
+
+    def clip_and_step(self, max_norm: float) -> None:
+        if self.dp is not None:
+            self.dp.reduce_gradients()
+        extra = self.dp.extra_sqsum() if self.dp is not None else None
+        self.optimizer.compute_clip(max_norm, extra)
+        self.optimizer.step()
+        if self.dp is not None:
+            self.dp.after_step()
+
+    def zero_grad(self) -> None:
+        self.optimizer.zero_grad()
+
+    def check(self) -> None:
+        check_status()
+
+    # ---------------------------------------------------- module interplay
+    def sync_to_modules(self) -> None:
+        """Module parameters already alias the flat masters; re-point any that
+        were replaced (e.g. by ``load_state_dict``)."""
+        for f in self.flats:
+            f.pull_from_params()
+
+    def sync_from_modules(self) -> None:
+        for f in self.flats:
+            f.pull_from_params()
+        self.optimizer._bind_state()
+
+    def optimizer_state_for_checkpoint(self) -> dict:
+        """torch-AdamW state dict with standalone tensors (reference layout)."""
+        sd = self.optimizer.state_dict()
+        for st in sd["state"].values():
+            for k in ("exp_avg", "exp_avg_sq"):
+                if k in st:
+                    st[k] = st[k].clone()
+            if "step" in st:
+                st["step"] = st["step"].clone()
+        return sd

@@ -235,8 +235,13 @@ class Pretrainer:
         return torch.autocast(self.device.type, dtype=self.amp_dtype)
 
     def _update_moe_bias(self) -> None:
+        dp = getattr(self.engine, "dp", None) if self.engine is not None else None
         for moe in self.raw_model.moe_layers():
-            moe.update_gate_bias(speed=self.config.bias_update_speed)
+            if dp is not None and moe.expert_counts() is not None:
+                # every rank applies the same update from the global counts
+                moe.gate.update_bias(dp.global_counts(moe.expert_counts()), speed=self.config.bias_update_speed)
+            else:
+                moe.update_gate_bias(speed=self.config.bias_update_speed)
 
     def _moe_balance_metric(self) -> torch.Tensor:
         """Sum of per-layer balance metrics (device tensor; read lazily)."""
@@ -321,6 +326,7 @@ class Pretrainer:
     def _engine_step(self, tokens, targets, boundary: bool) -> Optional[Dict]:
         eng = self.engine
         out = eng.forward_backward(tokens, targets, loss_scale=1.0 / self.config.gradient_accumulation_steps)
+        out["balance_loss"] = self._moe_balance_metric()
         if self.config.nan_guard and not eng.last_loss_finite():
             self._log(f"[nan-guard] NaN/Inf loss, opt_steps={self._opt_steps}. Dropping accumulated gradients.")
             eng.zero_grad()

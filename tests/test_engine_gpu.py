@@ -1,0 +1,119 @@
+"""Fused training engine vs the eager PyTorch model (same weights), on a B200."""
+import copy
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+CFG = {
+    "vocab_size": 1000, "dim": 256, "n_layers": 3, "n_heads": 4, "n_dense_layers": 1,
+    "n_routed_experts": 8, "n_shared_experts": 1, "n_activated_experts": 2, "inter_dim": 512,
+    "moe_inter_dim": 128, "kv_lora_rank": 64, "q_lora_rank": 0, "qk_nope_head_dim": 48,
+    "qk_rope_head_dim": 16, "v_head_dim": 64, "max_seq_len": 128, "rope_theta": 10000,
+    "rope_factor": 1.0, "mscale": 1.0, "mtp_depth": 1, "mtp_loss_weight": 0.3,
+    "attn_impl": "sdpa", "weight_tying": True,
+}
+
+
+def _cos(a, b):
+    return F.cosine_similarity(a.flatten().double(), b.flatten().double(), dim=0).item()
+
+
+def test_engine_matches_eager():
+    from models.mtp import MultiTokenPrediction
+    from models.transformer import Transformer
+    from ops.engine import TrainEngine
+    from training.pretrain import TrainingConfig, _unique_params
+
+    torch.manual_seed(0)
+    ref = Transformer(dict(CFG)).cuda()
+    # Spread the router scores (the 0.006-std init leaves every sigmoid score
+    # within ~0.03 of 0.5, so bf16 operand rounding flips near-tied top-k picks
+    # and the comparison would test tie-breaking instead of the kernels), and
+    # give the selection bias a non-trivial value.
+    for moe in ref.moe_layers():
+        moe.gate.weight.data.mul_(40.0)
+        moe.gate.bias.uniform_(-0.05, 0.05)
+    ref_mtp = MultiTokenPrediction(dict(CFG), ref).cuda()
+    model = copy.deepcopy(ref)
+    mtp = MultiTokenPrediction(dict(CFG), model).cuda()
+    mtp.load_state_dict(ref_mtp.state_dict())
+
+    B, S = 4, 128
+    g = torch.Generator(device="cuda").manual_seed(1)
+    tokens = torch.randint(0, CFG["vocab_size"], (B, S), device="cuda", generator=g)
+    targets = torch.randint(0, CFG["vocab_size"], (B, S), device="cuda", generator=g)
+
+    # eager reference at the reference trainer's precision (bf16 autocast) for the losses
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        main_logits, pairs = ref_mtp(tokens)
+        _, main, mtp_loss = ref_mtp.compute_loss(main_logits, targets, pairs)
+    # ... and in fp32 for the gradients (autocast's bf16 routing scores make the
+    # router gradient itself noisy, so fp32 is the meaningful oracle there)
+    main_logits, pairs = ref_mtp(tokens)
+    total, _, _ = ref_mtp.compute_loss(main_logits, targets, pairs)
+    total.backward()
+
+    params = _unique_params(mtp)
+    groups = [{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
+              {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}]
+    eng = TrainEngine(model, mtp, TrainingConfig(lr=1e-3), groups)
+    out = eng.forward_backward(tokens, targets, loss_scale=1.0)
+    torch.cuda.synchronize()
+    eng.check()
+    assert abs(out["loss"].item() - main.item()) < 2e-2 * max(1.0, main.item())
+    assert abs(out["mtp_loss"].item() - mtp_loss.item()) < 2e-2 * max(1.0, mtp_loss.item())
+
+    ref_named = dict(ref_mtp.named_parameters())
+    cos_all, ours_all, ref_all = [], [], []
+    for name, p in mtp.named_parameters():
+        rp = ref_named[name]
+        if rp.grad is None or rp.grad.abs().sum() == 0:
+            continue
+        c = _cos(p.grad, rp.grad)
+        ratio = (p.grad.norm() / rp.grad.norm()).item()
+        cos_all.append(c)
+        ours_all.append(p.grad.flatten())
+        ref_all.append(rp.grad.flatten())
+        # a layout or transpose bug drives the cosine to ~0; bf16 operands
+        # (and the rare token routed differently at a near-tie) stay above this
+        assert c > 0.97, f"{name}: cosine {c:.4f}"
+        assert 0.8 < ratio < 1.25, f"{name}: norm ratio {ratio:.3f}"
+    assert len(cos_all) > 40
+    cos_all.sort()
+    assert cos_all[len(cos_all) // 2] > 0.99, f"median cosine {cos_all[len(cos_all) // 2]:.4f}"
+    assert _cos(torch.cat(ours_all), torch.cat(ref_all)) > 0.99
+
+    # one optimizer step moves the weights like torch AdamW would
+    before = model.layers[0].attn.wq.weight.detach().clone()
+    eng.clip_and_step(1.0)
+    eng.zero_grad()
+    torch.cuda.synchronize()
+    assert not torch.equal(before, model.layers[0].attn.wq.weight)
+    assert torch.isfinite(model.layers[0].attn.wq.weight).all()
+    eng.check()
+
+
+def test_pretrainer_uses_engine_and_learns(tmp_path):
+    from training.pretrain import Pretrainer, TrainingConfig
+    cfg = TrainingConfig(model_config=dict(CFG), checkpoint_dir=str(tmp_path), max_seq_len=128,
+                         vocab_size=CFG["vocab_size"], batch_size=4, gradient_accumulation_steps=2, max_steps=100,
+                         warmup_steps=0, lr=3e-3, mtp_weight=0.3, nan_guard=True, bias_update_every=1)
+    tr = Pretrainer(cfg)
+    assert tr.engine is not None
+    g = torch.Generator(device="cuda").manual_seed(3)
+    data = torch.randint(0, 50, (4, 129), device="cuda", generator=g)   # a learnable, tiny vocabulary subset
+    losses = []
+    for step in range(20):
+        out = tr.train_step(data[:, :-1], data[:, 1:], step)
+        losses.append(out["loss"].item())
+    assert losses[-1] < losses[0] - 1.0, losses
+    tr.save_checkpoint(20)
+    tr2 = Pretrainer(cfg)
+    assert tr2.load_checkpoint(20) == 20
+    for (n, a), (_, b) in zip(tr.raw_model.named_parameters(), tr2.raw_model.named_parameters()):
+        assert torch.equal(a, b), n
+    out2 = tr2.train_step(data[:, :-1], data[:, 1:], 0)
+    assert torch.isfinite(out2["loss"])

@@ -95,23 +95,24 @@ def test_flash_attention_vs_reference(C, B, S, H, dn, dr, dv):
     V = torch.empty(B * H, S, dv, device="cuda", dtype=torch.bfloat16)
     C.mla_pack(q, kvb, kpe, Q, K, V, B, S, H, dn, dr, dv, cos, sin, 0)
     scale = (dn + dr) ** -0.5
-    O = torch.empty(B * H, S, dv, device="cuda", dtype=torch.bfloat16)
+    O = torch.empty(B, S, H, dv, device="cuda", dtype=torch.bfloat16)   # token-major output
     L = torch.empty(B * H, S, device="cuda")
-    C.flash_fwd(Q, K, V, O, L, 0, scale, True)
+    C.flash_fwd(Q, K, V, O, L, 0, scale, True, H)
     Qr = Q.float().requires_grad_(True)
     Kr = K.float().requires_grad_(True)
     Vr = V.float().requires_grad_(True)
     mask = torch.ones(S, S, device="cuda", dtype=torch.bool).tril()
     att = (Qr @ Kr.transpose(1, 2) * scale).masked_fill(~mask, float("-inf")).softmax(-1)
     ref = att @ Vr
-    close(O, ref, rtol=2e-2, atol=2e-2)
-    dO = torch.randn_like(ref).bfloat16()
-    ref.backward(dO.float())
+    tok = lambda t: t.view(B, H, S, -1).permute(0, 2, 1, 3)
+    close(O, tok(ref), rtol=2e-2, atol=2e-2)
+    dO = torch.randn(B, S, H, dv, device="cuda").bfloat16()
+    ref.backward(dO.float().permute(0, 2, 1, 3).reshape(B * H, S, dv))
     dQ = torch.zeros(B * H, S, DP, device="cuda")
     dK = torch.empty(B * H, S, DP, device="cuda")
     dV = torch.empty(B * H, S, dv, device="cuda")
     delta = torch.empty(B * H, S, device="cuda")
-    C.flash_bwd(Q, K, V, O, dO, L, delta, dQ, dK, dV, 0, scale, True)
+    C.flash_bwd(Q, K, V, O, dO, L, delta, dQ, dK, dV, 0, scale, True, H)
     close(dV, Vr.grad, rtol=3e-2, atol=3e-2)
     close(dK, Kr.grad, rtol=3e-2, atol=3e-2)
     close(dQ, Qr.grad, rtol=3e-2, atol=3e-2)
