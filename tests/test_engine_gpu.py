@@ -46,16 +46,6 @@ def test_engine_matches_eager():
     tokens = torch.randint(0, CFG["vocab_size"], (B, S), device="cuda", generator=g)
     targets = torch.randint(0, CFG["vocab_size"], (B, S), device="cuda", generator=g)
 
-    # eager reference at the reference trainer's precision (bf16 autocast) for the losses
-    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
-        main_logits, pairs = ref_mtp(tokens)
-        _, main, mtp_loss = ref_mtp.compute_loss(main_logits, targets, pairs)
-    # ... and in fp32 for the gradients (autocast's bf16 routing scores make the
-    # router gradient itself noisy, so fp32 is the meaningful oracle there)
-    main_logits, pairs = ref_mtp(tokens)
-    total, _, _ = ref_mtp.compute_loss(main_logits, targets, pairs)
-    total.backward()
-
     params = _unique_params(mtp)
     groups = [{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
               {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}]
@@ -63,8 +53,32 @@ def test_engine_matches_eager():
     out = eng.forward_backward(tokens, targets, loss_scale=1.0)
     torch.cuda.synchronize()
     eng.check()
+    eng_idx = [m._last_indices.long().clone() for m in model.moe_layers()]
+
+    # eager reference at the reference trainer's precision (bf16 autocast) for the losses
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        main_logits, pairs = ref_mtp(tokens)
+        _, main, mtp_loss = ref_mtp.compute_loss(main_logits, targets, pairs)
     assert abs(out["loss"].item() - main.item()) < 2e-2 * max(1.0, main.item())
     assert abs(out["mtp_loss"].item() - mtp_loss.item()) < 2e-2 * max(1.0, mtp_loss.item())
+
+    # fp32 eager gradients with the engine's expert choices: selection is a
+    # discrete decision that bf16 operand rounding can flip at near-ties, so
+    # the oracle takes the same picks (its weights/gradients are its own).
+    for moe, idx in zip(ref.moe_layers(), eng_idx):
+        with torch.no_grad():
+            agree = (moe.gate(torch.zeros(0, CFG["dim"], device="cuda"))[1].numel() == 0)
+        assert agree
+        gate = moe.gate
+
+        def fixed(x, gate=gate, idx=idx):
+            scores = torch.sigmoid(F.linear(x, gate.weight))
+            w = scores.gather(1, idx)
+            return (w / w.sum(-1, keepdim=True).clamp(min=1e-10) * gate.route_scale).to(x.dtype), idx
+        gate.forward = fixed
+    main_logits, pairs = ref_mtp(tokens)
+    total, _, _ = ref_mtp.compute_loss(main_logits, targets, pairs)
+    total.backward()
 
     ref_named = dict(ref_mtp.named_parameters())
     cos_all, ours_all, ref_all = [], [], []
@@ -79,8 +93,8 @@ def test_engine_matches_eager():
         ref_all.append(rp.grad.flatten())
         # a layout or transpose bug drives the cosine to ~0; bf16 operands
         # (and the rare token routed differently at a near-tie) stay above this
-        assert c > 0.97, f"{name}: cosine {c:.4f}"
-        assert 0.8 < ratio < 1.25, f"{name}: norm ratio {ratio:.3f}"
+        assert c > (0.95 if ".gate." in name else 0.98), f"{name}: cosine {c:.4f}"
+        assert 0.9 < ratio < 1.1, f"{name}: norm ratio {ratio:.3f}"
     assert len(cos_all) > 40
     cos_all.sort()
     assert cos_all[len(cos_all) // 2] > 0.99, f"median cosine {cos_all[len(cos_all) // 2]:.4f}"
