@@ -178,6 +178,10 @@ def run_ours(args, rank, world, local):
     micro = args.micro_batch or min(per_rank, 16)
     accum = per_rank // micro
     cfg = config_from_yaml(y)
+    # The yaml keeps mtp_loss_weight under `model:`; the trainer reads it from
+    # `training:`.  The benchmarked config has MTP depth 1 at weight 0.3 on
+    # both arms.
+    cfg.mtp_weight = y.get("training", {}).get("mtp_loss_weight", y["model"].get("mtp_loss_weight", 0.3))
     cfg.batch_size, cfg.gradient_accumulation_steps = micro, accum
     cfg.max_steps = 10 ** 9
     cfg.warmup_steps = 10
@@ -225,7 +229,7 @@ def run_ours(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
         "dtype": "bf16", "data": "synthetic uniform tokens, random-init weights",
-        "config": {"model": "deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 V100018)",
+        "config": {"model": "deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 w0.3 V100018)",
                    "global_batch": args.global_seqs * S, "seq_len": S, "parallelism": f"dp{world}",
                    "micro_batch_seqs": micro, "grad_accum": accum,
                    "l2": "working set (weights+activations, GBs) far exceeds the 126 MB L2"},
@@ -255,7 +259,8 @@ def run_reference(args, rank, world, local):
                          gradient_accumulation_steps=accum, max_steps=10 ** 9, warmup_steps=10, lr=t["lr"],
                          min_lr_ratio=t["min_lr_ratio"], weight_decay=t["weight_decay"], max_grad_norm=t["grad_clip"],
                          grad_checkpoint=t["grad_checkpoint"], compile_model=t["compile"],
-                         mtp_weight=t["mtp_loss_weight"], bias_update_speed=t["bias_update_speed"],
+                         mtp_weight=t.get("mtp_loss_weight", m.get("mtp_loss_weight", 0.3)),
+                         bias_update_speed=t["bias_update_speed"],
                          bias_update_every=t["bias_update_every"], nan_guard=t["nan_guard"], mup_lr=t["mup_lr"],
                          log_per_component_params=False)
     trainer = Pretrainer(cfg)

@@ -317,9 +317,209 @@ __global__ void heads_unpack_kernel(const float* __restrict__ src, int H, int hd
   for (int c = threadIdx.x; c < hd; c += blockDim.x) d[c] = __float2bfloat16(r[c]);
 }
 
+// ---------------------------------------------- RMSNorm, width-specialised
+// PAIRS = D / 64: each lane owns PAIRS column pairs (2 * (lane + 32 i)), so a
+// warp reads 256 contiguous bytes of fp32 (128 of bf16) per step.
+template <typename T>
+__device__ __forceinline__ float2 ld2(const T* p);
+template <>
+__device__ __forceinline__ float2 ld2<float>(const float* p) { return *reinterpret_cast<const float2*>(p); }
+template <>
+__device__ __forceinline__ float2 ld2<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+
+template <typename TIn, int PAIRS>
+__global__ void rmsnorm_fwd_v(const TIn* __restrict__ x, long ldx, const float* __restrict__ w, float eps,
+                              __nv_bfloat16* __restrict__ y, long ldy, float* __restrict__ rstd, int T) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  constexpr int D = 64 * PAIRS;
+  float2 v[PAIRS];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    v[i] = ld2(x + (size_t)row * ldx + 2 * (lane + 32 * i));
+    ss += v[i].x * v[i].x + v[i].y * v[i].y;
+  }
+  const float r = rsqrtf(warp_sum(ss) / D + eps);
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    const int c = 2 * (lane + 32 * i);
+    const float2 wv = *reinterpret_cast<const float2*>(w + c);
+    *reinterpret_cast<uint32_t*>(y + (size_t)row * ldy + c) = pack_bf16x2(v[i].x * r * wv.x, v[i].y * r * wv.y);
+  }
+  if (lane == 0 && rstd) rstd[row] = r;
+}
+
+template <typename TIn, typename TDy, int PAIRS>
+__global__ void rmsnorm_bwd_v(const TDy* __restrict__ dy, long lddy, const TIn* __restrict__ x, long ldx,
+                              const float* __restrict__ w, const float* __restrict__ rstd, float* __restrict__ dx_acc,
+                              long ldacc, __nv_bfloat16* __restrict__ dx_out, long ldout,
+                              __nv_bfloat16* __restrict__ dx_copy, long ldcopy, float* __restrict__ dw, int T,
+                              int rows_per_block) {
+  constexpr int D = 64 * PAIRS;
+  __shared__ float dw_s[D];
+  const int warps = blockDim.x >> 5;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) dw_s[c] = 0.f;
+  __syncthreads();
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(T, r0 + rows_per_block);
+  float2 dwl[PAIRS], wv[PAIRS];
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    dwl[i] = make_float2(0.f, 0.f);
+    wv[i] = *reinterpret_cast<const float2*>(w + 2 * (lane + 32 * i));
+  }
+  for (int row = r0 + wid; row < r1; row += warps) {
+    const float r = rstd[row];
+    float2 xh[PAIRS], g[PAIRS];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      const int c = 2 * (lane + 32 * i);
+      const float2 xv = ld2(x + (size_t)row * ldx + c);
+      const float2 gy = ld2(dy + (size_t)row * lddy + c);
+      xh[i] = make_float2(xv.x * r, xv.y * r);
+      g[i] = make_float2(gy.x * wv[i].x, gy.y * wv[i].y);
+      dot += xh[i].x * g[i].x + xh[i].y * g[i].y;
+      dwl[i].x += gy.x * xh[i].x;
+      dwl[i].y += gy.y * xh[i].y;
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      const int c = 2 * (lane + 32 * i);
+      const float d0 = r * (g[i].x - xh[i].x * dot), d1 = r * (g[i].y - xh[i].y * dot);
+      if (dx_acc) {
+        float2* p = reinterpret_cast<float2*>(dx_acc + (size_t)row * ldacc + c);
+        float2 sv = *p;
+        sv.x += d0;
+        sv.y += d1;
+        *p = sv;
+        if (dx_copy) *reinterpret_cast<uint32_t*>(dx_copy + (size_t)row * ldcopy + c) = pack_bf16x2(sv.x, sv.y);
+      } else {
+        *reinterpret_cast<uint32_t*>(dx_out + (size_t)row * ldout + c) = pack_bf16x2(d0, d1);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    atomicAdd(&dw_s[2 * (lane + 32 * i)], dwl[i].x);
+    atomicAdd(&dw_s[2 * (lane + 32 * i) + 1], dwl[i].y);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], dw_s[c]);
+}
+
+// -------------------------------------------------- vectorised MLA packing
+// One block per token; each thread moves one 8-element (16-byte) chunk of Q,
+// K or V for one head.  Requires dn, dr, dv, DP to be multiples of 8.
+__global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kvb,
+                           const __nv_bfloat16* __restrict__ kpe, long ldk, __nv_bfloat16* __restrict__ Q,
+                           __nv_bfloat16* __restrict__ K, __nv_bfloat16* __restrict__ V, int S, int H, int dn, int dr,
+                           int dv, int DP, const float* __restrict__ cosv, const float* __restrict__ sinv, int start) {
+  const int t = blockIdx.x, b = t / S, s = t % S, p = s + start;
+  const int qk_chunks = DP / 8, v_chunks = dv / 8;
+  const int per_head = qk_chunks + v_chunks;
+  for (int idx = threadIdx.x; idx < H * per_head; idx += blockDim.x) {
+    const int h = idx / per_head, j = idx % per_head;
+    if (j >= qk_chunks) {
+      const int c = (j - qk_chunks) * 8;
+      *reinterpret_cast<uint4*>(V + (((size_t)b * H + h) * S + s) * dv + c) =
+          *reinterpret_cast<const uint4*>(kvb + ((size_t)t * H + h) * (dn + dv) + dn + c);
+      continue;
+    }
+    const int c = j * 8;
+    const size_t o = (((size_t)b * H + h) * S + s) * DP + c;
+    uint4 qv, kv;
+    if (c + 8 <= dn) {
+      qv = *reinterpret_cast<const uint4*>(q + ((size_t)t * H + h) * (dn + dr) + c);
+      kv = *reinterpret_cast<const uint4*>(kvb + ((size_t)t * H + h) * (dn + dv) + c);
+    } else if (c >= dn + dr) {
+      qv = make_uint4(0, 0, 0, 0);
+      kv = qv;
+    } else {
+      const uint4 qr = *reinterpret_cast<const uint4*>(q + ((size_t)t * H + h) * (dn + dr) + c);
+      const uint4 kr = *reinterpret_cast<const uint4*>(kpe + (size_t)t * ldk + (c - dn));
+      const __nv_bfloat162* qh = reinterpret_cast<const __nv_bfloat162*>(&qr);
+      const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kr);
+      uint32_t qo[4], ko[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = (c - dn) / 2 + e;
+        const float cs = cosv[(size_t)p * (dr / 2) + i], sn = sinv[(size_t)p * (dr / 2) + i];
+        const float2 a = __bfloat1622float2(qh[e]), k2 = __bfloat1622float2(kh[e]);
+        qo[e] = pack_bf16x2(a.x * cs - a.y * sn, a.x * sn + a.y * cs);
+        ko[e] = pack_bf16x2(k2.x * cs - k2.y * sn, k2.x * sn + k2.y * cs);
+      }
+      qv = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+      kv = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+    }
+    *reinterpret_cast<uint4*>(Q + o) = qv;
+    *reinterpret_cast<uint4*>(K + o) = kv;
+  }
+}
+
+// Gradient of mla_pack_v.  dQ, dK fp32 [B,H,S,DP], dV fp32 [B,H,S,dv].
+__global__ void mla_unpack_v(const float* __restrict__ dQ, const float* __restrict__ dK, const float* __restrict__ dV,
+                             __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dkvb,
+                             __nv_bfloat16* __restrict__ dkpe, long ldk, int S, int H, int dn, int dr, int dv, int DP,
+                             const float* __restrict__ cosv, const float* __restrict__ sinv, int start) {
+  extern __shared__ float pe_acc[];  // [dr]
+  const int t = blockIdx.x, b = t / S, s = t % S, p = s + start;
+  for (int c = threadIdx.x; c < dr; c += blockDim.x) pe_acc[c] = 0.f;
+  __syncthreads();
+  const int qk_chunks = (dn + dr) / 8, v_chunks = dv / 8;
+  const int per_head = qk_chunks + v_chunks;
+  for (int idx = threadIdx.x; idx < H * per_head; idx += blockDim.x) {
+    const int h = idx / per_head, j = idx % per_head;
+    if (j >= qk_chunks) {
+      const int c = (j - qk_chunks) * 8;
+      const float4* src = reinterpret_cast<const float4*>(dV + (((size_t)b * H + h) * S + s) * dv + c);
+      const float4 a = src[0], bb = src[1];
+      *reinterpret_cast<uint4*>(dkvb + ((size_t)t * H + h) * (dn + dv) + dn + c) =
+          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(bb.x, bb.y), pack_bf16x2(bb.z, bb.w));
+      continue;
+    }
+    const int c = j * 8;
+    const size_t o = (((size_t)b * H + h) * S + s) * DP + c;
+    float qv[8], kv[8];
+    *reinterpret_cast<float4*>(qv) = reinterpret_cast<const float4*>(dQ + o)[0];
+    *reinterpret_cast<float4*>(qv + 4) = reinterpret_cast<const float4*>(dQ + o)[1];
+    *reinterpret_cast<float4*>(kv) = reinterpret_cast<const float4*>(dK + o)[0];
+    *reinterpret_cast<float4*>(kv + 4) = reinterpret_cast<const float4*>(dK + o)[1];
+    uint32_t qo[4], ko[4];
+    if (c + 8 <= dn) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qo[e] = pack_bf16x2(qv[2 * e], qv[2 * e + 1]);
+        ko[e] = pack_bf16x2(kv[2 * e], kv[2 * e + 1]);
+      }
+      *reinterpret_cast<uint4*>(dkvb + ((size_t)t * H + h) * (dn + dv) + c) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = (c - dn) / 2 + e;
+        const float cs = cosv[(size_t)p * (dr / 2) + i], sn = sinv[(size_t)p * (dr / 2) + i];
+        qo[e] = pack_bf16x2(qv[2 * e] * cs + qv[2 * e + 1] * sn, -qv[2 * e] * sn + qv[2 * e + 1] * cs);
+        atomicAdd(&pe_acc[2 * i], kv[2 * e] * cs + kv[2 * e + 1] * sn);
+        atomicAdd(&pe_acc[2 * i + 1], -kv[2 * e] * sn + kv[2 * e + 1] * cs);
+      }
+    }
+    *reinterpret_cast<uint4*>(dq + ((size_t)t * H + h) * (dn + dr) + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < dr; c += blockDim.x) dkpe[(size_t)t * ldk + c] = __float2bfloat16(pe_acc[c]);
+}
+
 int blocks_for(long n, int per) { return (int)((n + per - 1) / per); }
 
 }  // namespace
+
+#define DSV3_PAIRS_LIST(X) X(1) X(2) X(3) X(4) X(6) X(8) X(12) X(16) X(24) X(32)
 
 void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, at::Tensor& y, at::Tensor& rstd) {
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && y.stride(1) == 1, "rmsnorm_fwd: 2-D row-major views");
@@ -328,13 +528,28 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps, at::Tenso
   const at::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
   float* r = rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr;
-  if (x.scalar_type() == at::kFloat)
+  auto* yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  const bool f = x.scalar_type() == at::kFloat;
+  const bool vec_ok = D % 64 == 0 && x.stride(0) % 2 == 0 && y.stride(0) % 2 == 0;
+#define DSV3_FWD_CASE(P)                                                                                        \
+  if (vec_ok && D == 64 * P) {                                                                                 \
+    if (f) rmsnorm_fwd_v<float, P><<<blocks_for(T, 8), 256, 0, st>>>(x.data_ptr<float>(), x.stride(0),        \
+        w.data_ptr<float>(), (float)eps, yp, y.stride(0), r, T);                                               \
+    else rmsnorm_fwd_v<__nv_bfloat16, P><<<blocks_for(T, 8), 256, 0, st>>>(                                    \
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), (float)eps, yp,  \
+        y.stride(0), r, T);                                                                                    \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                            \
+    return;                                                                                                    \
+  }
+  DSV3_PAIRS_LIST(DSV3_FWD_CASE)
+#undef DSV3_FWD_CASE
+  if (f)
     rmsnorm_fwd_kernel<float><<<blocks_for(T, 8), 256, 0, st>>>(x.data_ptr<float>(), x.stride(0), w.data_ptr<float>(),
-        (float)eps, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), r, T, D);
+        (float)eps, yp, y.stride(0), r, T, D);
   else
     rmsnorm_fwd_kernel<__nv_bfloat16><<<blocks_for(T, 8), 256, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), (float)eps,
-        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), r, T, D);
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), (float)eps, yp,
+        y.stride(0), r, T, D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -355,6 +570,25 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   long ldcp = dx_copy ? dx_copy->stride(0) : 0;
   const int grid = blocks_for(T, rows_per_block);
   const size_t smem = D * sizeof(float);
+  const bool vec_ok = D % 64 == 0 && x.stride(0) % 2 == 0 && dy.stride(0) % 2 == 0 && ldacc % 2 == 0 &&
+                      ldout % 2 == 0 && ldcp % 2 == 0;
+#define DSV3_BWD_V(TIN, TDY, P)                                                                                  \
+  rmsnorm_bwd_v<TIN, TDY, P><<<grid, 256, 0, st>>>(reinterpret_cast<const TDY*>(dy.data_ptr()), dy.stride(0),     \
+      reinterpret_cast<const TIN*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), rstd.data_ptr<float>(), acc,  \
+      ldacc, out, ldout, cp, ldcp, dw.data_ptr<float>(), T, rows_per_block)
+#define DSV3_BWD_CASE(P)                                                                                         \
+  if (vec_ok && D == 64 * P) {                                                                                  \
+    const bool xf_ = x.scalar_type() == at::kFloat, df_ = dy.scalar_type() == at::kFloat;                       \
+    if (xf_ && df_) DSV3_BWD_V(float, float, P);                                                                 \
+    else if (xf_) DSV3_BWD_V(float, __nv_bfloat16, P);                                                           \
+    else if (df_) DSV3_BWD_V(__nv_bfloat16, float, P);                                                           \
+    else DSV3_BWD_V(__nv_bfloat16, __nv_bfloat16, P);                                                            \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                             \
+    return;                                                                                                     \
+  }
+  DSV3_PAIRS_LIST(DSV3_BWD_CASE)
+#undef DSV3_BWD_CASE
+#undef DSV3_BWD_V
 #define DSV3_NORM_BWD(TIN, TDY)                                                                                   \
   rmsnorm_bwd_kernel<TIN, TDY><<<grid, 256, smem, st>>>(                                                          \
       reinterpret_cast<const TDY*>(dy.data_ptr()), dy.stride(0), reinterpret_cast<const TIN*>(x.data_ptr()),      \
@@ -388,6 +622,16 @@ void mla_pack(const at::Tensor& q, const at::Tensor& kvb, const at::Tensor& kpe,
               const at::Tensor& cosv, const at::Tensor& sinv, int64_t start) {
   const int DP = Q.size(-1);
   const at::cuda::CUDAGuard guard(q.device());
+  if (dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 && kpe.stride(0) % 8 == 0) {
+    mla_pack_v<<<B * S, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(kpe.data_ptr()), kpe.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(Q.data_ptr()), reinterpret_cast<__nv_bfloat16*>(K.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(V.data_ptr()), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
+        sinv.data_ptr<float>(), start);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid(B * S, H);
   mla_pack_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
@@ -407,6 +651,14 @@ void mla_unpack(const at::Tensor& dQ, const at::Tensor& dK, const at::Tensor& dV
   auto* dqp = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
   auto* dkp = reinterpret_cast<__nv_bfloat16*>(dkvb.data_ptr());
   auto* dpe = reinterpret_cast<__nv_bfloat16*>(dkpe.data_ptr());
+  if (dV.scalar_type() == at::kFloat && dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 &&
+      dkpe.stride(0) % 8 == 0) {
+    mla_unpack_v<<<B * S, 256, dr * sizeof(float), st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
+        dV.data_ptr<float>(), dqp, dkp, dpe, dkpe.stride(0), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
+        sinv.data_ptr<float>(), start);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   if (dV.scalar_type() == at::kFloat)
     mla_unpack_kernel<float><<<B * S, 64, dr * sizeof(float), st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
         dV.data_ptr<float>(), dqp, dkp, dpe, dkpe.stride(0), B, S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),

@@ -118,7 +118,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
   if (a.num_tiles <= 0) return;
   a.status = status_ptr();
   const int grid = std::min(a.num_tiles, num_sms());
-  kern<<<grid, 192, C::SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(ta, tb, a);
+  kern<<<grid, kGemmThreads, C::SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(ta, tb, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -140,8 +140,10 @@ int cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 }  // namespace
 
-// out (bf16, store) or out (fp32, accumulate) = a[M,K] @ w[N,K]^T
-void linear_fwd(const at::Tensor& a, const at::Tensor& w, at::Tensor& out) {
+// out = a[M,K] @ w[N,K]^T.  bf16 out: store.  fp32 out: accumulate (default),
+// plain store (accumulate=false), or out = resid + a @ w^T when resid is given.
+void linear_fwd(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, bool accumulate,
+                c10::optional<at::Tensor> resid) {
   check_bf16_rows(a, "a");
   check_bf16_rows(w, "w");
   const int64_t M = a.size(0), K = a.size(1), N = w.size(0);
@@ -156,21 +158,28 @@ void linear_fwd(const at::Tensor& a, const at::Tensor& w, at::Tensor& out) {
   const bool f32 = out.scalar_type() == at::kFloat;
   TORCH_CHECK(f32 || out.scalar_type() == at::kBFloat16, "linear_fwd: out must be bf16 or fp32");
   TORCH_CHECK(out.stride(0) % 8 == 0, "linear_fwd: out row stride must be a multiple of 8");
-  if (N <= 128) {
-    g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, 128); g.kb_per_split = cdiv(K, 64);
-    g.num_tiles = g.m_tiles * g.n_tiles;
-    if (f32) launch<128, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
-    else launch<128, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
-  } else {
-    g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
-    g.num_tiles = g.m_tiles * g.n_tiles;
-    if (f32) launch<256, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
-    else launch<256, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+  int mode = f32 ? (resid ? 2 : (accumulate ? 1 : 3)) : 0;  // 0 bf16, 1 add, 2 resid, 3 store f32
+  if (resid) {
+    TORCH_CHECK(resid->scalar_type() == at::kFloat && resid->size(0) == M && resid->size(1) == N &&
+                resid->stride(1) == 1 && resid->stride(0) % 4 == 0, "linear_fwd: resid must be fp32 [M, N]");
+    g.aux = resid->data_ptr(); g.ld_aux = resid->stride(0);
   }
+  const int bn = N <= 128 ? 128 : 256;
+  g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, bn); g.kb_per_split = cdiv(K, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+#define DSV3_LIN(BN_)                                                                            \
+  switch (mode) {                                                                                \
+    case 0: launch<BN_, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g); break;            \
+    case 1: launch<BN_, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g); break;               \
+    case 2: launch<BN_, 0, 0, Sched::Dense, Epi::ResidF32, false>(ta, tb, g); break;             \
+    default: launch<BN_, 0, 0, Sched::Dense, Epi::StoreF32, false>(ta, tb, g); break;            \
+  }
+  if (bn == 128) { DSV3_LIN(128) } else { DSV3_LIN(256) }
+#undef DSV3_LIN
 }
 
-// out [M,K] (bf16 store or fp32 accumulate) = dy[M,N] @ w[N,K]
-void linear_dgrad(const at::Tensor& dy, const at::Tensor& w, at::Tensor& out) {
+// out [M,K] = dy[M,N] @ w[N,K]  (bf16 store; fp32 accumulate, or store when accumulate=false)
+void linear_dgrad(const at::Tensor& dy, const at::Tensor& w, at::Tensor& out, bool accumulate) {
   check_bf16_rows(dy, "dy");
   check_bf16_rows(w, "w");
   const int64_t M = dy.size(0), N = dy.size(1), K = w.size(1);
@@ -186,7 +195,8 @@ void linear_dgrad(const at::Tensor& dy, const at::Tensor& w, at::Tensor& out) {
   const bool f32 = out.scalar_type() == at::kFloat;
   g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(K, 256); g.kb_per_split = cdiv(N, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
-  if (f32) launch<256, 0, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+  if (f32 && accumulate) launch<256, 0, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+  else if (f32) launch<256, 0, 1, Sched::Dense, Epi::StoreF32, false>(ta, tb, g);
   else launch<256, 0, 1, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
 }
 
@@ -345,7 +355,8 @@ void ce_fwd_partials(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   const int64_t T = x.size(0), D = x.size(1), V = w.size(0);
   const int nt = cdiv(V, 256);
   TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == T, "targets: int64 [T]");
-  TORCH_CHECK(part_max.numel() == T * nt && part_sum.numel() == T * nt && tgt_logit.numel() == T, "ce partial shapes");
+  TORCH_CHECK(part_max.numel() == 2 * T * nt && part_sum.numel() == 2 * T * nt && tgt_logit.numel() == T,
+              "ce partial shapes: [T, 2 * ceil(V / 256)]");
   const at::cuda::CUDAGuard guard(x.device());
   GemmArgs g = blank_args();
   g.M = T; g.N = V; g.K = D;
@@ -386,8 +397,11 @@ void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& t
 
 namespace dsv3 {
 void register_gemm(pybind11::module_& m) {
-  m.def("linear_fwd", &linear_fwd, "out = a @ w^T (bf16 store, or fp32 accumulate when out is fp32)");
-  m.def("linear_dgrad", &linear_dgrad, "out = dy @ w (bf16 store, or fp32 accumulate)");
+  m.def("linear_fwd", &linear_fwd, "out = a @ w^T (bf16 store; fp32: accumulate / store / resid + a @ w^T)",
+        pybind11::arg("a"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("accumulate") = true,
+        pybind11::arg("resid") = pybind11::none());
+  m.def("linear_dgrad", &linear_dgrad, "out = dy @ w (bf16 store; fp32 accumulate or store)", pybind11::arg("dy"),
+        pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("accumulate") = true);
   m.def("linear_wgrad", &linear_wgrad, "dw (fp32) += dy^T @ x");
   m.def("swiglu_fwd", &swiglu_fwd, "h, gu from x @ [w1|w3]^T (dense or expert-grouped)");
   m.def("swiglu_dgrad", &swiglu_dgrad, "dgu from (dy @ w2) and the saved gate/up");

@@ -28,7 +28,20 @@
 namespace dsv3 {
 
 enum class Sched : int { Dense = 0, GroupedM = 1, GroupedK = 2 };
-enum class Epi : int { StoreBF16 = 0, AddF32 = 1, AtomicAddF32 = 2, SwigluFwd = 3, SwigluBwd = 4, CeFwd = 5, CeBwd = 6 };
+enum class Epi : int {
+  StoreBF16 = 0,     // out (bf16) = acc
+  AddF32 = 1,        // out (fp32) += acc
+  AtomicAddF32 = 2,  // out (fp32) += acc, atomically (split-K)
+  SwigluFwd = 3,     // h = silu(g) * u, gu = [g | u]
+  SwigluBwd = 4,     // dgu from dh = acc and the saved gu
+  CeFwd = 5,         // per-row (max, sum-exp) partials + target logit
+  CeBwd = 6,         // (softmax - onehot) * scale, bf16
+  StoreF32 = 7,      // out (fp32) = acc
+  ResidF32 = 8       // out (fp32) = aux (fp32) + acc   (out-of-place residual add)
+};
+
+constexpr int kEpiWarps = 8;                 // two warpgroups drain TMEM
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 
 struct GemmArgs {
   int M;                 // valid output rows (per group for GroupedK)
@@ -108,7 +121,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
 // tensor map [G][2][I][K]; BN must be 256 and the epilogue pairs column c of
 // the gate half with column c of the up half.
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using C = GemmCfg<BN>;
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
@@ -124,6 +137,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  static_assert(BN % 32 == 0, "BN must split into two 16-column-aligned halves");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -132,7 +146,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -246,8 +260,10 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // --------------------------------------------------------- epilogue
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;              // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;          // which half of the tile's columns
     const int r_in_tile = quarter * 32 + lane;
+    constexpr int HALF = BN / 2;
     int local = 0;
     for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
       TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
@@ -261,12 +277,13 @@ __global__ void __launch_bounds__(192, 1)
       const bool row_ok = row < args.M;
       uint32_t r[16];
 
-      if constexpr (E == Epi::StoreBF16 || E == Epi::AddF32 || E == Epi::AtomicAddF32) {
+      if constexpr (E == Epi::StoreBF16 || E == Epi::AddF32 || E == Epi::AtomicAddF32 || E == Epi::StoreF32 ||
+                    E == Epi::ResidF32) {
         char* base = reinterpret_cast<char*>(args.out);
         if constexpr (S == Sched::GroupedK)
           base += (size_t)ti.g * args.out_group_stride * (E == Epi::StoreBF16 ? 2 : 4);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
           __syncwarp();
           tmem_ld16(tbase + c, r);
           tmem_ld_wait();
@@ -290,12 +307,13 @@ __global__ void __launch_bounds__(192, 1)
             } else {
               for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] = __float2bfloat16(__uint_as_float(r[j]));
             }
-          } else if constexpr (E == Epi::AddF32) {
+          } else if constexpr (E == Epi::AddF32 || E == Epi::ResidF32) {
             float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
+            const float* src = E == Epi::AddF32 ? o : reinterpret_cast<const float*>(args.aux) + (size_t)row * args.ld_aux + col;
             if (full16) {
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
-                float4 v = *reinterpret_cast<float4*>(o + j);
+                float4 v = *reinterpret_cast<const float4*>(src + j);
                 v.x += __uint_as_float(r[j]);
                 v.y += __uint_as_float(r[j + 1]);
                 v.z += __uint_as_float(r[j + 2]);
@@ -303,7 +321,18 @@ __global__ void __launch_bounds__(192, 1)
                 *reinterpret_cast<float4*>(o + j) = v;
               }
             } else {
-              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] += __uint_as_float(r[j]);
+              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] = src[j] + __uint_as_float(r[j]);
+            }
+          } else if constexpr (E == Epi::StoreF32) {
+            float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
+            if (full16) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *reinterpret_cast<float4*>(o + j) =
+                    make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                __uint_as_float(r[j + 3]));
+            } else {
+              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] = __uint_as_float(r[j]);
             }
           } else {
             float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
@@ -317,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
         __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out2);
         uint32_t u[16];
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
+        for (int c = half * 64; c < half * 64 + 64; c += 16) {
           __syncwarp();
           tmem_ld16(tbase + c, r);
           tmem_ld16(tbase + 128 + c, u);
@@ -364,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
         const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(args.aux);
         __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
           __syncwarp();
           tmem_ld16(tbase + c, r);
           tmem_ld_wait();
@@ -421,7 +450,7 @@ __global__ void __launch_bounds__(192, 1)
         const long tgt = row_ok ? args.targets[row] : -1;
         float run_max = -INFINITY, run_sum = 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
           __syncwarp();
           tmem_ld16(tbase + c, r);
           tmem_ld_wait();
@@ -444,9 +473,9 @@ __global__ void __launch_bounds__(192, 1)
               if (col + j == tgt && row_ok) args.tgt_logit[row] = __uint_as_float(r[j]);
           }
         }
-        if (row_ok) {
-          args.part_max[(size_t)row * args.n_tiles + ti.n_tile] = run_max;
-          args.part_sum[(size_t)row * args.n_tiles + ti.n_tile] = run_sum;
+        if (row_ok) {  // two partials per (row, tile): one per column half
+          args.part_max[(size_t)row * 2 * args.n_tiles + 2 * ti.n_tile + half] = run_max;
+          args.part_sum[(size_t)row * 2 * args.n_tiles + 2 * ti.n_tile + half] = run_sum;
         }
       } else if constexpr (E == Epi::CeBwd) {
         const long tgt = row_ok ? args.targets[row] : -1;
@@ -454,7 +483,7 @@ __global__ void __launch_bounds__(192, 1)
         const float sc = row_ok ? args.row_scale[row] : 0.0f;
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
           __syncwarp();
           tmem_ld16(tbase + c, r);
           tmem_ld_wait();

@@ -178,16 +178,15 @@ class TrainEngine:
 
     def _linear(self, x, p, out_dtype=BF16):
         y = torch.empty(x.shape[0], p.shape[0], dtype=out_dtype, device=self.device)
-        if out_dtype == F32:
-            y.zero_()
-        self.C.linear_fwd(x, self.w(p), y)
+        self.C.linear_fwd(x, self.w(p), y, False)
         return y
 
-    def _linear_bwd(self, dy, x, p, dx_acc=None):
-        """dW += dy^T x; returns dx (bf16) unless ``dx_acc`` (fp32) is given."""
+    def _linear_bwd(self, dy, x, p, dx_acc=None, accumulate=True):
+        """dW += dy^T x; returns dx (bf16) unless ``dx_acc`` (fp32) is given,
+        which is accumulated into (or overwritten when ``accumulate`` is False)."""
         self.C.linear_wgrad(dy, x, self.g(p))
         if dx_acc is not None:
-            self.C.linear_dgrad(dy, self.w(p), dx_acc)
+            self.C.linear_dgrad(dy, self.w(p), dx_acc, accumulate)
             return dx_acc
         dx = torch.empty(dy.shape[0], p.shape[1], dtype=BF16, device=self.device)
         self.C.linear_dgrad(dy, self.w(p), dx)
@@ -231,37 +230,38 @@ class TrainEngine:
         dlat = self._linear_bwd(dkvb, ctx.lat, attn.wkv_b.weight)
         C.rmsnorm_bwd(dlat, ctx.kv_a[:, :R], self.f32(attn.kv_norm.weight), ctx.rkv, None, dkv_a[:, :R], None,
                       self.g(attn.kv_norm.weight))
-        self._linear_bwd(dkv_a, ctx.xn, attn.wkv_a.weight, dx_acc=dxn_acc)
+        self._linear_bwd(dkv_a, ctx.xn, attn.wkv_a.weight, dx_acc=dxn_acc, accumulate=False)
         self._linear_bwd(dq, ctx.xn, attn.wq.weight, dx_acc=dxn_acc)
 
     # ------------------------------------------------------------------ FFN
-    def _swiglu_dense_fwd(self, w1, w2, xn, resid):
-        """resid += w2(silu(w1 x) * w3 x) with one fused gate/up GEMM."""
+    def _swiglu_dense_fwd(self, w1, w2, xn, out, resid_in=None):
+        """out += w2(silu(w1 x) * w3 x) (or out = resid_in + ...) with one fused gate/up GEMM."""
         T = xn.shape[0]
         I = w1.shape[0]
         h = torch.empty(T, I, dtype=BF16, device=self.device)
         gu = torch.empty(T, 2 * I, dtype=BF16, device=self.device)
         self.C.swiglu_fwd(xn, self.swiglu_w13(w1, 1), self._empty_i32, h, gu)
-        self.C.linear_fwd(h, self.w(w2), resid)
+        self.C.linear_fwd(h, self.w(w2), out, True, resid_in)
         return _Ctx(h=h, gu=gu)
 
-    def _swiglu_dense_bwd(self, w1, w2, ctx, xn, dres_bf16, dxn_acc):
+    def _swiglu_dense_bwd(self, w1, w2, ctx, xn, dres_bf16, dxn_acc, accumulate=True):
         I = w1.shape[0]
         T = xn.shape[0]
         dgu = torch.empty(T, 2 * I, dtype=BF16, device=self.device)
         self.C.swiglu_dgrad(dres_bf16, self.stacked(w2, 1), self._empty_i32, ctx.gu, dgu)
         self.C.linear_wgrad(dres_bf16, ctx.h, self.g(w2))
         w13 = self.swiglu_w13(w1, 1).view(2 * I, -1)
-        self.C.linear_dgrad(dgu, w13, dxn_acc)
+        self.C.linear_dgrad(dgu, w13, dxn_acc, accumulate)
         self.C.linear_wgrad(dgu, xn, self.swiglu_g13(w1, 1).view(2 * I, -1))
 
-    def _moe_fwd(self, moe, xn, resid):
+    def _moe_fwd(self, moe, xn, resid_in):
+        """Returns (ctx, resid_in + MoE(xn)) as a new fp32 tensor."""
         C = self.C
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
         Ep = _pad(E, 8)
-        logits = torch.zeros(T, Ep, dtype=F32, device=self.device)
-        C.linear_fwd(xn, self.w(moe.gate.weight), logits[:, :E])
+        logits = torch.empty(T, Ep, dtype=F32, device=self.device)
+        C.linear_fwd(xn, self.w(moe.gate.weight), logits[:, :E], False)
         idx = torch.empty(T, k, dtype=torch.int32, device=self.device)
         wts = torch.empty(T, k, dtype=F32, device=self.device)
         ssel = torch.empty(T, k, dtype=F32, device=self.device)
@@ -283,20 +283,25 @@ class TrainEngine:
         C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu)
         ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
         C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys)
-        C.combine_fwd(ys, dst, wts, resid)
-        shared = [self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, resid) for e in moe.shared_experts]
+        out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
+        shared = []
+        for i, e in enumerate(moe.shared_experts):
+            shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
+        C.combine_fwd(ys, dst, wts, out)
         moe._last_indices = idx
         moe._last_weights = wts
         moe._last_counts = counts
         return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
-                    h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts)
+                    h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts), out
 
     def _moe_bwd(self, moe, ctx, xn, dres_bf16, dxn_acc):
         C = self.C
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
-        for e, sctx in zip(moe.shared_experts, ctx.shared):
-            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc)
+        if not moe.shared_experts:
+            dxn_acc.zero_()
+        for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
+            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
         P = ctx.xs.shape[0]
         dys = torch.empty(P, self.D, dtype=BF16, device=self.device)
         dw = torch.empty(T, k, dtype=F32, device=self.device)
@@ -341,11 +346,11 @@ class TrainEngine:
         O = torch.empty(T, D, dtype=BF16, device=self.device)
         L = torch.empty(Bm * H, Sm, dtype=F32, device=self.device)
         C.flash_fwd(Q, K, Vt, O, L, 0, hd ** -0.5, True, H)
-        f2 = f.clone()
-        C.linear_fwd(O, self.w(blk.attn.out_proj.weight), f2)
+        f2 = torch.empty_like(f)
+        C.linear_fwd(O, self.w(blk.attn.out_proj.weight), f2, True, f)
         x_ffn, rf = self._norm(f2, blk.norm_ffn.weight)
-        f3 = f2.clone()
-        ffn = self._swiglu_dense_fwd(blk.w1.weight, blk.w2.weight, x_ffn, f3)
+        f3 = torch.empty_like(f2)
+        ffn = self._swiglu_dense_fwd(blk.w1.weight, blk.w2.weight, x_ffn, f3, f2)
         hn, rn = self._norm(f3, mod.norm.weight)
         ctx = _Ctx(h_prev=h_prev, emb=emb, cat=cat, rh=rh, re=re, f=f, a_in=a_in, ra=ra, qkv=qkv, Q=Q, K=K, V=Vt,
                    O=O, L=L, f2=f2, x_ffn=x_ffn, rf=rf, ffn=ffn, f3=f3, rn=rn, hn=hn, Bm=Bm, Sm=Sm)
@@ -363,8 +368,8 @@ class TrainEngine:
         df = torch.zeros(T, D, dtype=F32, device=self.device)
         dfb = torch.empty(T, D, dtype=BF16, device=self.device)
         C.rmsnorm_bwd(dhn, ctx.f3, self.f32(mod.norm.weight), ctx.rn, df, None, dfb, self.g(mod.norm.weight))
-        dx_ffn = torch.zeros(T, D, dtype=F32, device=self.device)
-        self._swiglu_dense_bwd(blk.w1.weight, blk.w2.weight, ctx.ffn, ctx.x_ffn, dfb, dx_ffn)
+        dx_ffn = torch.empty(T, D, dtype=F32, device=self.device)
+        self._swiglu_dense_bwd(blk.w1.weight, blk.w2.weight, ctx.ffn, ctx.x_ffn, dfb, dx_ffn, accumulate=False)
         C.rmsnorm_bwd(dx_ffn, ctx.f2, self.f32(blk.norm_ffn.weight), ctx.rf, df, None, dfb, self.g(blk.norm_ffn.weight))
         dO = self._linear_bwd(dfb, ctx.O, blk.attn.out_proj.weight)
         dQ = torch.zeros(Bm * H, Sm, hd, dtype=F32, device=self.device)
@@ -376,8 +381,8 @@ class TrainEngine:
         C.heads_unpack(dQ, H, hd, Sm, dqkv, 0)
         C.heads_unpack(dK, H, hd, Sm, dqkv, D)
         C.heads_unpack(dV, H, hd, Sm, dqkv, 2 * D)
-        da = torch.zeros(T, D, dtype=F32, device=self.device)
-        self._linear_bwd(dqkv, ctx.a_in, blk.attn.in_proj_weight, dx_acc=da)
+        da = torch.empty(T, D, dtype=F32, device=self.device)
+        self._linear_bwd(dqkv, ctx.a_in, blk.attn.in_proj_weight, dx_acc=da, accumulate=False)
         C.rmsnorm_bwd(da, ctx.f, self.f32(blk.norm_attn.weight), ctx.ra, df, None, dfb, self.g(blk.norm_attn.weight))
         dcat = self._linear_bwd(dfb, ctx.cat, blk.proj.weight)
         C.rmsnorm_bwd(dcat[:, :D], ctx.h_prev, self.f32(blk.norm_h.weight), ctx.rh, dprev_acc, None, None,
@@ -409,14 +414,14 @@ class TrainEngine:
         for layer in m.layers:
             xn1, r1 = self._norm(x, layer.attn_norm.weight)
             actx = self._mla_fwd(layer.attn, xn1, B, S)
-            x_mid = x.clone()
-            C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid)
+            x_mid = torch.empty_like(x)
+            C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid, True, x)
             xn2, r2 = self._norm(x_mid, layer.ffn_norm.weight)
-            x_next = x_mid.clone()
             if hasattr(layer.ffn, "experts"):
-                fctx = self._moe_fwd(layer.ffn, xn2, x_next)
+                fctx, x_next = self._moe_fwd(layer.ffn, xn2, x_mid)
             else:
-                fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next)
+                x_next = torch.empty_like(x_mid)
+                fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next, x_mid)
             saved.append((x, r1, actx, x_mid, xn2, r2, fctx))
             x = x_next
         hL = x
@@ -451,8 +456,8 @@ class TrainEngine:
         # fused LM head + cross-entropy over every row
         head_w = self.w(m.head.weight)
         nt = (self.V + 255) // 256
-        pmax = torch.empty(Tt, nt, dtype=F32, device=self.device)
-        psum = torch.empty(Tt, nt, dtype=F32, device=self.device)
+        pmax = torch.empty(Tt, 2 * nt, dtype=F32, device=self.device)   # one partial per 128-column half tile
+        psum = torch.empty(Tt, 2 * nt, dtype=F32, device=self.device)
         tl = torch.zeros(Tt, dtype=F32, device=self.device)
         C.ce_fwd_partials(allx, head_w, allt, pmax, psum, tl)
         lse = torch.empty(Tt, dtype=F32, device=self.device)
@@ -468,14 +473,14 @@ class TrainEngine:
         self._last_losses = losses
 
         # ---------------- backward
-        dall = torch.zeros(Tt, D, dtype=F32, device=self.device)
+        dall = torch.empty(Tt, D, dtype=F32, device=self.device)
         dlog = torch.empty(min(self.ce_chunk, Tt), self.Vp, dtype=BF16, device=self.device)
         for a in range(0, Tt, self.ce_chunk):
             b = min(Tt, a + self.ce_chunk)
             dl = dlog[:b - a]
             C.ce_bwd_logits(allx[a:b], head_w, allt[a:b], lse[a:b], rscale[a:b], dl)
             C.linear_wgrad(dl[:, :self.V], allx[a:b], self.g(m.head.weight))
-            C.linear_dgrad(dl[:, :self.V], head_w, dall[a:b])
+            C.linear_dgrad(dl[:, :self.V], head_w, dall[a:b], False)
         del dlog
         dres = torch.zeros(T, D, dtype=F32, device=self.device)
         if mtp_ctx:
@@ -500,14 +505,15 @@ class TrainEngine:
         dres_b = torch.empty(T, D, dtype=BF16, device=self.device)
         C.rmsnorm_bwd(dall[:T], hL, self.f32(m.norm.weight), rf, dres, None, dres_b, self.g(m.norm.weight))
         for layer, (x_in, r1, actx, x_mid, xn2, r2, fctx) in zip(reversed(m.layers), reversed(saved)):
-            dxn2 = torch.zeros(T, D, dtype=F32, device=self.device)
+            dxn2 = torch.empty(T, D, dtype=F32, device=self.device)
             if hasattr(layer.ffn, "experts"):
                 self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)
             else:
-                self._swiglu_dense_bwd(layer.ffn.w1.weight, layer.ffn.w2.weight, fctx, xn2, dres_b, dxn2)
+                self._swiglu_dense_bwd(layer.ffn.w1.weight, layer.ffn.w2.weight, fctx, xn2, dres_b, dxn2,
+                                       accumulate=False)
             C.rmsnorm_bwd(dxn2, x_mid, self.f32(layer.ffn_norm.weight), r2, dres, None, dres_b,
                           self.g(layer.ffn_norm.weight))
-            dxn1 = torch.zeros(T, D, dtype=F32, device=self.device)
+            dxn1 = torch.empty(T, D, dtype=F32, device=self.device)
             self._mla_bwd(layer.attn, actx, dres_b, dxn1, B, S)
             C.rmsnorm_bwd(dxn1, x_in, self.f32(layer.attn_norm.weight), r1, dres, None, dres_b,
                           self.g(layer.attn_norm.weight))

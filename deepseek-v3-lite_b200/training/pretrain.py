@@ -147,6 +147,26 @@ class PretrainDataset(Dataset):
         return chunk[:-1], chunk[1:]
 
 
+class _LazyMetric:
+    """A diagnostic computed only when read (``float()`` / ``.item()``), so the
+    per-micro-step hot path does not pay for it."""
+
+    def __init__(self, fn):
+        self._fn = fn
+        self._v = None
+
+    def _get(self) -> torch.Tensor:
+        if self._v is None:
+            self._v = self._fn()
+        return self._v
+
+    def item(self) -> float:
+        return float(self._get().item())
+
+    def __float__(self) -> float:
+        return self.item()
+
+
 def _unique_params(module: nn.Module):
     seen, out = set(), []
     for p in module.parameters():
@@ -326,7 +346,7 @@ class Pretrainer:
     def _engine_step(self, tokens, targets, boundary: bool) -> Optional[Dict]:
         eng = self.engine
         out = eng.forward_backward(tokens, targets, loss_scale=1.0 / self.config.gradient_accumulation_steps)
-        out["balance_loss"] = self._moe_balance_metric()
+        out["balance_loss"] = _LazyMetric(self._moe_balance_metric)
         if self.config.nan_guard and not eng.last_loss_finite():
             self._log(f"[nan-guard] NaN/Inf loss, opt_steps={self._opt_steps}. Dropping accumulated gradients.")
             eng.zero_grad()

@@ -140,7 +140,7 @@ def test_ce_partials_and_grad(C):
     x, w = bf(T, D, seed=13), bf(V, D, scale=0.1, seed=14)
     tgt = torch.randint(0, V, (T,), device="cuda")
     tgt[5] = -100
-    nt = (V + 255) // 256
+    nt = 2 * ((V + 255) // 256)   # two partials per 256-column tile
     pm = torch.empty(T, nt, device="cuda")
     ps = torch.empty(T, nt, device="cuda")
     tl = torch.zeros(T, device="cuda")

@@ -247,7 +247,7 @@ def test_ce_finalize(C):
     w = (torch.randn(V, 256, device="cuda") * 0.1).bfloat16()
     tgt = torch.randint(0, V, (T,), device="cuda")
     tgt[:7] = -100
-    nt = (V + 255) // 256
+    nt = 2 * ((V + 255) // 256)   # two partials per 256-column tile
     pm, ps = torch.empty(T, nt, device="cuda"), torch.empty(T, nt, device="cuda")
     tl = torch.zeros(T, device="cuda")
     C.ce_fwd_partials(x, w, tgt, pm, ps, tl)
