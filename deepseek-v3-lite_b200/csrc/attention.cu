@@ -16,7 +16,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "attention_sm100.cuh"
 #include "common.cuh"
+#include "status.h"
+#include "tma_host.h"
 
 namespace dsv3 {
 
@@ -468,6 +471,36 @@ void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, cons
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+template <int NA, int NB, int DV>
+void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                   int q_off, double scale, bool causal, int H) {
+  const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1), DP = q.size(2);
+  using Cfg = FaCfg<NA, NB, DV>;
+  auto mk = [](const at::Tensor& t, int S, int D, uint32_t box0, CUtensorMapSwizzle swz) {
+    uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)t.size(0)};
+    uint64_t st[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+    uint32_t box[3] = {box0, 128, 1};
+    return make_map(t.data_ptr(), 3, dims, st, box, swz);
+  };
+  CUtensorMap qa = mk(q, Sq, DP, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap ka = mk(k, Sk, DP, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap qb = NB ? mk(q, Sq, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : qa;
+  CUtensorMap kb = NB ? mk(k, Sk, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : ka;
+  CUtensorMap vm = mk(v, Sk, DV, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = fa_fwd_sm100_kernel<NA, NB, DV>;
+  static bool cfg = false;
+  if (!cfg) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg = true;
+  }
+  dim3 grid((Sq + 127) / 128, BH);
+  kern<<<grid, 192, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
+      reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq, Sk, H, q_off,
+      (float)(scale * 1.4426950408889634), causal ? 1 : 0, status_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 #define DSV3_FA_DISPATCH(DQK_, DV_, CALL)                                                          \
   if (dqk == DQK_ && dvv == DV_) {                                                                 \
     CALL;                                                                                          \
@@ -510,8 +543,12 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
 
 // q_lat [B, H, R], q_pe [B, H, dr], kv [B, S, R] (batch stride kv.stride(0)),
 // pe [B, S, dr], lens [B] int32 -> out [B, H, R] bf16.
+// Query rows may outnumber cache rows: row b reads cache batch b / qpb, where
+// qpb = q_lat.size(0) / kv.size(0) (1 for plain decode, S for a chunk of S
+// queries per sequence).
 void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv, const at::Tensor& pe,
-                   const at::Tensor& lens, double scale, int64_t max_len, at::Tensor& scratch, at::Tensor& out) {
+                   const at::Tensor& lens, double scale, int64_t max_len, at::Tensor& scratch, at::Tensor& out,
+                   int64_t qpb) {
   const int B = q_lat.size(0), H = q_lat.size(1), R = q_lat.size(2), dr = q_pe.size(2);
   TORCH_CHECK(R <= 1024 && dr <= 128, "latent_decode: R <= 1024, dr <= 128");
   const at::cuda::CUDAGuard guard(q_lat.device());
@@ -528,17 +565,44 @@ void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, st>>>(
       reinterpret_cast<const bf16*>(q_lat.data_ptr()), reinterpret_cast<const bf16*>(q_pe.data_ptr()),
       reinterpret_cast<const bf16*>(kv.data_ptr()), reinterpret_cast<const bf16*>(pe.data_ptr()),
-      lens.data_ptr<int>(), H, R, dr, kv.stride(0), pe.stride(0), chunk, nsplit, B * H, (float)scale, pm, pl, po);
+      lens.data_ptr<int>(), H, R, dr, kv.stride(0), pe.stride(0), (int)std::max<int64_t>(1, qpb), chunk, nsplit, B * H,
+      (float)scale, pm, pl, po);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   latent_decode_merge_kernel<<<B * H, 128, 0, st>>>(pm, pl, po, nsplit, R, B * H,
                                                     reinterpret_cast<bf16*>(out.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// The tcgen05 forward (attention_sm100.cuh).  Same contract as flash_fwd.
+void flash_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                  int64_t q_off, double scale, bool causal, int64_t H) {
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dqk = q.size(2), dvv = v.size(2);
+  DSV3_FA_DISPATCH(80, 64, (run_fwd_sm100<1, 1, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_fwd_sm100<1, 0, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(128, 128, (run_fwd_sm100<2, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  TORCH_CHECK(false, "flash_fwd_tc: unsupported head dims");
+}
+
+// The warp-level (mma.sync) forward, kept callable for comparison tests.
+void flash_fwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                   int64_t q_off, double scale, bool causal, int64_t H) {
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dqk = q.size(2), dvv = v.size(2);
+  DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  TORCH_CHECK(false, "flash_fwd_mma: unsupported head dims");
+}
+
 void register_attention(pybind11::module_& m) {
+  m.def("flash_fwd_mma", &flash_fwd_mma, "warp-level mma.sync flash attention forward");
+  m.def("flash_fwd_tc", &flash_fwd_tc, "tcgen05 flash attention forward");
   m.def("flash_fwd", &flash_fwd, "causal flash attention forward (stores log2-domain LSE)");
   m.def("flash_bwd", &flash_bwd, "flash attention backward (dQ fp32 accumulated, dK/dV fp32)");
-  m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)");
+  m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)", pybind11::arg("q_lat"),
+        pybind11::arg("q_pe"), pybind11::arg("kv"), pybind11::arg("pe"), pybind11::arg("lens"), pybind11::arg("scale"),
+        pybind11::arg("max_len"), pybind11::arg("scratch"), pybind11::arg("out"), pybind11::arg("qpb") = 1);
 }
 
 }  // namespace dsv3

@@ -1,0 +1,307 @@
+// Flash-attention forward on the 5th-generation tensor cores (tcgen05).
+//
+// One CTA per (128-query tile, batch*head).  Warp 0 streams K/V tiles of 128
+// keys with TMA (2-stage ring, Q loaded once), warp 1 issues the MMAs from one
+// thread, warps 2-5 own one query row per thread:
+//
+//   S_j   = Q K_j^T          tcgen05.mma, M=128, N=128, fp32 in TMEM (2 buffers)
+//   P_j   = exp2(S_j * c - m) softmax threads: tcgen05.ld a whole row of S,
+//                            row max / sum in registers (no shuffles), P
+//                            written to shared memory in the 128B-swizzled
+//                            K-major layout the next MMA reads
+//   O    += P_j V_j          tcgen05.mma, M=128, N=DV, V read MN-major
+//
+// S_{j+1} is issued while the softmax threads work on S_j.  The running max is
+// only moved (and O in TMEM rescaled through tcgen05.ld/st) when it grows by
+// more than 2^8; otherwise P is computed against the stale max, which keeps P
+// below 256 and leaves the final O / l exact.
+//
+// Head dimension DQK = 64 * NA + 16 * NB: NA 128B-swizzled blocks of 64 plus
+// an optional 32B-swizzled block of 16 (so 72 = 48 + 24 pads only to 80).
+// Output O is token-major [B, S, H, DV]; L[bh, q] = m + log2(l) (log2 domain),
+// the same contract as the mma.sync kernels it replaces.
+#pragma once
+
+#include "common.cuh"
+
+namespace dsv3 {
+
+template <int NA, int NB, int DV>
+struct FaCfg {
+  static constexpr int QA_B = NA * 16384;
+  static constexpr int QB_B = NB * 4096;
+  static constexpr int Q_B = QA_B + QB_B;
+  static constexpr int K_B = Q_B;
+  static constexpr int V_B = (DV / 64) * 16384;
+  static constexpr int ST = 2;
+  static constexpr int P_B = 32768;
+  static constexpr int OFF_K = Q_B;
+  static constexpr int OFF_V = OFF_K + ST * K_B;
+  static constexpr int OFF_P = OFF_V + ST * V_B;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_B;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+};
+
+template <int NA, int NB, int DV>
+__global__ void __launch_bounds__(192, 1)
+    fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
+                        const __grid_constant__ CUtensorMap tmKa, const __grid_constant__ CUtensorMap tmKb,
+                        const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
+                        float* __restrict__ L, int Sq, int Sk, int H, int q_off, float scale_log2, int causal,
+                        unsigned int* status) {
+  using C = FaCfg<NA, NB, DV>;
+  static_assert(DV % 64 == 0 && DV <= 128, "DV must be 64 or 128");
+  extern __shared__ __align__(1024) uint8_t fa_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sP = smem + C::OFF_P;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bar;
+  uint64_t* kv_full = bar + 1;   // [ST]
+  uint64_t* kv_empty = bar + 3;  // [ST]
+  uint64_t* s_full = bar + 5;    // [2]
+  uint64_t* s_free = bar + 7;    // [2]
+  uint64_t* p_full = bar + 9;    // [2]
+  uint64_t* pv_done = bar + 11;  // [2]
+  uint64_t* drain = bar + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, m0 = blockIdx.x * 128;
+  int n_blocks = (Sk + 127) / 128;
+  if (causal) n_blocks = min(n_blocks, (q_off + m0 + 128 + 127) / 128);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------- producer
+      mbar_arrive_expect_tx(q_full, C::Q_B);
+#pragma unroll
+      for (int a = 0; a < NA; ++a) tma_load_3d(sQ + a * 16384, &tmQa, q_full, a * 64, m0, bh);
+      if (NB) tma_load_3d(sQ + C::QA_B, &tmQb, q_full, NA * 64, m0, bh);
+      uint32_t issued = 0, last_phase = 0;
+      for (int j = 0; j < n_blocks; ++j) {
+        const int st = j % C::ST;
+        const uint32_t ph = (j / C::ST) & 1;
+        if (!mbar_wait_bounded(&kv_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&kv_full[st], C::K_B + C::V_B);
+        uint8_t* k = sK + st * C::K_B;
+        uint8_t* v = sV + st * C::V_B;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) tma_load_3d(k + a * 16384, &tmKa, &kv_full[st], a * 64, j * 128, bh);
+        if (NB) tma_load_3d(k + C::QA_B, &tmKb, &kv_full[st], NA * 64, j * 128, bh);
+#pragma unroll
+        for (int d = 0; d < DV / 64; ++d) tma_load_3d(v + d * 16384, &tmV, &kv_full[st], d * 64, j * 128, bh);
+        issued |= 1u << st;
+        last_phase = (last_phase & ~(1u << st)) | (ph << st);
+      }
+      mbar_wait_bounded(q_full, 0, nullptr, status, DSV3_ERR_WAIT_FULL);
+      for (int st = 0; st < C::ST; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(&kv_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------ MMA issuer
+      constexpr uint32_t IDS = idesc_bf16_f32(128, 128, 0, 0);
+      constexpr uint32_t IDO = idesc_bf16_f32(128, DV, 0, 1);
+      const uint32_t tO = tmem + 256;
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
+      bool any = false;
+      for (int j = 0; ok && j <= n_blocks; ++j) {
+        if (j < n_blocks) {
+          const int st = j % C::ST, sb = j & 1;
+          if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+          if (j >= 2 && !mbar_wait_bounded(&s_free[sb], ((j - 2) >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))
+            break;
+          tc_fence_after();
+          const uint32_t q = smem_u32(sQ), k = smem_u32(sK + st * C::K_B);
+          uint32_t acc = 0;
+#pragma unroll
+          for (int a = 0; a < NA; ++a)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              umma_bf16(tmem + sb * 128, smem_desc_sw128(q + a * 16384 + kk * 32, 16, 1024),
+                        smem_desc_sw128(k + a * 16384 + kk * 32, 16, 1024), IDS, acc);
+              acc = 1;
+            }
+          if (NB) umma_bf16(tmem + sb * 128, smem_desc_sw32(q + C::QA_B, 256), smem_desc_sw32(k + C::QA_B, 256), IDS, acc);
+          umma_commit(&s_full[sb]);
+          any = true;
+        }
+        if (j >= 1) {
+          const int pj = j - 1, pb = pj & 1;
+          if (!mbar_wait_bounded(&p_full[pb], (pj >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+          tc_fence_after();
+          const uint32_t p = smem_u32(sP + pb * C::P_B), v = smem_u32(sV + (pj % C::ST) * C::V_B);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tO, smem_desc_sw128(p + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                      smem_desc_sw128(v + kk * 2048, 16384, 1024), IDO, (pj > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&pv_done[pb]);
+          umma_commit(&kv_empty[pj % C::ST]);
+        }
+      }
+      if (any) {
+        umma_commit(drain);
+        mbar_wait_bounded(drain, 0, nullptr, status, DSV3_ERR_WAIT_TMEM);
+      }
+    }
+  } else {
+    // ----------------------------------------------- softmax / epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = m0 + row;
+    const int qpos = q_off + qrow;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tO = tmem + lane_base + 256;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_blocks && ok; ++j) {
+      const int sb = j & 1;
+      // Waits are made warp-uniform: the TMEM loads/stores below are
+      // warp-collective and must never run with part of the warp gone.
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], (j >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t raw[8][16];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tmem_ld16(tmem + lane_base + sb * 128 + c * 16, raw[c]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) s[c * 16 + e] = __uint_as_float(raw[c][e]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[sb]);
+      const int n0 = j * 128;
+      // keys < lim are visible to this row (causal by global position, and < Sk)
+      const int lim = causal ? min(Sk, qpos + 1) - n0 : Sk - n0;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float v = c < lim ? s[c] * scale_log2 : -INFINITY;
+        s[c] = v;
+        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+      }
+      const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float m_new = fmaxf(m_used, rmax);
+      if (j == 0) {
+        m_used = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
+        // Some row of this warp moved its max by more than 2^8: rescale the
+        // warp's rows of O (warp-uniform; rows that did not move get a factor
+        // <= 1 as well, which is always valid).  O must not be read before
+        // PV_{j-1} has finished writing it.
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, status,
+                                                        DSV3_ERR_WAIT_TMEM))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_new);
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < DV / 16; ++d) {
+          uint32_t r[16];
+          tmem_ld16(tO + d * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+          tmem_st16(tO + d * 16, r);
+        }
+        tmem_st_wait();
+        m_used = m_new;
+      }
+      // The P buffer being written was last read by PV_{j-2}.
+      if (j >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[sb], ((j - 2) >> 1) & 1, abort_flag, status,
+                                                     DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = sP + sb * C::P_B + row * 128;
+      // m_used == -inf only if every key so far is masked; then s is -inf too and 2^(s - 0) = 0.
+      const float msub = m_used == -INFINITY ? 0.f : m_used;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(s[c * 8 + 2 * e] - msub);
+          const float p1 = ex2_approx(s[c * 8 + 2 * e + 1] - msub);
+          rs4[e] += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        const int blk = c >> 3, cc = c & 7;
+        *reinterpret_cast<uint4*>(prow + blk * 16384 + ((cc ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
+    }
+    if (ok && n_blocks > 0 &&
+        __all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(n_blocks - 1) & 1], ((n_blocks - 1) >> 1) & 1, abort_flag,
+                                                  status, DSV3_ERR_WAIT_TMEM))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int b = bh / H, h = bh % H;
+      __nv_bfloat16* orow = O + (((size_t)b * Sq + qrow) * H + h) * DV;
+#pragma unroll
+      for (int d = 0; d < DV / 16; ++d) {
+        uint32_t r[16];
+        tmem_ld16(tO + d * 16, r);
+        tmem_ld_wait();
+        if (qrow < Sq) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pk[e] = pack_bf16x2(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+          reinterpret_cast<uint4*>(orow + d * 16)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(orow + d * 16)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      if (qrow < Sq) L[(size_t)bh * Sq + qrow] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace dsv3

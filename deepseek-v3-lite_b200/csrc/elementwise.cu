@@ -417,7 +417,7 @@ __global__ void rmsnorm_bwd_v(const TDy* __restrict__ dy, long lddy, const TIn* 
 // -------------------------------------------------- vectorised MLA packing
 // One block per token; each thread moves one 8-element (16-byte) chunk of Q,
 // K or V for one head.  Requires dn, dr, dv, DP to be multiples of 8.
-__global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kvb,
+__global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, long ldq, const __nv_bfloat16* __restrict__ kvb,
                            const __nv_bfloat16* __restrict__ kpe, long ldk, __nv_bfloat16* __restrict__ Q,
                            __nv_bfloat16* __restrict__ K, __nv_bfloat16* __restrict__ V, int S, int H, int dn, int dr,
                            int dv, int DP, const float* __restrict__ cosv, const float* __restrict__ sinv, int start) {
@@ -436,13 +436,13 @@ __global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, const __nv_bfloa
     const size_t o = (((size_t)b * H + h) * S + s) * DP + c;
     uint4 qv, kv;
     if (c + 8 <= dn) {
-      qv = *reinterpret_cast<const uint4*>(q + ((size_t)t * H + h) * (dn + dr) + c);
+      qv = *reinterpret_cast<const uint4*>(q + (size_t)t * ldq + (size_t)h * (dn + dr) + c);
       kv = *reinterpret_cast<const uint4*>(kvb + ((size_t)t * H + h) * (dn + dv) + c);
     } else if (c >= dn + dr) {
       qv = make_uint4(0, 0, 0, 0);
       kv = qv;
     } else {
-      const uint4 qr = *reinterpret_cast<const uint4*>(q + ((size_t)t * H + h) * (dn + dr) + c);
+      const uint4 qr = *reinterpret_cast<const uint4*>(q + (size_t)t * ldq + (size_t)h * (dn + dr) + c);
       const uint4 kr = *reinterpret_cast<const uint4*>(kpe + (size_t)t * ldk + (c - dn));
       const __nv_bfloat162* qh = reinterpret_cast<const __nv_bfloat162*>(&qr);
       const __nv_bfloat162* kh = reinterpret_cast<const __nv_bfloat162*>(&kr);
@@ -465,7 +465,7 @@ __global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, const __nv_bfloa
 
 // Gradient of mla_pack_v.  dQ, dK fp32 [B,H,S,DP], dV fp32 [B,H,S,dv].
 __global__ void mla_unpack_v(const float* __restrict__ dQ, const float* __restrict__ dK, const float* __restrict__ dV,
-                             __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dkvb,
+                             __nv_bfloat16* __restrict__ dq, long lddq, __nv_bfloat16* __restrict__ dkvb,
                              __nv_bfloat16* __restrict__ dkpe, long ldk, int S, int H, int dn, int dr, int dv, int DP,
                              const float* __restrict__ cosv, const float* __restrict__ sinv, int start) {
   extern __shared__ float pe_acc[];  // [dr]
@@ -509,7 +509,7 @@ __global__ void mla_unpack_v(const float* __restrict__ dQ, const float* __restri
         atomicAdd(&pe_acc[2 * i + 1], -kv[2 * e] * sn + kv[2 * e + 1] * cs);
       }
     }
-    *reinterpret_cast<uint4*>(dq + ((size_t)t * H + h) * (dn + dr) + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+    *reinterpret_cast<uint4*>(dq + (size_t)t * lddq + (size_t)h * (dn + dr) + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
   }
   __syncthreads();
   for (int c = threadIdx.x; c < dr; c += blockDim.x) dkpe[(size_t)t * ldk + c] = __float2bfloat16(pe_acc[c]);
@@ -622,9 +622,10 @@ void mla_pack(const at::Tensor& q, const at::Tensor& kvb, const at::Tensor& kpe,
               const at::Tensor& cosv, const at::Tensor& sinv, int64_t start) {
   const int DP = Q.size(-1);
   const at::cuda::CUDAGuard guard(q.device());
-  if (dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 && kpe.stride(0) % 8 == 0) {
+  if (dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 && kpe.stride(0) % 8 == 0 && q.stride(0) % 8 == 0) {
     mla_pack_v<<<B * S, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
         reinterpret_cast<const __nv_bfloat16*>(kpe.data_ptr()), kpe.stride(0),
         reinterpret_cast<__nv_bfloat16*>(Q.data_ptr()), reinterpret_cast<__nv_bfloat16*>(K.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(V.data_ptr()), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
@@ -632,6 +633,7 @@ void mla_pack(const at::Tensor& q, const at::Tensor& kvb, const at::Tensor& kpe,
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
+  TORCH_CHECK(q.stride(0) == H * (dn + dr), "mla_pack: strided q needs 8-element aligned head dims");
   dim3 grid(B * S, H);
   mla_pack_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kvb.data_ptr()),
@@ -652,9 +654,9 @@ void mla_unpack(const at::Tensor& dQ, const at::Tensor& dK, const at::Tensor& dV
   auto* dkp = reinterpret_cast<__nv_bfloat16*>(dkvb.data_ptr());
   auto* dpe = reinterpret_cast<__nv_bfloat16*>(dkpe.data_ptr());
   if (dV.scalar_type() == at::kFloat && dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 &&
-      dkpe.stride(0) % 8 == 0) {
+      dkpe.stride(0) % 8 == 0 && dq.stride(0) % 8 == 0) {
     mla_unpack_v<<<B * S, 256, dr * sizeof(float), st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
-        dV.data_ptr<float>(), dqp, dkp, dpe, dkpe.stride(0), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
+        dV.data_ptr<float>(), dqp, dq.stride(0), dkp, dpe, dkpe.stride(0), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
         sinv.data_ptr<float>(), start);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
@@ -673,6 +675,7 @@ void mla_unpack(const at::Tensor& dQ, const at::Tensor& dK, const at::Tensor& dV
 void embedding_fwd(const at::Tensor& tok, const at::Tensor& w, at::Tensor& out) {
   const int T = tok.numel(), D = w.size(1);
   TORCH_CHECK(D % 4 == 0 && tok.scalar_type() == at::kLong, "embedding_fwd: D % 4 == 0, int64 ids");
+  TORCH_CHECK(tok.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "embedding_fwd: contiguous tensors");
   const at::cuda::CUDAGuard guard(w.device());
   embedding_fwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
       w.data_ptr<float>(), out.data_ptr<float>(), T, D);
@@ -681,6 +684,7 @@ void embedding_fwd(const at::Tensor& tok, const at::Tensor& w, at::Tensor& out) 
 
 void embedding_bwd(const at::Tensor& tok, const at::Tensor& g, at::Tensor& dw) {
   const int T = tok.numel(), D = dw.size(1);
+  TORCH_CHECK(tok.is_contiguous() && g.is_contiguous() && dw.is_contiguous(), "embedding_bwd: contiguous tensors");
   const at::cuda::CUDAGuard guard(dw.device());
   embedding_bwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
       g.data_ptr<float>(), dw.data_ptr<float>(), T, D);
@@ -700,6 +704,7 @@ void cast_f32_bf16(const at::Tensor& a, at::Tensor& b) {
 void ce_rows(const at::Tensor& pmax, const at::Tensor& psum, const at::Tensor& tl, const at::Tensor& tgt,
              at::Tensor& lse, at::Tensor& loss) {
   const int T = pmax.size(0), nt = pmax.size(1);
+  TORCH_CHECK(tgt.is_contiguous() && pmax.is_contiguous() && psum.is_contiguous(), "ce_rows: contiguous tensors");
   const at::cuda::CUDAGuard guard(pmax.device());
   ce_rows_kernel<<<blocks_for(T, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(pmax.data_ptr<float>(),
       psum.data_ptr<float>(), tl.data_ptr<float>(), tgt.data_ptr<int64_t>(), T, nt, lse.data_ptr<float>(),

@@ -10,51 +10,11 @@
 
 #include "gemm_sm100.cuh"
 #include "status.h"
+#include "tma_host.h"
 
 namespace dsv3 {
 
 namespace {
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p != nullptr,
-                "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
-    fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// bf16 tensor map, 128-byte swizzle, zero fill out of bounds.  dims[0] is the
-// contiguous dimension; strides are in bytes for dims[1..rank-1].
-CUtensorMap make_map(const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                     const uint32_t* box) {
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base address must be 16-byte aligned");
-  for (int i = 0; i + 1 < rank; ++i)
-    TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
-  CUtensorMap m;
-  cuuint64_t d[5], s[4];
-  cuuint32_t b[5], e[5];
-  for (int i = 0; i < rank; ++i) {
-    d[i] = dims[i];
-    b[i] = box[i];
-    e[i] = 1;
-  }
-  for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), d, s, b, e,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));
-  return m;
-}
 
 // A operand, K-major: logical [rows, K] with row stride ld (elements).
 CUtensorMap map_a_kmajor(const at::Tensor& t, int64_t rows, int64_t K, int64_t ld) {
@@ -354,7 +314,8 @@ void ce_fwd_partials(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   check_bf16_rows(w, "w");
   const int64_t T = x.size(0), D = x.size(1), V = w.size(0);
   const int nt = cdiv(V, 256);
-  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == T, "targets: int64 [T]");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == T && targets.is_contiguous(),
+              "targets: contiguous int64 [T]");
   TORCH_CHECK(part_max.numel() == 2 * T * nt && part_sum.numel() == 2 * T * nt && tgt_logit.numel() == T,
               "ce partial shapes: [T, 2 * ceil(V / 256)]");
   const at::cuda::CUDAGuard guard(x.device());
@@ -379,6 +340,7 @@ void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& t
   check_bf16_rows(dlogits, "dlogits");
   const int64_t T = x.size(0), D = x.size(1), V = w.size(0);
   TORCH_CHECK(dlogits.size(0) == T && dlogits.size(1) >= V, "dlogits shape");
+  TORCH_CHECK(targets.is_contiguous() && lse.is_contiguous() && row_scale.is_contiguous(), "ce_bwd: contiguous rows");
   const at::cuda::CUDAGuard guard(x.device());
   GemmArgs g = blank_args();
   g.M = T; g.N = V; g.K = D;

@@ -336,8 +336,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           } else {
             float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
-            for (int j = 0; j < 16; ++j)
-              if (col + j < args.N) atomicAdd(o + j, __uint_as_float(r[j]));
+            if (full16 && (args.ldo & 3) == 0) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + j), "f"(__uint_as_float(r[j])),
+                             "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j + 2])),
+                             "f"(__uint_as_float(r[j + 3]))
+                             : "memory");
+            } else {
+              for (int j = 0; j < 16; ++j)
+                if (col + j < args.N) atomicAdd(o + j, __uint_as_float(r[j]));
+            }
           }
         }
       } else if constexpr (E == Epi::SwigluFwd) {

@@ -13,14 +13,17 @@
 __global__ void latent_decode_split_kernel(const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe,
                                            const bf16* __restrict__ kv, const bf16* __restrict__ pe,
                                            const int* __restrict__ lens, int H, int R, int dr, long kv_bs, long pe_bs,
-                                           int chunk, int nsplit, int BH, float scale, float* __restrict__ part_m,
+                                           int qpb, int chunk, int nsplit, int BH, float scale,
+                                           float* __restrict__ part_m,
                                            float* __restrict__ part_l, float* __restrict__ part_o) {
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int split = warp_global % nsplit;
   const int bh = warp_global / nsplit;
+  // query row b (its own causal length lens[b]) reads cache batch b / qpb
   const int b = bh / H, h = bh % H;
   if (bh >= BH) return;
+  const int cb = b / qpb;
   const int len = lens[b];
   const int r0 = split * chunk, r1 = min(len, r0 + chunk);
   float ql[32], qp[4];  // R <= 1024 (32 per lane), dr <= 128
@@ -30,8 +33,8 @@ __global__ void latent_decode_split_kernel(const bf16* __restrict__ q_lat, const
   float acc[32];
   for (int i = 0; i < 32; ++i) acc[i] = 0.f;
   for (int r = r0; r < r1; ++r) {
-    const bf16* kr = kv + (size_t)b * kv_bs + (size_t)r * R;
-    const bf16* pr = pe + (size_t)b * pe_bs + (size_t)r * dr;
+    const bf16* kr = kv + (size_t)cb * kv_bs + (size_t)r * R;
+    const bf16* pr = pe + (size_t)cb * pe_bs + (size_t)r * dr;
     float kvv[32];
     float dot = 0.f;
     for (int i = 0; i < 32; ++i) {

@@ -62,7 +62,7 @@ extern "C" __attribute__((visibility("default"))) int dsv3_latent_decode_noalloc
   const int warps = B * H * nsplit;
   dsv3::latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(q_lat), static_cast<const __nv_bfloat16*>(q_pe), static_cast<const __nv_bfloat16*>(kv),
-      static_cast<const __nv_bfloat16*>(pe), lens, H, R, dr, (long)kv_batch_stride, (long)pe_batch_stride, chunk, nsplit,
+      static_cast<const __nv_bfloat16*>(pe), lens, H, R, dr, (long)kv_batch_stride, (long)pe_batch_stride, 1, chunk, nsplit,
       B * H, scale, pm, pl, po);
   dsv3::latent_decode_merge_kernel<<<B * H, 128, 0, stream>>>(pm, pl, po, nsplit, R, B * H, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError() == cudaSuccess ? DSV3_NOALLOC_OK : DSV3_NOALLOC_CUDA_ERROR;

@@ -126,13 +126,36 @@ class Transformer(nn.Module):
         """Final RMSNorm applied to a trunk hidden state."""
         return norm_ops.rms_norm(h, self.norm.weight, self.norm.eps)
 
+    def native_inference(self):
+        """The sm_100a inference engine bound to this model (created on first use).
+
+        Cached, gradient-free calls on CUDA tensors with ``use_cache=True`` run
+        on it (prefill + latent-cache decode); training and CPU calls use the
+        module path below.
+        """
+        dev = self.embed.weight.device
+        eng = self.__dict__.get("_infer_engine")
+        if eng is None or eng.device != dev:
+            from ops.infer import InferenceEngine
+            eng = InferenceEngine(self)
+            self.__dict__["_infer_engine"] = eng
+        return eng
+
+    def _use_native(self, tokens: torch.Tensor, use_cache: bool) -> bool:
+        return tokens.is_cuda and use_cache and not torch.is_grad_enabled()
+
     def forward(self, tokens: torch.Tensor, start_pos: int = 0, use_cache: bool = True) -> torch.Tensor:
         """Logits ``[B, S, vocab]``; ``start_pos`` is the cache offset of ``tokens``."""
+        if self._use_native(tokens, use_cache):
+            return self.native_inference().forward(tokens, start_pos=start_pos)[0].float()
         return self.head(self.final_hidden(self._trunk(tokens, start_pos, use_cache)))
 
     def forward_with_hidden(self, tokens: torch.Tensor, start_pos: int = 0,
                             use_cache: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
         """``(logits, pre-final-norm hidden)``; the hidden feeds MTP."""
+        if self._use_native(tokens, use_cache):
+            logits, h = self.native_inference().forward(tokens, start_pos=start_pos, want_hidden=True)
+            return logits.float(), h
         h = self._trunk(tokens, start_pos, use_cache)
         return self.head(self.final_hidden(h)), h
 

@@ -117,6 +117,9 @@ class TrainEngine:
                 blocks.append(block)
 
         for layer in m.layers:
+            # q and kv_a projections share their input: one [wq; wkv_a] block
+            # makes them one GEMM (and one data-gradient, one weight-gradient)
+            add([layer.attn.wq.weight, layer.attn.wkv_a.weight])
             ffn = layer.ffn
             if hasattr(ffn, "experts"):
                 add([w for e in ffn.experts for w in (e.w1.weight, e.w3.weight)])
@@ -168,6 +171,12 @@ class TrainEngine:
         fl = self._fl(w)
         return fl.block_view(fl.grad if grad else fl.shadow, w, (n_groups,) + tuple(w.shape))
 
+    def qkva_block(self, attn, grad: bool = False) -> torch.Tensor:
+        """``[wq; wkv_a]`` as one ``[H*(dn+dr) + R + dr, D]`` operand (shadow or grad)."""
+        fl = self._fl(attn.wq.weight)
+        rows = attn.wq.weight.shape[0] + attn.wkv_a.weight.shape[0]
+        return fl.block_view(fl.grad if grad else fl.shadow, attn.wq.weight, (rows, self.D))
+
     # --------------------------------------------------------------- helpers
     def _norm(self, x, weight_param, eps=1e-6):
         T = x.shape[0]
@@ -197,8 +206,11 @@ class TrainEngine:
         C, H, dn, dr, dv, R = self.C, self.H, self.dn, self.dr, self.dv, self.R
         T = B * S
         ctx = _Ctx(xn=xn)
-        q = self._linear(xn, attn.wq.weight)                          # [T, H*(dn+dr)]
-        kv_a = self._linear(xn, attn.wkv_a.weight)                    # [T, R+dr]
+        Nq = H * (dn + dr)
+        wqa = self.qkva_block(attn)
+        qkva = torch.empty(T, wqa.shape[0], dtype=BF16, device=self.device)
+        C.linear_fwd(xn, wqa, qkva)                                   # [T, H*(dn+dr) + R + dr]
+        q, kv_a = qkva[:, :Nq], qkva[:, Nq:]
         lat = torch.empty(T, R, dtype=BF16, device=self.device)
         rkv = torch.empty(T, dtype=F32, device=self.device)
         C.rmsnorm_fwd(kv_a[:, :R], self.f32(attn.kv_norm.weight), 1e-6, lat, rkv)
@@ -223,15 +235,16 @@ class TrainEngine:
         dV = torch.empty(B * H, S, dv, dtype=F32, device=self.device)
         delta = torch.empty(B * H, S, dtype=F32, device=self.device)
         C.flash_bwd(ctx.Q, ctx.K, ctx.V, ctx.O, dO, ctx.L, delta, dQ, dK, dV, 0, attn.softmax_scale, True, H)
-        dq = torch.empty(T, H * (dn + dr), dtype=BF16, device=self.device)
+        Nq = H * (dn + dr)
+        dqkva = torch.empty(T, Nq + R + dr, dtype=BF16, device=self.device)
+        dq, dkv_a = dqkva[:, :Nq], dqkva[:, Nq:]
         dkvb = torch.empty(T, H * (dn + dv), dtype=BF16, device=self.device)
-        dkv_a = torch.empty(T, R + dr, dtype=BF16, device=self.device)
         C.mla_unpack(dQ, dK, dV, dq, dkvb, dkv_a[:, R:], B, S, H, dn, dr, dv, self.cos, self.sin, 0)
         dlat = self._linear_bwd(dkvb, ctx.lat, attn.wkv_b.weight)
         C.rmsnorm_bwd(dlat, ctx.kv_a[:, :R], self.f32(attn.kv_norm.weight), ctx.rkv, None, dkv_a[:, :R], None,
                       self.g(attn.kv_norm.weight))
-        self._linear_bwd(dkv_a, ctx.xn, attn.wkv_a.weight, dx_acc=dxn_acc, accumulate=False)
-        self._linear_bwd(dq, ctx.xn, attn.wq.weight, dx_acc=dxn_acc)
+        C.linear_wgrad(dqkva, ctx.xn, self.qkva_block(attn, grad=True))
+        C.linear_dgrad(dqkva, self.qkva_block(attn), dxn_acc, False)
 
     # ------------------------------------------------------------------ FFN
     def _swiglu_dense_fwd(self, w1, w2, xn, out, resid_in=None):
@@ -406,8 +419,8 @@ class TrainEngine:
         C, m, D = self.C, self.model, self.D
         B, S = tokens.shape
         T = B * S
-        tok = tokens.reshape(-1).long()
-        tgt = targets.reshape(-1).long()
+        tok = tokens.reshape(-1).long().contiguous()
+        tgt = targets.reshape(-1).long().contiguous()
         x = torch.empty(T, D, dtype=F32, device=self.device)
         C.embedding_fwd(tok, self.f32(m.embed.weight), x)
         saved = []
@@ -446,7 +459,7 @@ class TrainEngine:
                 ctx.etok = etok
                 mtp_ctx.append(ctx)
                 rows.append(hn)
-                tgts.append(tokens[:, d + 2:d + 2 + Sm].reshape(-1).long())
+                tgts.append(tokens[:, d + 2:d + 2 + Sm].reshape(-1).long().contiguous())
                 seg.append(seg[-1] + B * Sm)
                 prev = hn.float().view(B, Sm, D)  # next depth chains on the normalised hidden
         allx = torch.cat(rows, 0) if len(rows) > 1 else xf

@@ -263,3 +263,37 @@ def test_ce_finalize(C):
     ref1 = F.cross_entropy(logits[200:], tgt[200:], ignore_index=-100)
     close(loss, torch.stack([ref0, ref1]), rtol=1e-4, atol=1e-4)
     assert rsc[0].item() == 0 and abs(rsc[10].item() - 0.5 / 193) < 1e-7
+
+
+def _attn_ref(Q, K, V, scale, causal, q_off=0):
+    s = Q.float() @ K.float().transpose(1, 2) * scale
+    if causal:
+        sq, sk = Q.shape[1], K.shape[1]
+        qi = torch.arange(sq, device=Q.device)[:, None] + q_off
+        ki = torch.arange(sk, device=Q.device)[None, :]
+        s = s.masked_fill(ki > qi, float("-inf"))
+    return s.softmax(-1) @ V.float()
+
+
+@pytest.mark.parametrize("B,H,S,DP,DV", [(2, 3, 2048, 80, 64), (1, 2, 300, 80, 64), (2, 2, 1000, 64, 64),
+                                         (1, 2, 640, 128, 128)])
+def test_flash_fwd_tcgen05(C, B, H, S, DP, DV):
+    torch.manual_seed(0)
+    Q = torch.randn(B * H, S, DP, device="cuda").bfloat16()
+    K = torch.randn(B * H, S, DP, device="cuda").bfloat16()
+    V = torch.randn(B * H, S, DV, device="cuda").bfloat16()
+    if DP == 80:
+        Q[..., 72:] = 0
+        K[..., 72:] = 0
+    scale = 0.11
+    O = torch.empty(B, S, H, DV, device="cuda", dtype=torch.bfloat16)
+    L = torch.empty(B * H, S, device="cuda")
+    C.flash_fwd_tc(Q, K, V, O, L, 0, scale, True, H)
+    ref = _attn_ref(Q, K, V, scale, True).view(B, H, S, DV).permute(0, 2, 1, 3)
+    close(O, ref, rtol=2e-2, atol=2e-2)
+    # log-sum-exp (log2 domain) agrees with the warp-level kernel
+    O2 = torch.empty_like(O)
+    L2 = torch.empty_like(L)
+    C.flash_fwd_mma(Q, K, V, O2, L2, 0, scale, True, H)
+    close(L, L2, rtol=1e-3, atol=1e-2)
+    close(O, O2, rtol=2e-2, atol=2e-2)
