@@ -247,6 +247,12 @@ def run_reference(args, rank, world, local):
     if not (ref_root / "training" / "pretrain.py").exists():
         return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
     sys.path.insert(0, str(ref_root))
+    # The reference's stock mode (max-autotune) wraps its graphs in CUDA graphs
+    # and then fails ("accessing tensor output of CUDAGraphs that has been
+    # overwritten") on the causal-mask tensor its Transformer caches across
+    # calls.  Its own TORCH_COMPILE_MODE hook selects the same autotuning
+    # without CUDA graphs.
+    os.environ.setdefault("TORCH_COMPILE_MODE", "max-autotune-no-cudagraphs")
     from training.pretrain import Pretrainer, TrainingConfig  # the reference's own modules
     y = load_yaml(str(ref_root / "configs" / "pretrain_a100_422m.yaml"))
     t, m = y["training"], y["model"]

@@ -516,12 +516,14 @@ void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(), "flash_fwd: contiguous");
   const at::cuda::CUDAGuard guard(q.device());
   const int dqk = q.size(2), dvv = v.size(2);
-  DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  // tcgen05 kernels where the head dims map onto 64/16-element swizzle blocks
+  DSV3_FA_DISPATCH(80, 64, (run_fwd_sm100<1, 1, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_fwd_sm100<1, 0, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(128, 128, (run_fwd_sm100<2, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  // warp-level mma.sync kernels for the remaining shapes
   DSV3_FA_DISPATCH(32, 16, (run_fwd<32, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(16, 16, (run_fwd<16, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(32, 32, (run_fwd<32, 32>(q, k, v, o, lse, q_off, scale, causal, H)))
-  DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
-  DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(192, 128, (run_fwd<192, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   TORCH_CHECK(false, "flash_fwd: unsupported head dims ", dqk, "/", dvv);
 }

@@ -147,14 +147,23 @@ class Transformer(nn.Module):
     def forward(self, tokens: torch.Tensor, start_pos: int = 0, use_cache: bool = True) -> torch.Tensor:
         """Logits ``[B, S, vocab]``; ``start_pos`` is the cache offset of ``tokens``."""
         if self._use_native(tokens, use_cache):
-            return self.native_inference().forward(tokens, start_pos=start_pos)[0].float()
+            eng = self.native_inference()
+            if tokens.shape[1] == 1:   # decode step: CUDA-graph replay
+                pos = torch.full((tokens.shape[0],), start_pos, dtype=torch.int32, device=tokens.device)
+                return eng.decode(tokens[:, 0], pos)[0].float().unsqueeze(1)
+            return eng.forward(tokens, start_pos=start_pos)[0].float()
         return self.head(self.final_hidden(self._trunk(tokens, start_pos, use_cache)))
 
     def forward_with_hidden(self, tokens: torch.Tensor, start_pos: int = 0,
                             use_cache: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
         """``(logits, pre-final-norm hidden)``; the hidden feeds MTP."""
         if self._use_native(tokens, use_cache):
-            logits, h = self.native_inference().forward(tokens, start_pos=start_pos, want_hidden=True)
+            eng = self.native_inference()
+            if tokens.shape[1] == 1:
+                pos = torch.full((tokens.shape[0],), start_pos, dtype=torch.int32, device=tokens.device)
+                logits, h = eng.decode(tokens[:, 0], pos)
+                return logits.float().unsqueeze(1), h.unsqueeze(1)
+            logits, h = eng.forward(tokens, start_pos=start_pos, want_hidden=True)
             return logits.float(), h
         h = self._trunk(tokens, start_pos, use_cache)
         return self.head(self.final_hidden(h)), h

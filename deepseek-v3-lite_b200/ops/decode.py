@@ -69,8 +69,8 @@ def batched_decode_step(model, tokens: torch.Tensor, pos: torch.Tensor):
     ``hidden`` is the pre-final-norm state (the MTP input).
     """
     if tokens.is_cuda:
-        logits, hid = model.native_inference().forward(tokens.view(-1, 1), pos=pos, want_hidden=True)
-        return logits[:, 0].float(), hid[:, 0]
+        logits, hid = model.native_inference().decode(tokens.reshape(-1), pos)
+        return logits.float(), hid.clone()   # graph outputs are overwritten by the next replay
     h = model.embed(tokens.long()).unsqueeze(1)
     for layer in model.layers:
         x = norm_ops.rms_norm(h, layer.attn_norm.weight, layer.attn_norm.eps)

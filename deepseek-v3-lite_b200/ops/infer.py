@@ -52,6 +52,7 @@ class InferenceEngine:
         self.device = next(model.parameters()).device
         self.cos, self.sin = rope_cos_sin(c["max_seq_len"], self.dr, float(c["rope_theta"]), self.device)
         self._cache: Dict[tuple, torch.Tensor] = {}
+        self._graphs: Dict[tuple, tuple] = {}
         if c.get("q_lora_rank", 0) > 0:
             raise NotImplementedError("q_lora_rank > 0 is not wired into the native inference path yet")
 
@@ -256,3 +257,41 @@ class InferenceEngine:
         C.linear_fwd(xf, self.bf16(m.head.weight), logits[:, :self.V])
         out = logits[:, :self.V].view(B, S, self.V)
         return out, (x.view(B, S, self.D) if want_hidden else None)
+
+    # ------------------------------------------------------- graph decode
+    def _graph_key(self, B: int) -> tuple:
+        m = self.model
+        caches = tuple(layer.attn.kv_cache.data_ptr() for layer in m.layers)
+        probe = (m.embed.weight, m.layers[0].attn.wq.weight, m.layers[-1].attn.wo.weight, m.head.weight)
+        return (B, caches, tuple((p.data_ptr(), p._version) for p in probe))
+
+    @torch.no_grad()
+    def decode(self, tokens: torch.Tensor, pos: torch.Tensor):
+        """One decode step for ``tokens [B]`` at positions ``pos [B]``, replayed
+        from a CUDA graph (captured on first use per batch size / cache
+        buffers / weight version).  Returns ``(logits [B, V] bf16, hidden [B, D])``."""
+        B = tokens.shape[0]
+        for layer in self.model.layers:
+            layer.attn._ensure_cache(B, self.device, BF16)
+        key = self._graph_key(B)
+        entry = self._graphs.get(key)
+        if entry is None:
+            for k in [k for k in self._graphs if k[0] == B]:
+                del self._graphs[k]
+            st = tokens.reshape(B, 1).long().clone()
+            sp = pos.to(torch.int32).clone()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):   # warm-up fills the weight caches outside the capture
+                self.forward(st, pos=sp, want_hidden=True)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = self.forward(st, pos=sp, want_hidden=True)
+            entry = (graph, st, sp, out)
+            self._graphs[key] = entry
+        graph, st, sp, (logits, hidden) = entry
+        st.copy_(tokens.reshape(B, 1))
+        sp.copy_(pos)
+        graph.replay()
+        return logits[:, 0], hidden[:, 0]

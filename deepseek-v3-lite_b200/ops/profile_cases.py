@@ -1,0 +1,128 @@
+"""Small, self-contained kernel cases for Nsight Compute captures.
+
+``python -m ops.profile_cases <case>`` (run from ``deepseek-v3-lite_b200/``)
+launches each kernel of one case twice on realistic shapes of the 412M
+training step and exits; the second launch is the one to capture, e.g.::
+
+    python -m ops.profile_cases swiglu_dgrad && \\
+    ncu --set full --clock-control none -k regex:gemm_sm100 -s 1 -c 1 -o prof \\
+        python -m ops.profile_cases swiglu_dgrad
+
+``train_step`` runs one full 412M micro-step (16 x 2048 tokens) between
+``cudaProfilerStart`` / ``cudaProfilerStop`` for a launch list
+(``ncu --metrics gpu__time_duration.sum --profile-from-start off``).
+Every case keeps well under a few GB on the device.
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from ._ext import native
+
+
+def _bf(*shape):
+    return torch.randn(*shape, device="cuda").to(torch.bfloat16)
+
+
+def case_gemm_dense():
+    C = native()
+    a, w = _bf(16384, 768), _bf(2304, 768)
+    out = torch.empty(16384, 2304, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        C.linear_fwd(a, w, out)
+
+
+def case_swiglu_dgrad():
+    C = native()
+    E, D, I = 20, 768, 384
+    rows = [16384 * 4 // E // 128 * 128] * E
+    tiles = [e for e, r in enumerate(rows) for _ in range(r // 128)]
+    P = sum(rows)
+    tg = torch.tensor(tiles, dtype=torch.int32, device="cuda")
+    dy, w2, gu = _bf(P, D), _bf(E, D, I), _bf(P, 2 * I)
+    dgu = torch.empty_like(gu)
+    for _ in range(2):
+        C.swiglu_dgrad(dy, w2, tg, gu, dgu)
+
+
+def case_dense_dgrad_f32():
+    C = native()
+    dy, w = _bf(16384, 1080), _bf(1080, 768)
+    out = torch.empty(16384, 768, device="cuda")
+    for _ in range(2):
+        C.linear_dgrad(dy, w, out, False)
+
+
+def _attn_inputs(B=2, H=12, S=2048, DP=80, DV=64):
+    Q, K, V = _bf(B * H, S, DP), _bf(B * H, S, DP), _bf(B * H, S, DV)
+    O = torch.empty(B, S, H, DV, device="cuda", dtype=torch.bfloat16)
+    L = torch.empty(B * H, S, device="cuda")
+    return B, H, S, DP, DV, Q, K, V, O, L
+
+
+def case_fa_fwd_tc():
+    C = native()
+    B, H, S, DP, DV, Q, K, V, O, L = _attn_inputs()
+    for _ in range(2):
+        C.flash_fwd_tc(Q, K, V, O, L, 0, 0.1, True, H)
+
+
+def case_fa_fwd():
+    C = native()
+    B, H, S, DP, DV, Q, K, V, O, L = _attn_inputs()
+    for _ in range(2):
+        C.flash_fwd(Q, K, V, O, L, 0, 0.1, True, H)
+
+
+def case_fa_bwd():
+    C = native()
+    B, H, S, DP, DV, Q, K, V, O, L = _attn_inputs()
+    C.flash_fwd(Q, K, V, O, L, 0, 0.1, True, H)
+    dQ = torch.zeros(B * H, S, DP, device="cuda")
+    dK, dV = torch.empty_like(dQ), torch.empty(B * H, S, DV, device="cuda")
+    delta = torch.empty(B * H, S, device="cuda")
+    for _ in range(2):
+        C.flash_bwd(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H)
+
+
+def case_train_step():
+    import os
+    import yaml
+    from training.pretrain import Pretrainer, config_from_yaml
+    here = os.path.dirname(os.path.abspath(__file__))
+    y = yaml.safe_load(open(os.path.join(here, "..", "configs", "pretrain_412m.yaml")))
+    cfg = config_from_yaml(y)
+    cfg.batch_size, cfg.gradient_accumulation_steps = 16, 1000
+    cfg.max_steps, cfg.log_per_component_params, cfg.checkpoint_dir = 10 ** 9, False, "/tmp/dsv3_prof_ckpt"
+    tr = Pretrainer(cfg)
+    S = y["model"]["max_seq_len"]
+    d = torch.randint(0, y["model"]["vocab_size"], (16, S + 1), device="cuda")
+    for i in range(2):
+        tr.train_step(d[:, :-1], d[:, 1:], i)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    tr.train_step(d[:, :-1], d[:, 1:], 2)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+
+
+CASES = {k[5:]: v for k, v in globals().items() if k.startswith("case_")}
+
+
+def main():
+    name = sys.argv[1] if len(sys.argv) > 1 else ""
+    if name not in CASES:
+        raise SystemExit(f"usage: python -m ops.profile_cases {{{'|'.join(sorted(CASES))}}}")
+    torch.manual_seed(0)
+    CASES[name]()
+    torch.cuda.synchronize()
+    code = native().status_read()
+    print(f"{name}: ok (status {code})")
+    if code:
+        raise SystemExit(1)
+
+
+if __name__ == "__main__":
+    main()
