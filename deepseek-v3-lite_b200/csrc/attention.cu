@@ -501,6 +501,47 @@ void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int NA, int NB, int DV>
+void run_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                   const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+                   at::Tensor& dv, int q_off, double scale, bool causal, int H) {
+  const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1), DP = q.size(2);
+  const int B = BH / H;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const long rows = (long)BH * Sq;
+  fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
+      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  using Cfg = FabCfg<NA, NB, DV>;
+  auto mk = [](const at::Tensor& t, int S, int D, uint32_t box0, CUtensorMapSwizzle swz) {
+    uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)t.size(0)};
+    uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+    uint32_t box[3] = {box0, 128, 1};
+    return make_map(t.data_ptr(), 3, dims, strides, box, swz);
+  };
+  CUtensorMap qa = mk(q, Sq, DP, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap ka = mk(k, Sk, DP, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap qb = NB ? mk(q, Sq, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : qa;
+  CUtensorMap kb = NB ? mk(k, Sk, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : ka;
+  CUtensorMap vm = mk(v, Sk, DV, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  // dO is token-major [B, Sq, H, DV]
+  uint64_t ddims[4] = {(uint64_t)DV, (uint64_t)H, (uint64_t)Sq, (uint64_t)B};
+  uint64_t dstr[3] = {(uint64_t)DV * 2, (uint64_t)H * DV * 2, (uint64_t)Sq * H * DV * 2};
+  uint32_t dbox[4] = {64, 1, 128, 1};
+  CUtensorMap dom = make_map(dout.data_ptr(), 4, ddims, dstr, dbox, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = fa_bwd_sm100_kernel<NA, NB, DV>;
+  static bool cfg = false;
+  if (!cfg) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    cfg = true;
+  }
+  dim3 grid((Sk + 127) / 128, BH);
+  kern<<<grid, 320, Cfg::SMEM, st>>>(qa, qb, ka, kb, vm, dom, lse.data_ptr<float>(), delta.data_ptr<float>(),
+      dq.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(), Sq, Sk, H, q_off,
+      (float)(scale * 1.4426950408889634), (float)scale, causal ? 1 : 0, status_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 #define DSV3_FA_DISPATCH(DQK_, DV_, CALL)                                                          \
   if (dqk == DQK_ && dvv == DV_) {                                                                 \
     CALL;                                                                                          \
@@ -533,7 +574,8 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
                at::Tensor& dv, int64_t q_off, double scale, bool causal, int64_t H) {
   const at::cuda::CUDAGuard guard(q.device());
   const int dqk = q.size(2), dvv = v.size(2);
-  DSV3_FA_DISPATCH(80, 64, (run_bwd<80, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(80, 64, (run_bwd_sm100<1, 1, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_bwd_sm100<1, 0, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(32, 16, (run_bwd<32, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(16, 16, (run_bwd<16, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(32, 32, (run_bwd<32, 32>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
@@ -586,6 +628,17 @@ void flash_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   TORCH_CHECK(false, "flash_fwd_tc: unsupported head dims");
 }
 
+// The warp-level (mma.sync) backward, kept callable for comparison tests.
+void flash_bwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                   const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+                   at::Tensor& dv, int64_t q_off, double scale, bool causal, int64_t H) {
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dqk = q.size(2), dvv = v.size(2);
+  DSV3_FA_DISPATCH(80, 64, (run_bwd<80, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(64, 64, (run_bwd<64, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
+  TORCH_CHECK(false, "flash_bwd_mma: unsupported head dims");
+}
+
 // The warp-level (mma.sync) forward, kept callable for comparison tests.
 void flash_fwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                    int64_t q_off, double scale, bool causal, int64_t H) {
@@ -600,6 +653,7 @@ void flash_fwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
 void register_attention(pybind11::module_& m) {
   m.def("flash_fwd_mma", &flash_fwd_mma, "warp-level mma.sync flash attention forward");
   m.def("flash_fwd_tc", &flash_fwd_tc, "tcgen05 flash attention forward");
+  m.def("flash_bwd_mma", &flash_bwd_mma, "warp-level mma.sync flash attention backward");
   m.def("flash_fwd", &flash_fwd, "causal flash attention forward (stores log2-domain LSE)");
   m.def("flash_bwd", &flash_bwd, "flash attention backward (dQ fp32 accumulated, dK/dV fp32)");
   m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)", pybind11::arg("q_lat"),

@@ -305,3 +305,351 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 }  // namespace dsv3
+
+namespace dsv3 {
+
+// ----------------------------------------------------------------------------
+// Flash-attention backward on tcgen05.  One CTA per (128-key tile, b*h); it
+// walks the query tiles that can see its keys (causal) and keeps dK / dV for
+// its keys in TMEM:
+//
+//   S^T  = K Q_i^T      dP^T = V dO_i^T                  (TMEM, 128 x 128 each)
+//   P^T  = exp2(S^T c - L[q]),  dS^T = P^T (dP^T - delta[q])   (softmax warps,
+//          one key row per thread, written to smem as bf16 K-major tiles)
+//   dV  += P^T dO_i     dK += dS^T Q_i                   (TMEM accumulators)
+//   dQ_i = dS K          -> TMEM, drained by four more warps with fp32
+//                           vector reductions into the global dQ
+//
+// Q_i / K are used both K-major (for S^T) and MN-major (for dK / dQ): a
+// 128-row tile of 64 (or 16) head-dim columns in 128B (32B) swizzle is the
+// canonical layout of either role.  TMEM: S^T 128 + dP^T 128 + dV DV +
+// dK DQK + dQ DQK columns (<= 512 for DQK = 80, DV = 64).
+// ----------------------------------------------------------------------------
+template <int NA, int NB, int DV>
+struct FabCfg {
+  static constexpr int DQK = NA * 64 + NB * 16;
+  static constexpr int T_B = NA * 16384 + NB * 4096;  // one 128-row Q or K tile
+  static constexpr int V_B = (DV / 64) * 16384;       // one 128-row V or dO tile
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + T_B;
+  static constexpr int OFF_Q = OFF_V + V_B;             // 2 stages
+  static constexpr int OFF_DO = OFF_Q + 2 * T_B;        // 2 stages
+  static constexpr int OFF_P = OFF_DO + 2 * V_B;        // P^T [128 keys][128 q]
+  static constexpr int OFF_DS = OFF_P + 32768;          // dS^T
+  static constexpr int OFF_LD = OFF_DS + 32768;         // L / delta, 2 buffers x 2 x 128 floats
+  static constexpr int OFF_BAR = OFF_LD + 2048;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int DQKP = (DQK + 31) / 32 * 32;   // TMEM regions start on 32-column boundaries
+  static constexpr int C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + DV, C_DQ = 256 + DV + DQKP;
+  static_assert(C_DQ + DQKP <= 512, "TMEM budget");
+};
+
+template <int NA, int NB, int DV>
+__global__ void __launch_bounds__(320, 1)
+    fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
+                        const __grid_constant__ CUtensorMap tmKa, const __grid_constant__ CUtensorMap tmKb,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                        const float* __restrict__ L, const float* __restrict__ delta, float* __restrict__ dQ,
+                        float* __restrict__ dK, float* __restrict__ dVo, int Sq, int Sk, int H, int q_off,
+                        float scale_log2, float scale, int causal, unsigned int* status) {
+  using C = FabCfg<NA, NB, DV>;
+  constexpr int DQK = C::DQK;
+  extern __shared__ __align__(1024) uint8_t fab_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fab_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* kv_full = bar;        // K, V loaded
+  uint64_t* qd_full = bar + 1;    // [2] Q_i, dO_i loaded
+  uint64_t* qd_empty = bar + 3;   // [2]
+  uint64_t* s_full = bar + 5;     // S^T, dP^T ready
+  uint64_t* s_free = bar + 6;     // softmax has them in registers
+  uint64_t* p_full = bar + 7;     // P^T, dS^T written
+  uint64_t* p_free = bar + 8;     // MMAs reading P^T, dS^T done
+  uint64_t* dq_full = bar + 9;
+  uint64_t* dq_free = bar + 10;
+  uint64_t* acc_done = bar + 11;  // final dK, dV in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sLD = reinterpret_cast<float*>(smem + C::OFF_LD);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, n0 = blockIdx.x * 128;
+  const int b = bh / H, h = bh % H;
+  const int qstart = causal ? max(0, (n0 - q_off) / 128) : 0;
+  const int nq = (Sq + 127) / 128;
+  const int iters = max(0, nq - qstart);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 128);
+    mbar_init(p_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // -------------------------------------------------------- producer
+      mbar_arrive_expect_tx(kv_full, C::T_B + C::V_B);
+#pragma unroll
+      for (int a = 0; a < NA; ++a) tma_load_3d(smem + C::OFF_K + a * 16384, &tmKa, kv_full, a * 64, n0, bh);
+      if (NB) tma_load_3d(smem + C::OFF_K + NA * 16384, &tmKb, kv_full, NA * 64, n0, bh);
+#pragma unroll
+      for (int d = 0; d < DV / 64; ++d) tma_load_3d(smem + C::OFF_V + d * 16384, &tmV, kv_full, d * 64, n0, bh);
+      uint32_t issued = 0, last_phase = 0;
+      for (int it = 0; it < iters; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const int q0 = (qstart + it) * 128;
+        if (!mbar_wait_bounded(&qd_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&qd_full[st], C::T_B + C::V_B);
+        uint8_t* q = smem + C::OFF_Q + st * C::T_B;
+        uint8_t* o = smem + C::OFF_DO + st * C::V_B;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) tma_load_3d(q + a * 16384, &tmQa, &qd_full[st], a * 64, q0, bh);
+        if (NB) tma_load_3d(q + NA * 16384, &tmQb, &qd_full[st], NA * 64, q0, bh);
+#pragma unroll
+        for (int d = 0; d < DV / 64; ++d) tma_load_4d(o + d * 16384, &tmdO, &qd_full[st], d * 64, h, q0, b);
+        issued |= 1u << st;
+        last_phase = (last_phase & ~(1u << st)) | (ph << st);
+      }
+      mbar_wait_bounded(kv_full, 0, nullptr, status, DSV3_ERR_WAIT_FULL);
+      for (int st = 0; st < 2; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(&qd_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issuer
+      constexpr uint32_t I_S = idesc_bf16_f32(128, 128, 0, 0);       // S^T, dP^T
+      constexpr uint32_t I_DV = idesc_bf16_f32(128, DV, 0, 1);       // dV += P^T dO
+      constexpr uint32_t I_A64 = idesc_bf16_f32(128, 64, 0, 1);      // dK (SW128 part)
+      constexpr uint32_t I_A16 = idesc_bf16_f32(128, 16, 0, 1);      // dK (SW32 part)
+      constexpr uint32_t I_Q64 = idesc_bf16_f32(128, 64, 1, 1);      // dQ (A = dS, MN-major)
+      constexpr uint32_t I_Q16 = idesc_bf16_f32(128, 16, 1, 1);
+      const uint32_t k_s = smem_u32(smem + C::OFF_K), v_s = smem_u32(smem + C::OFF_V);
+      const uint32_t p_s = smem_u32(smem + C::OFF_P), ds_s = smem_u32(smem + C::OFF_DS);
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
+      bool any = false;
+      for (int it = 0; ok && it < iters; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = it & 1;
+        if (!mbar_wait_bounded(&qd_full[st], (it >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+        if (it > 0 && !mbar_wait_bounded(s_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+        tc_fence_after();
+        const uint32_t q_s = smem_u32(smem + C::OFF_Q + st * C::T_B), o_s = smem_u32(smem + C::OFF_DO + st * C::V_B);
+        // S^T = K Q^T
+        uint32_t acc = 0;
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_bf16(tmem + C::C_S, smem_desc_sw128(k_s + a * 16384 + kk * 32, 16, 1024),
+                      smem_desc_sw128(q_s + a * 16384 + kk * 32, 16, 1024), I_S, acc);
+            acc = 1;
+          }
+        if (NB) umma_bf16(tmem + C::C_S, smem_desc_sw32(k_s + NA * 16384, 256), smem_desc_sw32(q_s + NA * 16384, 256), I_S, 1);
+        // dP^T = V dO^T
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
+          umma_bf16(tmem + C::C_DP, smem_desc_sw128(v_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                    smem_desc_sw128(o_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), I_S, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        any = true;
+        if (!mbar_wait_bounded(p_full, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+        if (it > 0 && !mbar_wait_bounded(dq_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+        tc_fence_after();
+        // dV += P^T dO  (K = the 128 queries, 16 per step)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16(tmem + C::C_DV, smem_desc_sw128(p_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                    smem_desc_sw128(o_s + kk * 2048, 16384, 1024), I_DV, (it > 0 || kk > 0) ? 1u : 0u);
+        // dK += dS^T Q   (Q read MN-major: 64-wide SW128 blocks, then the 16-wide SW32 block)
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + C::C_DK + a * 64, smem_desc_sw128(ds_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                      smem_desc_sw128(q_s + a * 16384 + kk * 2048, 16384, 1024), I_A64, (it > 0 || kk > 0) ? 1u : 0u);
+        if (NB)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + C::C_DK + NA * 64, smem_desc_sw128(ds_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                      smem_desc_sw32(q_s + NA * 16384 + kk * 512, 256), I_A16, (it > 0 || kk > 0) ? 1u : 0u);
+        // dQ = dS K   (A = dS^T read MN-major: queries contiguous; K = the 128 keys)
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + C::C_DQ + a * 64, smem_desc_sw128(ds_s + kk * 2048, 16384, 1024),
+                      smem_desc_sw128(k_s + a * 16384 + kk * 2048, 16384, 1024), I_Q64, kk > 0 ? 1u : 0u);
+        if (NB)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + C::C_DQ + NA * 64, smem_desc_sw128(ds_s + kk * 2048, 16384, 1024),
+                      smem_desc_sw32(k_s + NA * 16384 + kk * 512, 256), I_Q16, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(p_free);
+        umma_commit(&qd_empty[st]);
+      }
+      if (any) {
+        umma_commit(acc_done);
+        mbar_wait_bounded(acc_done, 0, nullptr, status, DSV3_ERR_WAIT_TMEM);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------ softmax (key rows)
+    const int quarter = warp & 3;
+    const int kr = quarter * 32 + lane;
+    const int key = n0 + kr;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    bool ok = true;
+    for (int it = 0; it < iters && ok; ++it) {
+      const uint32_t ph = it & 1;
+      const int q0 = (qstart + it) * 128;
+      float* Lb = sLD + (it & 1) * 256;
+      float* Db = Lb + 128;
+      {
+        const int q = q0 + kr;
+        Lb[kr] = q < Sq ? L[(size_t)bh * Sq + q] : 0.f;
+        Db[kr] = q < Sq ? delta[(size_t)bh * Sq + q] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(p_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      // keys >= lim[q] are masked: key <= q_off + q  <=>  q >= key - q_off
+      const int qmin = causal ? key - q_off : -0x7fffffff;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sr[4][16], dr[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld16(tmem + lane_base + C::C_S + half * 64 + c * 16, sr[c]);
+          tmem_ld16(tmem + lane_base + C::C_DP + half * 64 + c * 16, dr[c]);
+        }
+        tmem_ld_wait();
+        if (half == 1) {
+          tc_fence_before();
+          mbar_arrive(s_free);
+        }
+        uint8_t* prow = smem + C::OFF_P + half * 16384 + kr * 128;
+        uint8_t* dsrow = smem + C::OFF_DS + half * 16384 + kr * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t pk[4], dk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float pv[2], dv2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int col = c * 8 + 2 * e + u;           // within this half
+              const int qi = half * 64 + col;
+              const int q = q0 + qi;
+              const bool valid = q < Sq && key < Sk && q >= qmin;
+              const float s = __uint_as_float(sr[col >> 4][col & 15]);
+              const float dp = __uint_as_float(dr[col >> 4][col & 15]);
+              const float p = valid ? ex2_approx(s * scale_log2 - Lb[qi]) : 0.f;
+              pv[u] = p;
+              dv2[u] = p * (dp - Db[qi]);
+            }
+            pk[e] = pack_bf16x2(pv[0], pv[1]);
+            dk[e] = pack_bf16x2(dv2[0], dv2[1]);
+          }
+          const int sw = (c ^ (kr & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + sw) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(dsrow + sw) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // final dK, dV for this thread's key row
+    if (ok && iters > 0 &&
+        __all_sync(0xffffffffu, mbar_wait_bounded(acc_done, 0, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+      tc_fence_after();
+      float* dkr = dK + ((size_t)bh * Sk + key) * DQK;
+      float* dvr = dVo + ((size_t)bh * Sk + key) * DV;
+#pragma unroll
+      for (int c = 0; c < DQK / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DK + c * 16, r);
+        tmem_ld_wait();
+        if (key < Sk)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(dkr + c * 16 + e) =
+                make_float4(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale,
+                            __uint_as_float(r[e + 2]) * scale, __uint_as_float(r[e + 3]) * scale);
+      }
+#pragma unroll
+      for (int c = 0; c < DV / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DV + c * 16, r);
+        tmem_ld_wait();
+        if (key < Sk)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(dvr + c * 16 + e) = make_float4(
+                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+      }
+    }
+  } else {
+    // ------------------------------------------------ dQ drain (query rows)
+    const int quarter = warp & 3;
+    const int qr = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int it = 0; it < iters; ++it) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_full, it & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) break;
+      tc_fence_after();
+      const int q = (qstart + it) * 128 + qr;
+      float* dqr = dQ + ((size_t)bh * Sq + q) * DQK;
+#pragma unroll
+      for (int c = 0; c < DQK / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DQ + c * 16, r);
+        tmem_ld_wait();
+        if (q < Sq)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dqr + c * 16 + e),
+                         "f"(__uint_as_float(r[e]) * scale), "f"(__uint_as_float(r[e + 1]) * scale),
+                         "f"(__uint_as_float(r[e + 2]) * scale), "f"(__uint_as_float(r[e + 3]) * scale)
+                         : "memory");
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace dsv3

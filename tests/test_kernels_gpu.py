@@ -297,3 +297,34 @@ def test_flash_fwd_tcgen05(C, B, H, S, DP, DV):
     C.flash_fwd_mma(Q, K, V, O2, L2, 0, scale, True, H)
     close(L, L2, rtol=1e-3, atol=1e-2)
     close(O, O2, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("B,H,S,DP,DV", [(2, 3, 2048, 80, 64), (1, 2, 300, 80, 64), (2, 2, 1000, 64, 64)])
+def test_flash_bwd_tcgen05(C, B, H, S, DP, DV):
+    torch.manual_seed(1)
+    Q = torch.randn(B * H, S, DP, device="cuda").bfloat16()
+    K = torch.randn(B * H, S, DP, device="cuda").bfloat16()
+    V = torch.randn(B * H, S, DV, device="cuda").bfloat16()
+    if DP == 80:
+        Q[..., 72:] = 0
+        K[..., 72:] = 0
+    scale = 0.11
+    O = torch.empty(B, S, H, DV, device="cuda", dtype=torch.bfloat16)
+    L = torch.empty(B * H, S, device="cuda")
+    C.flash_fwd(Q, K, V, O, L, 0, scale, True, H)
+    dO = torch.randn(B, S, H, DV, device="cuda").bfloat16()
+    grads = []
+    for fn in (C.flash_bwd, C.flash_bwd_mma):
+        dQ = torch.zeros(B * H, S, DP, device="cuda")
+        dK = torch.empty(B * H, S, DP, device="cuda")
+        dV = torch.empty(B * H, S, DV, device="cuda")
+        delta = torch.empty(B * H, S, device="cuda")
+        fn(Q, K, V, O, dO, L, delta, dQ, dK, dV, 0, scale, True, H)
+        grads.append((dQ, dK, dV))
+    Qr, Kr, Vr = (t.float().requires_grad_(True) for t in (Q, K, V))
+    ref = _attn_ref(Qr, Kr, Vr, scale, True)
+    ref.backward(dO.float().permute(0, 2, 1, 3).reshape(B * H, S, DV))
+    for got in grads:
+        close(got[2], Vr.grad, rtol=3e-2, atol=3e-2)
+        close(got[1], Kr.grad, rtol=3e-2, atol=3e-2)
+        close(got[0], Qr.grad, rtol=3e-2, atol=3e-2)
