@@ -539,6 +539,12 @@ class TrainEngine:
 
     # ------------------------------------------------------------ optimizer
     def last_loss_finite(self) -> bool:
+        """Whether the last micro-batch's losses are finite on *every* rank
+        (ranks must agree, or they would take different collective paths)."""
+        if self.dp is not None:
+            flag = self._finite.to(torch.int32).reshape(1)
+            torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN, group=self.dp.group)
+            return bool(flag.item())
         return bool(self._finite)
 
     def clip_and_step(self, max_norm: float) -> None:
