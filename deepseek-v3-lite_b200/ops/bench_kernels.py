@@ -1,0 +1,86 @@
+"""Kernel microbenchmarks (CUDA-event timing, warm-up, no profiler).
+
+``python -m ops.bench_kernels`` (from ``deepseek-v3-lite_b200/``) prints one
+JSON line per case: the tcgen05 GEMM engine on square and training-step
+shapes (forward, data gradient, weight gradient; cuBLAS via ``torch.matmul``
+on the same forward shape for reference) and the attention kernels (tcgen05
+vs warp-level mma.sync) on the 412M, MTP and MLA-microbenchmark head dims.
+"""
+from __future__ import annotations
+
+import json
+
+import torch
+
+from ._ext import native
+
+
+def _time(fn, iters=10):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def gemm_cases(C):
+    out = []
+    for (M, N, K) in [(8192, 8192, 8192), (32768, 1080, 768), (32768, 768, 768), (32768, 2304, 768),
+                      (32768, 768, 1536)]:
+        a = torch.randn(M, K, device="cuda").bfloat16()
+        w = torch.randn(N, K, device="cuda").bfloat16()
+        o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        dy = torch.randn(M, N, device="cuda").bfloat16()
+        dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+        dw = torch.zeros(N, K, device="cuda")
+        fl = 2.0 * M * N * K
+        f = _time(lambda: C.linear_fwd(a, w, o))
+        cb = _time(lambda: torch.matmul(a, w.t(), out=o))
+        d = _time(lambda: C.linear_dgrad(dy, w, dx))
+        g = _time(lambda: C.linear_wgrad(dy, a, dw))
+        out.append({"case": f"gemm {M}x{N}x{K}", "fwd_tflops": round(fl / f / 1e9, 1),
+                    "dgrad_tflops": round(fl / d / 1e9, 1), "wgrad_tflops": round(fl / g / 1e9, 1),
+                    "cublas_fwd_tflops": round(fl / cb / 1e9, 1)})
+    return out
+
+
+def attention_cases(C):
+    out = []
+    for (B, H, S, DP, DV, dqk) in [(16, 12, 2048, 80, 64, 72), (16, 12, 2046, 64, 64, 64),
+                                   (8, 16, 4096, 128, 128, 128)]:
+        Q = torch.randn(B * H, S, DP, device="cuda").bfloat16()
+        K = torch.randn_like(Q)
+        V = torch.randn(B * H, S, DV, device="cuda").bfloat16()
+        O = torch.empty(B, S, H, DV, device="cuda", dtype=torch.bfloat16)
+        L = torch.empty(B * H, S, device="cuda")
+        fl = 2.0 * B * H * S * S / 2 * (dqk + DV)   # causal forward FLOPs (useful work)
+        r = {"case": f"attention B{B} H{H} S{S} dqk{dqk} dv{DV} causal"}
+        r["fwd_tcgen05_tflops"] = round(fl / _time(lambda: C.flash_fwd_tc(Q, K, V, O, L, 0, 0.1, True, H)) / 1e9, 1)
+        r["fwd_mma_sync_tflops"] = round(fl / _time(lambda: C.flash_fwd_mma(Q, K, V, O, L, 0, 0.1, True, H)) / 1e9, 1)
+        if DP <= 80:
+            dQ = torch.zeros(B * H, S, DP, device="cuda")
+            dK, dV = torch.empty_like(dQ), torch.empty(B * H, S, DV, device="cuda")
+            delta = torch.empty(B * H, S, device="cuda")
+            tb = _time(lambda: C.flash_bwd(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H), 5)
+            tm = _time(lambda: C.flash_bwd_mma(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H), 5)
+            r["bwd_tcgen05_tflops"] = round(2.5 * fl / tb / 1e9, 1)
+            r["bwd_mma_sync_tflops"] = round(2.5 * fl / tm / 1e9, 1)
+        out.append(r)
+    return out
+
+
+def main():
+    C = native()
+    for r in gemm_cases(C) + attention_cases(C):
+        print(json.dumps(r), flush=True)
+    if C.status_read():
+        raise SystemExit("kernel status word set")
+
+
+if __name__ == "__main__":
+    main()
