@@ -95,6 +95,10 @@ class TrainEngine:
             self.rank = self.dp.rank
         self._last_losses: Optional[torch.Tensor] = None
         self._finite = torch.ones(1, dtype=torch.bool, device=self.device)
+        self._segcache: Dict[tuple, tuple] = {}
+        self._graphs: Dict[tuple, tuple] = {}
+        # Capture the micro-step in a CUDA graph (DSV3_CUDA_GRAPH=0 turns it off).
+        self.use_graphs = os.environ.get("DSV3_CUDA_GRAPH", "1") == "1"
 
     # ---------------------------------------------------------------- layout
     def _build_flat(self, groups) -> None:
@@ -414,8 +418,54 @@ class TrainEngine:
         """One micro-batch: forward, loss, backward (gradients accumulate).
 
         Returns device tensors ``loss`` (main CE), ``mtp_loss`` (or None) and
-        ``balance_loss``; nothing here synchronises with the host.
+        ``balance_loss``; nothing here synchronises with the host.  With
+        ``use_graphs`` the whole micro-step is captured once per input shape
+        into a CUDA graph and replayed (no per-kernel host launch cost).
         """
+        if self.use_graphs and torch.cuda.is_current_stream_capturing() is False:
+            return self._graphed(tokens, targets, loss_scale)
+        return self._forward_backward(tokens, targets, loss_scale)
+
+    def _graphed(self, tokens, targets, loss_scale):
+        key = (tuple(tokens.shape), float(loss_scale))
+        entry = self._graphs.get(key)
+        if entry is None:
+            st_tok = tokens.detach().clone()
+            st_tgt = targets.detach().clone()
+            # The warm-up run really executes: keep the gradients it adds out.
+            saved = [f.grad.clone() for f in self.flats]
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self._forward_backward(st_tok, st_tgt, loss_scale)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = self._forward_backward(st_tok, st_tgt, loss_scale)
+            for f, g in zip(self.flats, saved):
+                f.grad.copy_(g)
+            del saved
+            entry = (graph, st_tok, st_tgt, out, self._finite)
+            self._graphs[key] = entry
+        graph, st_tok, st_tgt, out, finite = entry
+        st_tok.copy_(tokens)
+        st_tgt.copy_(targets)
+        graph.replay()
+        self._finite = finite
+        res = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in out.items()}
+        self._last_losses = res["loss"]
+        return res
+
+    def _seg_tensors(self, seg, segw):
+        key = (tuple(seg), tuple(segw))
+        got = self._segcache.get(key)
+        if got is None:
+            got = (torch.tensor(seg, dtype=torch.int32, device=self.device),
+                   torch.tensor(segw, dtype=F32, device=self.device))
+            self._segcache[key] = got
+        return got
+
+    def _forward_backward(self, tokens: torch.Tensor, targets: torch.Tensor, loss_scale: float = 1.0) -> Dict:
         C, m, D = self.C, self.model, self.D
         B, S = tokens.shape
         T = B * S
@@ -478,8 +528,7 @@ class TrainEngine:
         C.ce_rows(pmax, psum, tl, allt, lse, lrows)
         nseg = len(seg) - 1
         segw = [1.0] + [self.mtp.mtp_weight / max(1, nseg - 1)] * (nseg - 1) if self.mtp is not None else [1.0]
-        seg_t = torch.tensor(seg, dtype=torch.int32, device=self.device)
-        segw_t = torch.tensor(segw, dtype=F32, device=self.device)
+        seg_t, segw_t = self._seg_tensors(seg, segw)
         losses = torch.empty(nseg, dtype=F32, device=self.device)
         rscale = torch.empty(Tt, dtype=F32, device=self.device)
         C.ce_reduce(lrows, allt, seg_t, segw_t, float(loss_scale), losses, rscale)
