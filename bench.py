@@ -4,8 +4,10 @@
 runs the flagship training step on N GPUs of one node: the 412M config with
 the yaml's dims, bf16 compute, synthetic uniform-random tokens over the vocab,
 random-init weights, global batch 256 x 2048 = 524,288 tokens per optimizer
-step split over the ranks (data parallel; strong scaling), AdamW + grad
-clipping + router bias update every step.
+step split over the ranks (strong scaling): data parallel, with the routed
+experts spread over all ranks (expert parallel, tokens moved by the
+peer-memory dispatch/combine kernels) for N > 1; AdamW + grad clipping +
+router bias update every step.
 
 Two timed phases, both on the same trainer:
 
@@ -49,6 +51,9 @@ def parse():
     ap.add_argument("--micro-batch", type=int, default=0, help="sequences per micro-step per rank (0 = auto)")
     ap.add_argument("--global-seqs", type=int, default=GLOBAL_SEQS)
     ap.add_argument("--config", type=str, default="")
+    ap.add_argument("--ep", type=int, default=-1,
+                    help="expert-parallel size: -1 = all ranks (the benchmarked DP + EP=world config), 1 = experts "
+                         "replicated (plain data parallelism)")
     return ap.parse_args()
 
 
@@ -187,6 +192,7 @@ def run_ours(args, rank, world, local):
     cfg.warmup_steps = 10
     cfg.log_per_component_params = False
     cfg.checkpoint_dir = "/tmp/dsv3_bench_ckpt"
+    cfg.ep_size = 0 if args.ep < 0 else args.ep
     trainer = Pretrainer(cfg)
     vocab = y["model"]["vocab_size"]
     dev = torch.device("cuda", local)
@@ -221,6 +227,8 @@ def run_ours(args, rank, world, local):
     launches = _ext.count_launches(False) // max(1, args.steps)
     e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, args.steps, world, local)
     trainer.engine.check()
+    ep_on = trainer.engine.use_ep
+    trainer.engine.close()
     tokens_per_step = args.global_seqs * S
     value = tokens_per_step / (ms / 1000.0)
     e2e = tokens_per_step / (max(e2e_ms, e2e_wall_ms) / 1000.0)
@@ -230,7 +238,7 @@ def run_ours(args, rank, world, local):
         "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
         "dtype": "bf16", "data": "synthetic uniform tokens, random-init weights",
         "config": {"model": "deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 w0.3 V100018)",
-                   "global_batch": args.global_seqs * S, "seq_len": S, "parallelism": f"dp{world}",
+                   "global_batch": args.global_seqs * S, "seq_len": S, "parallelism": f"dp{world}+ep{world}" if ep_on else f"dp{world}",
                    "micro_batch_seqs": micro, "grad_accum": accum,
                    "l2": "working set (weights+activations, GBs) far exceeds the 126 MB L2"},
         "clocks": clocks,

@@ -11,6 +11,7 @@ void register_moe(pybind11::module_& m);
 void register_attention(pybind11::module_& m);
 void register_optim(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
+void register_ep(pybind11::module_& m);
 }  // namespace dsv3
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -23,4 +24,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   dsv3::register_attention(m);
   dsv3::register_optim(m);
   dsv3::register_comm(m);
+  dsv3::register_ep(m);
 }

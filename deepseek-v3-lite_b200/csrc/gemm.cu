@@ -300,10 +300,18 @@ void grouped_wgrad(const at::Tensor& a, const at::Tensor& b, const at::Tensor& r
   g.out = out.data_ptr(); g.ldo = Nb; g.out_group_stride = Ma * Nb;
   g.group_row_off = row_off.data_ptr<int>();
   g.m_tiles = cdiv(Ma, 128); g.n_tiles = cdiv(Nb, 256);
-  g.num_tiles = g.m_tiles * g.n_tiles * G;
+  // Few groups (expert parallelism leaves a rank a handful of experts, each
+  // with many rows): split every group's rows so the grid fills the GPU and
+  // reduce the partial tiles with vector atomics.
+  const int base = g.m_tiles * g.n_tiles * (int)G;
+  int splits = 1;
+  if (base < num_sms()) splits = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(2 * num_sms(), base), P / (G * 512)));
+  g.k_splits = splits;
+  g.num_tiles = base * splits;
   CUtensorMap ta = map_a_mnmajor(a, Ma, P, a.stride(0));
   CUtensorMap tb = map_b_mnmajor(b, 1, P, Nb, b.stride(0), P * b.stride(0));
-  launch<256, 1, 1, Sched::GroupedK, Epi::AddF32, false>(ta, tb, g);
+  if (splits > 1) launch<256, 1, 1, Sched::GroupedK, Epi::AtomicAddF32, false>(ta, tb, g);
+  else launch<256, 1, 1, Sched::GroupedK, Epi::AddF32, false>(ta, tb, g);
 }
 
 // Fused LM head + cross-entropy, forward half: per (row, 256-column tile)

@@ -109,9 +109,15 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
     ti.kb1 = (a.K + 63) / 64;
     ti.run = ti.g >= 0;
   } else {
-    ti.g = outer;
-    ti.kb0 = a.group_row_off[outer] / 64;
-    ti.kb1 = a.group_row_off[outer + 1] / 64;
+    // outer = group * k_splits + split; the group's row range (known only on
+    // the device) is cut into k_splits equal chunks of 64-row blocks.
+    const int splits = a.k_splits;
+    ti.g = outer / splits;
+    const int sp = outer - ti.g * splits;
+    const int lo = a.group_row_off[ti.g] / 64, hi = a.group_row_off[ti.g + 1] / 64;
+    const int chunk = (hi - lo + splits - 1) / splits;
+    ti.kb0 = lo + sp * chunk;
+    ti.kb1 = min(hi, ti.kb0 + chunk);
   }
   ti.run = ti.run && (ti.kb1 > ti.kb0);
   return ti;

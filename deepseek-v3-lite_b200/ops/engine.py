@@ -93,6 +93,14 @@ class TrainEngine:
             self.dp = DataParallel(self, group=dp_group)
             self.world_size = self.dp.world_size
             self.rank = self.dp.rank
+        # Expert parallelism: routed experts spread over the data-parallel
+        # ranks, tokens moved by the peer-memory kernels of parallel/ep.py.
+        self.ep = None
+        self.ep_size = int(getattr(config, "ep_size", 1))
+        if self.ep_size not in (0, 1) and self.ep_size != self.world_size:
+            raise NotImplementedError("the expert-parallel group spans all ranks (ep_size 0 or the world size)")
+        self.use_ep = self.dp is not None and self.world_size > 1 and self.ep_size != 1
+        self._moe_slot = {id(mod): i for i, mod in enumerate(model.moe_layers())}
         self._last_losses: Optional[torch.Tensor] = None
         self._finite = torch.ones(1, dtype=torch.bool, device=self.device)
         self._segcache: Dict[tuple, tuple] = {}
@@ -271,11 +279,24 @@ class TrainEngine:
         self.C.linear_dgrad(dgu, w13, dxn_acc, accumulate)
         self.C.linear_wgrad(dgu, xn, self.swiglu_g13(w1, 1).view(2 * I, -1))
 
-    def _moe_fwd(self, moe, xn, resid_in):
-        """Returns (ctx, resid_in + MoE(xn)) as a new fp32 tensor."""
+    def _ep_group(self, tokens: int):
+        """The expert-parallel buffers, created on first use (a collective:
+        every rank reaches it at the same MoE layer)."""
+        if self.ep is None:
+            from parallel.ep import ExpertParallel
+            c = self.cfg
+            self.ep = ExpertParallel(c["n_routed_experts"], c["n_activated_experts"], self.D, tokens,
+                                     n_slots=len(self._moe_slot), group=self.dp.group,
+                                     capacity_factor=float(getattr(self.config, "ep_capacity_factor", 0.0)))
+        if self.ep.T != tokens:
+            raise RuntimeError(f"expert-parallel buffers are sized for {self.ep.T} tokens per micro-batch, got "
+                               f"{tokens}; keep the micro-batch shape fixed")
+        return self.ep
+
+    def _router(self, moe, xn):
         C = self.C
         T = xn.shape[0]
-        E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
+        E, k = moe.n_routed_experts, moe.topk
         Ep = _pad(E, 8)
         logits = torch.empty(T, Ep, dtype=F32, device=self.device)
         C.linear_fwd(xn, self.w(moe.gate.weight), logits[:, :E], False)
@@ -284,6 +305,57 @@ class TrainEngine:
         ssel = torch.empty(T, k, dtype=F32, device=self.device)
         counts = torch.zeros(E, dtype=torch.int32, device=self.device)
         C.router_topk(logits, moe.gate.bias, E, k, float(moe.gate.route_scale), idx, wts, ssel, counts)
+        moe._last_indices = idx
+        moe._last_weights = wts
+        moe._last_counts = counts
+        return idx, wts, ssel, counts, Ep
+
+    def _moe_fwd_ep(self, moe, xn, resid_in):
+        from parallel.ep import moe_forward_ep
+        T = xn.shape[0]
+        E, I = moe.n_routed_experts, moe.moe_inter_dim
+        ep = self._ep_group(T)
+        idx, wts, ssel, counts, Ep = self._router(moe, xn)
+        out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
+        shared = []
+        for i, e in enumerate(moe.shared_experts):
+            shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
+        w13 = self.swiglu_w13(moe.experts[0].w1.weight, E)[ep.lo:ep.hi]
+        w2 = self.stacked(moe.experts[0].w2.weight, E)[ep.lo:ep.hi]
+        ectx = moe_forward_ep(ep, self._moe_slot[id(moe)], xn, idx, wts, counts, w13, w2, out, I)
+        return _Ctx(ep=ectx, idx=idx, wts=wts, ssel=ssel, shared=shared, Ep=Ep, counts=counts), out
+
+    def _moe_bwd_ep(self, moe, ctx, xn, dres_bf16, dxn_acc):
+        from parallel.ep import moe_backward_ep
+        C, ep = self.C, self.ep
+        E, I = moe.n_routed_experts, moe.moe_inter_dim
+        if not moe.shared_experts:
+            dxn_acc.zero_()
+        for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
+            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
+        w1, w2 = moe.experts[0].w1.weight, moe.experts[0].w2.weight
+        dw = moe_backward_ep(ep, ctx.ep, dres_bf16, self.swiglu_w13(w1, E)[ep.lo:ep.hi],
+                             self.stacked(w2, E)[ep.lo:ep.hi], self.swiglu_g13(w1, E)[ep.lo:ep.hi],
+                             self.stacked(w2, E, grad=True)[ep.lo:ep.hi], dxn_acc, I)
+        self._router_bwd(moe, ctx, xn, dw, dxn_acc)
+
+    def _router_bwd(self, moe, ctx, xn, dw, dxn_acc):
+        C = self.C
+        T, E = xn.shape[0], moe.n_routed_experts
+        dlog = torch.empty(T, ctx.Ep, dtype=BF16, device=self.device)
+        C.router_bwd(dw, ctx.ssel, ctx.idx, float(moe.gate.route_scale), dlog)
+        gw = moe.gate.weight
+        C.linear_wgrad(dlog[:, :E], xn, self.g(gw))
+        C.linear_dgrad(dlog[:, :E], self.w(gw), dxn_acc)
+
+    def _moe_fwd(self, moe, xn, resid_in):
+        """Returns (ctx, resid_in + MoE(xn)) as a new fp32 tensor."""
+        if self.use_ep:
+            return self._moe_fwd_ep(moe, xn, resid_in)
+        C = self.C
+        T = xn.shape[0]
+        E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
+        idx, wts, ssel, counts, Ep = self._router(moe, xn)
         P = _pad(T * k + E * 127, 128)
         row_off = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         tile_group = torch.empty(P // 128, dtype=torch.int32, device=self.device)
@@ -305,13 +377,12 @@ class TrainEngine:
         for i, e in enumerate(moe.shared_experts):
             shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
         C.combine_fwd(ys, dst, wts, out)
-        moe._last_indices = idx
-        moe._last_weights = wts
-        moe._last_counts = counts
         return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
                     h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts), out
 
     def _moe_bwd(self, moe, ctx, xn, dres_bf16, dxn_acc):
+        if self.use_ep:
+            return self._moe_bwd_ep(moe, ctx, xn, dres_bf16, dxn_acc)
         C = self.C
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
@@ -332,11 +403,7 @@ class TrainEngine:
         C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs)
         C.grouped_wgrad(dgu, ctx.xs, ctx.row_off, self.swiglu_g13(w1, E))
         C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
-        dlog = torch.empty(T, ctx.Ep, dtype=BF16, device=self.device)
-        C.router_bwd(dw, ctx.ssel, ctx.idx, float(moe.gate.route_scale), dlog)
-        gw = moe.gate.weight
-        C.linear_wgrad(dlog[:, :E], xn, self.g(gw))
-        C.linear_dgrad(dlog[:, :E], self.w(gw), dxn_acc)
+        self._router_bwd(moe, ctx, xn, dw, dxn_acc)
 
     # ------------------------------------------------------------------ MTP
     def _mtp_fwd(self, mod, h_prev, emb, Bm, Sm):
@@ -610,6 +677,15 @@ class TrainEngine:
 
     def check(self) -> None:
         check_status()
+
+    def close(self) -> None:
+        """Release captured graphs and the expert-parallel peer mappings
+        (before the process group goes away)."""
+        torch.cuda.synchronize(self.device)
+        self._graphs.clear()
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None
 
     # ---------------------------------------------------- module interplay
     def sync_to_modules(self) -> None:

@@ -1,0 +1,215 @@
+"""Correctness check of the expert-parallel MoE path on the GPUs of one box.
+
+``python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1
+-m parallel.ep_selftest`` (from ``deepseek-v3-lite_b200/``; N = 1..8) runs a
+routed-expert layer forward + backward through the peer-memory dispatch /
+combine kernels on every rank, twice (so the signal counters advance across
+calls), and compares each rank's outputs, token gradients, gate-weight
+gradients and owned-expert weight gradients with an fp32 PyTorch evaluation
+of the same layer over the tokens of all ranks.  Exits non-zero on mismatch.
+Run without torchrun it checks the single-rank path (the rank stores into its
+own heap through the same kernels).  ``--engine`` instead trains the same tiny
+model with experts spread over the ranks and with experts replicated and
+compares losses and averaged gradients.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+import torch.nn.functional as F
+
+
+def make_case(E, k, D, I, T, rank, device):
+    """Identical expert weights on every rank; rank-specific tokens and grads."""
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    w1 = (torch.randn(E, I, D, generator=g) * 0.05)
+    w3 = (torch.randn(E, I, D, generator=g) * 0.05)
+    w2 = (torch.randn(E, D, I, generator=g) * 0.05)
+    gate = torch.randn(E, D, generator=g) * 0.05
+    gr = torch.Generator(device="cpu").manual_seed(100 + rank)
+    x = torch.randn(T, D, generator=gr)
+    dout = torch.randn(T, D, generator=gr) * 0.1
+    to = dict(device=device)
+    return (w1.to(**to), w3.to(**to), w2.to(**to), gate.to(**to), x.to(**to).bfloat16(),
+            dout.to(**to).bfloat16())
+
+
+def reference_layer(x, idx, wts, dout, w1, w3, w2):
+    """fp32 y[t] = sum_j w[t,j] * W2_e (silu(W1_e x) * W3_e x) and its gradients."""
+    xs = x.float().detach().requires_grad_(True)
+    ws = wts.float().detach().requires_grad_(True)
+    p1, p3, p2 = (w.detach().clone().requires_grad_(True) for w in (w1, w3, w2))
+    y = torch.zeros_like(xs)
+    T, k = idx.shape
+    for j in range(k):
+        e = idx[:, j].long()
+        h = F.silu(torch.einsum("tid,td->ti", p1[e], xs)) * torch.einsum("tid,td->ti", p3[e], xs)
+        y = y + ws[:, j:j + 1] * torch.einsum("tdi,ti->td", p2[e], h)
+    y.backward(dout.float())
+    return y.detach(), xs.grad, ws.grad, p1.grad, p3.grad, p2.grad
+
+
+def run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=True) -> bool:
+    sys.path.insert(0, __file__.rsplit("/parallel/", 1)[0])
+    import torch.distributed as dist
+    from ops._ext import native
+    from parallel.dist import init_distributed
+    from parallel.ep import ExpertParallel, moe_backward_ep, moe_forward_ep
+
+    rank, world, device = init_distributed(timeout_s=60)
+    C = native()
+    C.status_reset()
+    w1, w3, w2, gate, x, dout = make_case(E, k, D, I, T, rank, device)
+    w13 = torch.stack([w1, w3], 1).bfloat16().contiguous()            # [E, 2, I, D]
+    w2b = w2.bfloat16().contiguous()
+    logits = torch.zeros(T, (E + 7) // 8 * 8, device=device)
+    C.linear_fwd(x, gate.bfloat16(), logits[:, :E], False)
+    idx = torch.empty(T, k, dtype=torch.int32, device=device)
+    wts = torch.empty(T, k, device=device)
+    ssel = torch.empty(T, k, device=device)
+    counts = torch.zeros(E, dtype=torch.int32, device=device)
+    C.router_topk(logits, torch.zeros(E, device=device), E, k, 1.0, idx, wts, ssel, counts)
+
+    ep = ExpertParallel(E, k, D, T, n_slots=2, timeout_s=20)
+    lo, hi = ep.lo, ep.hi
+    ok = True
+    # every rank's tokens for the owned-expert weight-gradient reference
+    if world > 1:
+        gath = []
+        for t in (x, idx, wts, dout):
+            buf = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(buf, t.contiguous())
+            gath.append(torch.cat(buf, 0))
+        x_all, idx_all, w_all, d_all = gath
+    else:
+        x_all, idx_all, w_all, d_all = x, idx, wts, dout
+    w1r, w3r, w2r = (w.bfloat16().float() for w in (w1, w3, w2))
+    y_ref, dx_ref, dw_ref, _, _, _ = reference_layer(x, idx, wts, dout, w1r, w3r, w2r)
+    _, _, _, g1_ref, g3_ref, g2_ref = reference_layer(x_all, idx_all, w_all, d_all, w1r, w3r, w2r)
+
+    def close(name, a, b, tol):
+        nonlocal ok
+        err = (a.float() - b.float()).norm() / max(b.float().norm().item(), 1e-12)
+        if not (err <= tol):
+            ok = False
+            print(f"[rank {rank}] {name}: relative error {err:.3e} > {tol}", flush=True)
+        elif verbose:
+            print(f"[rank {rank}] {name}: relative error {err:.3e}", flush=True)
+
+    for it in range(iters):
+        slot = it % 2
+        out = torch.zeros(T, D, device=device)
+        ctx = moe_forward_ep(ep, slot, x, idx, wts, counts, w13[lo:hi], w2b[lo:hi], out, I)
+        dx = torch.zeros(T, D, device=device)
+        g13 = torch.zeros(hi - lo, 2 * I, D, device=device)
+        g2 = torch.zeros(hi - lo, D, I, device=device)
+        dw = moe_backward_ep(ep, ctx, dout, w13[lo:hi], w2b[lo:hi], g13, g2, dx, I).clone()
+        torch.cuda.synchronize()
+        cnt_global = ctx["cnt_all"].sum(0)
+        expect_global = torch.bincount(idx_all.long().flatten(), minlength=E).to(cnt_global)
+        if not torch.equal(cnt_global, expect_global):
+            ok = False
+            print(f"[rank {rank}] exchanged counts differ from the all-gathered routing", flush=True)
+        close(f"it{it} y", out, y_ref, 2e-2)
+        close(f"it{it} dx", dx, dx_ref, 3e-2)
+        close(f"it{it} dw", dw, dw_ref, 3e-2)
+        close(f"it{it} dW1", g13[:, :I], g1_ref[lo:hi], 3e-2)
+        close(f"it{it} dW3", g13[:, I:], g3_ref[lo:hi], 3e-2)
+        close(f"it{it} dW2", g2, g2_ref[lo:hi], 3e-2)
+    code = C.status_read()
+    if code:
+        ok = False
+        print(f"[rank {rank}] device status word {code}", flush=True)
+    ep.close()
+    return ok
+
+
+ENGINE_CFG = {
+    "vocab_size": 1000, "dim": 256, "n_layers": 3, "n_heads": 4, "n_dense_layers": 1,
+    "n_routed_experts": 8, "n_shared_experts": 1, "n_activated_experts": 2, "inter_dim": 512,
+    "moe_inter_dim": 128, "kv_lora_rank": 64, "q_lora_rank": 0, "qk_nope_head_dim": 48,
+    "qk_rope_head_dim": 16, "v_head_dim": 64, "max_seq_len": 128, "rope_theta": 10000,
+    "rope_factor": 1.0, "mscale": 1.0, "mtp_depth": 1, "mtp_loss_weight": 0.3,
+    "attn_impl": "sdpa", "weight_tying": True,
+}
+
+
+def run_engine(verbose=True) -> bool:
+    """The training engine with experts spread over the ranks vs the same
+    engine with experts replicated: same losses, same averaged gradients."""
+    import copy
+    import torch.distributed as dist
+    from models.mtp import MultiTokenPrediction
+    from models.transformer import Transformer
+    from ops.engine import TrainEngine
+    from parallel.dist import init_distributed
+    from training.pretrain import TrainingConfig, _unique_params
+
+    rank, world, device = init_distributed(timeout_s=60)
+    torch.manual_seed(0)
+    base = Transformer(dict(ENGINE_CFG)).to(device)
+    for moe in base.moe_layers():
+        moe.gate.weight.data.mul_(40.0)   # spread the router scores (no near-ties)
+    base_mtp = MultiTokenPrediction(dict(ENGINE_CFG), base).to(device)
+    engines = []
+    for ep_size in (1, 0):
+        mtp = copy.deepcopy(base_mtp)
+        model = mtp.main_model
+        params = _unique_params(mtp)
+        groups = [{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
+                  {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}]
+        engines.append(TrainEngine(model, mtp, TrainingConfig(lr=1e-3, ep_size=ep_size, batch_size=4), groups))
+    B, S = 4, 128
+    g = torch.Generator(device="cpu").manual_seed(7 + rank)
+    tokens = torch.randint(0, ENGINE_CFG["vocab_size"], (B, S), generator=g).to(device)
+    targets = torch.randint(0, ENGINE_CFG["vocab_size"], (B, S), generator=g).to(device)
+    ok = True
+    outs = []
+    for eng in engines:
+        eng.zero_grad()
+        for _ in range(2):   # second pass replays the captured graph
+            eng.zero_grad()
+            out = eng.forward_backward(tokens, targets, loss_scale=1.0)
+        torch.cuda.synchronize()
+        eng.check()
+        eng.dp.reduce_gradients()
+        outs.append((out["loss"].item(), [f.grad.clone() for f in eng.flats]))
+    (l0, g0), (l1, g1) = outs
+    if abs(l0 - l1) > 1e-3 * max(1.0, abs(l0)):
+        ok = False
+        print(f"[rank {rank}] loss {l0} (replicated experts) vs {l1} (expert parallel)", flush=True)
+    for i, (a, b) in enumerate(zip(g0, g1)):
+        err = ((a - b).norm() / a.norm().clamp_min(1e-12)).item()
+        if verbose:
+            print(f"[rank {rank}] flat grad {i}: relative difference {err:.3e}", flush=True)
+        if not err < 2e-2:
+            ok = False
+    for eng in engines:
+        eng.close()
+    return ok
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--engine", action="store_true", help="compare the training engine with and without EP")
+    ap.add_argument("--experts", type=int, default=8)
+    ap.add_argument("--topk", type=int, default=2)
+    ap.add_argument("--dim", type=int, default=256)
+    ap.add_argument("--inter", type=int, default=128)
+    ap.add_argument("--tokens", type=int, default=512)
+    a = ap.parse_args()
+    ok = run_engine() if a.engine else run(a.experts, a.topk, a.dim, a.inter, a.tokens)
+    import torch.distributed as dist
+    if dist.is_initialized():
+        flag = torch.tensor([1 if ok else 0], device="cuda")
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok = bool(flag.item())
+        dist.destroy_process_group()
+    print("EP_SELFTEST", "OK" if ok else "FAILED", flush=True)
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()

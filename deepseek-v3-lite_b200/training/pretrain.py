@@ -94,6 +94,13 @@ class TrainingConfig:
     mup_lr_reference_params: int = 757226496
     log_per_component_params: bool = True
     seed: int = 42
+    # Expert-parallel group size (new; not in the reference, which is
+    # single-device): 1 keeps every routed expert on every rank (plain data
+    # parallelism), 0 spreads them over all ranks of the job.
+    ep_size: int = 1
+    # Receive-buffer cap of expert parallelism as a multiple of the mean load
+    # (0: exact worst case, never overflows).
+    ep_capacity_factor: float = 0.0
 
 
 class PretrainDataset(Dataset):
@@ -496,6 +503,8 @@ def config_from_yaml(yaml_cfg: dict, data_path: Optional[str] = None, checkpoint
         mup_lr_reference_params=t.get("mup_lr_reference_params", 757226496),
         log_per_component_params=t.get("log_per_component_params", True),
         seed=t.get("seed", 42),
+        ep_size=int(yaml_cfg.get("parallel", {}).get("ep_size", 1)),
+        ep_capacity_factor=float(yaml_cfg.get("parallel", {}).get("ep_capacity_factor", 0.0)),
     )
 
 
