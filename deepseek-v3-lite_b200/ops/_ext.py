@@ -50,6 +50,28 @@ def count_launches(enable: bool) -> int:
     return n
 
 
+def add_launches(n: int) -> None:
+    """Account for ``n`` kernels launched outside the wrapper (a CUDA-graph replay)."""
+    if _counting[0]:
+        _counting[1] += n
+
+
+class launch_scope:
+    """Counts the kernel launches issued inside the ``with`` block (e.g. the
+    nodes a CUDA-graph capture records) without disturbing an outer count."""
+
+    def __enter__(self):
+        self._outer = (_counting[0], _counting[1])
+        _counting[0], _counting[1] = True, 0
+        self.count = 0
+        return self
+
+    def __exit__(self, *exc):
+        self.count = _counting[1]
+        _counting[0], _counting[1] = self._outer
+        return False
+
+
 def native():
     """The compiled kernel module; raises ``RuntimeError`` if it is not built."""
     global _mod, _err

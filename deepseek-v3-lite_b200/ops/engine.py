@@ -39,6 +39,7 @@ from typing import Dict, List, Optional
 
 import torch
 
+from . import _ext
 from ._ext import native, check_status
 from .flat import FlatAdamW, FlatParams
 from .rope import rope_cos_sin
@@ -318,11 +319,14 @@ class TrainEngine:
         idx, wts, ssel, counts, Ep = self._router(moe, xn)
         out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
         shared = []
-        for i, e in enumerate(moe.shared_experts):
-            shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
+
+        def shared_fwd():   # overlaps the dispatch (side stream, joined before the combine)
+            for i, e in enumerate(moe.shared_experts):
+                shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
         w13 = self.swiglu_w13(moe.experts[0].w1.weight, E)[ep.lo:ep.hi]
         w2 = self.stacked(moe.experts[0].w2.weight, E)[ep.lo:ep.hi]
-        ectx = moe_forward_ep(ep, self._moe_slot[id(moe)], xn, idx, wts, counts, w13, w2, out, I)
+        ectx = moe_forward_ep(ep, self._moe_slot[id(moe)], xn, idx, wts, counts, w13, w2, out, I,
+                              overlap=shared_fwd if moe.shared_experts else None)
         return _Ctx(ep=ectx, idx=idx, wts=wts, ssel=ssel, shared=shared, Ep=Ep, counts=counts), out
 
     def _moe_bwd_ep(self, moe, ctx, xn, dres_bf16, dxn_acc):
@@ -331,12 +335,15 @@ class TrainEngine:
         E, I = moe.n_routed_experts, moe.moe_inter_dim
         if not moe.shared_experts:
             dxn_acc.zero_()
-        for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
-            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
+
+        def shared_bwd():   # overlaps the gradient dispatch (joined before dxn_acc is summed into)
+            for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
+                self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
         w1, w2 = moe.experts[0].w1.weight, moe.experts[0].w2.weight
         dw = moe_backward_ep(ep, ctx.ep, dres_bf16, self.swiglu_w13(w1, E)[ep.lo:ep.hi],
                              self.stacked(w2, E)[ep.lo:ep.hi], self.swiglu_g13(w1, E)[ep.lo:ep.hi],
-                             self.stacked(w2, E, grad=True)[ep.lo:ep.hi], dxn_acc, I)
+                             self.stacked(w2, E, grad=True)[ep.lo:ep.hi], dxn_acc, I,
+                             overlap=shared_bwd if moe.shared_experts else None)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
 
     def _router_bwd(self, moe, ctx, xn, dw, dxn_acc):
@@ -507,17 +514,18 @@ class TrainEngine:
                 self._forward_backward(st_tok, st_tgt, loss_scale)
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            with _ext.launch_scope() as scope, torch.cuda.graph(graph):
                 out = self._forward_backward(st_tok, st_tgt, loss_scale)
             for f, g in zip(self.flats, saved):
                 f.grad.copy_(g)
             del saved
-            entry = (graph, st_tok, st_tgt, out, self._finite)
+            entry = (graph, st_tok, st_tgt, out, self._finite, scope.count)
             self._graphs[key] = entry
-        graph, st_tok, st_tgt, out, finite = entry
+        graph, st_tok, st_tgt, out, finite, n_kernels = entry
         st_tok.copy_(tokens)
         st_tgt.copy_(targets)
         graph.replay()
+        _ext.add_launches(n_kernels)
         self._finite = finite
         res = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in out.items()}
         self._last_losses = res["loss"]

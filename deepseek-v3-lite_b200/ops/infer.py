@@ -26,6 +26,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
+from . import _ext
 from ._ext import native
 from .rope import rope_cos_sin
 
@@ -286,12 +287,13 @@ class InferenceEngine:
                 self.forward(st, pos=sp, want_hidden=True)
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            with _ext.launch_scope() as scope, torch.cuda.graph(graph):
                 out = self.forward(st, pos=sp, want_hidden=True)
-            entry = (graph, st, sp, out)
+            entry = (graph, st, sp, out, scope.count)
             self._graphs[key] = entry
-        graph, st, sp, (logits, hidden) = entry
+        graph, st, sp, (logits, hidden), n_kernels = entry
         st.copy_(tokens.reshape(B, 1))
         sp.copy_(pos)
         graph.replay()
+        _ext.add_launches(n_kernels)
         return logits[:, 0], hidden[:, 0]

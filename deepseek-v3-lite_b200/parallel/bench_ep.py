@@ -19,7 +19,9 @@ reference  the reference's own modules (``AuxLossFreeGate``, ``Expert``;
 Time: CUDA events on every rank after warm-up, max over ranks.  Per rank the
 line also reports the bytes that crossed NVLink (rows sent to other ranks in
 the four transfer phases) and, for ours, the device time of each transfer
-phase and its fraction of the NVLink roofline (bytes / 770 GB/s per direction,
+phase (the shared experts run on a side stream meanwhile, so a phase also
+holds the wait for the slowest peer) and its fraction of the NVLink roofline
+(bytes / 770 GB/s per direction,
 the peer-copy bandwidth measured on this kind of box), and the whole layer's
 fraction of its roofline: the slower of its FLOPs at the measured bf16 peak
 and its bytes at that link bandwidth.
@@ -128,27 +130,28 @@ class OursLayer:
         counts = torch.zeros(E, dtype=torch.int32, device=dev)
         C.router_topk(logits, self.bias, E, TOPK, 1.0, idx, wts, ssel, counts)
         out = torch.zeros(T, D, device=dev)
-        shared = []
-        for w13, w2 in zip(self.sw13, self.sw2):
-            h = torch.empty(T, INTER, dtype=torch.bfloat16, device=dev)
-            gu = torch.empty(T, 2 * INTER, dtype=torch.bfloat16, device=dev)
-            C.swiglu_fwd(x, w13, self.empty_i32, h, gu)
-            C.linear_fwd(h, w2, out, True)
-            shared.append((h, gu))
-        self._mark("router+shared fwd")
-        ctx = moe_forward_ep(self.ep, 0, x, idx, wts, counts, self.w13, self.w2, out, INTER,
-                             marks=self._mark)
-        self.cnt_all = ctx["cnt_all"]
         dx = torch.zeros(T, D, device=dev)
-        for (h, gu), w13, w2, g13, g2 in zip(shared, self.sw13, self.sw2, self.sg13, self.sg2):
-            dgu = torch.empty(T, 2 * INTER, dtype=torch.bfloat16, device=dev)
-            C.swiglu_dgrad(self.dout, w2.view(1, D, INTER), self.empty_i32, gu, dgu)
-            C.linear_wgrad(self.dout, h, g2)
-            C.linear_dgrad(dgu, w13.view(2 * INTER, D), dx, True)
-            C.linear_wgrad(dgu, x, g13)
-        self._mark("shared bwd")
+        bufs = [(torch.empty(T, INTER, dtype=torch.bfloat16, device=dev),
+                 torch.empty(T, 2 * INTER, dtype=torch.bfloat16, device=dev),
+                 torch.empty(T, 2 * INTER, dtype=torch.bfloat16, device=dev)) for _ in self.sw13]
+        self._mark("router")
+
+        def shared_fwd():   # runs on a side stream while the rows are in flight
+            for (h, gu, _), w13, w2 in zip(bufs, self.sw13, self.sw2):
+                C.swiglu_fwd(x, w13, self.empty_i32, h, gu)
+                C.linear_fwd(h, w2, out, True)
+
+        def shared_bwd():
+            for (h, gu, dgu), w13, w2, g13, g2 in zip(bufs, self.sw13, self.sw2, self.sg13, self.sg2):
+                C.swiglu_dgrad(self.dout, w2.view(1, D, INTER), self.empty_i32, gu, dgu)
+                C.linear_wgrad(self.dout, h, g2)
+                C.linear_dgrad(dgu, w13.view(2 * INTER, D), dx, True)
+                C.linear_wgrad(dgu, x, g13)
+        ctx = moe_forward_ep(self.ep, 0, x, idx, wts, counts, self.w13, self.w2, out, INTER,
+                             marks=self._mark, overlap=shared_fwd)
+        self.cnt_all = ctx["cnt_all"]
         dw = moe_backward_ep(self.ep, ctx, self.dout, self.w13, self.w2, self.g13, self.g2, dx, INTER,
-                             marks=self._mark)
+                             marks=self._mark, overlap=shared_bwd)
         dlog = torch.empty(T, E, dtype=torch.bfloat16, device=dev)
         C.router_bwd(dw, ssel, idx, 1.0, dlog)
         C.linear_wgrad(dlog, x, self.ggate)

@@ -178,9 +178,25 @@ class ExpertParallel:
         return self.heap.tensor(self.off_flags, (5, MAX_RANKS), torch.int32)
 
     # ------------------------------------------------------------- forward
-    def dispatch(self, slot: int, x: torch.Tensor, idx: torch.Tensor, wts: torch.Tensor, counts: torch.Tensor) -> dict:
+    def _fork(self, overlap):
+        """Run ``overlap()`` on a side stream that starts after everything
+        issued so far; returns the stream (join it before using the results)."""
+        if overlap is None:
+            return None
+        if not hasattr(self, "_side"):
+            self._side = torch.cuda.Stream(device=self.device)
+        cur = torch.cuda.current_stream(self.device)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            overlap()
+        return self._side
+
+    def dispatch(self, slot: int, x: torch.Tensor, idx: torch.Tensor, wts: torch.Tensor, counts: torch.Tensor,
+                 overlap=None) -> dict:
         """Plan + P2P dispatch of ``x [T, D]`` along ``idx [T, k]``; waits for
-        every peer's rows.  Returns the receive-side plan."""
+        every peer's rows.  Returns the receive-side plan.  ``overlap()``
+        (independent work, e.g. the shared experts) runs on a side stream
+        while the rows are in flight; ``plan["side"]`` must be joined."""
         C, dev = self.C, self.device
         plan = {
             "cnt_all": torch.empty(self.world, self.E, dtype=torch.int32, device=dev),
@@ -195,6 +211,7 @@ class ExpertParallel:
                   plan["send_base"], plan["row_off"], plan["recv_cnt"], plan["tile_group"], self.cursor)
         C.ep_dispatch(self.heap.peers, offs, self.dims, x, idx, wts, plan["send_base"], self.cursor, plan["route"],
                       plan["row_off"], plan["recv_cnt"], self.done[0:1])
+        plan["side"] = self._fork(overlap)
         C.ep_wait(self.heap.peers, offs, self.dims, PH_DISPATCH, self.expect)
         return plan
 
@@ -205,10 +222,12 @@ class ExpertParallel:
         self.C.ep_wait(self.heap.peers, offs, self.dims, PH_COMBINE, self.expect)
 
     # ------------------------------------------------------------ backward
-    def dispatch_bwd(self, slot: int, g: torch.Tensor, route: torch.Tensor) -> None:
+    def dispatch_bwd(self, slot: int, g: torch.Tensor, route: torch.Tensor, overlap=None):
         offs = self.offs(slot)
         self.C.ep_dispatch_bwd(self.heap.peers, offs, self.dims, g, route, self.done[2:3])
+        side = self._fork(overlap)
         self.C.ep_wait(self.heap.peers, offs, self.dims, PH_BWD_DISPATCH, self.expect)
+        return side
 
     def bwd_prep(self, slot: int, ys: torch.Tensor, row_off: torch.Tensor, dys: torch.Tensor,
                  dw_rows: torch.Tensor) -> None:
@@ -229,16 +248,18 @@ def _no_mark(name: str) -> None:
 
 
 def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, counts, w13_local, w2_local,
-                   out: torch.Tensor, inter_dim: int, marks=_no_mark) -> dict:
+                   out: torch.Tensor, inter_dim: int, marks=_no_mark, overlap=None) -> dict:
     """Routed-expert part of a MoE layer under expert parallelism.
 
     ``w13_local [Eloc, 2, I, D]`` / ``w2_local [Eloc, D, I]``: the owned
     experts' bf16 weights.  Adds ``sum_j w[t, j] * expert_j(x[t])`` into the
     fp32 ``out``.  Returns the context the backward needs.  ``marks(name)``
-    is called after each phase (the microbenchmark records events there).
+    is called after each phase (the microbenchmark records events there);
+    ``overlap()`` runs on a side stream during the transfers and is joined
+    before the combine touches ``out``.
     """
     C = ep.C
-    plan = ep.dispatch(slot, xn, idx, wts, counts)
+    plan = ep.dispatch(slot, xn, idx, wts, counts, overlap=overlap)
     marks("dispatch")
     xs = ep.recv_rows(slot)
     h = torch.empty(ep.cap, inter_dim, dtype=torch.bfloat16, device=xn.device)
@@ -248,6 +269,9 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     C.grouped_fwd(h, w2_local, plan["tile_group"], ys)
     marks("experts fwd")
     ep.combine_send(slot, ys, plan["row_off"])
+    side = plan.pop("side")
+    if side is not None:
+        torch.cuda.current_stream(xn.device).wait_stream(side)
     C.combine_fwd(ep.comb, ep.slot_arange, wts, out)
     marks("combine fwd")
     plan.update(slot=slot, xs=xs, h=h, gu=gu, ys=ys)
@@ -255,14 +279,15 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
 
 
 def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_local, w2_local, g13_local,
-                    g2_local, dx_acc: torch.Tensor, inter_dim: int, marks=_no_mark) -> torch.Tensor:
+                    g2_local, dx_acc: torch.Tensor, inter_dim: int, marks=_no_mark, overlap=None) -> torch.Tensor:
     """Backward of ``moe_forward_ep``: accumulates expert weight gradients of
     the owned experts into ``g13_local [Eloc, 2I, D]`` / ``g2_local [Eloc, D, I]``,
     adds the token input gradients into ``dx_acc`` (fp32) and returns the
-    gate-weight gradients ``dw [T, k]`` (fp32, home side)."""
+    gate-weight gradients ``dw [T, k]`` (fp32, home side).  ``overlap()`` runs
+    on a side stream during the transfers, joined before ``dx_acc`` is read."""
     C = ep.C
     slot = ctx["slot"]
-    ep.dispatch_bwd(slot, dout_bf16, ctx["route"])
+    side = ep.dispatch_bwd(slot, dout_bf16, ctx["route"], overlap=overlap)
     marks("dispatch bwd")
     dys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
     dw_rows = torch.empty(ep.cap, dtype=torch.float32, device=dout_bf16.device)
@@ -275,6 +300,8 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
     marks("experts bwd")
     ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])
+    if side is not None:
+        torch.cuda.current_stream(dx_acc.device).wait_stream(side)
     C.unpermute_bwd(ep.comb, ep.slot_arange, dx_acc)
     marks("combine bwd")
     return ep.dw_inbox.view(ep.T, ep.k)

@@ -42,11 +42,13 @@ def reference_layer(x, idx, wts, dout, w1, w3, w2):
     ws = wts.float().detach().requires_grad_(True)
     p1, p3, p2 = (w.detach().clone().requires_grad_(True) for w in (w1, w3, w2))
     y = torch.zeros_like(xs)
-    T, k = idx.shape
-    for j in range(k):
-        e = idx[:, j].long()
-        h = F.silu(torch.einsum("tid,td->ti", p1[e], xs)) * torch.einsum("tid,td->ti", p3[e], xs)
-        y = y + ws[:, j:j + 1] * torch.einsum("tdi,ti->td", p2[e], h)
+    for e in range(p1.shape[0]):
+        rows, slots = (idx.long() == e).nonzero(as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        xe = xs[rows]
+        h = F.silu(xe @ p1[e].t()) * (xe @ p3[e].t())
+        y = y.index_add(0, rows, ws[rows, slots].unsqueeze(1) * (h @ p2[e].t()))
     y.backward(dout.float())
     return y.detach(), xs.grad, ws.grad, p1.grad, p3.grad, p2.grad
 
