@@ -66,20 +66,68 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
-  using C = GemmCfg<BN>;
-  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW>;
-  static bool configured = false;
-  if (!configured) {
+int cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// CTA-pair tiles (cta_group::2, 256 x BN per pair) for the schedules whose
+// tiles need not share one expert per 128 rows; DSV3_GEMM_PAIRS=0 disables.
+int g_pairs = -1;
+
+bool use_pairs() {
+  if (g_pairs < 0) {
+    const char* e = getenv("DSV3_GEMM_PAIRS");
+    g_pairs = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_pairs == 1;
+}
+
+template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW, int CG>
+void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
+  using C = GemmCfg<BN, CG>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW, CG>;
+  static int max_units = 0;   // resident CTAs (CG = 1) or clusters (CG = 2)
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  if constexpr (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (max_units == 0) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    configured = true;
+    if constexpr (CG == 2) {
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      int clusters = 0;
+      C10_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+      max_units = std::max(1, clusters);
+    } else {
+      max_units = num_sms();
+    }
   }
   if (a.num_tiles <= 0) return;
   a.status = status_ptr();
-  const int grid = std::min(a.num_tiles, num_sms());
-  kern<<<grid, kGemmThreads, C::SMEM_BYTES, at::cuda::getCurrentCUDAStream()>>>(ta, tb, a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int units = std::min(a.num_tiles, max_units);
+  cfg.gridDim = dim3(units * CG);
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+}
+
+template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
+  if constexpr (BN == 256 && S != Sched::GroupedM) {
+    if (use_pairs() && a.m_tiles > 0 && a.M >= 256) {
+      GemmArgs b = a;                      // re-tile the rows in 256-row pair tiles
+      b.m_tiles = cdiv(a.M, 256);
+      b.num_tiles = a.num_tiles / a.m_tiles * b.m_tiles;
+      launch_cg<BN, A_MN, B_MN, S, E, SW, 2>(ta, tb, b);
+      return;
+    }
+  }
+  launch_cg<BN, A_MN, B_MN, S, E, SW, 1>(ta, tb, a);
 }
 
 GemmArgs blank_args() {
@@ -96,7 +144,6 @@ void check_bf16_rows(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.stride(0) % 8 == 0, name, " row stride must be a multiple of 8 elements");
 }
 
-int cdiv(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
 }  // namespace
 
@@ -366,7 +413,14 @@ void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& t
 }  // namespace dsv3
 
 namespace dsv3 {
+// Query (-1) or set (0 / 1) whether eligible GEMMs run on CTA pairs.
+int64_t gemm_pairs(int64_t mode) {
+  if (mode >= 0) g_pairs = mode ? 1 : 0;
+  return use_pairs() ? 1 : 0;
+}
+
 void register_gemm(pybind11::module_& m) {
+  m.def("gemm_pairs", &gemm_pairs, "query (-1) or set (0/1) the CTA-pair (cta_group::2) GEMM tiles");
   m.def("linear_fwd", &linear_fwd, "out = a @ w^T (bf16 store; fp32: accumulate / store / resid + a @ w^T)",
         pybind11::arg("a"), pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("accumulate") = true,
         pybind11::arg("resid") = pybind11::none());

@@ -69,14 +69,17 @@ struct GemmArgs {
   unsigned int* status;  // device status word (bounded-wait failures)
 };
 
-template <int BN>
+// CG = 2: a CTA pair shares one 256-row tile (each CTA: 128 rows of A and
+// BN/2 rows of B in its own shared memory), which halves the B traffic per
+// MMA and leaves room for more pipeline stages.
+template <int BN, int CG = 1>
 struct GemmCfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;            // accumulator rows per CTA
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int STAGES = CG == 2 ? 6 : (BN >= 256 ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
@@ -88,7 +91,7 @@ struct TileInfo {
 };
 
 template <Sched S>
-__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN_) {
+__device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN_, int BM_ = 128) {
   TileInfo ti;
   int n = t % a.n_tiles;
   int rest = t / a.n_tiles;
@@ -96,7 +99,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
   int outer = rest / a.m_tiles;
   ti.n_tile = n;
   ti.n0 = n * BN_;
-  ti.m0 = m * 128;
+  ti.m0 = m * BM_;
   ti.g = 0;
   ti.run = true;
   if constexpr (S == Sched::Dense) {
@@ -126,11 +129,17 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
 // B_SWIGLU: B is read as two 128-row halves (gate rows, up rows) of a 4-D
 // tensor map [G][2][I][K]; BN must be 256 and the epilogue pairs column c of
 // the gate half with column c of the up half.
-template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU>
+template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, CG>;
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
+  static_assert(CG == 1 || (CG == 2 && BN == 256 && S != Sched::GroupedM), "CTA pairs: BN=256, no row-grouped schedule");
+  constexpr int BMT = 128 * CG;                   // rows of one (pair) tile
+  const uint32_t cta = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = cta == 0;
+  const int tile0 = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
@@ -152,7 +161,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 32 * kEpiWarps);
+      mbar_init(&tempty[b], kEpiWarps * CG);   // one arrival per epilogue warp of the pair
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -161,11 +170,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();   // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -175,17 +190,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, last_phase = 0;
-      for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
-        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+      for (int t = tile0; t < args.num_tiles && !*abort_flag; t += tstep) {
+        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN, BMT);
         if (!ti.run) continue;
         for (int kb = ti.kb0; kb < ti.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, args.status, DSV3_ERR_WAIT_EMPTY)) break;
           uint8_t* sA = smem + stage * C::STAGE_BYTES;
           uint8_t* sB = sA + C::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           const int k0 = kb * 64;
           // GroupedK walks global rows of A and B; their maps have no group axis.
           const int bg = (S == Sched::GroupedK) ? 0 : ti.g;
+          if constexpr (CG == 2) {
+            // Both CTAs' copies complete on the even CTA's barrier, which
+            // expects the bytes of the whole pair.
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t fb = cluster_map(smem_u32(&full[stage]), 0);
+            const int ma = ti.m0 + (int)cta * 128;
+            if constexpr (A_MN) {
+              tma_load_2d_pair(sA, &tmA, fb, ma, k0);
+              tma_load_2d_pair(sA + 8192, &tmA, fb, ma + 64, k0);
+            } else {
+              tma_load_2d_pair(sA, &tmA, fb, k0, ma);
+            }
+            if constexpr (B_SWIGLU) {
+              tma_load_4d_pair(sB, &tmB, fb, k0, ti.n0, (int)cta, bg);   // CTA 0: gate rows, CTA 1: up rows
+            } else if constexpr (B_MN) {
+              tma_load_3d_pair(sB, &tmB, fb, ti.n0 + (int)cta * 128, k0, bg);
+              tma_load_3d_pair(sB + 8192, &tmB, fb, ti.n0 + (int)cta * 128 + 64, k0, bg);
+            } else {
+              tma_load_3d_pair(sB, &tmB, fb, k0, ti.n0 + (int)cta * 128, bg);
+            }
+          } else {
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           if constexpr (A_MN) {
             tma_load_2d(sA, &tmA, &full[stage], ti.m0, k0);
             tma_load_2d(sA + 8192, &tmA, &full[stage], ti.m0 + 64, k0);
@@ -202,6 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j) tma_load_3d(sB + j * 16384, &tmB, &full[stage], k0, ti.n0 + 128 * j, bg);
           }
+          }
           issued_mask |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -210,20 +247,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      // Every issued copy must land before the CTA may exit.
+      // Every issued copy must land before the CTA may exit (the odd CTA of a
+      // pair sees that through the MMA's release of the stage).
       for (int s = 0; s < C::STAGES; ++s)
-        if (issued_mask & (1u << s)) mbar_wait_bounded(&full[s], (last_phase >> s) & 1u, nullptr, args.status, DSV3_ERR_WAIT_FULL);
+        if (issued_mask & (1u << s)) {
+          if (leader) mbar_wait_bounded(&full[s], (last_phase >> s) & 1u, nullptr, args.status, DSV3_ERR_WAIT_FULL);
+          else mbar_wait_bounded(&empty[s], (last_phase >> s) & 1u, nullptr, args.status, DSV3_ERR_WAIT_EMPTY);
+        }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16_f32(128, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(BMT, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
-        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+      for (int t = tile0; t < args.num_tiles && !*abort_flag; t += tstep) {
+        TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN, BMT);
         if (!ti.run) continue;
         const int buf = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
@@ -245,22 +286,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                      : smem_desc_sw128(a_base + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc_sw128(b_base + k * 2048, 8192, 1024)
                                      : smem_desc_sw128(b_base + k * 32, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, IDESC, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+            if constexpr (CG == 2) umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > ti.kb0 || k > 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, ad, bd, IDESC, (kb > ti.kb0 || k > 0) ? 1u : 0u);
           }
           issued_any = true;
-          umma_commit(&empty[stage]);
+          if constexpr (CG == 2) umma_commit_pair_both(&empty[stage], 0x3);
+          else umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[buf]);
+        if constexpr (CG == 2) umma_commit_pair_both(&tfull[buf], 0x3);
+        else umma_commit(&tfull[buf]);
         ++local;
       }
       // Drain: make sure no MMA still writes TMEM when it is freed.
       if (issued_any) {
-        umma_commit(drain);
+        if constexpr (CG == 2) umma_commit_pair(drain);
+        else umma_commit(drain);
         mbar_wait_bounded(drain, 0, nullptr, args.status, DSV3_ERR_WAIT_TMEM);
       }
     }
@@ -271,9 +316,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r_in_tile = quarter * 32 + lane;
     constexpr int HALF = BN / 2;
     int local = 0;
-    for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
-      TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN);
+    for (int t = tile0; t < args.num_tiles && !*abort_flag; t += tstep) {
+      TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN, BMT);
       if (!ti.run) continue;
+      ti.m0 += (int)cta * 128;                  // this CTA's rows of the pair tile
       const int buf = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!mbar_wait_bounded(&tfull[buf], aphase, abort_flag, args.status, DSV3_ERR_WAIT_TMEM)) break;
@@ -521,17 +567,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty[buf]);
+      __syncwarp();
+      if (lane == 0) {   // this warp's TMEM reads are done: release the buffer (on the even CTA)
+        if constexpr (CG == 2) mbar_arrive_cluster(cluster_map(smem_u32(&tempty[buf]), 0));
+        else mbar_arrive(&tempty[buf]);
+      }
       ++local;
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();   // the peer no longer touches this CTA's barriers or TMEM
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 

@@ -3,7 +3,8 @@
 ``python -m ops.bench_kernels`` (from ``deepseek-v3-lite_b200/``) prints one
 JSON line per case: the tcgen05 GEMM engine on square and training-step
 shapes (forward, data gradient, weight gradient; cuBLAS via ``torch.matmul``
-on the same forward shape for reference) and the attention kernels (tcgen05
+on the same forward shape for reference; with and without CTA-pair tiles)
+and the attention kernels (tcgen05
 vs warp-level mma.sync) on the 412M, MTP and MLA-microbenchmark head dims.
 """
 from __future__ import annotations
@@ -76,7 +77,13 @@ def attention_cases(C):
 
 def main():
     C = native()
-    for r in gemm_cases(C) + attention_cases(C):
+    for pairs in (1, 0):
+        C.gemm_pairs(pairs)
+        for r in gemm_cases(C):
+            r["cta_pairs"] = bool(pairs)
+            print(json.dumps(r), flush=True)
+    C.gemm_pairs(1)
+    for r in attention_cases(C):
         print(json.dumps(r), flush=True)
     if C.status_read():
         raise SystemExit("kernel status word set")

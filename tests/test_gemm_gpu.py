@@ -5,12 +5,17 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def C():
+@pytest.fixture(scope="module", params=[1, 0], ids=["cta_pairs", "single_cta"])
+def C(request):
+    """Every GEMM test runs with CTA-pair tiles (cta_group::2, where the
+    schedule allows them) and with single-CTA tiles."""
     from ops._ext import native
     m = native()
     m.status_reset()
+    prev = m.gemm_pairs(-1)
+    m.gemm_pairs(request.param)
     yield m
+    m.gemm_pairs(prev)
     assert m.status_read() == 0
 
 
