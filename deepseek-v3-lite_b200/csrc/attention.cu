@@ -27,33 +27,7 @@ namespace {
 
 typedef __nv_bfloat16 bf16;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-// D = A(16x16, row) * B(16x8, col) + D, bf16 in, fp32 accumulate.
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
+#include "mma_sync.cuh"
 
 constexpr int BM = 64;
 constexpr int BN = 64;
@@ -585,6 +559,50 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   TORCH_CHECK(false, "flash_bwd: unsupported head dims ", dqk, "/", dvv);
 }
 
+namespace {
+
+template <int R, int DRP>
+void launch_latent_mma(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv, const at::Tensor& pe,
+                       const at::Tensor& lens, int B, int H, int dr, int qpb, int chunk, int nsplit, double scale,
+                       float* pm, float* pl, float* po, cudaStream_t st) {
+  constexpr int KS = R + DRP + 8;
+  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * 64 * 4;
+  auto kern = latent_decode_mma_kernel<R, DRP>;
+  static bool configured = false;
+  if (!configured) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    configured = true;
+  }
+  dim3 grid(nsplit, (H + 15) / 16, B);
+  kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q_lat.data_ptr()),
+                                reinterpret_cast<const bf16*>(q_pe.data_ptr()),
+                                reinterpret_cast<const bf16*>(kv.data_ptr()),
+                                reinterpret_cast<const bf16*>(pe.data_ptr()), lens.data_ptr<int>(), H, dr,
+                                kv.stride(0), pe.stride(0), qpb, chunk, nsplit,
+                                (float)(scale * 1.4426950408889634), pm, pl, po);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Dispatch onto the instantiated (latent, padded rope) sizes; false if none fits.
+bool run_latent_mma(int R, int dr, const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv,
+                    const at::Tensor& pe, const at::Tensor& lens, int B, int H, int qpb, int chunk, int nsplit,
+                    double scale, float* pm, float* pl, float* po, cudaStream_t st) {
+  const int drp = (dr + 15) / 16 * 16;
+#define DSV3_LD_CASE(R_, DRP_)                                                                                 \
+  if (R == R_ && drp == DRP_) {                                                                                \
+    launch_latent_mma<R_, DRP_>(q_lat, q_pe, kv, pe, lens, B, H, dr, qpb, chunk, nsplit, scale, pm, pl, po, st); \
+    return true;                                                                                               \
+  }
+  DSV3_LD_CASE(512, 64)
+  DSV3_LD_CASE(192, 32)
+  DSV3_LD_CASE(128, 32)
+  DSV3_LD_CASE(64, 16)
+#undef DSV3_LD_CASE
+  return false;
+}
+
+}  // namespace
+
 // q_lat [B, H, R], q_pe [B, H, dr], kv [B, S, R] (batch stride kv.stride(0)),
 // pe [B, S, dr], lens [B] int32 -> out [B, H, R] bf16.
 // Query rows may outnumber cache rows: row b reads cache batch b / qpb, where
@@ -605,6 +623,17 @@ void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   float* pm = scratch.data_ptr<float>();
   float* pl = pm + (long)B * H * nsplit;
   float* po = pl + (long)B * H * nsplit;
+  TORCH_CHECK(kv.stride(1) == R && pe.stride(1) == dr && kv.stride(2) == 1 && pe.stride(2) == 1,
+              "latent_decode: cache rows must be contiguous");
+  const int qpb_ = (int)std::max<int64_t>(1, qpb);
+  // Tensor-core path: all heads of a query row share each staged cache tile.
+  if (dr % 8 == 0 && dr <= 64 && kv.stride(0) % 8 == 0 && pe.stride(0) % 8 == 0 &&
+      run_latent_mma(R, dr, q_lat, q_pe, kv, pe, lens, B, H, qpb_, chunk, nsplit, scale, pm, pl, po, st)) {
+    latent_decode_merge_kernel<<<B * H, 128, 0, st>>>(pm, pl, po, nsplit, R, B * H,
+                                                      reinterpret_cast<bf16*>(out.data_ptr()));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   const int warps = B * H * nsplit;
   latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, st>>>(
       reinterpret_cast<const bf16*>(q_lat.data_ptr()), reinterpret_cast<const bf16*>(q_pe.data_ptr()),

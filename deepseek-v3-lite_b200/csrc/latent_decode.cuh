@@ -4,6 +4,7 @@
 // anonymous namespace by each user.
 #pragma once
 #include "common.cuh"
+#include "mma_sync.cuh"
 
 // Absorbed decode: per (batch row b, head h): scores over cache rows
 // [0, len_b) = q_lat . kv + q_pe . pe, softmax, out = sum p * kv (latent R).
@@ -80,3 +81,199 @@ __global__ void latent_decode_merge_kernel(const float* __restrict__ part_m, con
   }
 }
 
+
+// Tensor-core absorbed decode (warp-level mma.sync m16n8k16).  One CTA per
+// (query row b, group of 16 heads, split of `chunk` cache rows).  Each 64-row
+// tile of the cache (R latent + DRP zero-padded rope columns) is staged in
+// shared memory once (cp.async, double-buffered) and serves all 16 heads:
+//   S[16 x 64]  = Q[16 x (R + DRP)] . K^T      warp w: cache rows 16w..16w+15
+//   row max / sum of the tile across the 4 warps through shared memory
+//   O[16 x R]  += P[16 x 64] . V[64 x R]       warp w: output columns w*R/4..
+// V is the latent part of the same tile, so every cache byte is read once
+// per 16 heads.  Partials (max in natural-log units, sum, O) have the layout
+// the merge kernel above expects.
+template <int R, int DRP>
+__global__ void __launch_bounds__(128) latent_decode_mma_kernel(
+    const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe, const bf16* __restrict__ kv,
+    const bf16* __restrict__ pe, const int* __restrict__ lens, int H, int dr, long kv_bs, long pe_bs, int qpb,
+    int chunk, int nsplit, float scale_log2, float* __restrict__ part_m, float* __restrict__ part_l,
+    float* __restrict__ part_o) {
+  constexpr int DK = R + DRP, KS = DK + 8, TK = 64, PS = TK + 8, RW = R / 4;
+  static_assert(R % 64 == 0 && DRP % 16 == 0 && RW % 16 == 0, "R a multiple of 64, rope padded to 16");
+  extern __shared__ __align__(16) uint8_t ld_smem[];
+  bf16* sQ = reinterpret_cast<bf16*>(ld_smem);           // [16][KS]
+  bf16* sK = sQ + 16 * KS;                                // [2][TK][KS]
+  bf16* sP = sK + 2 * TK * KS;                            // [16][PS]
+  float* red = reinterpret_cast<float*>(sP + 16 * PS);    // [2][4][16]: tile row max, tile row sum
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tig = lane & 3;
+  const int split = blockIdx.x, h0 = blockIdx.y * 16, b = blockIdx.z;
+  const int cb = b / qpb;
+  const int len = lens[b];
+  const int r0 = split * chunk, r1 = min(len, r0 + chunk);
+  const bf16* kvb = kv + (size_t)cb * kv_bs;
+  const bf16* peb = pe + (size_t)cb * pe_bs;
+  const int drc = dr / 8;                                 // 16-byte chunks of a rope row
+
+  if (r0 >= r1) {  // nothing of this row's cache in this split
+    for (int i = tid; i < 16 * R; i += 128) {
+      const int h = h0 + i / R;
+      if (h < H) part_o[((size_t)(b * H + h) * nsplit + split) * R + i % R] = 0.f;
+    }
+    if (tid < 16 && h0 + tid < H) {
+      part_m[(size_t)(b * H + h0 + tid) * nsplit + split] = -INFINITY;
+      part_l[(size_t)(b * H + h0 + tid) * nsplit + split] = 0.f;
+    }
+    return;
+  }
+
+  // queries of the 16 heads (zeros past H and past dr)
+  for (int c = tid; c < 16 * (DK / 8); c += 128) {
+    const int i = c / (DK / 8), cc = c % (DK / 8), h = h0 + i;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < H) {
+      if (cc < R / 8) v = *reinterpret_cast<const uint4*>(q_lat + ((size_t)b * H + h) * R + cc * 8);
+      else if (cc - R / 8 < drc) v = *reinterpret_cast<const uint4*>(q_pe + ((size_t)b * H + h) * dr + (cc - R / 8) * 8);
+    }
+    *reinterpret_cast<uint4*>(sQ + i * KS + cc * 8) = v;
+  }
+  auto load_tile = [&](int t, int st) {
+    bf16* dst = sK + st * TK * KS;
+    const int base = r0 + t * TK;
+    for (int c = tid; c < TK * (DK / 8); c += 128) {
+      const int i = c / (DK / 8), cc = c % (DK / 8), r = base + i;
+      const bool row_ok = r < r1;
+      if (cc < R / 8) {
+        cp_async16(dst + i * KS + cc * 8, kvb + (size_t)(row_ok ? r : r0) * R + cc * 8, row_ok);
+      } else {
+        const int pc = cc - R / 8;
+        const bool ok = row_ok && pc < drc;
+        cp_async16(dst + i * KS + cc * 8, peb + (size_t)(ok ? r : r0) * dr + (ok ? pc : 0) * 8, ok);
+      }
+    }
+  };
+
+  const int ntiles = (r1 - r0 + TK - 1) / TK;
+  load_tile(0, 0);
+  cp_async_commit();
+  float o[RW / 8][4];
+#pragma unroll
+  for (int n = 0; n < RW / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t & 1;
+    if (t + 1 < ntiles) load_tile(t + 1, st ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const bf16* ks = sK + st * TK * KS;
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll 4
+    for (int kk = 0; kk < DK / 16; ++kk) {
+      uint32_t a[4], bb[4];
+      ldsm_x4(a, sQ + ((lane & 7) + 8 * ((lane >> 3) & 1)) * KS + kk * 16 + 8 * (lane >> 4));
+      ldsm_x4(bb, ks + (warp * 16 + (lane & 7) + 8 * (lane >> 4)) * KS + kk * 16 + 8 * ((lane >> 3) & 1));
+      mma16816(s[0], a, bb[0], bb[1]);
+      mma16816(s[1], a, bb[2], bb[3]);
+    }
+    // scale + mask rows past the cache length; this warp's row maxima
+    const int kbase = r0 + t * TK + warp * 16;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = kbase + j * 8 + 2 * tig + (e & 1);
+        const float v = col < r1 ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    if (tig == 0) {
+      red[warp * 16 + g] = mx[0];
+      red[warp * 16 + g + 8] = mx[1];
+    }
+    __syncthreads();
+    float m_new[2], corr[2], msub[2], rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = g + 8 * r;
+      const float tmax = fmaxf(fmaxf(red[row], red[16 + row]), fmaxf(red[32 + row], red[48 + row]));
+      m_new[r] = fmaxf(m_run[r], tmax);
+      msub[r] = m_new[r] == -INFINITY ? 0.f : m_new[r];
+      corr[r] = m_run[r] == -INFINITY ? 0.f : exp2f(m_run[r] - m_new[r]);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float p0 = exp2f(s[j][0] - msub[0]), p1 = exp2f(s[j][1] - msub[0]);
+      const float p2 = exp2f(s[j][2] - msub[1]), p3 = exp2f(s[j][3] - msub[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      const int col = warp * 16 + j * 8 + 2 * tig;
+      *reinterpret_cast<uint32_t*>(sP + g * PS + col) = pack_bf16x2(p0, p1);
+      *reinterpret_cast<uint32_t*>(sP + (g + 8) * PS + col) = pack_bf16x2(p2, p3);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 1);
+      rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
+    }
+    if (tig == 0) {
+      red[64 + warp * 16 + g] = rs[0];
+      red[64 + warp * 16 + g + 8] = rs[1];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = g + 8 * r;
+      const float tsum = (red[64 + row] + red[80 + row]) + (red[96 + row] + red[112 + row]);
+      l_run[r] = l_run[r] * corr[r] + tsum;
+      m_run[r] = m_new[r];
+    }
+#pragma unroll
+    for (int n = 0; n < RW / 8; ++n) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+    // O[:, warp's columns] += P . V  (V = the latent columns of the tile)
+#pragma unroll
+    for (int kc = 0; kc < TK / 16; ++kc) {
+      uint32_t a[4];
+      ldsm_x4(a, sP + ((lane & 7) + 8 * ((lane >> 3) & 1)) * PS + kc * 16 + 8 * (lane >> 4));
+#pragma unroll
+      for (int dp = 0; dp < RW / 16; ++dp) {
+        uint32_t bb[4];
+        ldsm_x4_t(bb, ks + (kc * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * KS + warp * RW + dp * 16 + 8 * (lane >> 4));
+        mma16816(o[2 * dp], a, bb[0], bb[1]);
+        mma16816(o[2 * dp + 1], a, bb[2], bb[3]);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  constexpr float kLn2 = 0.69314718055994531f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int h = h0 + g + 8 * r;
+    if (h >= H) continue;
+    const size_t pi = (size_t)(b * H + h) * nsplit + split;
+    if (warp == 0 && tig == 0) {
+      part_m[pi] = m_run[r] * kLn2;
+      part_l[pi] = l_run[r];
+    }
+    float* po = part_o + pi * R + warp * RW;
+#pragma unroll
+    for (int n = 0; n < RW / 8; ++n)
+      *reinterpret_cast<float2*>(po + n * 8 + 2 * tig) = make_float2(o[n][2 * r], o[n][2 * r + 1]);
+  }
+}
