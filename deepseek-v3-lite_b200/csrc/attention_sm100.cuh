@@ -367,7 +367,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* dq_full = bar + 9;
   uint64_t* dq_free = bar + 10;
   uint64_t* acc_done = bar + 11;  // final dK, dV in TMEM
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* ld_ready = bar + 12;  // L / delta of the query tile staged
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sLD = reinterpret_cast<float*>(smem + C::OFF_LD);
 
@@ -385,12 +386,13 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 128);
-    mbar_init(p_full, 128);
+    mbar_init(s_free, 256);
+    mbar_init(p_full, 256);
     mbar_init(p_free, 1);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    mbar_init(dq_free, 256);
     mbar_init(acc_done, 1);
+    mbar_init(ld_ready, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -436,6 +438,9 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------- MMA issuer
+      // Per query tile i: S^T_i, dP^T_i (as soon as the compute warps hold
+      // tile i-1's in registers), then dV, dK once P^T_i / dS^T_i are in
+      // shared memory, then dQ_i once dQ_{i-1} has been drained.
       constexpr uint32_t I_S = idesc_bf16_f32(128, 128, 0, 0);       // S^T, dP^T
       constexpr uint32_t I_DV = idesc_bf16_f32(128, DV, 0, 1);       // dV += P^T dO
       constexpr uint32_t I_A64 = idesc_bf16_f32(128, 64, 0, 1);      // dK (SW128 part)
@@ -444,14 +449,8 @@ __global__ void __launch_bounds__(320, 1)
       constexpr uint32_t I_Q16 = idesc_bf16_f32(128, 16, 1, 1);
       const uint32_t k_s = smem_u32(smem + C::OFF_K), v_s = smem_u32(smem + C::OFF_V);
       const uint32_t p_s = smem_u32(smem + C::OFF_P), ds_s = smem_u32(smem + C::OFF_DS);
-      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
-      bool any = false;
-      for (int it = 0; ok && it < iters; ++it) {
+      auto issue_s_dp = [&](int it) {
         const int st = it & 1;
-        const uint32_t ph = it & 1;
-        if (!mbar_wait_bounded(&qd_full[st], (it >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
-        if (it > 0 && !mbar_wait_bounded(s_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
-        tc_fence_after();
         const uint32_t q_s = smem_u32(smem + C::OFF_Q + st * C::T_B), o_s = smem_u32(smem + C::OFF_DO + st * C::V_B);
         // S^T = K Q^T
         uint32_t acc = 0;
@@ -470,10 +469,30 @@ __global__ void __launch_bounds__(320, 1)
           umma_bf16(tmem + C::C_DP, smem_desc_sw128(v_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                     smem_desc_sw128(o_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), I_S, kk > 0 ? 1u : 0u);
         umma_commit(s_full);
-        any = true;
+      };
+      bool ok = mbar_wait_bounded(kv_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
+      bool any = false;
+      if (ok && iters > 0) {
+        ok = mbar_wait_bounded(&qd_full[0], 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
+        if (ok) {
+          tc_fence_after();
+          issue_s_dp(0);
+          any = true;
+        }
+      }
+      for (int it = 0; ok && it < iters; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = it & 1;
+        if (it + 1 < iters) {
+          // S / dP TMEM is free once the compute warps loaded tile it
+          if (!mbar_wait_bounded(s_free, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+          if (!mbar_wait_bounded(&qd_full[st ^ 1], ((it + 1) >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+          tc_fence_after();
+          issue_s_dp(it + 1);
+        }
         if (!mbar_wait_bounded(p_full, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
-        if (it > 0 && !mbar_wait_bounded(dq_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
         tc_fence_after();
+        const uint32_t q_s = smem_u32(smem + C::OFF_Q + st * C::T_B), o_s = smem_u32(smem + C::OFF_DO + st * C::V_B);
         // dV += P^T dO  (K = the 128 queries, 16 per step)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -491,7 +510,9 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < 8; ++kk)
             umma_bf16(tmem + C::C_DK + NA * 64, smem_desc_sw128(ds_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                       smem_desc_sw32(q_s + NA * 16384 + kk * 512, 256), I_A16, (it > 0 || kk > 0) ? 1u : 0u);
-        // dQ = dS K   (A = dS^T read MN-major: queries contiguous; K = the 128 keys)
+        // dQ = dS K (A = dS^T read MN-major; K = the 128 keys) once dQ_{it-1} left TMEM
+        if (it > 0 && !mbar_wait_bounded(dq_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+        tc_fence_after();
 #pragma unroll
         for (int a = 0; a < NA; ++a)
 #pragma unroll
@@ -512,122 +533,23 @@ __global__ void __launch_bounds__(320, 1)
         mbar_wait_bounded(acc_done, 0, nullptr, status, DSV3_ERR_WAIT_TMEM);
       }
     }
-  } else if (warp < 6) {
-    // ------------------------------------------------ softmax (key rows)
+  } else {
+    // ---------------------------------------------- compute (key rows)
+    // Warps 2-5 and 6-9 share each key row (same TMEM lane quarter): the
+    // first group takes query columns 0-63 of S^T / dP^T, the second 64-127.
+    // After handing tile i to the MMA warp they drain dQ_{i-1} (each group
+    // half of its columns) with fp32 vector reductions.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int kr = quarter * 32 + lane;
     const int key = n0 + kr;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    bool ok = true;
-    for (int it = 0; it < iters && ok; ++it) {
-      const uint32_t ph = it & 1;
-      const int q0 = (qstart + it) * 128;
-      float* Lb = sLD + (it & 1) * 256;
-      float* Db = Lb + 128;
-      {
-        const int q = q0 + kr;
-        Lb[kr] = q < Sq ? L[(size_t)bh * Sq + q] : 0.f;
-        Db[kr] = q < Sq ? delta[(size_t)bh * Sq + q] : 0.f;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(p_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
-        ok = false;
-        break;
-      }
-      // keys >= lim[q] are masked: key <= q_off + q  <=>  q >= key - q_off
-      const int qmin = causal ? key - q_off : -0x7fffffff;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sr[4][16], dr[4][16];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld16(tmem + lane_base + C::C_S + half * 64 + c * 16, sr[c]);
-          tmem_ld16(tmem + lane_base + C::C_DP + half * 64 + c * 16, dr[c]);
-        }
-        tmem_ld_wait();
-        if (half == 1) {
-          tc_fence_before();
-          mbar_arrive(s_free);
-        }
-        uint8_t* prow = smem + C::OFF_P + half * 16384 + kr * 128;
-        uint8_t* dsrow = smem + C::OFF_DS + half * 16384 + kr * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t pk[4], dk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float pv[2], dv2[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int col = c * 8 + 2 * e + u;           // within this half
-              const int qi = half * 64 + col;
-              const int q = q0 + qi;
-              const bool valid = q < Sq && key < Sk && q >= qmin;
-              const float s = __uint_as_float(sr[col >> 4][col & 15]);
-              const float dp = __uint_as_float(dr[col >> 4][col & 15]);
-              const float p = valid ? ex2_approx(s * scale_log2 - Lb[qi]) : 0.f;
-              pv[u] = p;
-              dv2[u] = p * (dp - Db[qi]);
-            }
-            pk[e] = pack_bf16x2(pv[0], pv[1]);
-            dk[e] = pack_bf16x2(dv2[0], dv2[1]);
-          }
-          const int sw = (c ^ (kr & 7)) << 4;
-          *reinterpret_cast<uint4*>(prow + sw) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(dsrow + sw) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    // final dK, dV for this thread's key row
-    if (ok && iters > 0 &&
-        __all_sync(0xffffffffu, mbar_wait_bounded(acc_done, 0, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
-      tc_fence_after();
-      float* dkr = dK + ((size_t)bh * Sk + key) * DQK;
-      float* dvr = dVo + ((size_t)bh * Sk + key) * DV;
-#pragma unroll
-      for (int c = 0; c < DQK / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + C::C_DK + c * 16, r);
-        tmem_ld_wait();
-        if (key < Sk)
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(dkr + c * 16 + e) =
-                make_float4(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale,
-                            __uint_as_float(r[e + 2]) * scale, __uint_as_float(r[e + 3]) * scale);
-      }
-#pragma unroll
-      for (int c = 0; c < DV / 16; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + C::C_DV + c * 16, r);
-        tmem_ld_wait();
-        if (key < Sk)
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(dvr + c * 16 + e) = make_float4(
-                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
-      }
-    }
-  } else {
-    // ------------------------------------------------ dQ drain (query rows)
-    const int quarter = warp & 3;
-    const int qr = quarter * 32 + lane;
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    for (int it = 0; it < iters; ++it) {
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_full, it & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) break;
-      tc_fence_after();
-      const int q = (qstart + it) * 128 + qr;
+    constexpr int NDQ = DQK / 16;                  // 16-column chunks of dQ / dK
+    const int dq_c0 = half ? (NDQ + 1) / 2 : 0, dq_c1 = half ? NDQ : (NDQ + 1) / 2;
+    auto drain_dq = [&](int it) {
+      const int q = (qstart + it) * 128 + kr;      // TMEM lane = query row of the dQ tile
       float* dqr = dQ + ((size_t)bh * Sq + q) * DQK;
-#pragma unroll
-      for (int c = 0; c < DQK / 16; ++c) {
+      for (int c = dq_c0; c < dq_c1; ++c) {
         uint32_t r[16];
         tmem_ld16(tmem + lane_base + C::C_DQ + c * 16, r);
         tmem_ld_wait();
@@ -641,6 +563,108 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_before();
       mbar_arrive(dq_free);
+    };
+    bool ok = true;
+    for (int it = 0; it < iters && ok; ++it) {
+      const uint32_t ph = it & 1;
+      const int q0 = (qstart + it) * 128;
+      float* Lb = sLD + (it & 1) * 256;
+      float* Db = Lb + 128;
+      if (half == 0) {
+        const int q = q0 + kr;
+        Lb[kr] = q < Sq ? L[(size_t)bh * Sq + q] : 0.f;
+        Db[kr] = q < Sq ? delta[(size_t)bh * Sq + q] : 0.f;
+        mbar_arrive(ld_ready);
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(ld_ready, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(s_full, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[4][16], dr[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld16(tmem + lane_base + C::C_S + half * 64 + c * 16, sr[c]);
+        tmem_ld16(tmem + lane_base + C::C_DP + half * 64 + c * 16, dr[c]);
+      }
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(s_free);
+      // P^T / dS^T of tile it-1 must have been consumed before they are overwritten
+      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(p_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      // keys >= lim[q] are masked: key <= q_off + q  <=>  q >= key - q_off
+      const int qmin = causal ? key - q_off : -0x7fffffff;
+      uint8_t* prow = smem + C::OFF_P + half * 16384 + kr * 128;
+      uint8_t* dsrow = smem + C::OFF_DS + half * 16384 + kr * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t pk[4], dk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float pv[2], dv2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c * 8 + 2 * e + u;           // within this half
+            const int qi = half * 64 + col;
+            const int q = q0 + qi;
+            const bool valid = q < Sq && key < Sk && q >= qmin;
+            const float s = __uint_as_float(sr[col >> 4][col & 15]);
+            const float dp = __uint_as_float(dr[col >> 4][col & 15]);
+            const float p = valid ? ex2_approx(s * scale_log2 - Lb[qi]) : 0.f;
+            pv[u] = p;
+            dv2[u] = p * (dp - Db[qi]);
+          }
+          pk[e] = pack_bf16x2(pv[0], pv[1]);
+          dk[e] = pack_bf16x2(dv2[0], dv2[1]);
+        }
+        const int sw = (c ^ (kr & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + sw) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(dsrow + sw) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      // dQ_{it-1} finished with the MMAs that released P^T / dS^T above
+      if (it > 0) {
+        tc_fence_after();
+        drain_dq(it - 1);
+      }
+    }
+    // last dQ tile, then final dK, dV for this thread's key row (its half of the columns)
+    if (ok && iters > 0 &&
+        __all_sync(0xffffffffu, mbar_wait_bounded(acc_done, 0, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+      tc_fence_after();
+      drain_dq(iters - 1);
+      float* dkr = dK + ((size_t)bh * Sk + key) * DQK;
+      float* dvr = dVo + ((size_t)bh * Sk + key) * DV;
+      for (int c = dq_c0; c < dq_c1; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DK + c * 16, r);
+        tmem_ld_wait();
+        if (key < Sk)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(dkr + c * 16 + e) =
+                make_float4(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale,
+                            __uint_as_float(r[e + 2]) * scale, __uint_as_float(r[e + 3]) * scale);
+      }
+      for (int c = half * (DV / 32); c < (half + 1) * (DV / 32); ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DV + c * 16, r);
+        tmem_ld_wait();
+        if (key < Sk)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4*>(dvr + c * 16 + e) = make_float4(
+                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+      }
     }
   }
   tc_fence_before();
