@@ -1,0 +1,100 @@
+"""Interoperability with the reference implementation itself (CPU).
+
+* Checkpoints written by this framework's ``Pretrainer`` load into the
+  reference's ``Pretrainer`` (its own ``load_checkpoint``), and the reference's
+  checkpoints load here; the model and the MTP head then give the same
+  logits on both sides.  Runs when the reference is installed in
+  ``baseline/_ref`` (``pip install --target baseline/_ref``); each side runs
+  in its own interpreter because both use the package names ``models`` /
+  ``training``.
+* The reference's own test files for the model, trainer, utilities and
+  inference run unmodified against this package when ``DSV3_REFERENCE_TESTS``
+  names the reference's ``tests`` directory.
+"""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+SRC = ROOT / "deepseek-v3-lite_b200"
+REF = ROOT / "baseline" / "_ref"
+
+CFG = {
+    "vocab_size": 1024, "dim": 64, "n_layers": 2, "n_heads": 4, "n_dense_layers": 1,
+    "n_routed_experts": 4, "n_shared_experts": 1, "n_activated_experts": 2, "inter_dim": 128,
+    "moe_inter_dim": 64, "kv_lora_rank": 16, "q_lora_rank": 0, "qk_nope_head_dim": 8,
+    "qk_rope_head_dim": 4, "v_head_dim": 8, "max_seq_len": 64, "rope_theta": 10000,
+    "rope_factor": 1.0, "mscale": 1.0, "mtp_depth": 1, "mtp_loss_weight": 0.3,
+    "attn_impl": "sdpa", "weight_tying": True,
+}
+
+# One side of the exchange: build a Pretrainer, optionally train one step and
+# save, or load the other side's checkpoint; print the logits of fixed tokens.
+SCRIPT = r'''
+import json, sys, torch
+from training.pretrain import Pretrainer, TrainingConfig
+cfg, ckdir, mode = json.loads(sys.argv[1]), sys.argv[2], sys.argv[3]
+tc = TrainingConfig(model_config=cfg, data_path="/nonexistent", checkpoint_dir=ckdir, max_seq_len=cfg["max_seq_len"],
+                    vocab_size=cfg["vocab_size"], batch_size=2, gradient_accumulation_steps=1, max_steps=4,
+                    warmup_steps=0, lr=1e-3, grad_checkpoint=False, compile_model=False, mtp_weight=0.3,
+                    save_every=100, log_every=100)
+torch.manual_seed(0 if mode == "save" else 123)
+tr = Pretrainer(tc)
+tok = torch.randint(0, cfg["vocab_size"], (2, 33), generator=torch.Generator().manual_seed(5))
+if mode == "save":
+    tr.train_step(tok[:, :-1], tok[:, 1:], 0)
+    tr.save_checkpoint(1)
+else:
+    assert tr.load_checkpoint(1) == 1
+tr.raw_model.eval()
+with torch.no_grad():
+    logits = tr.raw_model(tok[:, :-1], use_cache=False)
+    main, pairs = tr.mtp_wrapper(tok[:, :-1])
+print(json.dumps({"logits": logits.flatten()[:4096].tolist(),
+                  "mtp": pairs[0][0].flatten()[:4096].tolist() if pairs else [],
+                  "opt_steps": tr._opt_steps}))
+'''
+
+
+def _side(path, ckdir, mode):
+    env = dict(os.environ, PYTHONPATH=str(path), PYTHONDONTWRITEBYTECODE="1")
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    r = subprocess.run([sys.executable, "-c", SCRIPT, json.dumps(CFG), str(ckdir), mode], env=env,
+                       capture_output=True, text=True, timeout=600, cwd=str(ckdir))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def _close(a, b, tol=1e-4):
+    import torch
+    a, b = torch.tensor(a), torch.tensor(b)
+    assert a.shape == b.shape and a.numel() > 0
+    assert (a - b).abs().max().item() <= tol * max(1.0, b.abs().max().item())
+
+
+@pytest.mark.skipif(not (REF / "models" / "transformer.py").exists(), reason="reference not installed")
+@pytest.mark.parametrize("writer,reader", [("ours", "reference"), ("reference", "ours")])
+def test_checkpoints_cross_load(tmp_path, writer, reader):
+    sides = {"ours": SRC, "reference": REF}
+    saved = _side(sides[writer], tmp_path, "save")
+    loaded = _side(sides[reader], tmp_path, "load")
+    _close(loaded["logits"], saved["logits"])
+    _close(loaded["mtp"], saved["mtp"])
+    assert loaded["opt_steps"] == saved["opt_steps"] == 1
+
+
+REF_TESTS = os.environ.get("DSV3_REFERENCE_TESTS", "")
+
+
+@pytest.mark.skipif(not REF_TESTS, reason="DSV3_REFERENCE_TESTS not set")
+def test_reference_test_suite_passes_against_this_package(tmp_path):
+    files = ["test_models.py", "test_training.py", "test_utils.py", "test_inference.py"]
+    env = dict(os.environ, PYTHONPATH=str(SRC), PYTHONDONTWRITEBYTECODE="1")
+    r = subprocess.run([sys.executable, "-m", "pytest", "-p", "no:cacheprovider", "-q", "--rootdir", str(tmp_path)]
+                       + [str(Path(REF_TESTS) / f) for f in files], env=env, capture_output=True, text=True,
+                       timeout=3600, cwd=str(tmp_path))
+    assert r.returncode == 0, r.stdout[-4000:]
