@@ -12,6 +12,7 @@ void register_attention(pybind11::module_& m);
 void register_optim(pybind11::module_& m);
 void register_comm(pybind11::module_& m);
 void register_ep(pybind11::module_& m);
+void register_dp(pybind11::module_& m);
 }  // namespace dsv3
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -25,4 +26,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   dsv3::register_optim(m);
   dsv3::register_comm(m);
   dsv3::register_ep(m);
+  dsv3::register_dp(m);
 }

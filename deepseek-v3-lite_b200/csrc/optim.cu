@@ -9,6 +9,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "adamw.cuh"
 #include "common.cuh"
 
 namespace dsv3 {
@@ -60,16 +61,10 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
                              float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2_sqrt,
                              const float* __restrict__ coef_ptr) {
   const float coef = coef_ptr ? *coef_ptr : 1.0f;
-  const float step_size = lr / bc1;
+  const AdamHyper h{lr, beta1, beta2, eps, wd, bc1, bc2_sqrt};
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const float gi = g[i] * coef;
-    float pi = p[i];
-    if (i < n_decay) pi *= 1.0f - lr * wd;
-    float mi = m[i];
-    mi = mi + (1.0f - beta1) * (gi - mi);
-    const float vi = beta2 * v[i] + (1.0f - beta2) * gi * gi;
-    const float denom = sqrtf(vi) / bc2_sqrt + eps;
-    pi -= step_size * mi / denom;
+    float pi = p[i], mi = m[i], vi = v[i];
+    adamw_elem(pi, mi, vi, g[i] * coef, i < n_decay, h);
     p[i] = pi;
     m[i] = mi;
     v[i] = vi;

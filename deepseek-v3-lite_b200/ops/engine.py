@@ -82,6 +82,11 @@ class TrainEngine:
             raise NotImplementedError("q_lora_rank > 0 is not wired into the fused engine yet")
         self.max_seq_len = c["max_seq_len"]
         self.ce_chunk = int(os.environ.get("DSV3_CE_CHUNK_ROWS", "16384"))
+        dist_on = torch.distributed.is_available() and torch.distributed.is_initialized()
+        # data parallel step over peer memory (reduce-scatter + sharded AdamW +
+        # all-gather, csrc/dp.cu); DSV3_DP_NCCL=1 selects NCCL all-reduce instead
+        self._fused_dp = (dist_on and torch.distributed.get_world_size(dp_group) > 1
+                          and os.environ.get("DSV3_DP_NCCL", "0") != "1")
         self._build_flat(groups)
         self.optimizer = FlatAdamW(groups, self.flats, lr=config.lr, betas=(config.beta1, config.beta2))
         cos, sin = rope_cos_sin(self.max_seq_len, self.dr, float(c["rope_theta"]), self.device)
@@ -89,9 +94,10 @@ class TrainEngine:
         self.world_size = 1
         self.rank = 0
         self.dp = None
-        if torch.distributed.is_available() and torch.distributed.is_initialized():
-            from parallel.dp import DataParallel
-            self.dp = DataParallel(self, group=dp_group)
+        if dist_on:
+            from parallel.dp import DataParallel, FusedDataParallel
+            self.dp = (FusedDataParallel(self, self.dp_heap, group=dp_group) if self._fused_dp
+                       else DataParallel(self, group=dp_group))
             self.world_size = self.dp.world_size
             self.rank = self.dp.rank
         # Expert parallelism: routed experts spread over the data-parallel
@@ -152,8 +158,17 @@ class TrainEngine:
         decay_ids = {id(p) for p in groups[0]["params"]}
         if any(id(p) not in decay_ids for b in blocks for p in b):
             raise RuntimeError("a packed block contains an undecayed parameter")
-        self.flat_decay = FlatParams(blocks, self.device)
-        self.flat_nodecay = FlatParams([[p] for p in groups[1]["params"]], self.device)
+        nodecay_blocks = [[p] for p in groups[1]["params"]]
+        alloc_d = alloc_n = None
+        self.dp_heap = None
+        if self._fused_dp:
+            # flat buffers in a symmetric heap: the data-parallel step reads the
+            # peers' gradients and writes the peers' weights directly
+            from parallel.dp import FusedDataParallel
+            self.dp_heap, alloc_d, alloc_n = FusedDataParallel.make_heap(
+                [FlatParams.layout_numel(blocks), FlatParams.layout_numel(nodecay_blocks)])
+        self.flat_decay = FlatParams(blocks, self.device, alloc=alloc_d)
+        self.flat_nodecay = FlatParams(nodecay_blocks, self.device, alloc=alloc_n)
         self.flats = [self.flat_decay, self.flat_nodecay]
 
     def _fl(self, p) -> FlatParams:
@@ -672,6 +687,9 @@ class TrainEngine:
         return bool(self._finite)
 
     def clip_and_step(self, max_norm: float) -> None:
+        if self.dp is not None and hasattr(self.dp, "step"):
+            self.dp.step(self.optimizer, max_norm)   # reduce-scatter + sharded AdamW + all-gather
+            return
         if self.dp is not None:
             self.dp.reduce_gradients()
         extra = self.dp.extra_sqsum() if self.dp is not None else None
@@ -694,6 +712,15 @@ class TrainEngine:
         if self.ep is not None:
             self.ep.close()
             self.ep = None
+        if self.dp_heap is not None:
+            # the module parameters alias the heap: move them to plain memory first
+            for f in self.flats:
+                for name in ("master", "grad", "shadow"):
+                    setattr(f, name, getattr(f, name).clone())
+                f.rebind()
+            self.optimizer._bind_state()
+            self.dp_heap.close()
+            self.dp_heap = None
 
     # ---------------------------------------------------- module interplay
     def sync_to_modules(self) -> None:
@@ -709,6 +736,8 @@ class TrainEngine:
 
     def optimizer_state_for_checkpoint(self) -> dict:
         """torch-AdamW state dict with standalone tensors (reference layout)."""
+        if self.dp is not None and hasattr(self.dp, "gather_moments"):
+            self.dp.gather_moments(self.optimizer)   # collective: every rank calls it
         sd = self.optimizer.state_dict()
         for st in sd["state"].values():
             for k in ("exp_avg", "exp_avg_sq"):

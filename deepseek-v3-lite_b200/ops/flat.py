@@ -35,7 +35,18 @@ ALIGN = 64
 class FlatParams:
     """One fp32 master / fp32 grad / bf16 shadow buffer over blocks of parameters."""
 
-    def __init__(self, blocks: Sequence[Sequence[torch.nn.Parameter]], device):
+    @staticmethod
+    def layout_numel(blocks: Sequence[Sequence[torch.nn.Parameter]]) -> int:
+        """Elements of the buffers ``FlatParams(blocks)`` allocates."""
+        off = 0
+        for block in blocks:
+            off = (off + ALIGN - 1) // ALIGN * ALIGN
+            off += sum(p.numel() for p in block)
+        return (off + ALIGN - 1) // ALIGN * ALIGN
+
+    def __init__(self, blocks: Sequence[Sequence[torch.nn.Parameter]], device, alloc=None):
+        """``alloc(name, numel, dtype)`` may supply the three buffers (zeroed),
+        e.g. from a symmetric heap; by default they are plain device tensors."""
         self.params: List[torch.nn.Parameter] = []
         self.offsets: Dict[int, int] = {}
         self.block_offsets: List[int] = []
@@ -50,9 +61,12 @@ class FlatParams:
                 self.params.append(p)
                 off += p.numel()
         self.numel = (off + ALIGN - 1) // ALIGN * ALIGN
-        self.master = torch.zeros(self.numel, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(self.numel, dtype=torch.float32, device=device)
-        self.shadow = torch.zeros(self.numel, dtype=torch.bfloat16, device=device)
+        if alloc is None:
+            def alloc(name, n, dtype):
+                return torch.zeros(n, dtype=dtype, device=device)
+        self.master = alloc("master", self.numel, torch.float32)
+        self.grad = alloc("grad", self.numel, torch.float32)
+        self.shadow = alloc("shadow", self.numel, torch.bfloat16)
         for p in self.params:
             o = self.offsets[id(p)]
             self.master[o:o + p.numel()].copy_(p.data.reshape(-1).to(device=device, dtype=torch.float32))

@@ -46,3 +46,106 @@ class DataParallel:
         c = counts.clone()
         dist.all_reduce(c, op=dist.ReduceOp.SUM, group=self.group)
         return c
+
+
+def _shard(n: int, rank: int, world: int, align: int = 64) -> tuple:
+    """Contiguous, 64-element aligned shard [lo, hi) of n elements owned by rank."""
+    def cut(r):
+        return min(n, (r * n // world + align - 1) // align * align)
+    return cut(rank), cut(rank + 1)
+
+
+class FusedDataParallel(DataParallel):
+    """Data parallelism whose optimizer step runs over NVLink peer memory.
+
+    The flat fp32 gradient / fp32 master / bf16 shadow buffers of every rank
+    sit in one symmetric heap.  ``step`` replaces all-reduce + full AdamW with
+    (csrc/dp.cu): a barrier (every rank's gradients complete), a
+    reduce-scatter that averages this rank's shard straight from the peers'
+    buffers and takes its squared norm, an exchange of the norms (same clip
+    coefficient everywhere), and AdamW on the shard only, whose new master and
+    bf16 shadow values are stored into every rank's buffers (the
+    all-gather), then a closing barrier.  Adam moments are only advanced for
+    the rank's own shard; ``gather_moments`` assembles the full moments (for
+    checkpoints, in the torch AdamW layout).
+    """
+
+    PH_READY, PH_NORM, PH_GATHERED = 0, 1, 2
+
+    @staticmethod
+    def make_heap(numels):
+        """Symmetric heap holding the flat buffers of the given sizes plus the
+        step's flags; returns (heap, alloc_0, alloc_1, ...)."""
+        from .symm import SymmetricHeap, heap_layout
+        sizes = [4 * 8 * 4, 8 * 4]                      # flags [4 phases][8 ranks], norm partials [8]
+        for n in numels:
+            sizes += [n * 4, n * 4, n * 2]              # master, grad, shadow
+        offs = heap_layout(sizes)
+        heap = SymmetricHeap(offs[-1])
+        heap.dp_offs = offs
+        allocs = []
+        for i, n in enumerate(numels):
+            base = 2 + 3 * i
+            table = {"master": (offs[base], torch.float32), "grad": (offs[base + 1], torch.float32),
+                     "shadow": (offs[base + 2], torch.bfloat16)}
+
+            def alloc(name, numel, dtype, table=table, n=n):
+                off, dt = table[name]
+                assert numel == n and dtype == dt
+                return heap.tensor(off, (numel,), dtype)
+            allocs.append(alloc)
+        return (heap, *allocs)
+
+    def __init__(self, engine, heap, group=None):
+        import os
+        from ops._ext import native
+        self.heap = heap
+        self.C = native()
+        self.offs = [heap.dp_offs[0], heap.dp_offs[1]]
+        self.budget_ns = int(float(os.environ.get("DSV3_DP_TIMEOUT_S", "60")) * 1e9)
+        super().__init__(engine, group=group)
+        self.shards = [_shard(f.numel, self.rank, self.world_size) for f in engine.flats]
+        self.flat_offs = [(heap.dp_offs[2 + 3 * i], heap.dp_offs[3 + 3 * i], heap.dp_offs[4 + 3 * i])
+                          for i in range(len(engine.flats))]
+        dev = engine.flats[0].master.device
+        self.expect = torch.zeros(4 * 8, dtype=torch.int32, device=dev)
+        self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def _args(self):
+        return self.heap.peers, self.offs, self.rank, self.budget_ns
+
+    def reduce_gradients(self) -> None:
+        """Plain all-reduce of the full gradients (diagnostics and tests; the
+        training step uses ``step``)."""
+        super().reduce_gradients()
+
+    def step(self, optimizer, max_norm: float) -> None:
+        C = self.C
+        peers, offs, me, budget = self._args()
+        C.dp_barrier(peers, offs, me, budget, self.PH_READY, self.expect)
+        self.sq.zero_()
+        for (lo, hi), (_, off_g, _) in zip(self.shards, self.flat_offs):
+            C.dp_reduce(peers, offs, me, budget, off_g, lo, hi, 1.0 / self.world_size, self.sq)
+        C.dp_norm(peers, offs, me, budget, self.sq, self.expect, float(max_norm), optimizer.grad_norm, optimizer.clip)
+        optimizer.step_count += 1
+        for gi, group in enumerate(optimizer.param_groups):
+            f = optimizer.flats[gi]
+            lo, hi = self.shards[gi]
+            off_m, off_g, off_s = self.flat_offs[gi]
+            b1, b2 = group["betas"]
+            n_decay = f.numel if group["weight_decay"] > 0 else 0
+            C.dp_update(peers, offs, me, budget, off_m, off_g, off_s, optimizer.exp_avg[gi], optimizer.exp_avg_sq[gi],
+                        lo, hi, n_decay, float(group["lr"]), float(b1), float(b2), float(group["eps"]),
+                        float(group["weight_decay"]), optimizer.step_count, optimizer.clip)
+            for p in group["params"]:
+                optimizer.state[p]["step"].fill_(float(optimizer.step_count))
+        C.dp_barrier(peers, offs, me, budget, self.PH_GATHERED, self.expect)
+
+    def gather_moments(self, optimizer) -> None:
+        """Every rank's moment shards -> full moments on every rank (collective)."""
+        for gi, f in enumerate(optimizer.flats):
+            for buf in (optimizer.exp_avg[gi], optimizer.exp_avg_sq[gi]):
+                for r in range(self.world_size):
+                    lo, hi = _shard(f.numel, r, self.world_size)
+                    if hi > lo:
+                        dist.broadcast(buf[lo:hi], src=r, group=self.group)

@@ -15,7 +15,7 @@ os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
 os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 1)))
 
 SOURCES = ["csrc/bindings.cpp", "csrc/status.cu", "csrc/gemm.cu", "csrc/elementwise.cu", "csrc/moe.cu",
-           "csrc/attention.cu", "csrc/optim.cu", "csrc/comm.cu", "csrc/ep.cu",
+           "csrc/attention.cu", "csrc/optim.cu", "csrc/comm.cu", "csrc/ep.cu", "csrc/dp.cu",
            "csrc/latent_decode_noalloc.cu"]
 
 NVCC = ["-O3", "-lineinfo", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a",
