@@ -40,6 +40,20 @@ __device__ __forceinline__ void record_error(unsigned int* status, unsigned int 
   if (status) atomicCAS(status, 0u, code);
 }
 
+// Debug build (-DDSV3_CHECKS=1, setup.py honours DSV3_CHECKS=1 in the
+// environment): index checks in the routing / gather / scatter kernels.  A
+// failed check records DSV3_ERR_BOUNDS and makes the thread skip the access
+// (`action`, e.g. `return` or `continue`); release builds compile it away.
+#if defined(DSV3_CHECKS) && DSV3_CHECKS
+#define DSV3_CHECK(cond, status, action)          \
+  if (!(cond)) {                                  \
+    record_error((status), DSV3_ERR_BOUNDS);      \
+    action;                                       \
+  }
+#else
+#define DSV3_CHECK(cond, status, action)
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

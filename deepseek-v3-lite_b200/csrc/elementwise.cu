@@ -8,6 +8,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace dsv3 {
 
@@ -201,18 +202,31 @@ __global__ void mla_unpack_kernel(const float* __restrict__ dQ, const float* __r
 }
 
 // ---------------------------------------------------------------- embedding
+// Token ids come from user data: an id outside [0, V) is reported through the
+// status word (DSV3_ERR_BOUNDS) and its row is zero / skipped, never read.
 __global__ void embedding_fwd_kernel(const long* __restrict__ tok, const float* __restrict__ w,
-                                     float* __restrict__ out, int T, int D) {
+                                     float* __restrict__ out, int T, int D, long V, unsigned int* status) {
   const int row = blockIdx.x;
-  const float4* src = reinterpret_cast<const float4*>(w + (size_t)tok[row] * D);
+  const long id = tok[row];
   float4* dst = reinterpret_cast<float4*>(out + (size_t)row * D);
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) record_error(status, DSV3_ERR_BOUNDS);
+    for (int c = threadIdx.x; c < D / 4; c += blockDim.x) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(w + (size_t)id * D);
   for (int c = threadIdx.x; c < D / 4; c += blockDim.x) dst[c] = src[c];
 }
 
 __global__ void embedding_bwd_kernel(const long* __restrict__ tok, const float* __restrict__ g,
-                                     float* __restrict__ dw, int T, int D) {
+                                     float* __restrict__ dw, int T, int D, long V, unsigned int* status) {
   const int row = blockIdx.x;
-  float* dst = dw + (size_t)tok[row] * D;
+  const long id = tok[row];
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) record_error(status, DSV3_ERR_BOUNDS);
+    return;
+  }
+  float* dst = dw + (size_t)id * D;
   const float* src = g + (size_t)row * D;
   for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(dst + c, src[c]);
 }
@@ -678,7 +692,7 @@ void embedding_fwd(const at::Tensor& tok, const at::Tensor& w, at::Tensor& out) 
   TORCH_CHECK(tok.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "embedding_fwd: contiguous tensors");
   const at::cuda::CUDAGuard guard(w.device());
   embedding_fwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
-      w.data_ptr<float>(), out.data_ptr<float>(), T, D);
+      w.data_ptr<float>(), out.data_ptr<float>(), T, D, w.size(0), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -687,7 +701,7 @@ void embedding_bwd(const at::Tensor& tok, const at::Tensor& g, at::Tensor& dw) {
   TORCH_CHECK(tok.is_contiguous() && g.is_contiguous() && dw.is_contiguous(), "embedding_bwd: contiguous tensors");
   const at::cuda::CUDAGuard guard(dw.device());
   embedding_bwd_kernel<<<T, 128, 0, at::cuda::getCurrentCUDAStream()>>>(tok.data_ptr<int64_t>(),
-      g.data_ptr<float>(), dw.data_ptr<float>(), T, D);
+      g.data_ptr<float>(), dw.data_ptr<float>(), T, D, dw.size(0), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -16,6 +16,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace dsv3 {
 
@@ -129,18 +130,22 @@ __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* 
 }
 
 __global__ void permute_scatter_kernel(const int* __restrict__ idx, int n_assign, const int* __restrict__ row_off,
-                                       int* __restrict__ cursor, int* __restrict__ src, int* __restrict__ dst) {
+                                       int* __restrict__ cursor, int* __restrict__ src, int* __restrict__ dst,
+                                       int E, int P, unsigned int* status) {
   const int a = blockIdx.x * blockDim.x + threadIdx.x;
   if (a >= n_assign) return;
   const int e = idx[a];
+  DSV3_CHECK(e >= 0 && e < E, status, return)
   const int pos = row_off[e] + atomicAdd(&cursor[e], 1);
+  DSV3_CHECK(pos < P, status, return)
   src[pos] = a;
   dst[a] = pos;
 }
 
 // One warp per sorted row: copy token row (a / k) of x, or zeros for padding.
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, long ldx, const int* __restrict__ src,
-                                   int P, int k, int D, __nv_bfloat16* __restrict__ out, long ldo) {
+                                   int P, int k, int D, __nv_bfloat16* __restrict__ out, long ldo, int T,
+                                   unsigned int* status) {
   const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (p >= P) return;
@@ -150,6 +155,7 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, long ldx
     for (int c = lane; c < D / 8; c += 32) o[c] = make_uint4(0, 0, 0, 0);
     return;
   }
+  DSV3_CHECK(a / k < T, status, return)
   const uint4* s = reinterpret_cast<const uint4*>(x + (size_t)(a / k) * ldx);
   for (int c = lane; c < D / 8; c += 32) o[c] = s[c];
 }
@@ -157,7 +163,7 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, long ldx
 // out[t] (fp32) += sum_j w[t,j] * y[dst[t,j]]
 __global__ void combine_fwd_kernel(const __nv_bfloat16* __restrict__ y, long ldy, const int* __restrict__ dst,
                                    const float* __restrict__ w, int T, int k, int D, float* __restrict__ out,
-                                   long ldo) {
+                                   long ldo, int P, unsigned int* status) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -168,6 +174,7 @@ __global__ void combine_fwd_kernel(const __nv_bfloat16* __restrict__ y, long ldy
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int j = 0; j < k; ++j) {
       const int row = dst[(size_t)t * k + j];
+      DSV3_CHECK(row >= 0 && row < P, status, continue)
       const float wj = w[(size_t)t * k + j];
       const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)row * ldy + c);
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&v);
@@ -222,7 +229,8 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ dout, long 
 
 // dx[t] (fp32) += sum_j dxs[dst[t,j]]
 __global__ void unpermute_bwd_kernel(const __nv_bfloat16* __restrict__ dxs, long ldx, const int* __restrict__ dst,
-                                     int T, int k, int D, float* __restrict__ out, long ldo) {
+                                     int T, int k, int D, float* __restrict__ out, long ldo, int P,
+                                     unsigned int* status) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -233,6 +241,7 @@ __global__ void unpermute_bwd_kernel(const __nv_bfloat16* __restrict__ dxs, long
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int j = 0; j < k; ++j) {
       const int row = dst[(size_t)t * k + j];
+      DSV3_CHECK(row >= 0 && row < P, status, continue)
       const uint4 v = *reinterpret_cast<const uint4*>(dxs + (size_t)row * ldx + c);
       const uint16_t* h = reinterpret_cast<const uint16_t*>(&v);
 #pragma unroll
@@ -305,7 +314,8 @@ void permute_scatter(const at::Tensor& idx, const at::Tensor& row_off, at::Tenso
   const int n = idx.numel();
   const at::cuda::CUDAGuard guard(idx.device());
   permute_scatter_kernel<<<nblk(n, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(idx.data_ptr<int>(), n,
-      row_off.data_ptr<int>(), cursor.data_ptr<int>(), src.data_ptr<int>(), dst.data_ptr<int>());
+      row_off.data_ptr<int>(), cursor.data_ptr<int>(), src.data_ptr<int>(), dst.data_ptr<int>(),
+      (int)cursor.numel(), (int)src.numel(), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -314,7 +324,7 @@ void gather_rows(const at::Tensor& x, const at::Tensor& src, int64_t k, at::Tens
   TORCH_CHECK(D % 8 == 0 && x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "gather_rows: 16-byte rows");
   const at::cuda::CUDAGuard guard(x.device());
   gather_rows_kernel<<<nblk(P, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(x), x.stride(0),
-      src.data_ptr<int>(), P, k, D, bf(out), out.stride(0));
+      src.data_ptr<int>(), P, k, D, bf(out), out.stride(0), (int)x.size(0), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -323,7 +333,8 @@ void combine_fwd(const at::Tensor& y, const at::Tensor& dst, const at::Tensor& w
   TORCH_CHECK(D % 8 == 0 && out.scalar_type() == at::kFloat, "combine_fwd: D % 8, fp32 out");
   const at::cuda::CUDAGuard guard(y.device());
   combine_fwd_kernel<<<nblk(T, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(y), y.stride(0),
-      dst.data_ptr<int>(), w.data_ptr<float>(), T, k, D, out.data_ptr<float>(), out.stride(0));
+      dst.data_ptr<int>(), w.data_ptr<float>(), T, k, D, out.data_ptr<float>(), out.stride(0), (int)y.size(0),
+      status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -340,7 +351,7 @@ void unpermute_bwd(const at::Tensor& dxs, const at::Tensor& dst, at::Tensor& out
   const int T = dst.size(0), k = dst.size(1), D = dxs.size(1);
   const at::cuda::CUDAGuard guard(dxs.device());
   unpermute_bwd_kernel<<<nblk(T, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(dxs), dxs.stride(0),
-      dst.data_ptr<int>(), T, k, D, out.data_ptr<float>(), out.stride(0));
+      dst.data_ptr<int>(), T, k, D, out.data_ptr<float>(), out.stride(0), (int)dxs.size(0), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -114,6 +114,8 @@ class TrainEngine:
         self._graphs: Dict[tuple, tuple] = {}
         # Capture the micro-step in a CUDA graph (DSV3_CUDA_GRAPH=0 turns it off).
         self.use_graphs = os.environ.get("DSV3_CUDA_GRAPH", "1") == "1"
+        # NVTX ranges per layer / phase for timeline tools (DSV3_NVTX=1)
+        self.nvtx = os.environ.get("DSV3_NVTX", "0") == "1"
 
     # ---------------------------------------------------------------- layout
     def _build_flat(self, groups) -> None:
@@ -546,6 +548,14 @@ class TrainEngine:
         self._last_losses = res["loss"]
         return res
 
+    def _range(self, name: Optional[str]) -> None:
+        """Open (name) or close (None) an NVTX range when DSV3_NVTX=1."""
+        if self.nvtx:
+            if name is None:
+                torch.cuda.nvtx.range_pop()
+            else:
+                torch.cuda.nvtx.range_push(name)
+
     def _seg_tensors(self, seg, segw):
         key = (tuple(seg), tuple(segw))
         got = self._segcache.get(key)
@@ -564,7 +574,8 @@ class TrainEngine:
         x = torch.empty(T, D, dtype=F32, device=self.device)
         C.embedding_fwd(tok, self.f32(m.embed.weight), x)
         saved = []
-        for layer in m.layers:
+        for li, layer in enumerate(m.layers):
+            self._range(f"fwd layer {li}")
             xn1, r1 = self._norm(x, layer.attn_norm.weight)
             actx = self._mla_fwd(layer.attn, xn1, B, S)
             x_mid = torch.empty_like(x)
@@ -577,6 +588,7 @@ class TrainEngine:
                 fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next, x_mid)
             saved.append((x, r1, actx, x_mid, xn2, r2, fctx))
             x = x_next
+            self._range(None)
         hL = x
         xf, rf = self._norm(hL, m.norm.weight)
 
@@ -656,7 +668,8 @@ class TrainEngine:
                     carry, carry_rows = dprev, ctx.Sm
         dres_b = torch.empty(T, D, dtype=BF16, device=self.device)
         C.rmsnorm_bwd(dall[:T], hL, self.f32(m.norm.weight), rf, dres, None, dres_b, self.g(m.norm.weight))
-        for layer, (x_in, r1, actx, x_mid, xn2, r2, fctx) in zip(reversed(m.layers), reversed(saved)):
+        for li, (layer, (x_in, r1, actx, x_mid, xn2, r2, fctx)) in enumerate(zip(reversed(m.layers), reversed(saved))):
+            self._range(f"bwd layer {len(saved) - 1 - li}")
             dxn2 = torch.empty(T, D, dtype=F32, device=self.device)
             if hasattr(layer.ffn, "experts"):
                 self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)
@@ -669,6 +682,7 @@ class TrainEngine:
             self._mla_bwd(layer.attn, actx, dres_b, dxn1, B, S)
             C.rmsnorm_bwd(dxn1, x_in, self.f32(layer.attn_norm.weight), r1, dres, None, dres_b,
                           self.g(layer.attn_norm.weight))
+            self._range(None)
         C.embedding_bwd(tok, dres, self.g(m.embed.weight))
 
         balance = torch.zeros((), device=self.device)

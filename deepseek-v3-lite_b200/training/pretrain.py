@@ -31,7 +31,7 @@ import os
 import sys
 from dataclasses import asdict, dataclass, field
 from pathlib import Path
-from typing import Dict, Optional, Tuple
+from typing import List, Dict, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -270,6 +270,40 @@ class Pretrainer:
             else:
                 moe.update_gate_bias(speed=self.config.bias_update_speed)
 
+    def expert_load_histograms(self) -> Dict[int, List[int]]:
+        """Routed rows per expert of each MoE layer in the last micro-batch
+        (this rank's tokens; a by-product of the router kernel)."""
+        out = {}
+        for i, layer in enumerate(self.raw_model.layers):
+            ffn = layer.ffn
+            if hasattr(ffn, "expert_counts") and ffn.expert_counts() is not None:
+                out[i] = [int(c) for c in ffn.expert_counts().tolist()]
+        return out
+
+    def step_diagnostics(self) -> Dict[str, float]:
+        """Logged next to the loss: global gradient norm, worst per-layer
+        expert load (max / mean routed rows) and, under expert parallelism,
+        the bytes of token rows this rank sent to other ranks per MoE layer
+        and direction in the last micro-batch."""
+        d: Dict[str, float] = {}
+        eng = self.engine
+        if eng is not None:
+            d["grad_norm"] = float(eng.optimizer.grad_norm)
+        worst = 0.0
+        for counts in self.expert_load_histograms().values():
+            mean = sum(counts) / max(1, len(counts))
+            if mean > 0:
+                worst = max(worst, max(counts) / mean)
+        if worst:
+            d["expert_load_max_over_mean"] = worst
+        if eng is not None and getattr(eng, "ep", None) is not None:
+            ep = eng.ep
+            counts = next(iter(self.expert_load_histograms().values()), None)
+            if counts is not None:
+                remote = sum(counts) - sum(counts[ep.lo:ep.hi])
+                d["ep_bytes_sent_per_layer"] = float(remote * ep.D * 2)
+        return d
+
     def _moe_balance_metric(self) -> torch.Tensor:
         """Sum of per-layer balance metrics (device tensor; read lazily)."""
         vals = [moe.get_load_balance_loss() for moe in self.raw_model.moe_layers()]
@@ -462,6 +496,7 @@ class Pretrainer:
                     extras = {"balance_loss": float(metrics["balance_loss"])}
                     if metrics.get("mtp_loss") is not None:
                         extras["mtp_loss"] = float(metrics["mtp_loss"])
+                    extras.update(self.step_diagnostics())
                     self.logger.log(step, float(metrics["loss"]), lr=self.scheduler.get_last_lr()[0], metrics=extras)
                 if step % self.config.save_every == 0 and step > 0:
                     self.save_checkpoint(step)

@@ -241,6 +241,26 @@ def test_embedding(C):
     close(dw, ref, rtol=1e-5, atol=1e-5)
 
 
+def test_embedding_rejects_out_of_range_ids(C):
+    """An id outside [0, V) is never dereferenced: its row reads as zeros, its
+    gradient is dropped and the status word reports a bounds error."""
+    V, D = 100, 64
+    w = torch.randn(V, D, device="cuda")
+    tok = torch.tensor([3, V, -1, 7], device="cuda")
+    out = torch.full((4, D), 9.0, device="cuda")
+    C.status_reset()
+    C.embedding_fwd(tok, w, out)
+    assert C.status_read() == 5
+    assert torch.equal(out[0], w[3]) and torch.equal(out[3], w[7])
+    assert out[1].abs().sum().item() == 0 and out[2].abs().sum().item() == 0
+    C.status_reset()
+    dw = torch.zeros(V, D, device="cuda")
+    C.embedding_bwd(tok, torch.ones(4, D, device="cuda"), dw)
+    assert C.status_read() == 5
+    assert dw.sum().item() == 2 * D
+    C.status_reset()
+
+
 def test_ce_finalize(C):
     T, V = 300, 1000
     x = torch.randn(T, 256, device="cuda").bfloat16()

@@ -160,3 +160,14 @@ def test_yaml_mapping(small_cfg, tmp_dir):
     assert (c.batch_size, c.max_steps, c.max_grad_norm, c.mtp_weight, c.log_every, c.save_every) == (3, 9, 0.5, 0.3, 7, 11)
     assert c.data_path == "/d" and c.max_seq_len == small_cfg["max_seq_len"]
     assert config_from_yaml(y, no_checkpoint=True).grad_checkpoint is False
+
+
+def test_step_diagnostics_report_expert_load(small_cfg, tmp_dir):
+    tr = Pretrainer(_cfg(small_cfg, tmp_dir / "ck"))
+    tok = torch.randint(0, small_cfg["vocab_size"], (2, 33))
+    tr.train_step(tok[:, :-1], tok[:, 1:], 0)
+    hist = tr.expert_load_histograms()
+    assert hist and all(len(c) == small_cfg["n_routed_experts"] for c in hist.values())
+    assert all(sum(c) == 2 * 32 * small_cfg["n_activated_experts"] for c in hist.values())
+    d = tr.step_diagnostics()
+    assert d["expert_load_max_over_mean"] >= 1.0
