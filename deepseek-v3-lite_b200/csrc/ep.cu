@@ -9,7 +9,7 @@
 //                  stores + a signal, waits for every rank's counts and
 //                  derives, identically on every rank, the receive layout:
 //                  on rank d, local expert l owns rows [row_off[l],
-//                  row_off[l+1]) (128-row padded), inside which source s
+//                  row_off[l+1]) (256-row padded), inside which source s
 //                  writes its rows from  send_base[e] = row_off[l] +
 //                  sum_{s'<s} count[s'][e];  plus the tile -> expert map of the
 //                  grouped GEMMs.
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpArgs a, const int* __re
         s_off[e - e0] = min(seg, a.cap);
         recv_cnt[e - e0] = tot;
       }
-      seg += (tot + 127) / 128 * 128;
+      seg += (tot + 255) / 256 * 256;   // 256-row ranges: the grouped GEMMs may pair CTAs
     }
     if (d == a.me) {
       s_off[e1 - e0] = min(seg, a.cap);
@@ -249,8 +249,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpArgs a, const __nv_b
   __nv_bfloat16* xs = at_rank<__nv_bfloat16>(a, a.me, a.off_xs);
   int* origin = at_rank<int>(a, a.me, a.off_origin);
   float* wrow = at_rank<float>(a, a.me, a.off_w);
-  for (int p = warp; p < Eloc * 128; p += nwarps) {
-    const int l = p >> 7, j = p & 127;
+  for (int p = warp; p < Eloc * 256; p += nwarps) {
+    const int l = p >> 8, j = p & 255;
     const int r = row_off[l] + recv_cnt[l] + j;
     if (r < row_off[l + 1]) {
       uint4* o = reinterpret_cast<uint4*>(xs + (size_t)r * a.D);
@@ -386,7 +386,7 @@ EpArgs make_args(const std::vector<int64_t>& peers, const std::vector<int64_t>& 
   a.budget_ns = (unsigned long long)dims[7];
   TORCH_CHECK(a.me >= 0 && a.me < R, "ep: rank out of range");
   TORCH_CHECK(a.E >= R && a.E <= kMaxExperts, "ep: R <= E <= 256");
-  TORCH_CHECK(a.D % 8 == 0 && a.cap % 128 == 0, "ep: D % 8 == 0, capacity a multiple of 128");
+  TORCH_CHECK(a.D % 8 == 0 && a.cap % 256 == 0, "ep: D % 8 == 0, capacity a multiple of 256");
   TORCH_CHECK((long long)R * a.T * a.k < (1ll << 31), "ep: R*T*k must fit int32");
   return a;
 }

@@ -118,8 +118,10 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
 
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
-  if constexpr (BN == 256 && S != Sched::GroupedM) {
-    if (use_pairs() && a.m_tiles > 0 && a.M >= 256) {
+  if constexpr (BN == 256) {
+    // row-grouped tiles may pair only when every expert range is 256-aligned
+    const bool grouping_ok = S != Sched::GroupedM || a.tile_rows == 256;
+    if (use_pairs() && grouping_ok && a.m_tiles > 0 && a.M >= 256) {
       GemmArgs b = a;                      // re-tile the rows in 256-row pair tiles
       b.m_tiles = cdiv(a.M, 256);
       b.num_tiles = a.num_tiles / a.m_tiles * b.m_tiles;
@@ -135,6 +137,7 @@ GemmArgs blank_args() {
   memset(&a, 0, sizeof(a));
   a.k_splits = 1;
   a.groups = 1;
+  a.tile_rows = 128;
   return a;
 }
 
@@ -236,7 +239,7 @@ void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw) {
 // SwiGLU up-projection: x[P,D] against w13 [G,2,I,D] (dense when G == 1 and
 // tile_group is empty).  Writes h = silu(g) * u [P, I] and gu = [g | u] [P, 2I].
 void swiglu_fwd(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& tile_group, at::Tensor& h,
-                at::Tensor& gu) {
+                at::Tensor& gu, int64_t group_rows) {
   check_bf16_rows(x, "x");
   TORCH_CHECK(w13.scalar_type() == at::kBFloat16 && w13.is_contiguous() && w13.dim() == 4 && w13.size(1) == 2,
               "w13 must be contiguous bf16 [G, 2, I, D]");
@@ -258,6 +261,7 @@ void swiglu_fwd(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& ti
   if (tile_group.numel() > 0) {
     TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.numel() >= g.m_tiles, "tile_group: int32 [tiles]");
     g.tile_group = tile_group.data_ptr<int>();
+    g.tile_rows = (int)group_rows;
     launch<256, 0, 0, Sched::GroupedM, Epi::SwigluFwd, true>(ta, tb, g);
   } else {
     TORCH_CHECK(G == 1, "dense SwiGLU expects one weight group");
@@ -268,7 +272,7 @@ void swiglu_fwd(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& ti
 // SwiGLU backward through the down projection: dh = dy[P,D] @ w2[G](D x I),
 // then dgu = [dh * u * silu'(g) | dh * silu(g)] using the saved pre-activations.
 void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& tile_group, const at::Tensor& gu,
-                  at::Tensor& dgu) {
+                  at::Tensor& dgu, int64_t group_rows) {
   check_bf16_rows(dy, "dy");
   check_bf16_rows(gu, "gu");
   check_bf16_rows(dgu, "dgu");
@@ -286,6 +290,7 @@ void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& 
   CUtensorMap tb = map_b_mnmajor(w2, G, D, I, I, D * I);
   if (tile_group.numel() > 0) {
     g.tile_group = tile_group.data_ptr<int>();
+    g.tile_rows = (int)group_rows;
     launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
   } else {
     launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
@@ -293,7 +298,8 @@ void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& 
 }
 
 // Grouped forward: out[P,N] = a[P,K] @ w[g(tile)] ^T, w: [G, N, K].
-void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out) {
+void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out,
+                 int64_t group_rows) {
   check_bf16_rows(a, "a");
   check_bf16_rows(out, "out");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
@@ -304,6 +310,7 @@ void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& til
   g.M = P; g.N = N; g.K = K;
   g.out = out.data_ptr(); g.ldo = out.stride(0);
   g.tile_group = tile_group.data_ptr<int>();
+  g.tile_rows = (int)group_rows;
   g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(a, P, K, a.stride(0));
@@ -312,7 +319,8 @@ void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& til
 }
 
 // Grouped data gradient: out[P,K] = dy[P,N] @ w[g(tile)], w: [G, N, K].
-void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out) {
+void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out,
+                   int64_t group_rows) {
   check_bf16_rows(dy, "dy");
   check_bf16_rows(out, "out");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
@@ -323,6 +331,7 @@ void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& 
   g.M = P; g.N = K; g.K = N;
   g.out = out.data_ptr(); g.ldo = out.stride(0);
   g.tile_group = tile_group.data_ptr<int>();
+  g.tile_rows = (int)group_rows;
   g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(K, 256); g.kb_per_split = cdiv(N, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(dy, P, N, dy.stride(0));
@@ -427,10 +436,18 @@ void register_gemm(pybind11::module_& m) {
   m.def("linear_dgrad", &linear_dgrad, "out = dy @ w (bf16 store; fp32 accumulate or store)", pybind11::arg("dy"),
         pybind11::arg("w"), pybind11::arg("out"), pybind11::arg("accumulate") = true);
   m.def("linear_wgrad", &linear_wgrad, "dw (fp32) += dy^T @ x");
-  m.def("swiglu_fwd", &swiglu_fwd, "h, gu from x @ [w1|w3]^T (dense or expert-grouped)");
-  m.def("swiglu_dgrad", &swiglu_dgrad, "dgu from (dy @ w2) and the saved gate/up");
-  m.def("grouped_fwd", &grouped_fwd, "expert-grouped out = a @ w[e]^T");
-  m.def("grouped_dgrad", &grouped_dgrad, "expert-grouped out = dy @ w[e]");
+  // group_rows: the expert row ranges behind tile_group are multiples of this
+  // (256 lets the grouped GEMMs run on CTA pairs)
+  m.def("swiglu_fwd", &swiglu_fwd, "h, gu from x @ [w1|w3]^T (dense or expert-grouped)", pybind11::arg("x"),
+        pybind11::arg("w13"), pybind11::arg("tile_group"), pybind11::arg("h"), pybind11::arg("gu"),
+        pybind11::arg("group_rows") = 128);
+  m.def("swiglu_dgrad", &swiglu_dgrad, "dgu from (dy @ w2) and the saved gate/up", pybind11::arg("dy"),
+        pybind11::arg("w2"), pybind11::arg("tile_group"), pybind11::arg("gu"), pybind11::arg("dgu"),
+        pybind11::arg("group_rows") = 128);
+  m.def("grouped_fwd", &grouped_fwd, "expert-grouped out = a @ w[e]^T", pybind11::arg("a"), pybind11::arg("w"),
+        pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
+  m.def("grouped_dgrad", &grouped_dgrad, "expert-grouped out = dy @ w[e]", pybind11::arg("dy"), pybind11::arg("w"),
+        pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
   m.def("grouped_wgrad", &grouped_wgrad, "per-expert dw[e] (fp32) += a_e^T @ b_e");
   m.def("ce_fwd_partials", &ce_fwd_partials, "fused LM head + log-sum-exp partials");
   m.def("ce_bwd_logits", &ce_bwd_logits, "fused LM head + softmax-minus-onehot gradient");

@@ -51,6 +51,7 @@ struct GemmArgs {
   int num_tiles;
   int kb_per_split;      // Dense: K-blocks per split
   const int* tile_group;     // GroupedM: expert of each 128-row tile (< 0: unused tile)
+  int tile_rows;             // GroupedM: expert ranges are multiples of this (128 or 256; 256 allows CTA pairs)
   const int* group_row_off;  // GroupedK: [groups + 1] padded row offsets (multiples of 128)
   void* out;             // primary output
   long ldo;
@@ -107,7 +108,7 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
     ti.kb0 = outer * a.kb_per_split;
     ti.kb1 = min(total, ti.kb0 + a.kb_per_split);
   } else if constexpr (S == Sched::GroupedM) {
-    ti.g = a.tile_group[m];
+    ti.g = a.tile_group[m * (BM_ / 128)];   // a pair tile's two halves belong to one expert
     ti.kb0 = 0;
     ti.kb1 = (a.K + 63) / 64;
     ti.run = ti.g >= 0;
@@ -134,7 +135,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using C = GemmCfg<BN, CG>;
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
-  static_assert(CG == 1 || (CG == 2 && BN == 256 && S != Sched::GroupedM), "CTA pairs: BN=256, no row-grouped schedule");
+  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs: BN=256");
   constexpr int BMT = 128 * CG;                   // rows of one (pair) tile
   const uint32_t cta = CG == 2 ? cluster_ctarank() : 0u;
   const bool leader = cta == 0;

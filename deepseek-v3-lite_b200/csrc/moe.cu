@@ -1,7 +1,7 @@
 // DeepSeekMoE routing and token movement on one GPU:
 //   router_topk     sigmoid scores, bias-shifted top-k, normalised weights and
 //                   per-expert counts (one warp per token, fp32 throughout);
-//   permute_plan    per-expert row ranges padded to 128 rows (one GEMM tile),
+//   permute_plan    per-expert row ranges padded to 256 rows (one CTA-pair GEMM tile),
 //                   the tile -> expert map used by the grouped GEMMs;
 //   permute_scatter destination row of every (token, slot) assignment;
 //   gather_rows     expert-sorted copy of the activations (zero padding rows);
@@ -23,6 +23,7 @@ namespace dsv3 {
 namespace {
 
 constexpr int kMaxExpertsPerLane = 8;  // E <= 256
+constexpr int kGroupRows = 256;        // expert row ranges: multiples of one CTA-pair GEMM tile
 
 __global__ void router_topk_kernel(const float* __restrict__ logits, long ldl, const float* __restrict__ bias, int T,
                                    int E, int k, float route_scale, int* __restrict__ idx, float* __restrict__ w,
@@ -95,7 +96,7 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, long ldl, c
   }
 }
 
-// Single block.  row_off[e] = sum_{e'<e} pad128(counts[e']); tile_group[i] =
+// Single block.  row_off[e] = sum_{e'<e} pad256(counts[e']); tile_group[i] =
 // expert owning 128-row tile i (or -1); cursor zeroed; src[0..P) = -1.
 __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* __restrict__ row_off,
                                     int* __restrict__ tile_group, int max_tiles, int* __restrict__ cursor,
@@ -105,7 +106,7 @@ __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* 
     int acc = 0;
     for (int e = 0; e < E; ++e) {
       off_s[e] = acc;
-      acc += (counts[e] + 127) / 128 * 128;
+      acc += (counts[e] + kGroupRows - 1) / kGroupRows * kGroupRows;
     }
     off_s[E] = acc;
   }

@@ -380,7 +380,7 @@ class TrainEngine:
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
         idx, wts, ssel, counts, Ep = self._router(moe, xn)
-        P = _pad(T * k + E * 127, 128)
+        P = _pad(T * k + E * 255, 256)       # expert ranges are 256-row aligned (CTA-pair tiles)
         row_off = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         tile_group = torch.empty(P // 128, dtype=torch.int32, device=self.device)
         cursor = torch.empty(E, dtype=torch.int32, device=self.device)
@@ -393,9 +393,9 @@ class TrainEngine:
         w1 = moe.experts[0].w1.weight
         h = torch.empty(P, I, dtype=BF16, device=self.device)
         gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
-        C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu)
+        C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu, group_rows=256)
         ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys)
+        C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys, group_rows=256)
         out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
         shared = []
         for i, e in enumerate(moe.shared_experts):
@@ -421,10 +421,10 @@ class TrainEngine:
         w1 = moe.experts[0].w1.weight
         w2 = moe.experts[0].w2.weight
         dgu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
-        C.swiglu_dgrad(dys, self.stacked(w2, E), ctx.tile_group, ctx.gu, dgu)
+        C.swiglu_dgrad(dys, self.stacked(w2, E), ctx.tile_group, ctx.gu, dgu, group_rows=256)
         C.grouped_wgrad(dys, ctx.h, ctx.row_off, self.stacked(w2, E, grad=True))
         dxs = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs)
+        C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs, group_rows=256)
         C.grouped_wgrad(dgu, ctx.xs, ctx.row_off, self.swiglu_g13(w1, E))
         C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)

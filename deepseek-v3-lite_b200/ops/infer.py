@@ -150,7 +150,7 @@ class InferenceEngine:
         ssel = torch.empty(T, k, dtype=F32, device=self.device)
         counts = torch.zeros(E, dtype=torch.int32, device=self.device)
         C.router_topk(logits, moe.gate.bias, E, k, float(moe.gate.route_scale), idx, wts, ssel, counts)
-        P = _pad(T * k + E * 127, 128)
+        P = _pad(T * k + E * 255, 256)       # 256-row expert ranges (CTA-pair GEMM tiles)
         row_off = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         tg = torch.empty(P // 128, dtype=torch.int32, device=self.device)
         cursor = torch.empty(E, dtype=torch.int32, device=self.device)
@@ -163,9 +163,9 @@ class InferenceEngine:
         w13, w2 = self._experts(moe)
         h = torch.empty(P, I, dtype=BF16, device=self.device)
         gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
-        C.swiglu_fwd(xs, w13, tg, h, gu)
+        C.swiglu_fwd(xs, w13, tg, h, gu, group_rows=256)
         ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.grouped_fwd(h, w2, tg, ys)
+        C.grouped_fwd(h, w2, tg, ys, group_rows=256)
         C.combine_fwd(ys, dst, wts, out)
         for e in moe.shared_experts:
             self._dense_ffn(e.w1.weight, e.w3.weight, e.w2.weight, xn, out)

@@ -37,14 +37,14 @@ def case_gemm_dense():
 def case_swiglu_dgrad():
     C = native()
     E, D, I = 20, 768, 384
-    rows = [16384 * 4 // E // 128 * 128] * E
+    rows = [16384 * 4 // E // 256 * 256] * E
     tiles = [e for e, r in enumerate(rows) for _ in range(r // 128)]
     P = sum(rows)
     tg = torch.tensor(tiles, dtype=torch.int32, device="cuda")
     dy, w2, gu = _bf(P, D), _bf(E, D, I), _bf(P, 2 * I)
     dgu = torch.empty_like(gu)
     for _ in range(2):
-        C.swiglu_dgrad(dy, w2, tg, gu, dgu)
+        C.swiglu_dgrad(dy, w2, tg, gu, dgu, group_rows=256)
 
 
 def case_dense_dgrad_f32():

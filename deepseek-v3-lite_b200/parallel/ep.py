@@ -64,15 +64,15 @@ def receive_capacity(tokens: int, topk: int, n_experts: int, world: int, capacit
     """Rows of one rank's receive slot.
 
     Exact worst case by default: every token of every rank can send
-    ``min(k, local experts)`` rows to one rank, plus up to 127 padding rows
-    per local expert.  ``capacity_factor > 0`` caps it at that multiple of the
+    ``min(k, local experts)`` rows to one rank, plus up to 255 padding rows
+    per local expert (expert ranges are 256-row aligned).  ``capacity_factor > 0`` caps it at that multiple of the
     mean load (``tokens * k`` rows); overflowing rows are then reported as an
     error, never silently dropped.
     """
     eloc = max(hi - lo for lo, hi in (expert_range(r, n_experts, world) for r in range(world)))
     worst = world * tokens * min(topk, eloc)
     rows = worst if capacity_factor <= 0 else min(worst, int(math.ceil(capacity_factor * tokens * topk)))
-    return _pad(rows + eloc * 127, 128)
+    return _pad(rows + eloc * 255, 256)
 
 
 def plan_reference(cnt_all: torch.Tensor, rank: int, cap: int):
@@ -96,7 +96,7 @@ def plan_reference(cnt_all: torch.Tensor, rank: int, cap: int):
             if d == rank:
                 row_off[e - e0] = min(seg, cap)
                 recv_cnt[e - e0] = tot
-            seg += _pad(tot, 128)
+            seg += _pad(tot, 256)
         if d == rank:
             row_off[e1 - e0] = min(seg, cap)
     tiles = cap // 128
@@ -264,9 +264,9 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     xs = ep.recv_rows(slot)
     h = torch.empty(ep.cap, inter_dim, dtype=torch.bfloat16, device=xn.device)
     gu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=xn.device)
-    C.swiglu_fwd(xs, w13_local, plan["tile_group"], h, gu)
+    C.swiglu_fwd(xs, w13_local, plan["tile_group"], h, gu, group_rows=256)
     ys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=xn.device)
-    C.grouped_fwd(h, w2_local, plan["tile_group"], ys)
+    C.grouped_fwd(h, w2_local, plan["tile_group"], ys, group_rows=256)
     marks("experts fwd")
     ep.combine_send(slot, ys, plan["row_off"])
     side = plan.pop("side")
@@ -293,10 +293,10 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     dw_rows = torch.empty(ep.cap, dtype=torch.float32, device=dout_bf16.device)
     ep.bwd_prep(slot, ctx["ys"], ctx["row_off"], dys, dw_rows)
     dgu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=dout_bf16.device)
-    C.swiglu_dgrad(dys, w2_local, ctx["tile_group"], ctx["gu"], dgu)
+    C.swiglu_dgrad(dys, w2_local, ctx["tile_group"], ctx["gu"], dgu, group_rows=256)
     C.grouped_wgrad(dys, ctx["h"], ctx["row_off"], g2_local)
     dxs = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
-    C.grouped_dgrad(dgu, w13_local.reshape(ep.Eloc, 2 * inter_dim, ep.D), ctx["tile_group"], dxs)
+    C.grouped_dgrad(dgu, w13_local.reshape(ep.Eloc, 2 * inter_dim, ep.D), ctx["tile_group"], dxs, group_rows=256)
     C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
     marks("experts bwd")
     ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])

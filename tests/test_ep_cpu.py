@@ -27,7 +27,7 @@ def test_receive_capacity_covers_the_worst_case():
     cap = receive_capacity(T, k, E, R)
     assert cap % 128 == 0
     # 3 local experts at most; every token of every rank may send 3 rows to one rank
-    assert cap >= R * T * 3 + 3 * 127
+    assert cap >= R * T * 3 + 3 * 255
     capped = receive_capacity(T, k, E, R, capacity_factor=2.0)
     assert capped < cap and capped >= 2 * T * k
 
@@ -53,8 +53,8 @@ def test_plan_layout_is_consistent_across_ranks(R, E, k):
         _, row_off, recv_cnt, tile_group = plans[d]
         # per local expert: a 128-aligned range large enough for all sources' rows
         for l in range(hi - lo):
-            assert int(row_off[l]) % 128 == 0
-            assert int(row_off[l + 1]) - int(row_off[l]) == (int(recv_cnt[l]) + 127) // 128 * 128
+            assert int(row_off[l]) % 256 == 0
+            assert int(row_off[l + 1]) - int(row_off[l]) == (int(recv_cnt[l]) + 255) // 256 * 256
             assert int(recv_cnt[l]) == int(cnt[:, lo + l].sum())
         # the rows every source writes for expert e are disjoint and inside e's range
         for e in range(lo, hi):
@@ -78,11 +78,11 @@ def test_plan_skips_empty_experts():
     cnt = torch.tensor([[5, 0, 0, 3], [0, 0, 2, 1]], dtype=torch.int32)
     cap = receive_capacity(8, 2, 4, 2)
     send_base, row_off, recv_cnt, tg = plan_reference(cnt, 0, cap)
-    assert row_off.tolist() == [0, 128, 128]
+    assert row_off.tolist() == [0, 256, 256]
     assert recv_cnt.tolist() == [5, 0]
-    assert tg[0] == 0 and (tg[1:] == -1).all()
+    assert (tg[:2] == 0).all() and (tg[2:] == -1).all()   # one 256-row range = two 128-row tiles
     # rank 1 receives experts 2, 3; rank 1's rows for expert 3 follow rank 0's 3 rows
     _, row_off1, _, _ = plan_reference(cnt, 1, cap)
     sb1, _, _, _ = plan_reference(cnt, 1, cap)
-    assert row_off1.tolist() == [0, 128, 256]
-    assert sb1[3] == 128 + 3 and send_base[3] == 128
+    assert row_off1.tolist() == [0, 256, 512]
+    assert sb1[3] == 256 + 3 and send_base[3] == 256

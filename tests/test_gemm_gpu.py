@@ -63,9 +63,10 @@ def test_linear_wgrad(C, M, N, K):
     close(dw, ref, rtol=1e-3, atol=1e-2)
 
 
-def _groups(counts):
-    """Padded expert-sorted layout: row offsets and per-128-row-tile expert ids."""
-    pad = [((c + 127) // 128) * 128 for c in counts]
+def _groups(counts, rows=128):
+    """Padded expert-sorted layout (ranges multiples of ``rows``): row offsets
+    and per-128-row-tile expert ids."""
+    pad = [((c + rows - 1) // rows) * rows for c in counts]
     off = [0]
     for p in pad:
         off.append(off[-1] + p)
@@ -75,10 +76,11 @@ def _groups(counts):
     return off, tiles
 
 
+@pytest.mark.parametrize("group_rows", [128, 256])
 @pytest.mark.parametrize("I,D,counts", [(384, 768, [300, 0, 129, 512]), (128, 256, [64, 200])])
-def test_swiglu_grouped(C, I, D, counts):
+def test_swiglu_grouped(C, I, D, counts, group_rows):
     G = len(counts)
-    off, tiles = _groups(counts)
+    off, tiles = _groups(counts, group_rows)
     P = off[-1]
     x = bf(P, D, seed=7)
     for e in range(G):  # zero the padding rows like the permutation kernel does
@@ -87,7 +89,7 @@ def test_swiglu_grouped(C, I, D, counts):
     tg = torch.tensor(tiles + [-1, -1], dtype=torch.int32, device="cuda")
     h = torch.empty(P, I, device="cuda", dtype=torch.bfloat16)
     gu = torch.empty(P, 2 * I, device="cuda", dtype=torch.bfloat16)
-    C.swiglu_fwd(x, w13, tg, h, gu)
+    C.swiglu_fwd(x, w13, tg, h, gu, group_rows=group_rows)
     for e in range(G):
         rows = slice(off[e], off[e] + counts[e])
         g = x[rows].float() @ w13[e, 0].float().t()
@@ -98,14 +100,14 @@ def test_swiglu_grouped(C, I, D, counts):
     # down projection, grouped
     w2 = bf(G, D, I, scale=0.05, seed=9)
     y = torch.empty(P, D, device="cuda", dtype=torch.bfloat16)
-    C.grouped_fwd(h, w2, tg, y)
+    C.grouped_fwd(h, w2, tg, y, group_rows=group_rows)
     for e in range(G):
         rows = slice(off[e], off[e] + counts[e])
         close(y[rows], h[rows].float() @ w2[e].float().t())
     # backward: dgu from dy through w2 and the saved gate/up
     dy = bf(P, D, seed=10)
     dgu = torch.empty(P, 2 * I, device="cuda", dtype=torch.bfloat16)
-    C.swiglu_dgrad(dy, w2, tg, gu, dgu)
+    C.swiglu_dgrad(dy, w2, tg, gu, dgu, group_rows=group_rows)
     for e in range(G):
         rows = slice(off[e], off[e] + counts[e])
         dh = dy[rows].float() @ w2[e].float()
@@ -114,7 +116,7 @@ def test_swiglu_grouped(C, I, D, counts):
         close(dgu[rows, :I], dh * u * s * (1 + g * (1 - s)))
         close(dgu[rows, I:], dh * g * s)
     dx = torch.empty(P, D, device="cuda", dtype=torch.bfloat16)
-    C.grouped_dgrad(dgu, w13.view(G, 2 * I, D), tg, dx)
+    C.grouped_dgrad(dgu, w13.view(G, 2 * I, D), tg, dx, group_rows=group_rows)
     for e in range(G):
         rows = slice(off[e], off[e] + counts[e])
         close(dx[rows], dgu[rows].float() @ w13[e].view(2 * I, D).float())

@@ -158,7 +158,7 @@ def test_router_and_permutation(C):
     close(w, picked / picked.sum(-1, keepdim=True), rtol=1e-5, atol=1e-6)
     assert torch.equal(counts.long(), torch.bincount(idx.flatten().long(), minlength=E))
     # permutation
-    P = ((T * k + E * 127 + 127) // 128) * 128
+    P = ((T * k + E * 255 + 255) // 256) * 256
     row_off = torch.empty(E + 1, device="cuda", dtype=torch.int32)
     tg = torch.empty(P // 128, device="cuda", dtype=torch.int32)
     cursor = torch.empty(E, device="cuda", dtype=torch.int32)
