@@ -561,20 +561,20 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
 
 namespace {
 
-template <int R, int DRP>
+template <int R, int DRP, int NW>
 void launch_latent_mma(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv, const at::Tensor& pe,
                        const at::Tensor& lens, int B, int H, int dr, int qpb, int chunk, int nsplit, double scale,
                        float* pm, float* pl, float* po, cudaStream_t st) {
   constexpr int KS = R + DRP + 8;
-  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * 64 * 4;
-  auto kern = latent_decode_mma_kernel<R, DRP>;
+  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * NW * 16 * 4;
+  auto kern = latent_decode_mma_kernel<R, DRP, NW>;
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     configured = true;
   }
   dim3 grid(nsplit, (H + 15) / 16, B);
-  kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q_lat.data_ptr()),
+  kern<<<grid, 32 * NW, smem, st>>>(reinterpret_cast<const bf16*>(q_lat.data_ptr()),
                                 reinterpret_cast<const bf16*>(q_pe.data_ptr()),
                                 reinterpret_cast<const bf16*>(kv.data_ptr()),
                                 reinterpret_cast<const bf16*>(pe.data_ptr()), lens.data_ptr<int>(), H, dr,
@@ -588,15 +588,16 @@ bool run_latent_mma(int R, int dr, const at::Tensor& q_lat, const at::Tensor& q_
                     const at::Tensor& pe, const at::Tensor& lens, int B, int H, int qpb, int chunk, int nsplit,
                     double scale, float* pm, float* pl, float* po, cudaStream_t st) {
   const int drp = (dr + 15) / 16 * 16;
-#define DSV3_LD_CASE(R_, DRP_)                                                                                 \
+#define DSV3_LD_CASE(R_, DRP_, NW_)                                                                           \
   if (R == R_ && drp == DRP_) {                                                                                \
-    launch_latent_mma<R_, DRP_>(q_lat, q_pe, kv, pe, lens, B, H, dr, qpb, chunk, nsplit, scale, pm, pl, po, st); \
+    launch_latent_mma<R_, DRP_, NW_>(q_lat, q_pe, kv, pe, lens, B, H, dr, qpb, chunk, nsplit, scale, pm, pl, po, \
+                                     st);                                                                      \
     return true;                                                                                               \
   }
-  DSV3_LD_CASE(512, 64)
-  DSV3_LD_CASE(192, 32)
-  DSV3_LD_CASE(128, 32)
-  DSV3_LD_CASE(64, 16)
+  DSV3_LD_CASE(512, 64, 8)
+  DSV3_LD_CASE(192, 32, 4)
+  DSV3_LD_CASE(128, 32, 8)
+  DSV3_LD_CASE(64, 16, 4)
 #undef DSV3_LD_CASE
   return false;
 }

@@ -118,19 +118,25 @@ __device__ void grid_done_signal(const EpArgs& a, int phase, unsigned int* done)
   }
 }
 
-// Copy one D-element bf16 row with the warp's lanes (16-byte chunks).
+// Copy one D-element bf16 row with the warp's lanes (16-byte chunks): every
+// load of the lane is issued before the first store, so a lane keeps up to
+// eight 16-byte chunks in flight (rows up to 2048 elements in one pass).
 __device__ __forceinline__ void copy_row(const __nv_bfloat16* __restrict__ src, __nv_bfloat16* dst, int D8, int lane) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
   uint4* d = reinterpret_cast<uint4*>(dst);
-  int c = lane;
-  for (; c + 96 < D8; c += 128) {  // four chunks in flight per lane
-    const uint4 v0 = s[c], v1 = s[c + 32], v2 = s[c + 64], v3 = s[c + 96];
-    d[c] = v0;
-    d[c + 32] = v1;
-    d[c + 64] = v2;
-    d[c + 96] = v3;
+  for (int base = 0; base < D8; base += 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = base + lane + 32 * i;
+      if (c < D8) v[i] = s[c];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = base + lane + 32 * i;
+      if (c < D8) d[c] = v[i];
+    }
   }
-  for (; c < D8; c += 32) d[c] = s[c];
 }
 
 __global__ void __launch_bounds__(1024) ep_plan_kernel(EpArgs a, const int* __restrict__ counts, uint32_t* expect,

@@ -335,11 +335,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         char* base = reinterpret_cast<char*>(args.out);
         if constexpr (S == Sched::GroupedK)
           base += (size_t)ti.g * args.out_group_stride * (E == Epi::StoreBF16 ? 2 : 4);
+        static_assert(HALF % 32 == 0, "epilogue drains 32 columns per TMEM wait");
 #pragma unroll 1
-        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
+        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+          uint32_t rr[2][16];   // two TMEM loads in flight per wait
           __syncwarp();
-          tmem_ld16(tbase + c, r);
+          tmem_ld16(tbase + c2, rr[0]);
+          tmem_ld16(tbase + c2 + 16, rr[1]);
           tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+          const uint32_t (&r)[16] = rr[q];
+          const int c = c2 + 16 * q;
           const int col = ti.n0 + c;
           if (!row_ok || col >= args.N) continue;
           const bool full16 = col + 16 <= args.N;
@@ -400,6 +407,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int j = 0; j < 16; ++j)
                 if (col + j < args.N) atomicAdd(o + j, __uint_as_float(r[j]));
             }
+          }
           }
         }
       } else if constexpr (E == Epi::SwigluFwd) {

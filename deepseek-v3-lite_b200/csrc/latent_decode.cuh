@@ -86,25 +86,26 @@ __global__ void latent_decode_merge_kernel(const float* __restrict__ part_m, con
 // (query row b, group of 16 heads, split of `chunk` cache rows).  Each 64-row
 // tile of the cache (R latent + DRP zero-padded rope columns) is staged in
 // shared memory once (cp.async, double-buffered) and serves all 16 heads:
-//   S[16 x 64]  = Q[16 x (R + DRP)] . K^T      warp w: cache rows 16w..16w+15
-//   row max / sum of the tile across the 4 warps through shared memory
-//   O[16 x R]  += P[16 x 64] . V[64 x R]       warp w: output columns w*R/4..
+//   S[16 x 64]  = Q[16 x (R + DRP)] . K^T      warp w: cache rows w*64/NW ..
+//   row max / sum of the tile across the NW warps through shared memory
+//   O[16 x R]  += P[16 x 64] . V[64 x R]       warp w: output columns w*R/NW ..
 // V is the latent part of the same tile, so every cache byte is read once
-// per 16 heads.  Partials (max in natural-log units, sum, O) have the layout
-// the merge kernel above expects.
-template <int R, int DRP>
-__global__ void __launch_bounds__(128) latent_decode_mma_kernel(
+// per 16 heads.  With 8 warps each warp takes 8 cache rows and runs the two
+// halves of the score reduction as independent MMA chains.  Partials (max in
+// natural-log units, sum, O) have the layout the merge kernel above expects.
+template <int R, int DRP, int NW>
+__global__ void __launch_bounds__(32 * NW) latent_decode_mma_kernel(
     const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe, const bf16* __restrict__ kv,
     const bf16* __restrict__ pe, const int* __restrict__ lens, int H, int dr, long kv_bs, long pe_bs, int qpb,
     int chunk, int nsplit, float scale_log2, float* __restrict__ part_m, float* __restrict__ part_l,
     float* __restrict__ part_o) {
-  constexpr int DK = R + DRP, KS = DK + 8, TK = 64, PS = TK + 8, RW = R / 4;
-  static_assert(R % 64 == 0 && DRP % 16 == 0 && RW % 16 == 0, "R a multiple of 64, rope padded to 16");
+  constexpr int DK = R + DRP, KS = DK + 8, TK = 64, PS = TK + 8, RW = R / NW, KPW = TK / NW, NT = 32 * NW;
+  static_assert(DRP % 16 == 0 && RW % 16 == 0 && (KPW == 8 || KPW == 16), "latent decode tiling");
   extern __shared__ __align__(16) uint8_t ld_smem[];
   bf16* sQ = reinterpret_cast<bf16*>(ld_smem);           // [16][KS]
   bf16* sK = sQ + 16 * KS;                                // [2][TK][KS]
   bf16* sP = sK + 2 * TK * KS;                            // [16][PS]
-  float* red = reinterpret_cast<float*>(sP + 16 * PS);    // [2][4][16]: tile row max, tile row sum
+  float* red = reinterpret_cast<float*>(sP + 16 * PS);    // [2][NW][16]: tile row max, tile row sum
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tig = lane & 3;
   const int split = blockIdx.x, h0 = blockIdx.y * 16, b = blockIdx.z;
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
   const int drc = dr / 8;                                 // 16-byte chunks of a rope row
 
   if (r0 >= r1) {  // nothing of this row's cache in this split
-    for (int i = tid; i < 16 * R; i += 128) {
+    for (int i = tid; i < 16 * R; i += NT) {
       const int h = h0 + i / R;
       if (h < H) part_o[((size_t)(b * H + h) * nsplit + split) * R + i % R] = 0.f;
     }
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
   }
 
   // queries of the 16 heads (zeros past H and past dr)
-  for (int c = tid; c < 16 * (DK / 8); c += 128) {
+  for (int c = tid; c < 16 * (DK / 8); c += NT) {
     const int i = c / (DK / 8), cc = c % (DK / 8), h = h0 + i;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (h < H) {
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
   auto load_tile = [&](int t, int st) {
     bf16* dst = sK + st * TK * KS;
     const int base = r0 + t * TK;
-    for (int c = tid; c < TK * (DK / 8); c += 128) {
+    for (int c = tid; c < TK * (DK / 8); c += NT) {
       const int i = c / (DK / 8), cc = c % (DK / 8), r = base + i;
       const bool row_ok = r < r1;
       if (cc < R / 8) {
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
 #pragma unroll
   for (int n = 0; n < RW / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  constexpr int NS = KPW / 8;                             // 8-key score tiles per warp
 
   for (int t = 0; t < ntiles; ++t) {
     const int st = t & 1;
@@ -168,22 +170,41 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
     cp_async_wait<1>();
     __syncthreads();
     const bf16* ks = sK + st * TK * KS;
-    float s[2][4];
+    float s[NS][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    for (int j = 0; j < NS; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    if constexpr (KPW == 16) {
 #pragma unroll 4
-    for (int kk = 0; kk < DK / 16; ++kk) {
-      uint32_t a[4], bb[4];
-      ldsm_x4(a, sQ + ((lane & 7) + 8 * ((lane >> 3) & 1)) * KS + kk * 16 + 8 * (lane >> 4));
-      ldsm_x4(bb, ks + (warp * 16 + (lane & 7) + 8 * (lane >> 4)) * KS + kk * 16 + 8 * ((lane >> 3) & 1));
-      mma16816(s[0], a, bb[0], bb[1]);
-      mma16816(s[1], a, bb[2], bb[3]);
+      for (int kk = 0; kk < DK / 16; ++kk) {
+        uint32_t a[4], bb[4];
+        ldsm_x4(a, sQ + ((lane & 7) + 8 * ((lane >> 3) & 1)) * KS + kk * 16 + 8 * (lane >> 4));
+        ldsm_x4(bb, ks + (warp * 16 + (lane & 7) + 8 * (lane >> 4)) * KS + kk * 16 + 8 * ((lane >> 3) & 1));
+        mma16816(s[0], a, bb[0], bb[1]);
+        mma16816(s[NS - 1], a, bb[2], bb[3]);
+      }
+    } else {
+      // 8 cache rows per warp: one B load covers two k-steps, accumulated in
+      // two independent chains (even / odd k-steps) that are added at the end.
+      float s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int kk = 0; kk < DK / 16; kk += 2) {
+        uint32_t a0[4], a1[4], bb[4];
+        ldsm_x4(bb, ks + (warp * 8 + (lane & 7)) * KS + kk * 16 + 8 * (lane >> 3));
+        ldsm_x4(a0, sQ + ((lane & 7) + 8 * ((lane >> 3) & 1)) * KS + kk * 16 + 8 * (lane >> 4));
+        mma16816(s[0], a0, bb[0], bb[1]);
+        if (kk + 1 < DK / 16) {
+          ldsm_x4(a1, sQ + ((lane & 7) + 8 * ((lane >> 3) & 1)) * KS + (kk + 1) * 16 + 8 * (lane >> 4));
+          mma16816(s2, a1, bb[2], bb[3]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[0][e] += s2[e];
     }
     // scale + mask rows past the cache length; this warp's row maxima
-    const int kbase = r0 + t * TK + warp * 16;
+    const int kbase = r0 + t * TK + warp * KPW;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < NS; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int col = kbase + j * 8 + 2 * tig + (e & 1);
@@ -205,18 +226,20 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = g + 8 * r;
-      const float tmax = fmaxf(fmaxf(red[row], red[16 + row]), fmaxf(red[32 + row], red[48 + row]));
+      float tmax = red[row];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) tmax = fmaxf(tmax, red[w * 16 + row]);
       m_new[r] = fmaxf(m_run[r], tmax);
       msub[r] = m_new[r] == -INFINITY ? 0.f : m_new[r];
       corr[r] = m_run[r] == -INFINITY ? 0.f : exp2f(m_run[r] - m_new[r]);
     }
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < NS; ++j) {
       const float p0 = exp2f(s[j][0] - msub[0]), p1 = exp2f(s[j][1] - msub[0]);
       const float p2 = exp2f(s[j][2] - msub[1]), p3 = exp2f(s[j][3] - msub[1]);
       rs[0] += p0 + p1;
       rs[1] += p2 + p3;
-      const int col = warp * 16 + j * 8 + 2 * tig;
+      const int col = warp * KPW + j * 8 + 2 * tig;
       *reinterpret_cast<uint32_t*>(sP + g * PS + col) = pack_bf16x2(p0, p1);
       *reinterpret_cast<uint32_t*>(sP + (g + 8) * PS + col) = pack_bf16x2(p2, p3);
     }
@@ -226,14 +249,16 @@ __global__ void __launch_bounds__(128) latent_decode_mma_kernel(
       rs[r] += __shfl_xor_sync(0xffffffffu, rs[r], 2);
     }
     if (tig == 0) {
-      red[64 + warp * 16 + g] = rs[0];
-      red[64 + warp * 16 + g + 8] = rs[1];
+      red[NW * 16 + warp * 16 + g] = rs[0];
+      red[NW * 16 + warp * 16 + g + 8] = rs[1];
     }
     __syncthreads();
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = g + 8 * r;
-      const float tsum = (red[64 + row] + red[80 + row]) + (red[96 + row] + red[112 + row]);
+      float tsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) tsum += red[NW * 16 + w * 16 + row];
       l_run[r] = l_run[r] * corr[r] + tsum;
       m_run[r] = m_new[r];
     }

@@ -87,6 +87,39 @@ def case_fa_bwd():
         C.flash_bwd(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H)
 
 
+def case_latent_decode():
+    """Tensor-core absorbed decode: 64 rows x 16 heads over a 4096-row latent cache (R 512 + rope 64)."""
+    C = native()
+    B, H, R, dr, S = 64, 16, 512, 64, 4096
+    q_lat, q_pe = _bf(B, H, R), _bf(B, H, dr)
+    kv, pe = _bf(B, S, R), _bf(B, S, dr)
+    lens = torch.full((B,), S, dtype=torch.int32, device="cuda")
+    scratch = torch.empty(B * H * (S // 256) * (2 + R), device="cuda")
+    out = torch.empty(B, H, R, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        C.latent_decode(q_lat, q_pe, kv, pe, lens, 0.07, S, scratch, out)
+
+
+def case_ep_dispatch():
+    """Expert-parallel dispatch kernel on one rank (the rank stores into its own
+    heap): 32K tokens x top-4 of 20 experts, D 768."""
+    from parallel.ep import ExpertParallel
+    C = native()
+    T, E, k, D = 32768, 20, 4, 768
+    ep = ExpertParallel(E, k, D, T, n_slots=1)
+    x = _bf(T, D)
+    logits = torch.randn(T, 24, device="cuda")
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    ssel = torch.empty(T, k, device="cuda")
+    for _ in range(2):
+        counts = torch.zeros(E, dtype=torch.int32, device="cuda")
+        C.router_topk(logits, torch.zeros(E, device="cuda"), E, k, 1.0, idx, w, ssel, counts)
+        ep.dispatch(0, x, idx, w, counts)
+    torch.cuda.synchronize()
+    ep.close()
+
+
 def case_train_step():
     import os
     import yaml
