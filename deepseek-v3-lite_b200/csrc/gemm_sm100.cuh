@@ -463,27 +463,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(args.aux);
         __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
 #pragma unroll 1
-        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
+        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+          uint32_t rr[2][16];
+          uint16_t gvv[2][16], uvv[2][16];
           __syncwarp();
-          tmem_ld16(tbase + c, r);
+          tmem_ld16(tbase + c2, rr[0]);
+          tmem_ld16(tbase + c2 + 16, rr[1]);
+          // the saved gate / up values of both 16-column groups are requested
+          // before any is used
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int col = ti.n0 + c2 + 16 * q;
+            if (!row_ok || col >= args.N) continue;
+            const int nv = min(16, args.N - col);
+            const uint16_t* gsrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + col);
+            const uint16_t* usrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + args.inter + col);
+            if (nv == 16) {
+              *reinterpret_cast<uint4*>(gvv[q]) = reinterpret_cast<const uint4*>(gsrc)[0];
+              *reinterpret_cast<uint4*>(gvv[q] + 8) = reinterpret_cast<const uint4*>(gsrc)[1];
+              *reinterpret_cast<uint4*>(uvv[q]) = reinterpret_cast<const uint4*>(usrc)[0];
+              *reinterpret_cast<uint4*>(uvv[q] + 8) = reinterpret_cast<const uint4*>(usrc)[1];
+            } else {
+              for (int j = 0; j < 16; ++j) {
+                gvv[q][j] = j < nv ? gsrc[j] : 0;
+                uvv[q][j] = j < nv ? usrc[j] : 0;
+              }
+            }
+          }
           tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+          const uint32_t (&r)[16] = rr[q];
+          const uint16_t (&gv)[16] = gvv[q];
+          const uint16_t (&uv)[16] = uvv[q];
+          const int c = c2 + 16 * q;
           const int col = ti.n0 + c;
           if (!row_ok || col >= args.N) continue;
           const int nv = min(16, args.N - col);
-          const uint16_t* gsrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + col);
-          const uint16_t* usrc = reinterpret_cast<const uint16_t*>(gu + (size_t)row * args.ld_aux + args.inter + col);
-          uint16_t gv[16], uv[16];
-          if (nv == 16) {
-            *reinterpret_cast<uint4*>(gv) = reinterpret_cast<const uint4*>(gsrc)[0];
-            *reinterpret_cast<uint4*>(gv + 8) = reinterpret_cast<const uint4*>(gsrc)[1];
-            *reinterpret_cast<uint4*>(uv) = reinterpret_cast<const uint4*>(usrc)[0];
-            *reinterpret_cast<uint4*>(uv + 8) = reinterpret_cast<const uint4*>(usrc)[1];
-          } else {
-            for (int j = 0; j < 16; ++j) {
-              gv[j] = j < nv ? gsrc[j] : 0;
-              uv[j] = j < nv ? usrc[j] : 0;
-            }
-          }
           uint32_t dg[8], du[8];
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
@@ -515,16 +531,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               reinterpret_cast<uint16_t*>(uo)[j] = us[j];
             }
           }
+          }
         }
       } else if constexpr (E == Epi::CeFwd) {
         const long tgt = row_ok ? args.targets[row] : -1;
         float run_max = -INFINITY, run_sum = 0.0f;
 #pragma unroll 1
-        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
+        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+          uint32_t rr[2][16];
           __syncwarp();
-          tmem_ld16(tbase + c, r);
+          tmem_ld16(tbase + c2, rr[0]);
+          tmem_ld16(tbase + c2 + 16, rr[1]);
           tmem_ld_wait();
-          const int col = ti.n0 + c;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+          const uint32_t (&r)[16] = rr[q];
+          const int col = ti.n0 + c2 + 16 * q;
           float cmax = -INFINITY;
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -542,6 +564,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < 16; ++j)
               if (col + j == tgt && row_ok) args.tgt_logit[row] = __uint_as_float(r[j]);
           }
+          }
         }
         if (row_ok) {  // two partials per (row, tile): one per column half
           args.part_max[(size_t)row * 2 * args.n_tiles + 2 * ti.n_tile + half] = run_max;
@@ -553,11 +576,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float sc = row_ok ? args.row_scale[row] : 0.0f;
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo;
 #pragma unroll 1
-        for (int c = half * HALF; c < (half + 1) * HALF; c += 16) {
+        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+          uint32_t rr[2][16];
           __syncwarp();
-          tmem_ld16(tbase + c, r);
+          tmem_ld16(tbase + c2, rr[0]);
+          tmem_ld16(tbase + c2 + 16, rr[1]);
           tmem_ld_wait();
-          const int col = ti.n0 + c;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+          const uint32_t (&r)[16] = rr[q];
+          const int col = ti.n0 + c2 + 16 * q;
           if (!row_ok || col >= args.N) continue;
           uint32_t pk[8];
 #pragma unroll
@@ -572,6 +600,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             const uint16_t* ps = reinterpret_cast<const uint16_t*>(pk);
             for (int j = 0; col + j < args.N; ++j) reinterpret_cast<uint16_t*>(o + col)[j] = ps[j];
+          }
           }
         }
       }

@@ -87,6 +87,35 @@ def case_fa_bwd():
         C.flash_bwd(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H)
 
 
+def _ce_inputs(T=16384, V=100018, D=768):
+    x, w = _bf(T, D), _bf(V, D) * 0.05
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    return T, V, D, x, w, tgt
+
+
+def case_ce_fwd():
+    """Fused LM head + log-sum-exp partials, 16K rows x 100,018 vocab x 768."""
+    C = native()
+    T, V, D, x, w, tgt = _ce_inputs()
+    nt = (V + 255) // 256
+    pmax = torch.empty(T, 2 * nt, device="cuda")
+    psum = torch.empty(T, 2 * nt, device="cuda")
+    tl = torch.zeros(T, device="cuda")
+    for _ in range(2):
+        C.ce_fwd_partials(x, w, tgt, pmax, psum, tl)
+
+
+def case_ce_bwd():
+    """LM head + cross-entropy gradient epilogue (bf16 dlogits), same shape."""
+    C = native()
+    T, V, D, x, w, tgt = _ce_inputs()
+    lse = torch.full((T,), 12.0, device="cuda")
+    scale = torch.full((T,), 1.0 / T, device="cuda")
+    dl = torch.empty(T, (V + 63) // 64 * 64, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        C.ce_bwd_logits(x, w, tgt, lse, scale, dl)
+
+
 def case_latent_decode():
     """Tensor-core absorbed decode: 64 rows x 16 heads over a 4096-row latent cache (R 512 + rope 64)."""
     C = native()
