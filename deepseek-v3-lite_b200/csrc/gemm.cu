@@ -318,6 +318,44 @@ void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& til
   launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
 }
 
+// Grouped forward whose epilogue also stores every row into its home rank's
+// combine inbox over peer memory (expert-parallel combine fused with the down
+// projection); the last CTA raises flag [phase][me] on every rank.
+// peers: int64 [R] heap bases (device); origin: int32 [P] (src * tk + slot, -1 on padding).
+void grouped_fwd_scatter(const at::Tensor& a, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out,
+                         int64_t group_rows, const at::Tensor& peers, int64_t scatter_off, const at::Tensor& origin,
+                         int64_t tk, int64_t flags_off, int64_t me, int64_t phase, at::Tensor& done) {
+  check_bf16_rows(a, "a");
+  check_bf16_rows(out, "out");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
+  const int64_t P = a.size(0), K = a.size(1), G = w.size(0), N = w.size(1);
+  TORCH_CHECK(w.size(2) == K && out.size(0) == P && out.size(1) == N, "grouped_fwd_scatter: shapes");
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 1 && peers.numel() <= 8,
+              "grouped_fwd_scatter: peers int64 [R] on the device");
+  TORCH_CHECK(origin.scalar_type() == at::kInt && origin.numel() >= P, "grouped_fwd_scatter: origin int32 [P]");
+  TORCH_CHECK(N % 8 == 0 && scatter_off % 16 == 0, "grouped_fwd_scatter: 16-byte rows");
+  const at::cuda::CUDAGuard guard(a.device());
+  GemmArgs g = blank_args();
+  g.M = P; g.N = N; g.K = K;
+  g.out = out.data_ptr(); g.ldo = out.stride(0);
+  g.tile_group = tile_group.data_ptr<int>();
+  g.tile_rows = (int)group_rows;
+  g.peer_base = reinterpret_cast<const unsigned long long*>(peers.data_ptr<int64_t>());
+  g.origin = origin.data_ptr<int>();
+  g.scatter_off = scatter_off;
+  g.flags_off = flags_off;
+  g.scatter_tk = (int)tk;
+  g.scatter_me = (int)me;
+  g.scatter_ranks = (int)peers.numel();
+  g.scatter_phase = (int)phase;
+  g.done_ctr = reinterpret_cast<unsigned int*>(done.data_ptr());
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
+  g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap ta = map_a_kmajor(a, P, K, a.stride(0));
+  CUtensorMap tb = map_b_kmajor(w, G, N, K, K, N * K);
+  launch<256, 0, 0, Sched::GroupedM, Epi::ScatterBF16, false>(ta, tb, g);
+}
+
 // Grouped data gradient: out[P,K] = dy[P,N] @ w[g(tile)], w: [G, N, K].
 void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out,
                    int64_t group_rows) {
@@ -446,6 +484,8 @@ void register_gemm(pybind11::module_& m) {
         pybind11::arg("group_rows") = 128);
   m.def("grouped_fwd", &grouped_fwd, "expert-grouped out = a @ w[e]^T", pybind11::arg("a"), pybind11::arg("w"),
         pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
+  m.def("grouped_fwd_scatter", &grouped_fwd_scatter,
+        "expert-grouped out = a @ w[e]^T, rows also stored into their home ranks' combine inbox (P2P)");
   m.def("grouped_dgrad", &grouped_dgrad, "expert-grouped out = dy @ w[e]", pybind11::arg("dy"), pybind11::arg("w"),
         pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
   m.def("grouped_wgrad", &grouped_wgrad, "per-expert dw[e] (fp32) += a_e^T @ b_e");

@@ -37,7 +37,9 @@ enum class Epi : int {
   CeFwd = 5,         // per-row (max, sum-exp) partials + target logit
   CeBwd = 6,         // (softmax - onehot) * scale, bf16
   StoreF32 = 7,      // out (fp32) = acc
-  ResidF32 = 8       // out (fp32) = aux (fp32) + acc   (out-of-place residual add)
+  ResidF32 = 8,      // out (fp32) = aux (fp32) + acc   (out-of-place residual add)
+  ScatterBF16 = 9    // out (bf16) = acc, and each row also stored into its home rank's
+                     // combine inbox over peer memory (expert-parallel combine)
 };
 
 constexpr int kEpiWarps = 8;                 // two warpgroups drain TMEM
@@ -68,6 +70,15 @@ struct GemmArgs {
   const float* lse;      // CeBwd: [M]
   const float* row_scale;// CeBwd: [M]
   unsigned int* status;  // device status word (bounded-wait failures)
+  // ScatterBF16: row r goes to rank origin[r] / scatter_tk, slot origin[r] % scatter_tk
+  // of the inbox at heap offset scatter_off (rows of N bf16); the last CTA to
+  // finish raises flag [scatter_phase][scatter_me] on every rank.
+  const unsigned long long* peer_base;   // heap base of every rank (device array)
+  const int* origin;
+  long long scatter_off;
+  long long flags_off;
+  int scatter_tk, scatter_me, scatter_ranks, scatter_phase;
+  unsigned int* done_ctr;
 };
 
 // CG = 2: a CTA pair shares one 256-row tile (each CTA: 128 rows of A and
@@ -331,8 +342,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t r[16];
 
       if constexpr (E == Epi::StoreBF16 || E == Epi::AddF32 || E == Epi::AtomicAddF32 || E == Epi::StoreF32 ||
-                    E == Epi::ResidF32) {
+                    E == Epi::ResidF32 || E == Epi::ScatterBF16) {
         char* base = reinterpret_cast<char*>(args.out);
+        __nv_bfloat16* remote = nullptr;   // ScatterBF16: this row in its home rank's inbox
+        if constexpr (E == Epi::ScatterBF16) {
+          const int o = row_ok ? args.origin[row] : -1;
+          if (o >= 0) {
+            const int src = o / args.scatter_tk, slot = o - src * args.scatter_tk;
+            if (src < args.scatter_ranks)
+              remote = reinterpret_cast<__nv_bfloat16*>(args.peer_base[src] + args.scatter_off) + (size_t)slot * args.N;
+          }
+        }
         if constexpr (S == Sched::GroupedK)
           base += (size_t)ti.g * args.out_group_stride * (E == Epi::StoreBF16 ? 2 : 4);
         static_assert(HALF % 32 == 0, "epilogue drains 32 columns per TMEM wait");
@@ -350,7 +370,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int col = ti.n0 + c;
           if (!row_ok || col >= args.N) continue;
           const bool full16 = col + 16 <= args.N;
-          if constexpr (E == Epi::StoreBF16) {
+          if constexpr (E == Epi::StoreBF16 || E == Epi::ScatterBF16) {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + (size_t)row * args.ldo + col;
             if (full16) {
               uint4 v0, v1;
@@ -364,8 +384,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               v1.w = pack_bf16x2(__uint_as_float(r[14]), __uint_as_float(r[15]));
               reinterpret_cast<uint4*>(o)[0] = v0;
               reinterpret_cast<uint4*>(o)[1] = v1;
+              if constexpr (E == Epi::ScatterBF16) {
+                if (remote != nullptr) {
+                  reinterpret_cast<uint4*>(remote + col)[0] = v0;
+                  reinterpret_cast<uint4*>(remote + col)[1] = v1;
+                }
+              }
             } else {
-              for (int j = 0; j < 16 && col + j < args.N; ++j) o[j] = __float2bfloat16(__uint_as_float(r[j]));
+              for (int j = 0; j < 16 && col + j < args.N; ++j) {
+                o[j] = __float2bfloat16(__uint_as_float(r[j]));
+                if constexpr (E == Epi::ScatterBF16) {
+                  if (remote != nullptr) remote[col + j] = o[j];
+                }
+              }
             }
           } else if constexpr (E == Epi::AddF32 || E == Epi::ResidF32) {
             float* o = reinterpret_cast<float*>(base) + (size_t)row * args.ldo + col;
@@ -614,8 +645,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if constexpr (E == Epi::ScatterBF16) __threadfence_system();   // this CTA's peer stores before the signal
   tc_fence_before();
   __syncthreads();
+  if constexpr (E == Epi::ScatterBF16) {
+    if (threadIdx.x == 0) {
+      // the last CTA of the grid tells every rank that all rows have landed
+      const unsigned int prev = atomicAdd(args.done_ctr, 1u);
+      if (prev == gridDim.x - 1) {
+        *args.done_ctr = 0u;
+        __threadfence_system();
+        for (int p = 0; p < args.scatter_ranks; ++p) {
+          uint32_t* flag = reinterpret_cast<uint32_t*>(args.peer_base[p] + args.flags_off) +
+                           args.scatter_phase * 8 + args.scatter_me;
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+        }
+      }
+    }
+  }
   if constexpr (CG == 2) cluster_sync();   // the peer no longer touches this CTA's barriers or TMEM
   if (warp == 1) {
     __syncwarp();

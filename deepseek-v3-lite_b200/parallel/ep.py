@@ -9,9 +9,10 @@ forward
   counts over peer memory and the receive layout -> ``ep_dispatch``: each
   (token, slot) row stored straight into its expert owner's receive slot ->
   wait -> grouped SwiGLU GEMM and grouped down GEMM on the received rows
-  (operands in local memory, tcgen05) -> ``ep_send_back``: each output row
-  stored into its home rank's combine inbox at the token's slot -> wait ->
-  weighted combine into the fp32 residual (home side).
+  (operands in local memory, tcgen05) whose epilogue also stores each output
+  row into its home rank's combine inbox at the token's slot (the combine
+  fused with the down projection; ``ep_send_back`` is the unfused variant) ->
+  wait -> weighted combine into the fp32 residual (home side).
 backward
   ``ep_dispatch_bwd``: the output-gradient rows take the forward routes ->
   wait -> ``ep_bwd_prep`` (dy = w * dout, dw = <dout, y>) -> grouped
@@ -153,7 +154,11 @@ class ExpertParallel:
         # local bookkeeping (not symmetric)
         self.expect = torch.zeros(5 * MAX_RANKS, dtype=torch.int32, device=dev)
         self.sendcnt = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.done = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(5, dtype=torch.int32, device=dev)
+        self.peers_dev = torch.tensor(self.heap.peers, dtype=torch.int64, device=dev)
+        # combine fused into the down-projection GEMM's epilogue (P2P row stores);
+        # DSV3_EP_FUSED_COMBINE=0 uses the separate send-back kernel instead
+        self.fused_combine = os.environ.get("DSV3_EP_FUSED_COMBINE", "1") != "0"
         self.cursor = torch.zeros(n_experts, dtype=torch.int32, device=dev)
         self.dims = [self.rank, self.world, n_experts, topk, tokens, dim, self.cap, self.budget_ns]
         self.comb = self.heap.tensor(self.off_comb, (TK, dim), torch.bfloat16)
@@ -266,9 +271,18 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     gu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=xn.device)
     C.swiglu_fwd(xs, w13_local, plan["tile_group"], h, gu, group_rows=256)
     ys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=xn.device)
-    C.grouped_fwd(h, w2_local, plan["tile_group"], ys, group_rows=256)
-    marks("experts fwd")
-    ep.combine_send(slot, ys, plan["row_off"])
+    if ep.fused_combine:
+        # down projection whose epilogue stores every row into its home rank's
+        # combine inbox; the last CTA raises the combine flag on every rank
+        origin, _ = ep.recv_meta(slot)
+        C.grouped_fwd_scatter(h, w2_local, plan["tile_group"], ys, 256, ep.peers_dev, ep.off_comb, origin,
+                              ep.T * ep.k, ep.off_flags, ep.rank, PH_COMBINE, ep.done[4:5])
+        marks("experts fwd")
+        C.ep_wait(ep.heap.peers, ep.offs(slot), ep.dims, PH_COMBINE, ep.expect)
+    else:
+        C.grouped_fwd(h, w2_local, plan["tile_group"], ys, group_rows=256)
+        marks("experts fwd")
+        ep.combine_send(slot, ys, plan["row_off"])
     side = plan.pop("side")
     if side is not None:
         torch.cuda.current_stream(xn.device).wait_stream(side)
