@@ -318,22 +318,31 @@ void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& til
   launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
 }
 
-// Grouped forward whose epilogue also stores every row into its home rank's
-// combine inbox over peer memory (expert-parallel combine fused with the down
-// projection); the last CTA raises flag [phase][me] on every rank.
-// peers: int64 [R] heap bases (device); origin: int32 [P] (src * tk + slot, -1 on padding).
-void grouped_fwd_scatter(const at::Tensor& a, const at::Tensor& w, const at::Tensor& tile_group, at::Tensor& out,
-                         int64_t group_rows, const at::Tensor& peers, int64_t scatter_off, const at::Tensor& origin,
-                         int64_t tk, int64_t flags_off, int64_t me, int64_t phase, at::Tensor& done) {
+// Expert-grouped GEMM whose epilogue also stores every output row into its
+// home rank's inbox over peer memory (the expert-parallel combine fused with
+// the GEMM); the last CTA raises flag [phase][me] on every rank.
+//   transpose_w = false: out = a @ w[e]^T  (w [G, N, K]; forward down projection)
+//   transpose_w = true:  out = a @ w[e]    (w [G, K, N]; backward through gate/up)
+// peers: int64 [R] heap bases (device); origin: int32 [P] (src * tk + slot,
+// -1 on padding); extra (optional, fp32 [P]) goes to extra_off[slot].
+void grouped_scatter(const at::Tensor& a, const at::Tensor& w, bool transpose_w, const at::Tensor& tile_group,
+                     at::Tensor& out, int64_t group_rows, const at::Tensor& peers, int64_t scatter_off,
+                     const at::Tensor& origin, const c10::optional<at::Tensor>& extra, int64_t extra_off, int64_t tk,
+                     int64_t flags_off, int64_t me, int64_t phase, at::Tensor& done) {
   check_bf16_rows(a, "a");
   check_bf16_rows(out, "out");
-  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 [G, N, K]");
-  const int64_t P = a.size(0), K = a.size(1), G = w.size(0), N = w.size(1);
-  TORCH_CHECK(w.size(2) == K && out.size(0) == P && out.size(1) == N, "grouped_fwd_scatter: shapes");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.dim() == 3, "w: bf16 3-D");
+  const int64_t P = a.size(0), K = a.size(1), G = w.size(0);
+  const int64_t N = transpose_w ? w.size(2) : w.size(1);
+  TORCH_CHECK((transpose_w ? w.size(1) : w.size(2)) == K && out.size(0) == P && out.size(1) == N,
+              "grouped_scatter: shapes");
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.numel() >= 1 && peers.numel() <= 8,
-              "grouped_fwd_scatter: peers int64 [R] on the device");
-  TORCH_CHECK(origin.scalar_type() == at::kInt && origin.numel() >= P, "grouped_fwd_scatter: origin int32 [P]");
-  TORCH_CHECK(N % 8 == 0 && scatter_off % 16 == 0, "grouped_fwd_scatter: 16-byte rows");
+              "grouped_scatter: peers int64 [R] on the device");
+  TORCH_CHECK(origin.scalar_type() == at::kInt && origin.numel() >= P, "grouped_scatter: origin int32 [P]");
+  TORCH_CHECK(N % 8 == 0 && scatter_off % 16 == 0, "grouped_scatter: 16-byte rows");
+  if (extra.has_value())
+    TORCH_CHECK(extra->scalar_type() == at::kFloat && extra->numel() >= P && extra_off % 4 == 0,
+                "grouped_scatter: extra fp32 [P]");
   const at::cuda::CUDAGuard guard(a.device());
   GemmArgs g = blank_args();
   g.M = P; g.N = N; g.K = K;
@@ -342,6 +351,8 @@ void grouped_fwd_scatter(const at::Tensor& a, const at::Tensor& w, const at::Ten
   g.tile_rows = (int)group_rows;
   g.peer_base = reinterpret_cast<const unsigned long long*>(peers.data_ptr<int64_t>());
   g.origin = origin.data_ptr<int>();
+  g.scatter_extra = extra.has_value() ? extra->data_ptr<float>() : nullptr;
+  g.scatter_extra_off = extra_off;
   g.scatter_off = scatter_off;
   g.flags_off = flags_off;
   g.scatter_tk = (int)tk;
@@ -352,8 +363,13 @@ void grouped_fwd_scatter(const at::Tensor& a, const at::Tensor& w, const at::Ten
   g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(N, 256); g.kb_per_split = cdiv(K, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(a, P, K, a.stride(0));
-  CUtensorMap tb = map_b_kmajor(w, G, N, K, K, N * K);
-  launch<256, 0, 0, Sched::GroupedM, Epi::ScatterBF16, false>(ta, tb, g);
+  if (transpose_w) {
+    CUtensorMap tb = map_b_mnmajor(w, G, K, N, N, K * N);
+    launch<256, 0, 1, Sched::GroupedM, Epi::ScatterBF16, false>(ta, tb, g);
+  } else {
+    CUtensorMap tb = map_b_kmajor(w, G, N, K, K, N * K);
+    launch<256, 0, 0, Sched::GroupedM, Epi::ScatterBF16, false>(ta, tb, g);
+  }
 }
 
 // Grouped data gradient: out[P,K] = dy[P,N] @ w[g(tile)], w: [G, N, K].
@@ -484,8 +500,8 @@ void register_gemm(pybind11::module_& m) {
         pybind11::arg("group_rows") = 128);
   m.def("grouped_fwd", &grouped_fwd, "expert-grouped out = a @ w[e]^T", pybind11::arg("a"), pybind11::arg("w"),
         pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
-  m.def("grouped_fwd_scatter", &grouped_fwd_scatter,
-        "expert-grouped out = a @ w[e]^T, rows also stored into their home ranks' combine inbox (P2P)");
+  m.def("grouped_scatter", &grouped_scatter,
+        "expert-grouped GEMM whose rows also go to their home ranks' inbox over peer memory (fused combine)");
   m.def("grouped_dgrad", &grouped_dgrad, "expert-grouped out = dy @ w[e]", pybind11::arg("dy"), pybind11::arg("w"),
         pybind11::arg("tile_group"), pybind11::arg("out"), pybind11::arg("group_rows") = 128);
   m.def("grouped_wgrad", &grouped_wgrad, "per-expert dw[e] (fp32) += a_e^T @ b_e");

@@ -75,6 +75,8 @@ struct GemmArgs {
   // finish raises flag [scatter_phase][scatter_me] on every rank.
   const unsigned long long* peer_base;   // heap base of every rank (device array)
   const int* origin;
+  const float* scatter_extra;            // optional: one float per row, stored to scatter_extra_off[slot]
+  long long scatter_extra_off;
   long long scatter_off;
   long long flags_off;
   int scatter_tk, scatter_me, scatter_ranks, scatter_phase;
@@ -349,8 +351,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int o = row_ok ? args.origin[row] : -1;
           if (o >= 0) {
             const int src = o / args.scatter_tk, slot = o - src * args.scatter_tk;
-            if (src < args.scatter_ranks)
+            if (src < args.scatter_ranks) {
               remote = reinterpret_cast<__nv_bfloat16*>(args.peer_base[src] + args.scatter_off) + (size_t)slot * args.N;
+              if (args.scatter_extra != nullptr && ti.n0 == 0 && half == 0)   // once per row
+                reinterpret_cast<float*>(args.peer_base[src] + args.scatter_extra_off)[slot] = args.scatter_extra[row];
+            }
           }
         }
         if constexpr (S == Sched::GroupedK)

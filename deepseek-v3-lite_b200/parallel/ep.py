@@ -275,8 +275,8 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
         # down projection whose epilogue stores every row into its home rank's
         # combine inbox; the last CTA raises the combine flag on every rank
         origin, _ = ep.recv_meta(slot)
-        C.grouped_fwd_scatter(h, w2_local, plan["tile_group"], ys, 256, ep.peers_dev, ep.off_comb, origin,
-                              ep.T * ep.k, ep.off_flags, ep.rank, PH_COMBINE, ep.done[4:5])
+        C.grouped_scatter(h, w2_local, False, plan["tile_group"], ys, 256, ep.peers_dev, ep.off_comb, origin, None,
+                          0, ep.T * ep.k, ep.off_flags, ep.rank, PH_COMBINE, ep.done[4:5])
         marks("experts fwd")
         C.ep_wait(ep.heap.peers, ep.offs(slot), ep.dims, PH_COMBINE, ep.expect)
     else:
@@ -310,10 +310,21 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     C.swiglu_dgrad(dys, w2_local, ctx["tile_group"], ctx["gu"], dgu, group_rows=256)
     C.grouped_wgrad(dys, ctx["h"], ctx["row_off"], g2_local)
     dxs = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
-    C.grouped_dgrad(dgu, w13_local.reshape(ep.Eloc, 2 * inter_dim, ep.D), ctx["tile_group"], dxs, group_rows=256)
-    C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
-    marks("experts bwd")
-    ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])
+    w13_2d = w13_local.reshape(ep.Eloc, 2 * inter_dim, ep.D)
+    if ep.fused_combine:
+        # input-gradient GEMM whose epilogue sends each row (and its gate-weight
+        # gradient) to the home rank; the weight gradient runs meanwhile
+        origin, _ = ep.recv_meta(slot)
+        C.grouped_scatter(dgu, w13_2d, True, ctx["tile_group"], dxs, 256, ep.peers_dev, ep.off_comb, origin, dw_rows,
+                          ep.off_dw, ep.T * ep.k, ep.off_flags, ep.rank, PH_BWD_COMBINE, ep.done[4:5])
+        C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
+        marks("experts bwd")
+        C.ep_wait(ep.heap.peers, ep.offs(slot), ep.dims, PH_BWD_COMBINE, ep.expect)
+    else:
+        C.grouped_dgrad(dgu, w13_2d, ctx["tile_group"], dxs, group_rows=256)
+        C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
+        marks("experts bwd")
+        ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])
     if side is not None:
         torch.cuda.current_stream(dx_acc.device).wait_stream(side)
     C.unpermute_bwd(ep.comb, ep.slot_arange, dx_acc)
