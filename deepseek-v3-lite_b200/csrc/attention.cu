@@ -535,6 +535,7 @@ void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   DSV3_FA_DISPATCH(80, 64, (run_fwd_sm100<1, 1, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(64, 64, (run_fwd_sm100<1, 0, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(128, 128, (run_fwd_sm100<2, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(192, 128, (run_fwd_sm100<3, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   // warp-level mma.sync kernels for the remaining shapes
   DSV3_FA_DISPATCH(32, 16, (run_fwd<32, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(16, 16, (run_fwd<16, 16>(q, k, v, o, lse, q_off, scale, causal, H)))
@@ -655,6 +656,7 @@ void flash_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   DSV3_FA_DISPATCH(80, 64, (run_fwd_sm100<1, 1, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(64, 64, (run_fwd_sm100<1, 0, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(128, 128, (run_fwd_sm100<2, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(192, 128, (run_fwd_sm100<3, 0, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   TORCH_CHECK(false, "flash_fwd_tc: unsupported head dims");
 }
 
@@ -677,6 +679,7 @@ void flash_fwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   DSV3_FA_DISPATCH(80, 64, (run_fwd<80, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(64, 64, (run_fwd<64, 64>(q, k, v, o, lse, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(128, 128, (run_fwd<128, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
+  DSV3_FA_DISPATCH(192, 128, (run_fwd<192, 128>(q, k, v, o, lse, q_off, scale, causal, H)))
   TORCH_CHECK(false, "flash_fwd_mma: unsupported head dims");
 }
 

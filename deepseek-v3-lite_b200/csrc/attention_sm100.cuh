@@ -1,8 +1,9 @@
 // Flash-attention forward on the 5th-generation tensor cores (tcgen05).
 //
-// One CTA per (128-query tile, batch*head).  Warp 0 streams K/V tiles of 128
-// keys with TMA (2-stage ring, Q loaded once), warp 1 issues the MMAs from one
-// thread, warps 2-5 own one query row per thread:
+// One CTA per (128-query tile, batch*head).  Warp 0 streams K and V tiles of
+// 128 keys with TMA (lane 0: Q once, then K; lane 1: V; separate rings so K_{j+1}
+// streams in while V_j is in use), warp 1 issues the MMAs from one thread,
+// warps 2-5 own one query row per thread:
 //
 //   S_j   = Q K_j^T          tcgen05.mma, M=128, N=128, fp32 in TMEM (2 buffers)
 //   P_j   = exp2(S_j * c - m) softmax threads: tcgen05.ld a whole row of S,
@@ -33,7 +34,9 @@ struct FaCfg {
   static constexpr int Q_B = QA_B + QB_B;
   static constexpr int K_B = Q_B;
   static constexpr int V_B = (DV / 64) * 16384;
-  static constexpr int ST = 2;
+  // K and V rings (separate barriers, so K_{j+1} streams in while V_j is
+  // still in use); one stage each for wide heads (DQK 192) to fit smem
+  static constexpr int ST = NA >= 3 ? 1 : 2;
   static constexpr int P_B = 32768;
   static constexpr int OFF_K = Q_B;
   static constexpr int OFF_V = OFF_K + ST * K_B;
@@ -59,14 +62,16 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sP = smem + C::OFF_P;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bar;
-  uint64_t* kv_full = bar + 1;   // [ST]
-  uint64_t* kv_empty = bar + 3;  // [ST]
-  uint64_t* s_full = bar + 5;    // [2]
-  uint64_t* s_free = bar + 7;    // [2]
-  uint64_t* p_full = bar + 9;    // [2]
-  uint64_t* pv_done = bar + 11;  // [2]
-  uint64_t* drain = bar + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  uint64_t* k_full = bar + 1;    // [ST]
+  uint64_t* k_empty = bar + 3;   // [ST]
+  uint64_t* v_full = bar + 5;    // [ST]
+  uint64_t* v_empty = bar + 7;   // [ST]
+  uint64_t* s_full = bar + 9;    // [2]
+  uint64_t* s_free = bar + 11;   // [2]
+  uint64_t* p_full = bar + 13;   // [2]
+  uint64_t* pv_done = bar + 15;  // [2]
+  uint64_t* drain = bar + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -77,8 +82,10 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
@@ -99,7 +106,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ------------------------------------------------------- producer
+      // ------------------------------------------------ producer: Q and K
       mbar_arrive_expect_tx(q_full, C::Q_B);
 #pragma unroll
       for (int a = 0; a < NA; ++a) tma_load_3d(sQ + a * 16384, &tmQa, q_full, a * 64, m0, bh);
@@ -108,21 +115,34 @@ __global__ void __launch_bounds__(192, 1)
       for (int j = 0; j < n_blocks; ++j) {
         const int st = j % C::ST;
         const uint32_t ph = (j / C::ST) & 1;
-        if (!mbar_wait_bounded(&kv_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
-        mbar_arrive_expect_tx(&kv_full[st], C::K_B + C::V_B);
+        if (!mbar_wait_bounded(&k_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::K_B);
         uint8_t* k = sK + st * C::K_B;
-        uint8_t* v = sV + st * C::V_B;
 #pragma unroll
-        for (int a = 0; a < NA; ++a) tma_load_3d(k + a * 16384, &tmKa, &kv_full[st], a * 64, j * 128, bh);
-        if (NB) tma_load_3d(k + C::QA_B, &tmKb, &kv_full[st], NA * 64, j * 128, bh);
-#pragma unroll
-        for (int d = 0; d < DV / 64; ++d) tma_load_3d(v + d * 16384, &tmV, &kv_full[st], d * 64, j * 128, bh);
+        for (int a = 0; a < NA; ++a) tma_load_3d(k + a * 16384, &tmKa, &k_full[st], a * 64, j * 128, bh);
+        if (NB) tma_load_3d(k + C::QA_B, &tmKb, &k_full[st], NA * 64, j * 128, bh);
         issued |= 1u << st;
         last_phase = (last_phase & ~(1u << st)) | (ph << st);
       }
       mbar_wait_bounded(q_full, 0, nullptr, status, DSV3_ERR_WAIT_FULL);
       for (int st = 0; st < C::ST; ++st)
-        if (issued & (1u << st)) mbar_wait_bounded(&kv_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+        if (issued & (1u << st)) mbar_wait_bounded(&k_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+    } else if (lane == 1) {
+      // ------------------------------------------------------ producer: V
+      uint32_t issued = 0, last_phase = 0;
+      for (int j = 0; j < n_blocks; ++j) {
+        const int st = j % C::ST;
+        const uint32_t ph = (j / C::ST) & 1;
+        if (!mbar_wait_bounded(&v_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::V_B);
+        uint8_t* v = sV + st * C::V_B;
+#pragma unroll
+        for (int d = 0; d < DV / 64; ++d) tma_load_3d(v + d * 16384, &tmV, &v_full[st], d * 64, j * 128, bh);
+        issued |= 1u << st;
+        last_phase = (last_phase & ~(1u << st)) | (ph << st);
+      }
+      for (int st = 0; st < C::ST; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(&v_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -135,7 +155,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int j = 0; ok && j <= n_blocks; ++j) {
         if (j < n_blocks) {
           const int st = j % C::ST, sb = j & 1;
-          if (!mbar_wait_bounded(&kv_full[st], (j / C::ST) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+          if (!mbar_wait_bounded(&k_full[st], (j / C::ST) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
           if (j >= 2 && !mbar_wait_bounded(&s_free[sb], ((j - 2) >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))
             break;
           tc_fence_after();
@@ -151,11 +171,13 @@ __global__ void __launch_bounds__(192, 1)
             }
           if (NB) umma_bf16(tmem + sb * 128, smem_desc_sw32(q + C::QA_B, 256), smem_desc_sw32(k + C::QA_B, 256), IDS, acc);
           umma_commit(&s_full[sb]);
+          umma_commit(&k_empty[st]);   // K_j is free once S_j is computed
           any = true;
         }
         if (j >= 1) {
           const int pj = j - 1, pb = pj & 1;
           if (!mbar_wait_bounded(&p_full[pb], (pj >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM)) break;
+          if (!mbar_wait_bounded(&v_full[pj % C::ST], (pj / C::ST) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
           tc_fence_after();
           const uint32_t p = smem_u32(sP + pb * C::P_B), v = smem_u32(sV + (pj % C::ST) * C::V_B);
 #pragma unroll
@@ -163,7 +185,7 @@ __global__ void __launch_bounds__(192, 1)
             umma_bf16(tO, smem_desc_sw128(p + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                       smem_desc_sw128(v + kk * 2048, 16384, 1024), IDO, (pj > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&pv_done[pb]);
-          umma_commit(&kv_empty[pj % C::ST]);
+          umma_commit(&v_empty[pj % C::ST]);
         }
       }
       if (any) {

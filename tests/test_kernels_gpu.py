@@ -296,7 +296,7 @@ def _attn_ref(Q, K, V, scale, causal, q_off=0):
 
 
 @pytest.mark.parametrize("B,H,S,DP,DV", [(2, 3, 2048, 80, 64), (1, 2, 300, 80, 64), (2, 2, 1000, 64, 64),
-                                         (1, 2, 640, 128, 128)])
+                                         (1, 2, 640, 128, 128), (1, 2, 700, 192, 128)])
 def test_flash_fwd_tcgen05(C, B, H, S, DP, DV):
     torch.manual_seed(0)
     Q = torch.randn(B * H, S, DP, device="cuda").bfloat16()
