@@ -195,6 +195,11 @@ def run_ours(args, rank, world, local):
     cfg.ep_size = 0 if args.ep < 0 else args.ep
     trainer = Pretrainer(cfg)
     vocab = y["model"]["vocab_size"]
+    ym = y["model"]
+    model_name = ("deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 w0.3 V100018)" if not args.config else
+                  f"{Path(cfg_path).stem} (D{ym['dim']} L{ym['n_layers']} E{ym['n_routed_experts']} "
+                  f"top{ym['n_activated_experts']} MTP{ym.get('mtp_depth', 0)} V{ym['vocab_size']}"
+                  f"{', routed experts sharded' if trainer.engine.shard_experts else ''})")
     dev = torch.device("cuda", local)
     dev_data = [make_inputs(vocab, micro, S, 1000 + 97 * rank + i, dev) for i in range(accum)]
     host_data = [make_inputs(vocab, micro, S, 5000 + 97 * rank + i, "pinned") for i in range(accum)]
@@ -237,7 +242,7 @@ def run_ours(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None if BASELINE_TOKENS_PER_S is None else round(value / BASELINE_TOKENS_PER_S, 4),
         "dtype": "bf16", "data": "synthetic uniform tokens, random-init weights",
-        "config": {"model": "deepseek-v3-lite-412m (yaml dims: D768 L18 E20 top4 kv192 MTP1 w0.3 V100018)",
+        "config": {"model": model_name,
                    "global_batch": args.global_seqs * S, "seq_len": S, "parallelism": f"dp{world}+ep{world}" if ep_on else f"dp{world}",
                    "micro_batch_seqs": micro, "grad_accum": accum,
                    "l2": "working set (weights+activations, GBs) far exceeds the 126 MB L2"},

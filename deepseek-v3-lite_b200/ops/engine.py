@@ -87,8 +87,19 @@ class TrainEngine:
         # all-gather, csrc/dp.cu); DSV3_DP_NCCL=1 selects NCCL all-reduce instead
         self._fused_dp = (dist_on and torch.distributed.get_world_size(dp_group) > 1
                           and os.environ.get("DSV3_DP_NCCL", "0") != "1")
+        # Routed experts sharded over the expert-parallel ranks: each rank
+        # keeps weights, gradients and optimizer state of its own experts only.
+        world0 = torch.distributed.get_world_size(dp_group) if dist_on else 1
+        rank0 = torch.distributed.get_rank(dp_group) if dist_on else 0
+        ep_size0 = int(getattr(config, "ep_size", 1))
+        self.shard_experts = (dist_on and world0 > 1 and ep_size0 != 1
+                              and bool(getattr(config, "ep_shard_experts", False)))
+        if self.shard_experts:
+            from parallel.ep import expert_range
+            self._exp_range = expert_range(rank0, c["n_routed_experts"], world0)
         self._build_flat(groups)
-        self.optimizer = FlatAdamW(groups, self.flats, lr=config.lr, betas=(config.beta1, config.beta2))
+        self.optimizer = FlatAdamW(groups, self.flats, lr=config.lr, betas=(config.beta1, config.beta2),
+                                   flat_groups=[0, 1, 0][:len(self.flats)])
         cos, sin = rope_cos_sin(self.max_seq_len, self.dr, float(c["rope_theta"]), self.device)
         self.cos, self.sin = cos, sin
         self.world_size = 1
@@ -137,12 +148,31 @@ class TrainEngine:
             if block:
                 blocks.append(block)
 
+        expert_blocks: List[List[torch.nn.Parameter]] = []
+        remote: List[torch.nn.Parameter] = []
         for layer in m.layers:
             # q and kv_a projections share their input: one [wq; wkv_a] block
             # makes them one GEMM (and one data-gradient, one weight-gradient)
             add([layer.attn.wq.weight, layer.attn.wkv_a.weight])
             ffn = layer.ffn
-            if hasattr(ffn, "experts"):
+            if hasattr(ffn, "experts") and self.shard_experts:
+                lo, hi = self._exp_range
+                local = list(ffn.experts[lo:hi])
+                expert_blocks.append([w for e in local for w in (e.w1.weight, e.w3.weight)])
+                expert_blocks.append([e.w2.weight for e in local])
+                for e in list(ffn.experts[:lo]) + list(ffn.experts[hi:]):
+                    for p in (e.w1.weight, e.w2.weight, e.w3.weight):
+                        # other ranks own these: drop the storage before the
+                        # flat buffers are allocated (lower peak memory)
+                        p.data = torch.empty(0, dtype=p.dtype, device=p.device)
+                        p.grad = None
+                        remote.append(p)
+                for p in [w for b in expert_blocks[-2:] for w in b] + remote:
+                    placed.add(id(p))
+                for e in ffn.shared_experts:
+                    add([e.w1.weight, e.w3.weight])
+                    add([e.w2.weight])
+            elif hasattr(ffn, "experts"):
                 add([w for e in ffn.experts for w in (e.w1.weight, e.w3.weight)])
                 add([e.w2.weight for e in ffn.experts])
                 for e in ffn.shared_experts:
@@ -158,7 +188,7 @@ class TrainEngine:
         for p in groups[0]["params"]:
             add([p])
         decay_ids = {id(p) for p in groups[0]["params"]}
-        if any(id(p) not in decay_ids for b in blocks for p in b):
+        if any(id(p) not in decay_ids for b in blocks + expert_blocks for p in b):
             raise RuntimeError("a packed block contains an undecayed parameter")
         nodecay_blocks = [[p] for p in groups[1]["params"]]
         alloc_d = alloc_n = None
@@ -172,9 +202,33 @@ class TrainEngine:
         self.flat_decay = FlatParams(blocks, self.device, alloc=alloc_d)
         self.flat_nodecay = FlatParams(nodecay_blocks, self.device, alloc=alloc_n)
         self.flats = [self.flat_decay, self.flat_nodecay]
+        self.flat_expert = None
+        if self.shard_experts:
+            # this rank's routed experts: local memory, never averaged over ranks
+            self.flat_expert = FlatParams(expert_blocks, self.device)
+            self.flat_expert.rank_local = True
+            self.flats.append(self.flat_expert)
+            self._remote_experts = remote
 
     def _fl(self, p) -> FlatParams:
-        return self.flat_decay if id(p) in self.flat_decay.offsets else self.flat_nodecay
+        if id(p) in self.flat_decay.offsets:
+            return self.flat_decay
+        if self.flat_expert is not None and id(p) in self.flat_expert.offsets:
+            return self.flat_expert
+        return self.flat_nodecay
+
+    def _local_experts(self, moe, ep):
+        """bf16 weights and fp32 gradient views of this rank's routed experts:
+        (w13 [Eloc, 2, I, D], w2 [Eloc, D, I], g13 [Eloc, 2I, D], g2 [Eloc, D, I])."""
+        E = moe.n_routed_experts
+        if self.shard_experts:
+            first = moe.experts[ep.lo]
+            n = ep.hi - ep.lo
+            return (self.swiglu_w13(first.w1.weight, n), self.stacked(first.w2.weight, n),
+                    self.swiglu_g13(first.w1.weight, n), self.stacked(first.w2.weight, n, grad=True))
+        w1, w2 = moe.experts[0].w1.weight, moe.experts[0].w2.weight
+        return (self.swiglu_w13(w1, E)[ep.lo:ep.hi], self.stacked(w2, E)[ep.lo:ep.hi],
+                self.swiglu_g13(w1, E)[ep.lo:ep.hi], self.stacked(w2, E, grad=True)[ep.lo:ep.hi])
 
     def w(self, p) -> torch.Tensor:
         """bf16 shadow of parameter ``p``."""
@@ -340,8 +394,7 @@ class TrainEngine:
         def shared_fwd():   # overlaps the dispatch (side stream, joined before the combine)
             for i, e in enumerate(moe.shared_experts):
                 shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
-        w13 = self.swiglu_w13(moe.experts[0].w1.weight, E)[ep.lo:ep.hi]
-        w2 = self.stacked(moe.experts[0].w2.weight, E)[ep.lo:ep.hi]
+        w13, w2, _, _ = self._local_experts(moe, ep)
         ectx = moe_forward_ep(ep, self._moe_slot[id(moe)], xn, idx, wts, counts, w13, w2, out, I,
                               overlap=shared_fwd if moe.shared_experts else None)
         return _Ctx(ep=ectx, idx=idx, wts=wts, ssel=ssel, shared=shared, Ep=Ep, counts=counts), out
@@ -356,10 +409,8 @@ class TrainEngine:
         def shared_bwd():   # overlaps the gradient dispatch (joined before dxn_acc is summed into)
             for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
                 self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
-        w1, w2 = moe.experts[0].w1.weight, moe.experts[0].w2.weight
-        dw = moe_backward_ep(ep, ctx.ep, dres_bf16, self.swiglu_w13(w1, E)[ep.lo:ep.hi],
-                             self.stacked(w2, E)[ep.lo:ep.hi], self.swiglu_g13(w1, E)[ep.lo:ep.hi],
-                             self.stacked(w2, E, grad=True)[ep.lo:ep.hi], dxn_acc, I,
+        w13, w2, g13, g2 = self._local_experts(moe, ep)
+        dw = moe_backward_ep(ep, ctx.ep, dres_bf16, w13, w2, g13, g2, dxn_acc, I,
                              overlap=shared_bwd if moe.shared_experts else None)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
 

@@ -115,17 +115,28 @@ class FlatAdamW(torch.optim.Optimizer):
     """AdamW (torch semantics) over ``FlatParams`` buffers with fused kernels.
 
     ``param_groups`` are the reference's two groups (decayed params with
-    ``dim >= 2``, the rest undecayed) in the reference's order; ``flats`` maps
-    each group to the ``FlatParams`` holding its parameters.
+    ``dim >= 2``, the rest undecayed) in the reference's order.  ``flats``
+    hold the parameters; ``flat_groups[i]`` is the param group whose
+    hyperparameters apply to ``flats[i]`` (default: flat i <-> group i).  A
+    parameter held by no flat (a routed expert owned by another rank when
+    experts are sharded) has no optimizer state here.
     """
 
-    def __init__(self, groups, flats: Sequence[FlatParams], lr: float, betas=(0.9, 0.95), eps: float = 1e-8):
+    def __init__(self, groups, flats: Sequence[FlatParams], lr: float, betas=(0.9, 0.95), eps: float = 1e-8,
+                 flat_groups: Optional[Sequence[int]] = None):
         super().__init__(groups, dict(lr=lr, betas=betas, eps=eps, weight_decay=0.0, amsgrad=False,
                                       maximize=False, foreach=None, capturable=False, differentiable=False,
                                       fused=None))
-        if len(flats) != len(self.param_groups):
-            raise ValueError("one FlatParams per param group")
         self.flats = list(flats)
+        if flat_groups is None:
+            if len(self.flats) != len(self.param_groups):
+                raise ValueError("one FlatParams per param group unless flat_groups is given")
+            flat_groups = list(range(len(self.flats)))
+        self.flat_groups = list(flat_groups)
+        self._flat_of = {}
+        for fi, f in enumerate(self.flats):
+            for p in f.params:
+                self._flat_of[id(p)] = fi
         dev = self.flats[0].master.device
         self.exp_avg = [torch.zeros_like(f.master) for f in self.flats]
         self.exp_avg_sq = [torch.zeros_like(f.master) for f in self.flats]
@@ -137,17 +148,21 @@ class FlatAdamW(torch.optim.Optimizer):
         self._bind_state()
 
     def _bind_state(self) -> None:
-        for gi, group in enumerate(self.param_groups):
-            f = self.flats[gi]
+        for group in self.param_groups:
             for p in group["params"]:
+                fi = self._flat_of.get(id(p))
+                if fi is None:
+                    self.state.pop(p, None)
+                    continue
+                f = self.flats[fi]
                 self.state[p] = {
                     "step": torch.tensor(float(self.step_count)),
-                    "exp_avg": f.view(self.exp_avg[gi], p),
-                    "exp_avg_sq": f.view(self.exp_avg_sq[gi], p),
+                    "exp_avg": f.view(self.exp_avg[fi], p),
+                    "exp_avg_sq": f.view(self.exp_avg_sq[fi], p),
                 }
 
     def compute_clip(self, max_norm: float, extra_sqsum: Optional[torch.Tensor] = None) -> None:
-        """Global grad norm over all groups (plus ``extra_sqsum`` from other
+        """Global grad norm over all flats (plus ``extra_sqsum`` from other
         ranks / shards) and the clip coefficient, on the device."""
         C = native()
         C.grad_sqsum([f.grad for f in self.flats], self._scratch, self.sqsum)
@@ -155,20 +170,31 @@ class FlatAdamW(torch.optim.Optimizer):
             self.sqsum.add_(extra_sqsum)
         C.clip_coef(self.sqsum, float(max_norm), self.grad_norm, self.clip)
 
+    def step_flat(self, fi: int, coef: Optional[torch.Tensor] = None) -> None:
+        """AdamW over flat ``fi`` (the step counter must already be advanced)."""
+        C = native()
+        f = self.flats[fi]
+        group = self.param_groups[self.flat_groups[fi]]
+        b1, b2 = group["betas"]
+        n_decay = f.numel if group["weight_decay"] > 0 else 0
+        C.adamw_flat(f.master, f.grad, self.exp_avg[fi], self.exp_avg_sq[fi], f.shadow, n_decay,
+                     float(group["lr"]), float(b1), float(b2), float(group["eps"]),
+                     float(group["weight_decay"]), self.step_count, self.clip if coef is None else coef)
+
+    def mark_step(self) -> None:
+        """Advance the per-parameter ``step`` entries to ``step_count``."""
+        for group in self.param_groups:
+            for p in group["params"]:
+                st = self.state.get(p)
+                if st is not None:
+                    st["step"].fill_(float(self.step_count))
+
     @torch.no_grad()
     def step(self, closure=None):
-        C = native()
         self.step_count += 1
-        for gi, group in enumerate(self.param_groups):
-            f = self.flats[gi]
-            b1, b2 = group["betas"]
-            n_decay = f.numel if group["weight_decay"] > 0 else 0
-            C.adamw_flat(f.master, f.grad, self.exp_avg[gi], self.exp_avg_sq[gi], f.shadow, n_decay,
-                         float(group["lr"]), float(b1), float(b2), float(group["eps"]),
-                         float(group["weight_decay"]), self.step_count, self.clip)
-        for gi, group in enumerate(self.param_groups):
-            for p in group["params"]:
-                self.state[p]["step"].fill_(float(self.step_count))
+        for fi in range(len(self.flats)):
+            self.step_flat(fi)
+        self.mark_step()
         return None
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -179,13 +205,14 @@ class FlatAdamW(torch.optim.Optimizer):
         """Load a torch-AdamW state dict, copying moments into the flat buffers."""
         super().load_state_dict(state_dict)
         steps = []
-        for gi, group in enumerate(self.param_groups):
-            f = self.flats[gi]
+        for group in self.param_groups:
             for p in group["params"]:
                 st = self.state.get(p, {})
-                if "exp_avg" in st:
-                    f.view(self.exp_avg[gi], p).copy_(st["exp_avg"].reshape(p.shape))
-                    f.view(self.exp_avg_sq[gi], p).copy_(st["exp_avg_sq"].reshape(p.shape))
+                fi = self._flat_of.get(id(p))
+                if "exp_avg" in st and fi is not None:
+                    f = self.flats[fi]
+                    f.view(self.exp_avg[fi], p).copy_(st["exp_avg"].reshape(p.shape))
+                    f.view(self.exp_avg_sq[fi], p).copy_(st["exp_avg_sq"].reshape(p.shape))
                     steps.append(int(float(st["step"])))
         if steps:
             self.step_count = max(steps)

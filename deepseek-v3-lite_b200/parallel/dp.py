@@ -24,20 +24,40 @@ class DataParallel:
         self.rank = dist.get_rank(group)
         self._broadcast_params()
 
+    def _replicated(self):
+        return [f for f in self.engine.flats if not getattr(f, "rank_local", False)]
+
+    def _rank_local(self):
+        return [f for f in self.engine.flats if getattr(f, "rank_local", False)]
+
     def _broadcast_params(self) -> None:
-        """Start every rank from rank 0's weights (and router biases)."""
-        for f in self.engine.flats:
+        """Start every rank from rank 0's weights (and router biases); a rank's
+        own routed experts (when sharded) are its own."""
+        for f in self._replicated():
             dist.broadcast(f.master, src=0, group=self.group)
             f.refresh_shadow()
         for moe in self.engine.model.moe_layers():
             dist.broadcast(moe.gate.bias, src=0, group=self.group)
 
     def reduce_gradients(self) -> None:
-        for f in self.engine.flats:
+        for f in self._replicated():
             dist.all_reduce(f.grad, op=dist.ReduceOp.AVG, group=self.group)
+        # a sharded expert's gradient is complete on its owner (every rank's
+        # tokens reached it); the data-parallel mean divides it by the ranks
+        for f in self._rank_local():
+            f.grad.mul_(1.0 / self.world_size)
 
     def extra_sqsum(self) -> Optional[torch.Tensor]:
-        return None
+        """Squared gradient norm of the other ranks' sharded experts."""
+        local = self._rank_local()
+        if not local:
+            return None
+        from ops._ext import native
+        t = torch.zeros(1, device=local[0].grad.device)
+        native().grad_sqsum([f.grad for f in local], torch.empty(1024 * len(local), device=t.device), t)
+        tot = t.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM, group=self.group)
+        return tot - t
 
     def after_step(self) -> None:
         return None
@@ -104,9 +124,10 @@ class FusedDataParallel(DataParallel):
         self.offs = [heap.dp_offs[0], heap.dp_offs[1]]
         self.budget_ns = int(float(os.environ.get("DSV3_DP_TIMEOUT_S", "60")) * 1e9)
         super().__init__(engine, group=group)
-        self.shards = [_shard(f.numel, self.rank, self.world_size) for f in engine.flats]
+        self.n_heap = len(self._replicated())   # the heap holds the replicated flats, first in engine.flats
+        self.shards = [_shard(f.numel, self.rank, self.world_size) for f in engine.flats[:self.n_heap]]
         self.flat_offs = [(heap.dp_offs[2 + 3 * i], heap.dp_offs[3 + 3 * i], heap.dp_offs[4 + 3 * i])
-                          for i in range(len(engine.flats))]
+                          for i in range(self.n_heap)]
         dev = engine.flats[0].master.device
         self.expect = torch.zeros(4 * 8, dtype=torch.int32, device=dev)
         self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -126,24 +147,34 @@ class FusedDataParallel(DataParallel):
         self.sq.zero_()
         for (lo, hi), (_, off_g, _) in zip(self.shards, self.flat_offs):
             C.dp_reduce(peers, offs, me, budget, off_g, lo, hi, 1.0 / self.world_size, self.sq)
+        local = self._rank_local()
+        if local:
+            # sharded experts: the owner's gradient / ranks, its norm joins the exchange
+            for f in local:
+                f.grad.mul_(1.0 / self.world_size)
+            t = torch.zeros(1, device=self.sq.device)
+            C.grad_sqsum([f.grad for f in local], torch.empty(1024 * len(local), device=t.device), t)
+            self.sq.add_(t)
         C.dp_norm(peers, offs, me, budget, self.sq, self.expect, float(max_norm), optimizer.grad_norm, optimizer.clip)
         optimizer.step_count += 1
-        for gi, group in enumerate(optimizer.param_groups):
-            f = optimizer.flats[gi]
-            lo, hi = self.shards[gi]
-            off_m, off_g, off_s = self.flat_offs[gi]
+        for fi in range(self.n_heap):
+            f = optimizer.flats[fi]
+            group = optimizer.param_groups[optimizer.flat_groups[fi]]
+            lo, hi = self.shards[fi]
+            off_m, off_g, off_s = self.flat_offs[fi]
             b1, b2 = group["betas"]
             n_decay = f.numel if group["weight_decay"] > 0 else 0
-            C.dp_update(peers, offs, me, budget, off_m, off_g, off_s, optimizer.exp_avg[gi], optimizer.exp_avg_sq[gi],
+            C.dp_update(peers, offs, me, budget, off_m, off_g, off_s, optimizer.exp_avg[fi], optimizer.exp_avg_sq[fi],
                         lo, hi, n_decay, float(group["lr"]), float(b1), float(b2), float(group["eps"]),
                         float(group["weight_decay"]), optimizer.step_count, optimizer.clip)
-            for p in group["params"]:
-                optimizer.state[p]["step"].fill_(float(optimizer.step_count))
+        for fi in range(self.n_heap, len(optimizer.flats)):
+            optimizer.step_flat(fi)            # this rank's experts: plain local AdamW
+        optimizer.mark_step()
         C.dp_barrier(peers, offs, me, budget, self.PH_GATHERED, self.expect)
 
     def gather_moments(self, optimizer) -> None:
         """Every rank's moment shards -> full moments on every rank (collective)."""
-        for gi, f in enumerate(optimizer.flats):
+        for gi, f in enumerate(optimizer.flats[:self.n_heap]):
             for buf in (optimizer.exp_avg[gi], optimizer.exp_avg_sq[gi]):
                 for r in range(self.world_size):
                     lo, hi = _shard(f.numel, r, self.world_size)

@@ -10,7 +10,10 @@ of the same layer over the tokens of all ranks.  Exits non-zero on mismatch.
 Run without torchrun it checks the single-rank path (the rank stores into its
 own heap through the same kernels).  ``--engine`` instead trains the same tiny
 model with experts spread over the ranks and with experts replicated and
-compares losses and averaged gradients.
+compares losses and averaged gradients.  ``--shard`` compares expert-parallel
+training with the routed experts' weights, gradients and optimizer state
+sharded over the ranks against the same training with them replicated: three
+optimizer steps on identical synthetic gradients, then one real step.
 """
 from __future__ import annotations
 
@@ -193,16 +196,118 @@ def run_engine(verbose=True) -> bool:
     return ok
 
 
+def run_shard(verbose=True) -> bool:
+    """Expert-parallel training with routed experts sharded over the ranks
+    (``ep_shard_experts``) vs replicated: identical weights, norms, losses."""
+    import copy
+    from models.mtp import MultiTokenPrediction
+    from models.transformer import Transformer
+    from ops.engine import TrainEngine
+    from parallel.dist import init_distributed
+    from parallel.ep import expert_range
+    from training.pretrain import TrainingConfig, _unique_params
+
+    rank, world, device = init_distributed(timeout_s=60)
+    torch.manual_seed(0)
+    base = Transformer(dict(ENGINE_CFG)).to(device)
+    for moe in base.moe_layers():
+        moe.gate.weight.data.mul_(40.0)
+    base_mtp = MultiTokenPrediction(dict(ENGINE_CFG), base).to(device)
+    ok = True
+
+    def engine(shard):
+        mtp = copy.deepcopy(base_mtp)
+        params = _unique_params(mtp)
+        names = {id(p): n for n, p in mtp.named_parameters()}
+        groups = [{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
+                  {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}]
+        eng = TrainEngine(mtp.main_model, mtp, TrainingConfig(lr=1e-3, ep_size=0, batch_size=4,
+                                                               ep_shard_experts=shard), groups)
+        assert eng.shard_experts == (shard and world > 1)
+        return eng, [(names[id(p)], p) for p in params]
+
+    def owned(eng, name):
+        """(is a routed expert, owned by this rank)"""
+        if ".experts." not in name:
+            return False, True
+        e = int(name.split(".experts.")[1].split(".")[0])
+        lo, hi = expert_range(rank, ENGINE_CFG["n_routed_experts"], world)
+        return True, lo <= e < hi
+
+    def masters(eng, params):
+        out = {}
+        for name, p in params:
+            is_exp, mine = owned(eng, name)
+            if mine:
+                out[name] = eng._fl(p).view(eng._fl(p).master, p).clone()
+        return out
+
+    # (a) synthetic gradients: replicated parameters get rank-specific values,
+    # a routed expert's gradient is its owner's (zero on the other ranks)
+    res = {}
+    for shard in (False, True):
+        eng, params = engine(shard)
+        for step in range(3):
+            for f in eng.flats:
+                f.grad.zero_()
+            for i, (name, p) in enumerate(params):
+                is_exp, mine = owned(eng, name)
+                if not mine:
+                    continue
+                gen = torch.Generator(device="cpu").manual_seed(100000 * step + 10 * i + (0 if is_exp else 1 + rank))
+                fl = eng._fl(p)
+                fl.view(fl.grad, p).copy_(torch.randn(p.shape, generator=gen) * 1e-2)
+            eng.clip_and_step(1.0 if step != 1 else 1e-3)
+        torch.cuda.synchronize()
+        eng.check()
+        res[shard] = (masters(eng, params), float(eng.optimizer.grad_norm))
+        eng.close()
+    (m0, n0), (m1, n1) = res[False], res[True]
+    worst = max((m0[k] - m1[k]).abs().max().item() for k in m1)
+    if verbose:
+        print(f"[rank {rank}] synthetic steps: max |replicated - sharded| {worst:.3e}, norms {n0:.6f} / {n1:.6f}",
+              flush=True)
+    if not (worst <= 1e-5 and abs(n0 - n1) <= 1e-5 * max(1.0, n0)):
+        ok = False
+
+    # (b) one real step from the same weights: same loss, norm and update
+    g = torch.Generator(device="cpu").manual_seed(7 + rank)
+    tok = torch.randint(0, ENGINE_CFG["vocab_size"], (4, 129), generator=g).to(device)
+    res = {}
+    for shard in (False, True):
+        eng, params = engine(shard)
+        out = eng.forward_backward(tok[:, :-1], tok[:, 1:], loss_scale=1.0)
+        eng.clip_and_step(1.0)
+        torch.cuda.synchronize()
+        eng.check()
+        res[shard] = (out["loss"].item(), float(eng.optimizer.grad_norm), masters(eng, params))
+        eng.close()
+    (l0, n0, m0), (l1, n1, m1) = res[False], res[True]
+    worst = max((m0[k] - m1[k]).abs().max().item() for k in m1)
+    if verbose:
+        print(f"[rank {rank}] real step: loss {l0:.6f} / {l1:.6f}, norm {n0:.6f} / {n1:.6f}, "
+              f"max weight difference {worst:.3e}", flush=True)
+    if not (abs(l0 - l1) <= 1e-5 * max(1.0, abs(l0)) and abs(n0 - n1) <= 1e-4 * max(1.0, n0) and worst <= 1e-5):
+        ok = False
+    return ok
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--engine", action="store_true", help="compare the training engine with and without EP")
+    ap.add_argument("--shard", action="store_true", help="compare sharded with replicated routed experts")
     ap.add_argument("--experts", type=int, default=8)
     ap.add_argument("--topk", type=int, default=2)
     ap.add_argument("--dim", type=int, default=256)
     ap.add_argument("--inter", type=int, default=128)
     ap.add_argument("--tokens", type=int, default=512)
     a = ap.parse_args()
-    ok = run_engine() if a.engine else run(a.experts, a.topk, a.dim, a.inter, a.tokens)
+    if a.shard:
+        ok = run_shard()
+    elif a.engine:
+        ok = run_engine()
+    else:
+        ok = run(a.experts, a.topk, a.dim, a.inter, a.tokens)
     import torch.distributed as dist
     if dist.is_initialized():
         flag = torch.tensor([1 if ok else 0], device="cuda")

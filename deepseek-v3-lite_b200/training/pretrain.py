@@ -101,6 +101,9 @@ class TrainingConfig:
     # Receive-buffer cap of expert parallelism as a multiple of the mean load
     # (0: exact worst case, never overflows).
     ep_capacity_factor: float = 0.0
+    # Shard routed-expert weights / gradients / optimizer state over the
+    # expert-parallel ranks (needed when the experts do not fit on one GPU).
+    ep_shard_experts: bool = False
 
 
 class PretrainDataset(Dataset):
@@ -201,7 +204,10 @@ class Pretrainer:
 
         self._log("Initialising model...")
         model_cfg = config.model_config.get("model", config.model_config)
-        raw = Transformer(config.model_config, use_checkpoint=config.grad_checkpoint).to(self.device)
+        # built on the training device directly: a 14B-parameter model in fp32
+        # would otherwise take 55 GB of host memory per rank
+        with torch.device(self.device):
+            raw = Transformer(config.model_config, use_checkpoint=config.grad_checkpoint)
         total, trainable = count_parameters(raw)
         self._log(f"Parameters: {total:,} total / {trainable:,} trainable")
         if config.log_per_component_params:
@@ -209,7 +215,8 @@ class Pretrainer:
         self.mtp_wrapper: Optional[MultiTokenPrediction] = None
         training_model: nn.Module = raw
         if model_cfg.get("mtp_depth", 0) > 0 and config.mtp_weight > 0.0:
-            self.mtp_wrapper = MultiTokenPrediction(config.model_config, raw).to(self.device)
+            with torch.device(self.device):
+                self.mtp_wrapper = MultiTokenPrediction(config.model_config, raw)
             total, trainable = count_parameters(self.mtp_wrapper)
             self._log(f"MTP enabled (depth={self.mtp_wrapper.depth}, weight={config.mtp_weight}): "
                       f"{total:,} total / {trainable:,} trainable")
@@ -402,6 +409,9 @@ class Pretrainer:
     # ----------------------------------------------------------- checkpoints
     def save_checkpoint(self, step: int, tag: str = "") -> None:
         """Write model (+MTP) weights, optimizer state and metadata for ``step``."""
+        if self.engine is not None and getattr(self.engine, "shard_experts", False):
+            raise NotImplementedError("checkpoints of expert-sharded training need the owners' experts gathered "
+                                      "first, which is not built yet; train with parallel.shard_experts: false")
         if self.engine is not None:
             self.engine.sync_to_modules()
         state = self.raw_model.state_dict()
@@ -540,6 +550,7 @@ def config_from_yaml(yaml_cfg: dict, data_path: Optional[str] = None, checkpoint
         seed=t.get("seed", 42),
         ep_size=int(yaml_cfg.get("parallel", {}).get("ep_size", 1)),
         ep_capacity_factor=float(yaml_cfg.get("parallel", {}).get("ep_capacity_factor", 0.0)),
+        ep_shard_experts=bool(yaml_cfg.get("parallel", {}).get("shard_experts", False)),
     )
 
 

@@ -70,3 +70,9 @@ def test_ep_two_ranks_layer():
 def test_ep_two_ranks_engine_matches_replicated_experts():
     r = _torchrun(["--engine"], 2)
     assert r.returncode == 0 and "EP_SELFTEST OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_ep_two_ranks_sharded_experts_match_replicated():
+    r = _torchrun(["--shard"], 2)
+    assert r.returncode == 0 and "EP_SELFTEST OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
