@@ -586,6 +586,15 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(dq_free);
     };
+    // L / delta of the next query tile are fetched into registers one tile
+    // ahead, so their global-load latency overlaps the current tile.
+    float nL = 0.f, nD = 0.f;
+    auto fetch_ld = [&](int it) {
+      const int q = (qstart + it) * 128 + kr;
+      nL = q < Sq ? __ldg(L + (size_t)bh * Sq + q) : 0.f;
+      nD = q < Sq ? __ldg(delta + (size_t)bh * Sq + q) : 0.f;
+    };
+    if (half == 0 && iters > 0) fetch_ld(0);
     bool ok = true;
     for (int it = 0; it < iters && ok; ++it) {
       const uint32_t ph = it & 1;
@@ -593,10 +602,10 @@ __global__ void __launch_bounds__(320, 1)
       float* Lb = sLD + (it & 1) * 256;
       float* Db = Lb + 128;
       if (half == 0) {
-        const int q = q0 + kr;
-        Lb[kr] = q < Sq ? L[(size_t)bh * Sq + q] : 0.f;
-        Db[kr] = q < Sq ? delta[(size_t)bh * Sq + q] : 0.f;
+        Lb[kr] = nL;
+        Db[kr] = nD;
         mbar_arrive(ld_ready);
+        if (it + 1 < iters) fetch_ld(it + 1);
       }
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(ld_ready, ph, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
         ok = false;
@@ -623,25 +632,31 @@ __global__ void __launch_bounds__(320, 1)
       }
       // keys >= lim[q] are masked: key <= q_off + q  <=>  q >= key - q_off
       const int qmin = causal ? key - q_off : -0x7fffffff;
+      // tiles fully inside the sequences and the causal band skip the per-element mask
+      const bool all_valid = q0 + 128 <= Sq && key < Sk && q0 + half * 64 >= qmin;
       uint8_t* prow = smem + C::OFF_P + half * 16384 + kr * 128;
       uint8_t* dsrow = smem + C::OFF_DS + half * 16384 + kr * 128;
+      const float4* L4 = reinterpret_cast<const float4*>(Lb + half * 64);
+      const float4* D4 = reinterpret_cast<const float4*>(Db + half * 64);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t pk[4], dk[4];
+        const float4 la = L4[2 * c], lb = L4[2 * c + 1], da = D4[2 * c], db = D4[2 * c + 1];
+        const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+        const float dl[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float pv[2], dv2[2];
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int col = c * 8 + 2 * e + u;           // within this half
-            const int qi = half * 64 + col;
-            const int q = q0 + qi;
-            const bool valid = q < Sq && key < Sk && q >= qmin;
+            const int q = q0 + half * 64 + col;
             const float s = __uint_as_float(sr[col >> 4][col & 15]);
             const float dp = __uint_as_float(dr[col >> 4][col & 15]);
-            const float p = valid ? ex2_approx(s * scale_log2 - Lb[qi]) : 0.f;
+            float p = ex2_approx(s * scale_log2 - lv[2 * e + u]);
+            if (!all_valid && !(q < Sq && key < Sk && q >= qmin)) p = 0.f;
             pv[u] = p;
-            dv2[u] = p * (dp - Db[qi]);
+            dv2[u] = p * (dp - dl[2 * e + u]);
           }
           pk[e] = pack_bf16x2(pv[0], pv[1]);
           dk[e] = pack_bf16x2(dv2[0], dv2[1]);

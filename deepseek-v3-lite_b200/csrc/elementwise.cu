@@ -389,8 +389,14 @@ __global__ void rmsnorm_bwd_v(const TDy* __restrict__ dy, long lddy, const TIn* 
   }
   for (int row = r0 + wid; row < r1; row += warps) {
     const float r = rstd[row];
-    float2 xh[PAIRS], g[PAIRS];
+    float2 xh[PAIRS], g[PAIRS], av[PAIRS];
     float dot = 0.f;
+    if (dx_acc) {
+      // the accumulator is read with x and dy: one memory round trip per row
+#pragma unroll
+      for (int i = 0; i < PAIRS; ++i)
+        av[i] = *reinterpret_cast<const float2*>(dx_acc + (size_t)row * ldacc + 2 * (lane + 32 * i));
+    }
 #pragma unroll
     for (int i = 0; i < PAIRS; ++i) {
       const int c = 2 * (lane + 32 * i);
@@ -409,7 +415,7 @@ __global__ void rmsnorm_bwd_v(const TDy* __restrict__ dy, long lddy, const TIn* 
       const float d0 = r * (g[i].x - xh[i].x * dot), d1 = r * (g[i].y - xh[i].y * dot);
       if (dx_acc) {
         float2* p = reinterpret_cast<float2*>(dx_acc + (size_t)row * ldacc + c);
-        float2 sv = *p;
+        float2 sv = av[i];
         sv.x += d0;
         sv.y += d1;
         *p = sv;

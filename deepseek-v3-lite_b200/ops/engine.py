@@ -98,6 +98,9 @@ class TrainEngine:
             from parallel.ep import expert_range
             self._exp_range = expert_range(rank0, c["n_routed_experts"], world0)
         self._build_flat(groups)
+        if self.shard_experts:
+            ids = {id(p) for p in self.flat_expert.params}
+            self._local_expert_named = [(n, p) for n, p in model.named_parameters() if id(p) in ids]
         self.optimizer = FlatAdamW(groups, self.flats, lr=config.lr, betas=(config.beta1, config.beta2),
                                    flat_groups=[0, 1, 0][:len(self.flats)])
         cos, sin = rope_cos_sin(self.max_seq_len, self.dr, float(c["rope_theta"]), self.device)
@@ -798,6 +801,32 @@ class TrainEngine:
         for f in self.flats:
             f.pull_from_params()
         self.optimizer._bind_state()
+
+    def expert_shard_state(self) -> Dict[str, torch.Tensor]:
+        """This rank's routed experts (sharded training): fp32 weights under
+        their state-dict names and AdamW moments under ``exp_avg.`` /
+        ``exp_avg_sq.`` prefixes, as views into the flat buffers."""
+        f, opt = self.flat_expert, self.optimizer
+        fi = self.flats.index(f)
+        out: Dict[str, torch.Tensor] = {}
+        for n, p in self._local_expert_named:
+            out[n] = f.view(f.master, p)
+            out["exp_avg." + n] = f.view(opt.exp_avg[fi], p)
+            out["exp_avg_sq." + n] = f.view(opt.exp_avg_sq[fi], p)
+        return out
+
+    def load_expert_shard_state(self, tensors: Dict[str, torch.Tensor]) -> None:
+        """Inverse of ``expert_shard_state`` (the shard must cover exactly
+        this rank's experts)."""
+        mine = self.expert_shard_state()
+        missing = [k for k in mine if k not in tensors]
+        extra = [k for k in tensors if k not in mine]
+        if missing or extra:
+            raise RuntimeError(f"expert shard does not match this rank's experts: {len(missing)} missing "
+                               f"({missing[:3]}), {len(extra)} unexpected ({extra[:3]})")
+        for k, dst in mine.items():
+            dst.copy_(tensors[k].reshape(dst.shape))
+        self.flat_expert.refresh_shadow()
 
     def optimizer_state_for_checkpoint(self) -> dict:
         """torch-AdamW state dict with standalone tensors (reference layout)."""

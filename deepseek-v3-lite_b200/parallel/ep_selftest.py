@@ -289,6 +289,43 @@ def run_shard(verbose=True) -> bool:
               f"max weight difference {worst:.3e}", flush=True)
     if not (abs(l0 - l1) <= 1e-5 * max(1.0, abs(l0)) and abs(n0 - n1) <= 1e-4 * max(1.0, n0) and worst <= 1e-5):
         ok = False
+
+    # (c) checkpoint round trip through the trainer: per-rank expert shards,
+    # then a fresh trainer resumes and repeats the next step exactly
+    import shutil
+    import tempfile
+    import torch.distributed as dist
+    from training.pretrain import Pretrainer
+    box = [tempfile.mkdtemp(prefix="dsv3_shard_ckpt_") if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    ckdir = box[0]
+
+    def trainer():
+        cfg = TrainingConfig(model_config=dict(ENGINE_CFG), checkpoint_dir=ckdir, vocab_size=ENGINE_CFG["vocab_size"],
+                             max_seq_len=128, batch_size=4, gradient_accumulation_steps=1, warmup_steps=2,
+                             lr=1e-3, mtp_weight=0.3, grad_checkpoint=False, compile_model=False,
+                             log_per_component_params=False, ep_size=0, ep_shard_experts=True)
+        return Pretrainer(cfg)
+
+    toks = [torch.randint(0, ENGINE_CFG["vocab_size"], (4, 129), generator=g).to(device) for _ in range(3)]
+    tr = trainer()
+    for i in range(2):
+        tr.train_step(toks[i][:, :-1], toks[i][:, 1:], i)
+    tr.save_checkpoint(2)
+    want = float(tr.train_step(toks[2][:, :-1], toks[2][:, 1:], 2)["loss"])
+    tr.engine.close()
+    tr2 = trainer()
+    tr2.load_checkpoint(2)
+    got = float(tr2.train_step(toks[2][:, :-1], toks[2][:, 1:], 2)["loss"])
+    tr2.engine.close()
+    shards = sorted(p.name for p in __import__("pathlib").Path(ckdir).glob("experts_step_2_*"))
+    if verbose:
+        print(f"[rank {rank}] resume: loss {want:.6f} before / {got:.6f} after; shard files {shards}", flush=True)
+    if not (abs(want - got) <= 1e-5 * max(1.0, abs(want)) and len(shards) == world):
+        ok = False
+    dist.barrier()
+    if rank == 0:
+        shutil.rmtree(ckdir, ignore_errors=True)
     return ok
 
 

@@ -409,9 +409,7 @@ class Pretrainer:
     # ----------------------------------------------------------- checkpoints
     def save_checkpoint(self, step: int, tag: str = "") -> None:
         """Write model (+MTP) weights, optimizer state and metadata for ``step``."""
-        if self.engine is not None and getattr(self.engine, "shard_experts", False):
-            raise NotImplementedError("checkpoints of expert-sharded training need the owners' experts gathered "
-                                      "first, which is not built yet; train with parallel.shard_experts: false")
+        sharded = self.engine is not None and getattr(self.engine, "shard_experts", False)
         if self.engine is not None:
             self.engine.sync_to_modules()
         state = self.raw_model.state_dict()
@@ -424,6 +422,19 @@ class Pretrainer:
                 "tag": tag or f"step_{step}", "config": asdict(self.config),
                 "has_mtp": self.mtp_wrapper is not None}
         opt_state = self.engine.optimizer_state_for_checkpoint() if self.engine is not None else None
+        if sharded:
+            # routed experts: one file per owner, written before rank 0's
+            # metadata makes the step visible
+            eng = self.engine
+            state = {k: v for k, v in state.items() if ".experts." not in k}
+            expert_ids = {id(p) for n, p in self.raw_model.named_parameters() if ".experts." in n}
+            order = [p for g in self.optimizer.param_groups for p in g["params"]]
+            for i, p in enumerate(order):
+                if id(p) in expert_ids:
+                    opt_state["state"].pop(i, None)
+            meta["expert_shards"] = eng.world_size
+            self.ckpt_manager.save_expert_shard(step, eng.rank, eng.world_size, eng.expert_shard_state())
+            torch.distributed.barrier(group=eng.dp.group)
         if int(os.environ.get("RANK", "0")) == 0:
             self.ckpt_manager.save(self.raw_model, self.optimizer, step, extra_meta=meta, state_dict=state,
                                    optimizer_state=opt_state)
@@ -432,8 +443,17 @@ class Pretrainer:
     def load_checkpoint(self, step: int) -> int:
         """Restore ``step`` (weights, optimizer, MTP, scheduler, opt-step count)."""
         from safetensors.torch import load_file
+        sharded = self.engine is not None and getattr(self.engine, "shard_experts", False)
         meta = self.ckpt_manager.load(self.raw_model, step, device=str(self.device), optimizer=self.optimizer,
-                                      strict=False)
+                                      strict=False, merge_expert_shards=not sharded)
+        if sharded:
+            eng = self.engine
+            saved = int(meta.get("expert_shards", 0) or 0)
+            if saved != eng.world_size:
+                raise RuntimeError(f"step {step} holds {saved} expert shards; resume with {saved} ranks "
+                                   f"(or load it unsharded, which merges the shards' weights)")
+            eng.load_expert_shard_state(self.ckpt_manager.load_expert_shard(step, eng.rank, saved,
+                                                                            device=str(self.device)))
         if self.mtp_wrapper is not None and meta.get("has_mtp", False):
             wpath = self.ckpt_manager.save_dir / f"model_step_{step}.safetensors"
             if wpath.exists():

@@ -12,6 +12,14 @@ One checkpoint is three files in ``save_dir`` (reference
 Each file is written to a temporary file in the same directory and moved into
 place with ``os.replace``, so a crash leaves either the old file or none.  A
 step counts as present only when all three files exist.
+
+Training with routed experts sharded over the ranks adds one file per rank,
+``experts_step_N_rankRofW.safetensors``: that rank's routed-expert weights
+under their state-dict names plus their AdamW moments under ``exp_avg.`` /
+``exp_avg_sq.`` prefixes; the model file then holds everything else and the
+metadata records ``"expert_shards": W``.  Such a step counts as present only
+when all W shard files exist too.  Loading into an unsharded model merges the
+shards' weights (``merge_expert_shards``).
 """
 from __future__ import annotations
 
@@ -29,6 +37,8 @@ from safetensors.torch import load_file, save_file
 log = logging.getLogger(__name__)
 
 _FILES = ("model_step_{}.safetensors", "optim_step_{}.pt", "meta_step_{}.json")
+_SHARD = "experts_step_{}_rank{}of{}.safetensors"
+_MOMENT_PREFIXES = ("exp_avg.", "exp_avg_sq.")
 
 
 class CheckpointManager:
@@ -50,8 +60,21 @@ class CheckpointManager:
                 steps.append(int(tail))
         return steps
 
+    def expert_shard_path(self, step: int, rank: int, world: int) -> Path:
+        return self.save_dir / _SHARD.format(step, rank, world)
+
+    def _meta(self, step: int) -> dict:
+        try:
+            with open(self._path(2, step)) as f:
+                return json.load(f)
+        except (OSError, ValueError):
+            return {}
+
     def _checkpoint_complete(self, step: int) -> bool:
-        return all(self._path(i, step).exists() for i in range(3))
+        if not all(self._path(i, step).exists() for i in range(3)):
+            return False
+        w = int(self._meta(step).get("expert_shards", 0) or 0)
+        return all(self.expert_shard_path(step, r, w).exists() for r in range(w))
 
     def latest_step(self) -> Optional[int]:
         """Newest step whose three files all exist, or ``None``."""
@@ -112,18 +135,46 @@ class CheckpointManager:
         self._atomic_save_json({"step": step, **meta}, self._path(2, step))
         log.info("[checkpoint] saved step %d -> %s", step, self.save_dir)
 
+    def save_expert_shard(self, step: int, rank: int, world: int, tensors: Dict[str, torch.Tensor]) -> None:
+        """Write one rank's routed experts (weights and prefixed moments).
+        Every entry is copied to host memory first (the device tensors are
+        views into flat buffers)."""
+        host = {k: v.detach().to("cpu", copy=True).contiguous() for k, v in tensors.items()}
+        with self._atomic_write(self.expert_shard_path(step, rank, world), ".safetensors.tmp") as tmp:
+            save_file(host, tmp)
+
+    def load_expert_shard(self, step: int, rank: int, world: int, device: str = "cpu") -> Dict[str, torch.Tensor]:
+        path = self.expert_shard_path(step, rank, world)
+        if not path.exists():
+            raise FileNotFoundError(f"expert shard not found: {path}")
+        return load_file(str(path), device=str(device))
+
+    def expert_shard_weights(self, step: int, device: str = "cpu") -> Dict[str, torch.Tensor]:
+        """The routed-expert weights of every shard of ``step`` (no moments)."""
+        w = int(self._meta(step).get("expert_shards", 0) or 0)
+        out: Dict[str, torch.Tensor] = {}
+        for r in range(w):
+            for k, v in self.load_expert_shard(step, r, w, device).items():
+                if not k.startswith(_MOMENT_PREFIXES):
+                    out[k] = v
+        return out
+
     # ------------------------------------------------------------------- load
     def load(self, model: torch.nn.Module, step: int, device: str = "cuda", optimizer=None,
-             strict: bool = True) -> dict:
+             strict: bool = True, merge_expert_shards: bool = True) -> dict:
         """Restore ``step`` into ``model`` (and ``optimizer``); return the metadata.
 
         With ``strict`` a missing or unexpected key raises ``RuntimeError``;
-        otherwise it is logged.
+        otherwise it is logged.  A step saved with sharded experts has its
+        shards' weights merged in unless ``merge_expert_shards`` is false (a
+        sharded run loads its own shard instead).
         """
         wpath = self._path(0, step)
         if not wpath.exists():
             raise FileNotFoundError(f"Checkpoint not found: {wpath}\nAvailable steps: {sorted(self._list_steps())}")
         weights = load_file(str(wpath), device=str(device))
+        if merge_expert_shards:
+            weights.update(self.expert_shard_weights(step, device=str(device)))
         missing, unexpected = model.load_state_dict(weights, strict=False)
         for what, keys in (("missing", missing), ("unexpected", unexpected)):
             if not keys:

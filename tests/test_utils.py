@@ -51,6 +51,36 @@ class TestCheckpointManager:
         assert m2.head.weight.data_ptr() == m2.embed.weight.data_ptr()
         assert torch.equal(m2.head.weight, m.head.weight)
 
+    def test_expert_shards_merge_and_completeness(self, small_cfg, tmp_dir):
+        """A step saved with routed experts sharded over two ranks: the model
+        file without them, one shard file per rank; the step is complete only
+        with every shard, and an unsharded load merges the shards' weights."""
+        m = Transformer(small_cfg)
+        full = m.state_dict()
+        experts = {k: v for k, v in full.items() if ".experts." in k}
+        assert experts, "the test config needs routed experts"
+        mgr = CheckpointManager(str(tmp_dir))
+        E = small_cfg["n_routed_experts"]
+        for r in range(2):
+            lo, hi = r * E // 2, (r + 1) * E // 2
+            mine = {k: v for k, v in experts.items() if lo <= int(k.split(".experts.")[1].split(".")[0]) < hi}
+            shard = dict(mine)
+            shard.update({"exp_avg." + k: torch.zeros_like(v) for k, v in mine.items()})
+            shard.update({"exp_avg_sq." + k: torch.ones_like(v) for k, v in mine.items()})
+            mgr.save_expert_shard(7, r, 2, shard)
+        mgr.save(m, _opt(m), 7, extra_meta={"expert_shards": 2},
+                 state_dict={k: v for k, v in full.items() if k not in experts})
+        assert mgr.latest_step() == 7
+        m2 = Transformer(small_cfg)
+        mgr.load(m2, 7, device="cpu", strict=False)   # tied head.weight is written once
+        for k, v in m2.state_dict().items():
+            assert torch.equal(v, full[k]), k
+        back = mgr.load_expert_shard(7, 1, 2)
+        assert all(torch.equal(back["exp_avg_sq." + k], torch.ones_like(experts[k]))
+                   for k in back if not k.startswith("exp_avg"))
+        os.remove(mgr.expert_shard_path(7, 1, 2))
+        assert mgr.latest_step() is None
+
     def test_crash_leaves_no_temp(self, small_cfg, tmp_dir):
         m = Transformer(small_cfg)
         mgr = CheckpointManager(str(tmp_dir))
