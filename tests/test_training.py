@@ -171,3 +171,29 @@ def test_step_diagnostics_report_expert_load(small_cfg, tmp_dir):
     assert all(sum(c) == 2 * 32 * small_cfg["n_activated_experts"] for c in hist.values())
     d = tr.step_diagnostics()
     assert d["expert_load_max_over_mean"] >= 1.0
+
+
+def test_small_shard_builder_feeds_pretrain_dataset(tmp_path):
+    """Synthetic source + byte tokenizer -> shard_0000.bin (uint32), read by
+    PretrainDataset; the synthetic source is identical run to run."""
+    from data.build_small_shard import build_shard, open_source, open_tokenizer, synthetic_documents
+    from training.pretrain import PretrainDataset
+    encode, eos, vocab = open_tokenizer("bytes")
+    path = build_shard(str(tmp_path), open_source("synthetic"), encode, eos, target_tokens=5000)
+    t = torch.load(path, weights_only=True)
+    assert t.dtype == torch.uint32 and t.numel() == 5000 and int(t.long().max()) <= eos
+    assert list(synthetic_documents(3)) == list(synthetic_documents(3))
+    ds = PretrainDataset(str(tmp_path), max_seq_len=64, vocab_size=vocab)
+    x, y = ds[3]
+    x, y = x.long(), y.long()
+    assert len(ds) == (5000 - 1) // 64 and x.shape == (64,) and torch.equal(x[1:], y[:-1])
+
+
+def test_prepare_data_without_external_pipeline(tmp_path):
+    import yaml
+    from data import prepare_data
+    out = tmp_path / "data_config.yaml"
+    rc = prepare_data.main(["--config-out", str(out)])
+    cfg = yaml.safe_load(out.read_text())
+    assert rc == 2 and cfg["pipeline"]["tokenizer"]["vocab_size"] == 100_018
+    assert cfg["pipeline"]["tokenizer"]["eos_token_id"] == 100_017
