@@ -137,3 +137,70 @@ class TestMemory:
     def test_sharded_estimate_shrinks(self, small_cfg):
         m = Transformer(small_cfg)
         assert memory.estimate_sharded_training_gb(m, 64, 2, 4, 4) < memory.estimate_sharded_training_gb(m, 64, 2)
+
+
+def test_consolidate_sharded_experts(small_cfg, tmp_dir):
+    """A checkpoint saved with routed experts sharded over two ranks (model
+    and optimizer files without experts, one shard file per rank) merges back
+    into the plain checkpoint an unsharded trainer writes: same weights, same
+    optimizer state at the single-process parameter indices."""
+    from dataclasses import asdict
+    from models.mtp import MultiTokenPrediction
+    from training.consolidate import consolidate, optimizer_index
+    from training.pretrain import TrainingConfig, _unique_params
+    from safetensors.torch import load_file
+
+    torch.manual_seed(0)
+    raw = Transformer(small_cfg)
+    wrap = MultiTokenPrediction(small_cfg, raw)
+    params = _unique_params(wrap)
+    opt = torch.optim.AdamW([{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
+                             {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}], lr=1e-3)
+    for p in params:
+        p.grad = torch.randn_like(p)
+    opt.step()
+    full = {k: v for k, v in raw.state_dict().items() if k != "head.weight"}
+    full.update({"mtp." + k: v for k, v in wrap.state_dict().items() if k.startswith("mtp_modules.")})
+    full_opt = opt.state_dict()
+    index = optimizer_index(small_cfg, has_mtp=True)
+    assert sorted(index.values()) == list(range(len(params)))
+
+    # what the sharded trainer writes (two ranks, two experts each)
+    mgr = CheckpointManager(str(tmp_dir / "sharded"))
+    E = small_cfg["n_routed_experts"]
+    experts = [k for k in full if ".experts." in k]
+    for r in range(2):
+        lo, hi = r * E // 2, (r + 1) * E // 2
+        shard = {}
+        for k in experts:
+            if lo <= int(k.split(".experts.")[1].split(".")[0]) < hi:
+                st = full_opt["state"][index[k]]
+                shard.update({k: full[k], "exp_avg." + k: st["exp_avg"], "exp_avg_sq." + k: st["exp_avg_sq"]})
+        mgr.save_expert_shard(4, r, 2, shard)
+    opt_sharded = {"state": {i: v for i, v in full_opt["state"].items() if i not in {index[k] for k in experts}},
+                   "param_groups": full_opt["param_groups"]}
+    meta = {"expert_shards": 2, "has_mtp": True, "config": asdict(TrainingConfig(model_config=dict(small_cfg)))}
+    mgr.save(raw, opt, 4, extra_meta=meta, state_dict={k: v for k, v in full.items() if k not in experts},
+             optimizer_state=opt_sharded)
+
+    assert consolidate(str(tmp_dir / "sharded"), str(tmp_dir / "plain")) == 4
+    plain = CheckpointManager(str(tmp_dir / "plain"))
+    assert plain.latest_step() == 4
+    w = load_file(str(tmp_dir / "plain" / "model_step_4.safetensors"))
+    written = CheckpointManager._unique_storage(full)   # tied tensors are written once
+    assert w.keys() == written.keys() and all(torch.equal(w[k], written[k]) for k in written)
+    got = torch.load(tmp_dir / "plain" / "optim_step_4.pt", weights_only=True)
+    assert got["state"].keys() == full_opt["state"].keys()
+    for i, st in full_opt["state"].items():
+        for name in ("exp_avg", "exp_avg_sq", "step"):
+            assert torch.equal(got["state"][i][name], st[name]), (i, name)
+    # a fresh single-process model and optimizer load it
+    raw2 = Transformer(small_cfg)
+    wrap2 = MultiTokenPrediction(small_cfg, raw2)
+    p2 = _unique_params(wrap2)
+    opt2 = torch.optim.AdamW([{"params": [p for p in p2 if p.dim() >= 2], "weight_decay": 0.1},
+                              {"params": [p for p in p2 if p.dim() < 2], "weight_decay": 0.0}], lr=1e-3)
+    plain.load(raw2, 4, device="cpu", optimizer=opt2, strict=False)
+    assert torch.equal(raw2.layers[1].ffn.experts[3].w2.weight, raw.layers[1].ffn.experts[3].w2.weight)
+    with pytest.raises(ValueError):
+        consolidate(str(tmp_dir / "plain"), str(tmp_dir / "again"))
