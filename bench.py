@@ -37,7 +37,7 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-BASELINE_TOKENS_PER_S = None  # the reference publishes no measured number
+BASELINE_TOKENS_PER_S = None  # the reference publishes no measured tokens/s for this config
 METRIC = "train tokens/sec (device, max over ranks)"
 GLOBAL_SEQS = 256
 
