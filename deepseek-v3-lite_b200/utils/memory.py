@@ -92,9 +92,13 @@ def assert_fits_in_available_gpu(estimate_gb: float, safety_margin_gb: float = 0
 
 
 def estimate_sharded_training_gb(model: nn.Module, seq_len: int, batch_size: int, ep_size: int = 1,
-                                 dp_size: int = 1, overhead_gb: float = 2.0) -> float:
-    """Per-rank training memory with routed experts split over ``ep_size`` ranks
-    and fp32 optimizer state split over ``dp_size`` ranks (ZeRO-1 style)."""
+                                 dp_size: int = 1, overhead_gb: float = 2.0, moments_sharded: bool = False) -> float:
+    """Per-rank training memory with routed experts (weights, gradients and
+    AdamW moments) split over ``ep_size`` ranks, as ``parallel.shard_experts``
+    trains.  The moments of the replicated parameters are full-size on every
+    rank, as the peer-memory data-parallel step keeps them; with
+    ``moments_sharded`` they are counted split over ``dp_size`` ranks instead
+    (ZeRO-1 style)."""
     expert_params, dense_params, seen = 0, 0, set()
     for name, p in model.named_parameters():
         if id(p) in seen:
@@ -107,7 +111,8 @@ def estimate_sharded_training_gb(model: nn.Module, seq_len: int, batch_size: int
     local = dense_params + expert_params / max(1, ep_size)
     # fp32 master + fp32 grad + bf16 shadow per local parameter; moments sharded.
     param_bytes = local * (4 + 4 + 2)
-    moment_bytes = 8 * (dense_params / max(1, dp_size) + expert_params / max(1, ep_size))
+    dense_moment_share = dense_params / max(1, dp_size) if moments_sharded else dense_params
+    moment_bytes = 8 * (dense_moment_share + expert_params / max(1, ep_size))
     dim, n_layers = _infer_dim_n_layers(model)
     act = _activation_bytes(seq_len, batch_size, dim, n_layers, False)
     return (param_bytes + moment_bytes + act) / 1024 ** 3 + overhead_gb

@@ -204,3 +204,21 @@ def test_consolidate_sharded_experts(small_cfg, tmp_dir):
     assert torch.equal(raw2.layers[1].ffn.experts[3].w2.weight, raw.layers[1].ffn.experts[3].w2.weight)
     with pytest.raises(ValueError):
         consolidate(str(tmp_dir / "plain"), str(tmp_dir / "again"))
+
+
+def test_scaled_config_fits_only_with_sharded_experts():
+    """The 14B scaled config (instantiated on the meta device): ~12.7B routed
+    expert parameters; one B200 (180 GB) cannot hold it with AdamW state when
+    experts are replicated, eight ranks with sharded experts can."""
+    import yaml
+    from pathlib import Path
+    cfg = yaml.safe_load(open(Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200" / "configs"
+                              / "scaled_13b.yaml"))
+    with torch.device("meta"):
+        m = Transformer(cfg["model"])
+    experts = sum(p.numel() for n, p in m.named_parameters() if ".experts." in n)
+    total = sum(p.numel() for p in m.parameters())
+    assert 12.5e9 < experts < 13.0e9 and 13.5e9 < total < 14.2e9
+    S, B = cfg["model"]["max_seq_len"], cfg["training"]["micro_batch_size"]
+    assert memory.estimate_sharded_training_gb(m, S, B, ep_size=1, dp_size=8) > 180
+    assert memory.estimate_sharded_training_gb(m, S, B, ep_size=8, dp_size=8) < 120
