@@ -84,8 +84,10 @@ class DeepSeekMoE(nn.Module):
         self.n_shared_experts = config["n_shared_experts"]
         self.moe_inter_dim = config["moe_inter_dim"]
         self.topk = config["n_activated_experts"]
-        dispatch = config.get("moe_dispatch", "stacked")
-        self.moe_dispatch = "grouped" if dispatch == "triton_grouped" else dispatch
+        # the configured value, as the reference keeps it; every accepted value
+        # runs the same native grouped kernels on CUDA and the same PyTorch
+        # math on the CPU
+        self.moe_dispatch = config.get("moe_dispatch", "stacked")
         self.gate = AuxLossFreeGate(config)
         self.experts = nn.ModuleList(Expert(self.dim, self.moe_inter_dim) for _ in range(self.n_routed_experts))
         self.shared_experts = nn.ModuleList(Expert(self.dim, self.moe_inter_dim) for _ in range(self.n_shared_experts))

@@ -304,3 +304,30 @@ def test_count_parameters_dedups(small_cfg):
     assert total == trainable == sum(p.numel() for p in set(m.parameters()))
     untied, _ = count_parameters(Transformer({**small_cfg, "weight_tying": False}))
     assert untied - total == small_cfg["vocab_size"] * small_cfg["dim"]
+
+
+def test_triton_module_import_surface():
+    """The reference's Triton module paths import here: CPU oracles work, the
+    Triton entry points raise ImportError (this build has no Triton kernels),
+    and the configured dispatch value is kept on the module."""
+    import torch.nn.functional as F
+    from models import mla_triton, moe_triton
+    from models.moe import DeepSeekMoE
+    assert mla_triton.HAS_TRITON is False and moe_triton.HAS_TRITON is False
+    with pytest.raises(ImportError, match="triton"):
+        moe_triton.triton_grouped_moe_dispatch()
+    with pytest.raises(ImportError, match="triton"):
+        mla_triton.triton_mla_attention()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(10, 8, generator=g)
+    w1, w3 = torch.randn(3, 6, 8, generator=g), torch.randn(3, 6, 8, generator=g)
+    w2 = torch.randn(3, 8, 6, generator=g)
+    off = torch.tensor([0, 4, 4, 10])
+    gw = torch.rand(10, generator=g)
+    y = moe_triton.grouped_moe_pytorch(x, w1, w2, w3, off, gw)
+    e = [0] * 4 + [2] * 6
+    want = torch.stack([(F.silu(w1[k] @ x[i]) * (w3[k] @ x[i])) @ w2[k].t() * gw[i] for i, k in enumerate(e)])
+    assert torch.allclose(y, want, atol=1e-5)
+    cfg = {"dim": 16, "n_routed_experts": 4, "n_shared_experts": 1, "moe_inter_dim": 8, "n_activated_experts": 2,
+           "moe_dispatch": "triton_grouped"}
+    assert DeepSeekMoE(cfg).moe_dispatch == "triton_grouped"
