@@ -259,6 +259,12 @@ def run_reference(args, rank, world, local):
     ref_root = ROOT / "baseline" / "_ref"
     if not (ref_root / "training" / "pretrain.py").exists():
         return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    default_cfg = ROOT / "deepseek-v3-lite_b200" / "configs" / "pretrain_412m.yaml"
+    if args.config and Path(args.config).resolve() != default_cfg.resolve():
+        # the reference arm runs the reference's own 412M yaml only; it has no
+        # multi-GPU code and no expert sharding for the scaled model
+        return {"impl": "reference", "unavailable": f"the reference arm runs the 412M config only, not {args.config} "
+                                                    "(single-device reference, no expert sharding)"}
     sys.path.insert(0, str(ref_root))
     # The reference's stock mode (max-autotune) wraps its graphs in CUDA graphs
     # and then fails ("accessing tensor output of CUDAGraphs that has been
