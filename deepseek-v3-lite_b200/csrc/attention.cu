@@ -519,26 +519,28 @@ void run_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// Wide-head backward (qk 64 * NA, v DV) as two tcgen05 kernels: dK / dV per
-// key tile over 64-query sub-tiles, then dQ per query tile (attention_bwd_wide.cuh).
-template <int NA, int DV>
+// Two-kernel tcgen05 backward (qk 64 * NA + 16 * NB, v DV): dK / dV per key
+// tile over 64-query sub-tiles, then dQ per query tile (attention_bwd_wide.cuh).
+template <int NA, int NB, int DV>
 void run_bwd_sm100_wide(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
                         const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq,
                         at::Tensor& dk, at::Tensor& dv, int q_off, double scale, bool causal, int H) {
   const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1), DP = q.size(2);
-  TORCH_CHECK(DP == NA * 64 && v.size(2) == DV, "flash backward (wide): head dims");
+  TORCH_CHECK(DP == NA * 64 + NB * 16 && v.size(2) == DV, "flash backward (two-kernel): head dims");
   const int B = BH / H;
   auto st = at::cuda::getCurrentCUDAStream();
   const long rows = (long)BH * Sq;
   fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
       reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  // [b*h, S, D] bf16 with 64-column, `box_rows`-row boxes in 128B swizzle
-  auto mk = [](const at::Tensor& t, int S, int D, uint32_t box_rows) {
+  // [b*h, S, D] bf16 with `box_rows`-row boxes: 64 columns in 128B swizzle
+  // (or the 16-column block in 32B swizzle)
+  auto mk = [](const at::Tensor& t, int S, int D, uint32_t box_rows, bool narrow = false) {
     uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)t.size(0)};
     uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
-    uint32_t box[3] = {64, box_rows, 1};
-    return make_map(t.data_ptr(), 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    uint32_t box[3] = {narrow ? 16u : 64u, box_rows, 1};
+    return make_map(t.data_ptr(), 3, dims, strides, box,
+                    narrow ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_128B);
   };
   // dO is token-major [B, Sq, H, DV]
   auto mk_do = [&](uint32_t box_rows) {
@@ -548,23 +550,25 @@ void run_bwd_sm100_wide(const at::Tensor& q, const at::Tensor& k, const at::Tens
     return make_map(dout.data_ptr(), 4, ddims, dstr, dbox, CU_TENSOR_MAP_SWIZZLE_128B);
   };
   const CUtensorMap q64 = mk(q, Sq, DP, 64), q128 = mk(q, Sq, DP, 128), k128 = mk(k, Sk, DP, 128);
+  const CUtensorMap q64b = NB ? mk(q, Sq, DP, 64, true) : q64, q128b = NB ? mk(q, Sq, DP, 128, true) : q128;
+  const CUtensorMap k128b = NB ? mk(k, Sk, DP, 128, true) : k128;
   const CUtensorMap v128 = mk(v, Sk, DV, 128), do64 = mk_do(64), do128 = mk_do(128);
   const float sl2 = (float)(scale * 1.4426950408889634), sc = (float)scale;
-  using Ckv = FabKvCfg<NA, DV>;
-  using Cq = FabQCfg<NA, DV>;
-  auto kkv = fa_bwd_kv_sm100_kernel<NA, DV>;
-  auto kq = fa_bwd_dq_sm100_kernel<NA, DV>;
+  using Ckv = FabKvCfg<NA, NB, DV>;
+  using Cq = FabQCfg<NA, NB, DV>;
+  auto kkv = fa_bwd_kv_sm100_kernel<NA, NB, DV>;
+  auto kq = fa_bwd_dq_sm100_kernel<NA, NB, DV>;
   static bool cfg = false;
   if (!cfg) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, Ckv::SMEM));
     C10_CUDA_CHECK(cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, Cq::SMEM));
     cfg = true;
   }
-  kkv<<<dim3((Sk + 127) / 128, BH), 320, Ckv::SMEM, st>>>(q64, k128, v128, do64, lse.data_ptr<float>(),
+  kkv<<<dim3((Sk + 127) / 128, BH), 320, Ckv::SMEM, st>>>(q64, q64b, k128, k128b, v128, do64, lse.data_ptr<float>(),
       delta.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(), Sq, Sk, H, q_off, sl2, sc,
       causal ? 1 : 0, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  kq<<<dim3((Sq + 127) / 128, BH), 320, Cq::SMEM, st>>>(q128, k128, v128, do128, lse.data_ptr<float>(),
+  kq<<<dim3((Sq + 127) / 128, BH), 320, Cq::SMEM, st>>>(q128, q128b, k128, k128b, v128, do128, lse.data_ptr<float>(),
       delta.data_ptr<float>(), dq.data_ptr<float>(), Sq, Sk, H, q_off, sl2, sc, causal ? 1 : 0, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -616,9 +620,9 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   DSV3_FA_DISPATCH(80, 64, (run_bwd_sm100<1, 1, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   DSV3_FA_DISPATCH(64, 64, (run_bwd_sm100<1, 0, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
   if (wide_bwd_enabled()) {
-    DSV3_FA_DISPATCH(192, 128, (run_bwd_sm100_wide<3, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
+    DSV3_FA_DISPATCH(192, 128, (run_bwd_sm100_wide<3, 0, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
                                                            causal, H)))
-    DSV3_FA_DISPATCH(128, 128, (run_bwd_sm100_wide<2, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
+    DSV3_FA_DISPATCH(128, 128, (run_bwd_sm100_wide<2, 0, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
                                                            causal, H)))
   }
   DSV3_FA_DISPATCH(32, 16, (run_bwd<32, 16>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale, causal, H)))
@@ -741,9 +745,10 @@ void flash_bwd_mma(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   TORCH_CHECK(false, "flash_bwd_mma: unsupported head dims");
 }
 
-// The two-kernel tcgen05 backward for qk 128 / 192 with v 128, callable
-// directly (flash_bwd selects it only with DSV3_FA_BWD_WIDE=1).  dq is
-// overwritten, not accumulated.
+// The two-kernel tcgen05 backward for qk 128 / 192 with v 128 (and the 412M
+// head dims 80 / 64 for comparison with the single-kernel backward), callable
+// directly; flash_bwd selects it for qk 128 / 192 only with
+// DSV3_FA_BWD_WIDE=1.  dq is overwritten, not accumulated.
 void flash_bwd_wide(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
                     const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
                     at::Tensor& dv, int64_t q_off, double scale, bool causal, int64_t H) {
@@ -751,10 +756,12 @@ void flash_bwd_wide(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
               "flash_bwd_wide: contiguous inputs");
   const at::cuda::CUDAGuard guard(q.device());
   const int dqk = q.size(2), dvv = v.size(2);
-  DSV3_FA_DISPATCH(192, 128, (run_bwd_sm100_wide<3, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
+  DSV3_FA_DISPATCH(192, 128, (run_bwd_sm100_wide<3, 0, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
                                                          causal, H)))
-  DSV3_FA_DISPATCH(128, 128, (run_bwd_sm100_wide<2, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
+  DSV3_FA_DISPATCH(128, 128, (run_bwd_sm100_wide<2, 0, 128>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
                                                          causal, H)))
+  DSV3_FA_DISPATCH(80, 64, (run_bwd_sm100_wide<1, 1, 64>(q, k, v, o, dout, lse, delta, dq, dk, dv, q_off, scale,
+                                                        causal, H)))
   TORCH_CHECK(false, "flash_bwd_wide: unsupported head dims ", dqk, "/", dvv);
 }
 
@@ -774,7 +781,7 @@ void register_attention(pybind11::module_& m) {
   m.def("flash_fwd_mma", &flash_fwd_mma, "warp-level mma.sync flash attention forward");
   m.def("flash_fwd_tc", &flash_fwd_tc, "tcgen05 flash attention forward");
   m.def("flash_bwd_mma", &flash_bwd_mma, "warp-level mma.sync flash attention backward");
-  m.def("flash_bwd_wide", &flash_bwd_wide, "two-kernel tcgen05 flash attention backward for qk 128/192, v 128");
+  m.def("flash_bwd_wide", &flash_bwd_wide, "two-kernel tcgen05 flash attention backward (qk 192/128/80)");
   m.def("flash_fwd", &flash_fwd, "causal flash attention forward (stores log2-domain LSE)");
   m.def("flash_bwd", &flash_bwd, "flash attention backward (dQ fp32 accumulated, dK/dV fp32)");
   m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)", pybind11::arg("q_lat"),

@@ -1,8 +1,9 @@
-// Flash-attention backward on tcgen05 for wide heads: qk = 64 * NA (128 or
-// 192), v = DV (128).  The single-kernel backward (attention_sm100.cuh) keeps
-// S^T, dP^T, dV, dK and dQ in TMEM; at these widths that is 768 columns, more
-// than the 512 a CTA can hold.  The work is therefore split in two kernels
-// that each fit:
+// Flash-attention backward on tcgen05 as two kernels, for heads of
+// qk = 64 * NA + 16 * NB (NA 128B-swizzled blocks of 64, an optional
+// 32B-swizzled block of 16) and v = DV.  The single-kernel backward
+// (attention_sm100.cuh) keeps S^T, dP^T, dV, dK and dQ in TMEM; at qk 192 /
+// v 128 that is 768 columns, more than the 512 a CTA can hold.  The work is
+// split in two kernels that each fit (columns given for qk 192 / v 128):
 //
 //   fa_bwd_kv_sm100_kernel   one CTA per (128-key tile, b*h), walking 64-query
 //                            sub-tiles:  S^T = K Q^T, dP^T = V dO^T  (64 + 64
@@ -31,12 +32,12 @@
 
 namespace dsv3 {
 
-template <int NA, int DV>
+template <int NA, int NB, int DV>
 struct FabKvCfg {
-  static constexpr int DQK = NA * 64;
-  static constexpr int K_B = NA * 16384;         // K tile: 128 keys x DQK
-  static constexpr int V_B = (DV / 64) * 16384;  // V tile: 128 keys x DV
-  static constexpr int QS_B = NA * 8192;         // Q sub-tile: 64 queries x DQK
+  static constexpr int DQK = NA * 64 + NB * 16;
+  static constexpr int K_B = NA * 16384 + NB * 4096;  // K tile: 128 keys x DQK
+  static constexpr int V_B = (DV / 64) * 16384;       // V tile: 128 keys x DV
+  static constexpr int QS_B = NA * 8192 + NB * 2048;  // Q sub-tile: 64 queries x DQK
   static constexpr int OS_B = (DV / 64) * 8192;  // dO sub-tile: 64 queries x DV
   static constexpr int PT_B = 16384;             // P^T or dS^T: 128 keys x 64 queries, bf16
   static constexpr int OFF_K = 0;
@@ -48,20 +49,22 @@ struct FabKvCfg {
   static constexpr int OFF_LD = OFF_DS + 2 * PT_B; // L / delta: 2 buffers x 2 x 64 floats
   static constexpr int OFF_BAR = OFF_LD + 1024;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int DQKP = (DQK + 31) / 32 * 32;  // TMEM regions start on 32-column boundaries
   static constexpr int C_S = 0, C_DP = 64, C_DV = 128, C_DK = 128 + DV;
   static_assert(DV % 64 == 0 && DV <= 128, "DV must be 64 or 128");
-  static_assert(C_DK + DQK <= 512, "TMEM budget");
+  static_assert(C_DK + DQKP <= 512, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-template <int NA, int DV>
+template <int NA, int NB, int DV>
 __global__ void __launch_bounds__(320, 1)
-    fa_bwd_kv_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    fa_bwd_kv_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQb,
+                           const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmKb,
                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                            const float* __restrict__ L, const float* __restrict__ delta, float* __restrict__ dK,
                            float* __restrict__ dVo, int Sq, int Sk, int H, int q_off, float scale_log2, float scale,
                            int causal, unsigned int* status) {
-  using C = FabKvCfg<NA, DV>;
+  using C = FabKvCfg<NA, NB, DV>;
   constexpr int DQK = C::DQK;
   extern __shared__ __align__(1024) uint8_t fkv_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fkv_raw) + 1023) & ~uintptr_t(1023));
@@ -117,6 +120,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(kv_full, C::K_B + C::V_B);
 #pragma unroll
       for (int a = 0; a < NA; ++a) tma_load_3d(smem + C::OFF_K + a * 16384, &tmK, kv_full, a * 64, n0, bh);
+      if (NB) tma_load_3d(smem + C::OFF_K + NA * 16384, &tmKb, kv_full, NA * 64, n0, bh);
 #pragma unroll
       for (int d = 0; d < DV / 64; ++d) tma_load_3d(smem + C::OFF_V + d * 16384, &tmV, kv_full, d * 64, n0, bh);
       uint32_t issued = 0, last_phase = 0;
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(320, 1)
         uint8_t* o = smem + C::OFF_DO + st * C::OS_B;
 #pragma unroll
         for (int a = 0; a < NA; ++a) tma_load_3d(q + a * 8192, &tmQ, &qd_full[st], a * 64, q0, bh);
+        if (NB) tma_load_3d(q + NA * 8192, &tmQb, &qd_full[st], NA * 64, q0, bh);
 #pragma unroll
         for (int d = 0; d < DV / 64; ++d) tma_load_4d(o + d * 8192, &tmdO, &qd_full[st], d * 64, h, q0, b);
         issued |= 1u << st;
@@ -144,6 +149,7 @@ __global__ void __launch_bounds__(320, 1)
       // ------------------------------------------------------- MMA issuer
       constexpr uint32_t I_S = idesc_bf16_f32(128, 64, 0, 0);    // S^T, dP^T: N = the 64 queries
       constexpr uint32_t I_MN = idesc_bf16_f32(128, 64, 0, 1);   // dV, dK: 64-column chunks, B MN-major
+      constexpr uint32_t I_MN16 = idesc_bf16_f32(128, 16, 0, 1); // dK: the 16-column block
       const uint32_t k_s = smem_u32(smem + C::OFF_K), v_s = smem_u32(smem + C::OFF_V);
       auto issue_s_dp = [&](int it) {
         const int st = it & 1;
@@ -158,6 +164,7 @@ __global__ void __launch_bounds__(320, 1)
                       smem_desc_sw128(q_s + a * 8192 + kk * 32, 16, 1024), I_S, acc);
             acc = 1;
           }
+        if (NB) umma_bf16(tmem + C::C_S, smem_desc_sw32(k_s + NA * 16384, 256), smem_desc_sw32(q_s + NA * 8192, 256), I_S, 1);
         // dP^T = V dO^T
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk)
@@ -203,6 +210,11 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16(tmem + C::C_DK + a * 64, smem_desc_sw128(ds_s + kk * 32, 16, 1024),
                       smem_desc_sw128(q_s + a * 8192 + kk * 2048, 8192, 1024), I_MN, (it > 0 || kk > 0) ? 1u : 0u);
+        if (NB)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + C::C_DK + NA * 64, smem_desc_sw128(ds_s + kk * 32, 16, 1024),
+                      smem_desc_sw32(q_s + NA * 8192 + kk * 512, 256), I_MN16, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&p_free[pb]);
         umma_commit(&qd_empty[st]);
       }
@@ -354,12 +366,12 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
-template <int NA, int DV>
+template <int NA, int NB, int DV>
 struct FabQCfg {
-  static constexpr int DQK = NA * 64;
-  static constexpr int Q_B = NA * 16384;         // Q tile: 128 queries x DQK
-  static constexpr int O_B = (DV / 64) * 16384;  // dO tile: 128 queries x DV
-  static constexpr int K_B = NA * 16384;         // K tile: 128 keys x DQK
+  static constexpr int DQK = NA * 64 + NB * 16;
+  static constexpr int Q_B = NA * 16384 + NB * 4096;  // Q tile: 128 queries x DQK
+  static constexpr int O_B = (DV / 64) * 16384;       // dO tile: 128 queries x DV
+  static constexpr int K_B = NA * 16384 + NB * 4096;  // K tile: 128 keys x DQK
   static constexpr int V_B = (DV / 64) * 16384;  // V tile: 128 keys x DV
   static constexpr int S_B = 32768;              // dS [128 queries][128 keys] bf16
   // two K stages where they fit (qk 128), one at qk 192
@@ -371,20 +383,22 @@ struct FabQCfg {
   static constexpr int OFF_S = OFF_V + V_B;
   static constexpr int OFF_BAR = OFF_S + S_B;
   static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int DQKP = (DQK + 31) / 32 * 32;
   static constexpr int C_S = 0, C_DP = 128, C_DQ = 256;
   static_assert(DV % 64 == 0 && DV <= 128, "DV must be 64 or 128");
-  static_assert(C_DQ + DQK <= 512, "TMEM budget");
+  static_assert(C_DQ + DQKP <= 512, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-template <int NA, int DV>
+template <int NA, int NB, int DV>
 __global__ void __launch_bounds__(320, 1)
-    fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    fa_bwd_dq_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmQb,
+                           const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmKb,
                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                            const float* __restrict__ L, const float* __restrict__ delta, float* __restrict__ dQ,
                            int Sq, int Sk, int H, int q_off, float scale_log2, float scale, int causal,
                            unsigned int* status) {
-  using C = FabQCfg<NA, DV>;
+  using C = FabQCfg<NA, NB, DV>;
   constexpr int DQK = C::DQK;
   constexpr int KST = C::KST;
   extern __shared__ __align__(1024) uint8_t fdq_raw[];
@@ -441,6 +455,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_arrive_expect_tx(q_full, C::Q_B + C::O_B);
 #pragma unroll
       for (int a = 0; a < NA; ++a) tma_load_3d(smem + C::OFF_Q + a * 16384, &tmQ, q_full, a * 64, m0, bh);
+      if (NB) tma_load_3d(smem + C::OFF_Q + NA * 16384, &tmQb, q_full, NA * 64, m0, bh);
 #pragma unroll
       for (int d = 0; d < DV / 64; ++d) tma_load_4d(smem + C::OFF_O + d * 16384, &tmdO, q_full, d * 64, h, m0, b);
       uint32_t issued = 0, last_phase = 0;
@@ -452,6 +467,7 @@ __global__ void __launch_bounds__(320, 1)
         uint8_t* k = smem + C::OFF_K + st * C::K_B;
 #pragma unroll
         for (int a = 0; a < NA; ++a) tma_load_3d(k + a * 16384, &tmK, &k_full[st], a * 64, j * 128, bh);
+        if (NB) tma_load_3d(k + NA * 16384, &tmKb, &k_full[st], NA * 64, j * 128, bh);
         issued |= 1u << st;
         last_phase = (last_phase & ~(1u << st)) | (ph << st);
       }
@@ -475,6 +491,7 @@ __global__ void __launch_bounds__(320, 1)
       // ------------------------------------------------------- MMA issuer
       constexpr uint32_t I_S = idesc_bf16_f32(128, 128, 0, 0);   // S, dP
       constexpr uint32_t I_Q = idesc_bf16_f32(128, 64, 0, 1);    // dQ: 64-column chunks, K read MN-major
+      constexpr uint32_t I_Q16 = idesc_bf16_f32(128, 16, 0, 1);  // dQ: the 16-column block
       const uint32_t q_s = smem_u32(smem + C::OFF_Q), o_s = smem_u32(smem + C::OFF_O);
       const uint32_t v_s = smem_u32(smem + C::OFF_V), ds_s = smem_u32(smem + C::OFF_S);
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
@@ -497,6 +514,7 @@ __global__ void __launch_bounds__(320, 1)
                       smem_desc_sw128(k_s + a * 16384 + kk * 32, 16, 1024), I_S, acc);
             acc = 1;
           }
+        if (NB) umma_bf16(tmem + C::C_S, smem_desc_sw32(q_s + NA * 16384, 256), smem_desc_sw32(k_s + NA * 16384, 256), I_S, 1);
         // dP = dO V^T
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk)
@@ -514,6 +532,11 @@ __global__ void __launch_bounds__(320, 1)
           for (int kk = 0; kk < 8; ++kk)
             umma_bf16(tmem + C::C_DQ + a * 64, smem_desc_sw128(ds_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                       smem_desc_sw128(k_s + a * 16384 + kk * 2048, 16384, 1024), I_Q, (j > 0 || kk > 0) ? 1u : 0u);
+        if (NB)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_bf16(tmem + C::C_DQ + NA * 64, smem_desc_sw128(ds_s + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                      smem_desc_sw32(k_s + NA * 16384 + kk * 512, 256), I_Q16, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(p_free);
         umma_commit(&k_empty[st]);
       }

@@ -6,9 +6,11 @@ shapes (forward, data gradient, weight gradient; cuBLAS via ``torch.matmul``
 on the same forward shape for reference; with and without CTA-pair tiles)
 and the attention kernels (tcgen05
 vs warp-level mma.sync) on the 412M, MTP and MLA-microbenchmark head dims.
+``--wide-bwd`` adds the two-kernel tcgen05 backward (``flash_bwd_wide``).
 """
 from __future__ import annotations
 
+import argparse
 import json
 
 import torch
@@ -50,10 +52,10 @@ def gemm_cases(C):
     return out
 
 
-def attention_cases(C):
+def attention_cases(C, wide_bwd=False):
     out = []
     for (B, H, S, DP, DV, dqk) in [(16, 12, 2048, 80, 64, 72), (16, 12, 2046, 64, 64, 64),
-                                   (8, 16, 4096, 128, 128, 128)]:
+                                   (8, 16, 4096, 128, 128, 128), (8, 16, 4096, 192, 128, 192)]:
         Q = torch.randn(B * H, S, DP, device="cuda").bfloat16()
         K = torch.randn_like(Q)
         V = torch.randn(B * H, S, DV, device="cuda").bfloat16()
@@ -71,19 +73,31 @@ def attention_cases(C):
             tm = _time(lambda: C.flash_bwd_mma(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H), 5)
             r["bwd_tcgen05_tflops"] = round(2.5 * fl / tb / 1e9, 1)
             r["bwd_mma_sync_tflops"] = round(2.5 * fl / tm / 1e9, 1)
+        if wide_bwd and DP in (80, 128, 192):
+            # the two-kernel tcgen05 backward (opt-in until validated); the
+            # rate counts the useful 2.5x forward FLOPs, not its recomputation
+            dQ = torch.zeros(B * H, S, DP, device="cuda")
+            dK, dV = torch.empty_like(dQ), torch.empty(B * H, S, DV, device="cuda")
+            delta = torch.empty(B * H, S, device="cuda")
+            tw = _time(lambda: C.flash_bwd_wide(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H), 5)
+            r["bwd_two_kernel_tcgen05_tflops"] = round(2.5 * fl / tw / 1e9, 1)
         out.append(r)
     return out
 
 
 def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--wide-bwd", action="store_true", help="also time the two-kernel tcgen05 attention backward")
+    ap.add_argument("--attention-only", action="store_true")
+    a = ap.parse_args()
     C = native()
-    for pairs in (1, 0):
+    for pairs in (() if a.attention_only else (1, 0)):
         C.gemm_pairs(pairs)
         for r in gemm_cases(C):
             r["cta_pairs"] = bool(pairs)
             print(json.dumps(r), flush=True)
     C.gemm_pairs(1)
-    for r in attention_cases(C):
+    for r in attention_cases(C, wide_bwd=a.wide_bwd):
         print(json.dumps(r), flush=True)
     if C.status_read():
         raise SystemExit("kernel status word set")
