@@ -13,11 +13,14 @@ model with experts spread over the ranks and with experts replicated and
 compares losses and averaged gradients.  ``--shard`` compares expert-parallel
 training with the routed experts' weights, gradients and optimizer state
 sharded over the ranks against the same training with them replicated: three
-optimizer steps on identical synthetic gradients, then one real step.
+optimizer steps on identical synthetic gradients (with the peer-memory and
+with the NCCL data-parallel step), one real step, and a checkpoint round
+trip through the trainer.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 
 import torch
@@ -245,8 +248,17 @@ def run_shard(verbose=True) -> bool:
     # (a) synthetic gradients: replicated parameters get rank-specific values,
     # a routed expert's gradient is its owner's (zero on the other ranks)
     res = {}
-    for shard in (False, True):
-        eng, params = engine(shard)
+    modes = {"sharded": (True, "0"), "sharded, NCCL step": (True, "1"), "replicated": (False, "0")}
+    for mode, (shard, nccl) in modes.items():
+        saved_env = os.environ.get("DSV3_DP_NCCL")
+        os.environ["DSV3_DP_NCCL"] = nccl
+        try:
+            eng, params = engine(shard)
+        finally:
+            if saved_env is None:
+                os.environ.pop("DSV3_DP_NCCL", None)
+            else:
+                os.environ["DSV3_DP_NCCL"] = saved_env
         for step in range(3):
             for f in eng.flats:
                 f.grad.zero_()
@@ -260,15 +272,17 @@ def run_shard(verbose=True) -> bool:
             eng.clip_and_step(1.0 if step != 1 else 1e-3)
         torch.cuda.synchronize()
         eng.check()
-        res[shard] = (masters(eng, params), float(eng.optimizer.grad_norm))
+        res[mode] = (masters(eng, params), float(eng.optimizer.grad_norm))
         eng.close()
-    (m0, n0), (m1, n1) = res[False], res[True]
-    worst = max((m0[k] - m1[k]).abs().max().item() for k in m1)
-    if verbose:
-        print(f"[rank {rank}] synthetic steps: max |replicated - sharded| {worst:.3e}, norms {n0:.6f} / {n1:.6f}",
-              flush=True)
-    if not (worst <= 1e-5 and abs(n0 - n1) <= 1e-5 * max(1.0, n0)):
-        ok = False
+    m0, n0 = res["replicated"]
+    for mode in ("sharded", "sharded, NCCL step"):
+        m1, n1 = res[mode]
+        worst = max((m0[k] - m1[k]).abs().max().item() for k in m1)
+        if verbose:
+            print(f"[rank {rank}] synthetic steps: max |replicated - {mode}| {worst:.3e}, norms {n0:.6f} / {n1:.6f}",
+                  flush=True)
+        if not (worst <= 1e-5 and abs(n0 - n1) <= 1e-5 * max(1.0, n0)):
+            ok = False
 
     # (b) one real step from the same weights: same loss, norm and update
     g = torch.Generator(device="cpu").manual_seed(7 + rank)
