@@ -197,3 +197,17 @@ def test_prepare_data_without_external_pipeline(tmp_path):
     cfg = yaml.safe_load(out.read_text())
     assert rc == 2 and cfg["pipeline"]["tokenizer"]["vocab_size"] == 100_018
     assert cfg["pipeline"]["tokenizer"]["eos_token_id"] == 100_017
+
+
+def test_scaled_config_parallel_section():
+    """The scaled config's `parallel:` section reaches the trainer: experts over
+    all ranks, sharded, receive buffers at twice the mean load."""
+    import yaml
+    from pathlib import Path
+    y = yaml.safe_load(open(Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200" / "configs"
+                            / "scaled_13b.yaml"))
+    c = config_from_yaml(y)
+    assert c.ep_size == 0 and c.ep_shard_experts is True and c.ep_capacity_factor == 2.0
+    c412 = config_from_yaml(yaml.safe_load(open(Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200"
+                                                / "configs" / "pretrain_412m.yaml")))
+    assert c412.ep_shard_experts is False
