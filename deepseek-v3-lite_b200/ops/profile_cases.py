@@ -87,6 +87,20 @@ def case_fa_bwd():
         C.flash_bwd(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H)
 
 
+def case_fa_bwd_wide():
+    """The two-kernel tcgen05 backward on the 412M case above and on the
+    DeepSeek-V3 head dims (qk 192, v 128; B2 H16 S2048)."""
+    C = native()
+    for dims in ({}, {"B": 2, "H": 16, "S": 2048, "DP": 192, "DV": 128}):
+        B, H, S, DP, DV, Q, K, V, O, L = _attn_inputs(**dims)
+        C.flash_fwd(Q, K, V, O, L, 0, 0.1, True, H)
+        dQ = torch.zeros(B * H, S, DP, device="cuda")
+        dK, dV = torch.empty_like(dQ), torch.empty(B * H, S, DV, device="cuda")
+        delta = torch.empty(B * H, S, device="cuda")
+        for _ in range(2):
+            C.flash_bwd_wide(Q, K, V, O, O, L, delta, dQ, dK, dV, 0, 0.1, True, H)
+
+
 def _ce_inputs(T=16384, V=100018, D=768):
     x, w = _bf(T, D), _bf(V, D) * 0.05
     tgt = torch.randint(0, V, (T,), device="cuda")
