@@ -239,6 +239,7 @@ class Pretrainer:
         ]
         self.engine = None
         if self.device.type == "cuda":
+            self._memory_hint(config)
             from ops.engine import TrainEngine
             self.engine = TrainEngine(self.raw_model, self.mtp_wrapper, config, groups)
             self.optimizer = self.engine.optimizer
@@ -252,6 +253,21 @@ class Pretrainer:
         self._opt_steps = 0
 
     # --------------------------------------------------------------- helpers
+    def _memory_hint(self, config: TrainingConfig) -> None:
+        """Warn (never fail) when the estimated per-rank training state does
+        not fit the device, naming expert sharding when that would fix it."""
+        try:
+            from utils.memory import expert_sharding_hint
+            dist_on = torch.distributed.is_available() and torch.distributed.is_initialized()
+            world = torch.distributed.get_world_size() if dist_on else 1
+            device_gb = torch.cuda.get_device_properties(self.device).total_memory / 1024 ** 3
+            hint = expert_sharding_hint(self.raw_model, config.max_seq_len, config.batch_size, world,
+                                        int(config.ep_size), bool(config.ep_shard_experts), device_gb)
+            if hint:
+                self._log(f"[warn] {hint}")
+        except Exception as exc:  # an estimate must never stop training
+            self._log(f"[warn] memory estimate skipped: {exc}")
+
     @staticmethod
     def _pick_device() -> torch.device:
         if not torch.cuda.is_available():

@@ -13,6 +13,8 @@ optimizer state over the data-parallel group.
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 import torch.nn as nn
 
@@ -116,3 +118,23 @@ def estimate_sharded_training_gb(model: nn.Module, seq_len: int, batch_size: int
     dim, n_layers = _infer_dim_n_layers(model)
     act = _activation_bytes(seq_len, batch_size, dim, n_layers, False)
     return (param_bytes + moment_bytes + act) / 1024 ** 3 + overhead_gb
+
+
+def expert_sharding_hint(model: nn.Module, seq_len: int, batch_size: int, world_size: int, ep_size: int,
+                         shard_experts: bool, device_gb: float) -> Optional[str]:
+    """A warning when this run's per-rank training state will not fit
+    ``device_gb`` but would with routed experts sharded over the ranks (or
+    ``None``).  ``ep_size`` 0 means all ranks."""
+    ep = world_size if ep_size in (0, world_size) else 1
+    shards = ep if (shard_experts and ep > 1) else 1
+    need = estimate_sharded_training_gb(model, seq_len, batch_size, ep_size=shards, dp_size=world_size)
+    if need <= device_gb:
+        return None
+    if shards == 1 and world_size > 1:
+        with_shards = estimate_sharded_training_gb(model, seq_len, batch_size, ep_size=world_size, dp_size=world_size)
+        if with_shards <= device_gb:
+            return (f"estimated {need:.0f} GB per rank exceeds the {device_gb:.0f} GB device; with routed experts "
+                    f"sharded over the {world_size} ranks it is ~{with_shards:.0f} GB "
+                    f"(parallel: {{ep_size: 0, shard_experts: true}})")
+    return (f"estimated {need:.0f} GB per rank exceeds the {device_gb:.0f} GB device (more ranks with sharded "
+            f"experts, or a smaller micro-batch)")

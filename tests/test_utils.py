@@ -222,3 +222,20 @@ def test_scaled_config_fits_only_with_sharded_experts():
     S, B = cfg["model"]["max_seq_len"], cfg["training"]["micro_batch_size"]
     assert memory.estimate_sharded_training_gb(m, S, B, ep_size=1, dp_size=8) > 180
     assert memory.estimate_sharded_training_gb(m, S, B, ep_size=8, dp_size=8) < 120
+
+
+def test_expert_sharding_hint():
+    """The start-up hint names expert sharding exactly when it would make the
+    scaled config fit a 180 GB device on 8 ranks."""
+    import yaml
+    from pathlib import Path
+    cfg = yaml.safe_load(open(Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200" / "configs"
+                              / "scaled_13b.yaml"))
+    with torch.device("meta"):
+        m = Transformer(cfg["model"])
+    S, B = cfg["model"]["max_seq_len"], cfg["training"]["micro_batch_size"]
+    hint = memory.expert_sharding_hint(m, S, B, world_size=8, ep_size=0, shard_experts=False, device_gb=180)
+    assert hint is not None and "shard_experts: true" in hint
+    assert memory.expert_sharding_hint(m, S, B, world_size=8, ep_size=0, shard_experts=True, device_gb=180) is None
+    one = memory.expert_sharding_hint(m, S, B, world_size=1, ep_size=1, shard_experts=False, device_gb=180)
+    assert one is not None and "shard_experts" not in one
