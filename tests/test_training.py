@@ -133,6 +133,24 @@ class TestPretrainer:
             tr.train()
 
 
+def test_corrupted_latest_checkpoint_does_not_stop_training(small_cfg, tmp_dir, token_file):
+    """A latest checkpoint whose weight file is corrupted (a crash outside the
+    atomic write, a bad disk) is reported and training starts fresh, as the
+    reference's loop does; the run still reaches max_steps and saves."""
+    cfg = _cfg(small_cfg, tmp_dir, gradient_accumulation_steps=1, data_path=token_file, max_seq_len=16, max_steps=3)
+    tr = Pretrainer(cfg)
+    tr.save_checkpoint(2)
+    wpath = tmp_dir / "model_step_2.safetensors"
+    wpath.write_bytes(wpath.read_bytes()[:64])          # truncated: unreadable
+    tr2 = Pretrainer(cfg)
+    logged = []
+    real_log = tr2._log
+    tr2._log = lambda msg: (logged.append(msg), real_log(msg))
+    tr2.train()
+    assert any("Could not load checkpoint" in m for m in logged)
+    assert tr2.ckpt_manager.latest_step() == 3
+
+
 class TestCheckpointRoundTrip:
     def test_weights_optimizer_meta(self, small_cfg, tmp_dir):
         tr = Pretrainer(_cfg(small_cfg, tmp_dir, mtp_weight=0.3, gradient_accumulation_steps=1))
