@@ -104,6 +104,9 @@ class TrainingConfig:
     # Shard routed-expert weights / gradients / optimizer state over the
     # expert-parallel ranks (needed when the experts do not fit on one GPU).
     ep_shard_experts: bool = False
+    # Write checkpoints from a background thread after a host snapshot (new;
+    # the reference saves synchronously).
+    async_checkpoint: bool = False
 
 
 class PretrainDataset(Dataset):
@@ -453,8 +456,8 @@ class Pretrainer:
             torch.distributed.barrier(group=eng.dp.group)
         if int(os.environ.get("RANK", "0")) == 0:
             self.ckpt_manager.save(self.raw_model, self.optimizer, step, extra_meta=meta, state_dict=state,
-                                   optimizer_state=opt_state)
-        self._log(f"Checkpoint saved at step {step}")
+                                   optimizer_state=opt_state, background=self.config.async_checkpoint)
+        self._log(f"Checkpoint {'queued' if self.config.async_checkpoint else 'saved'} at step {step}")
 
     def load_checkpoint(self, step: int) -> int:
         """Restore ``step`` (weights, optimizer, MTP, scheduler, opt-step count)."""
@@ -548,6 +551,7 @@ class Pretrainer:
                     self.save_checkpoint(step)
                 step += 1
         self.save_checkpoint(step, tag="final")
+        self.ckpt_manager.wait()
         self._log("Training complete.")
 
 
@@ -587,6 +591,7 @@ def config_from_yaml(yaml_cfg: dict, data_path: Optional[str] = None, checkpoint
         ep_size=int(yaml_cfg.get("parallel", {}).get("ep_size", 1)),
         ep_capacity_factor=float(yaml_cfg.get("parallel", {}).get("ep_capacity_factor", 0.0)),
         ep_shard_experts=bool(yaml_cfg.get("parallel", {}).get("shard_experts", False)),
+        async_checkpoint=bool(t.get("async_checkpoint", False)),
     )
 
 

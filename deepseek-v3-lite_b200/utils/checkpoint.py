@@ -28,6 +28,7 @@ import json
 import logging
 import os
 import tempfile
+import threading
 from pathlib import Path
 from typing import Dict, Optional
 
@@ -41,12 +42,25 @@ _SHARD = "experts_step_{}_rank{}of{}.safetensors"
 _MOMENT_PREFIXES = ("exp_avg.", "exp_avg_sq.")
 
 
+def _to_host(obj):
+    """Copy every tensor inside nested dicts / lists / tuples to host memory."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().to("cpu", copy=True)
+    if isinstance(obj, dict):
+        return {k: _to_host(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_to_host(v) for v in obj)
+    return obj
+
+
 class CheckpointManager:
     """Save and restore model / optimizer / metadata triples by step."""
 
     def __init__(self, save_dir: str):
         self.save_dir = Path(save_dir)
         self.save_dir.mkdir(parents=True, exist_ok=True)
+        self._writer: Optional[threading.Thread] = None
+        self._writer_error: Optional[BaseException] = None
 
     # ------------------------------------------------------------------ paths
     def _path(self, kind: int, step: int) -> Path:
@@ -120,20 +134,53 @@ class CheckpointManager:
                 json.dump(obj, f, indent=2, default=str)
 
     def save(self, model: torch.nn.Module, optimizer, step: int, extra_meta: Optional[dict] = None,
-             state_dict: Optional[dict] = None, optimizer_state: Optional[dict] = None) -> None:
+             state_dict: Optional[dict] = None, optimizer_state: Optional[dict] = None,
+             background: bool = False) -> None:
         """Write the three files for ``step``.
 
         ``state_dict`` overrides ``model.state_dict()``; ``optimizer_state``
         overrides ``optimizer.state_dict()`` (used by sharded optimizers that
-        gather to the reference layout first).
+        gather to the reference layout first).  With ``background`` the
+        tensors are first copied to host memory (a consistent snapshot of this
+        step) and a writer thread writes the files while the caller goes on;
+        one save is in flight at a time (a new one, a load or ``wait()`` waits
+        for it).  The metadata file is written last either way, so a step is
+        never reported complete before all of its files exist.
         """
         state = state_dict if state_dict is not None else model.state_dict()
-        self._atomic_save_safetensors(state, self._path(0, step))
         opt_state = optimizer_state if optimizer_state is not None else optimizer.state_dict()
-        self._atomic_save_torch(opt_state, self._path(1, step))
         meta = {k: v for k, v in (extra_meta or {}).items() if k != "step"}
+        if not background:
+            self._write(step, state, opt_state, meta)
+            return
+        self.wait()
+        snap_state = {k: v.detach().to("cpu", copy=True) for k, v in self._unique_storage(state).items()}
+        snap_opt = _to_host(opt_state)
+        self._writer_error = None
+        self._writer = threading.Thread(target=self._write_guarded, args=(step, snap_state, snap_opt, meta),
+                                        name=f"checkpoint-{step}")
+        self._writer.start()
+
+    def _write(self, step: int, state: dict, opt_state, meta: dict) -> None:
+        self._atomic_save_safetensors(state, self._path(0, step))
+        self._atomic_save_torch(opt_state, self._path(1, step))
         self._atomic_save_json({"step": step, **meta}, self._path(2, step))
         log.info("[checkpoint] saved step %d -> %s", step, self.save_dir)
+
+    def _write_guarded(self, step: int, state: dict, opt_state, meta: dict) -> None:
+        try:
+            self._write(step, state, opt_state, meta)
+        except BaseException as exc:  # reported by wait()
+            self._writer_error = exc
+
+    def wait(self) -> None:
+        """Block until a background save finished; re-raise its error."""
+        if self._writer is not None:
+            self._writer.join()
+            self._writer = None
+        if self._writer_error is not None:
+            err, self._writer_error = self._writer_error, None
+            raise RuntimeError("background checkpoint write failed") from err
 
     def save_expert_shard(self, step: int, rank: int, world: int, tensors: Dict[str, torch.Tensor]) -> None:
         """Write one rank's routed experts (weights and prefixed moments).
@@ -169,6 +216,7 @@ class CheckpointManager:
         shards' weights merged in unless ``merge_expert_shards`` is false (a
         sharded run loads its own shard instead).
         """
+        self.wait()
         wpath = self._path(0, step)
         if not wpath.exists():
             raise FileNotFoundError(f"Checkpoint not found: {wpath}\nAvailable steps: {sorted(self._list_steps())}")

@@ -229,3 +229,17 @@ def test_scaled_config_parallel_section():
     c412 = config_from_yaml(yaml.safe_load(open(Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200"
                                                 / "configs" / "pretrain_412m.yaml")))
     assert c412.ep_shard_experts is False
+
+
+def test_async_checkpoint_training_loop(small_cfg, tmp_dir, token_file):
+    """With async_checkpoint the loop's periodic and final checkpoints are
+    written by the background writer and complete when train() returns."""
+    cfg = _cfg(small_cfg, tmp_dir, gradient_accumulation_steps=1, data_path=token_file, max_seq_len=16, max_steps=4,
+               save_every=2, async_checkpoint=True)
+    tr = Pretrainer(cfg)
+    tr.train()
+    assert tr.ckpt_manager.latest_step() == 4 and 2 in tr.ckpt_manager._list_steps()
+    tr2 = Pretrainer(cfg)
+    assert tr2.load_checkpoint(4) == 4
+    for (n, a), (_, b) in zip(tr.raw_model.named_parameters(), tr2.raw_model.named_parameters()):
+        assert torch.equal(a, b), n

@@ -239,3 +239,43 @@ def test_expert_sharding_hint():
     assert memory.expert_sharding_hint(m, S, B, world_size=8, ep_size=0, shard_experts=True, device_gb=180) is None
     one = memory.expert_sharding_hint(m, S, B, world_size=1, ep_size=1, shard_experts=False, device_gb=180)
     assert one is not None and "shard_experts" not in one
+
+
+class TestBackgroundCheckpoint:
+    def test_background_save_round_trip_and_visibility(self, small_cfg, tmp_dir):
+        """A background save snapshots the step, reports it complete only once
+        every file is written, and loads like a synchronous one."""
+        import threading
+        from safetensors.torch import save_file as real_save_file
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        gate = threading.Event()
+
+        def slow_save_file(tensors, path):
+            gate.wait(10)
+            real_save_file(tensors, path)
+
+        want = {k: v.clone() for k, v in m.state_dict().items()}
+        with patch("utils.checkpoint.save_file", side_effect=slow_save_file):
+            mgr.save(m, _opt(m), 6, background=True)
+            with torch.no_grad():
+                for p in m.parameters():
+                    p.add_(1.0)          # training goes on: the snapshot must not see this
+            assert mgr.latest_step() is None
+            gate.set()
+            mgr.wait()
+        assert mgr.latest_step() == 6
+        m2 = Transformer(small_cfg)
+        mgr.load(m2, 6, device="cpu", strict=False)
+        for k, v in m2.state_dict().items():
+            assert torch.equal(v, want[k]), k
+
+    def test_background_error_surfaces_on_wait(self, small_cfg, tmp_dir):
+        m = Transformer(small_cfg)
+        mgr = CheckpointManager(str(tmp_dir))
+        with patch("utils.checkpoint.save_file", side_effect=OSError("disk full")):
+            mgr.save(m, _opt(m), 1, background=True)
+            with pytest.raises(RuntimeError, match="background checkpoint write failed"):
+                mgr.wait()
+        assert list(tmp_dir.iterdir()) == [] and mgr.latest_step() is None
+        mgr.wait()   # the error is reported once
