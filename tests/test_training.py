@@ -243,3 +243,18 @@ def test_async_checkpoint_training_loop(small_cfg, tmp_dir, token_file):
     assert tr2.load_checkpoint(4) == 4
     for (n, a), (_, b) in zip(tr.raw_model.named_parameters(), tr2.raw_model.named_parameters()):
         assert torch.equal(a, b), n
+
+
+def test_tiny_benchmark_script_runs_on_cpu():
+    """training/bench_tiny.py (the tiny-config step + decode benchmark) prints
+    its JSON line; on the CPU it runs this package's PyTorch path."""
+    import subprocess
+    import sys as _sys
+    from pathlib import Path
+    pkg = Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200"
+    r = subprocess.run([_sys.executable, "training/bench_tiny.py", "--steps", "1", "--new", "2"], cwd=pkg,
+                       capture_output=True, text=True, timeout=600, env={**__import__("os").environ,
+                                                                         "CUDA_VISIBLE_DEVICES": ""})
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "ours" and line["step_ms"] > 0 and line["decode_tokens"] == 2
