@@ -37,9 +37,75 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
+T_START = time.perf_counter()
 BASELINE_TOKENS_PER_S = None  # the reference publishes no measured tokens/s for this config
 METRIC = "train tokens/sec (device, max over ranks)"
 GLOBAL_SEQS = 256
+
+
+REF_DIR = ROOT / "baseline" / "_ref"
+REF_PACKAGES = ("models", "training", "inference", "utils")
+
+
+def _reference_source_candidates():
+    """Where the unmodified reference source may be: $DSV3_REFERENCE_SRC, then BASELINE.json's `reference_path`."""
+    out = []
+    if os.environ.get("DSV3_REFERENCE_SRC"):
+        out.append(Path(os.environ["DSV3_REFERENCE_SRC"]))
+    try:
+        out.append(Path(json.loads((ROOT / "BASELINE.json").read_text())["reference_path"]))
+    except (OSError, KeyError, ValueError):
+        pass
+    return out
+
+
+def ensure_reference(quiet: bool = False):
+    """Install the unmodified reference into ``baseline/_ref`` if it is not there yet.
+
+    The reference ships no packaging file, so pip cannot install its tree as
+    is.  Its source is copied to a temporary directory, a ``pyproject.toml``
+    naming its ``models`` / ``training`` / ``inference`` / ``utils`` packages
+    and its ``configs`` data is added to the copy (no source file is touched),
+    and ``pip install --no-index --no-build-isolation --no-deps --target
+    baseline/_ref`` installs it.  Afterwards every installed ``.py`` / ``.yaml``
+    file is compared byte for byte with the original.
+
+    Returns ``(ok, message)``; never raises.
+    """
+    import filecmp
+    import shutil
+    import tempfile
+    if (REF_DIR / "training" / "pretrain.py").exists():
+        return True, f"already installed in {REF_DIR}"
+    tried = []
+    for src in _reference_source_candidates():
+        tried.append(str(src))
+        if not (src / "training" / "pretrain.py").exists():
+            continue
+        tmp = Path(tempfile.mkdtemp(prefix="dsv3_ref_src_"))
+        try:
+            copy = tmp / "ref"
+            shutil.copytree(src, copy, ignore=shutil.ignore_patterns(".git", "__pycache__", "*.pyc"))
+            (copy / "pyproject.toml").write_text(
+                "[build-system]\nrequires = [\"setuptools\"]\nbuild-backend = \"setuptools.build_meta\"\n\n"
+                "[project]\nname = \"deepseek-v3-lite-reference\"\nversion = \"0.0.0\"\n\n"
+                "[tool.setuptools]\npackages = [" + ", ".join(f'"{p}"' for p in REF_PACKAGES + ("configs",)) + "]\n"
+                "include-package-data = true\n\n[tool.setuptools.package-data]\nconfigs = [\"*.yaml\"]\n")
+            cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                   "--find-links", "/opt/wheelhouse", "--target", str(REF_DIR), str(copy)]
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                return False, f"pip install of {src} failed: {(r.stderr or r.stdout).strip().splitlines()[-1:]}"
+        finally:
+            shutil.rmtree(tmp, ignore_errors=True)
+        for pkg in REF_PACKAGES + ("configs",):
+            for f in (src / pkg).glob("*"):
+                if f.suffix in (".py", ".yaml") and not filecmp.cmp(f, REF_DIR / pkg / f.name, shallow=False):
+                    return False, f"installed {pkg}/{f.name} differs from the reference source"
+        if not quiet:
+            print(f"reference installed from {src} into {REF_DIR}")
+        return True, f"installed from {src}"
+    return False, "reference source not found (tried: " + ", ".join(tried or ["no candidate path"]) + ")"
 
 
 def parse():
@@ -51,6 +117,10 @@ def parse():
     ap.add_argument("--micro-batch", type=int, default=0, help="sequences per micro-step per rank (0 = auto)")
     ap.add_argument("--global-seqs", type=int, default=GLOBAL_SEQS)
     ap.add_argument("--config", type=str, default="")
+    ap.add_argument("--phases", action="store_true",
+                    help="after the timed steps, run one more optimizer step with CUDA events between the phases "
+                         "of every layer (CUDA graph off) and add the per-phase device time (max and min over "
+                         "ranks) to the JSON line as phases_ms")
     ap.add_argument("--ep", type=int, default=-1,
                     help="expert-parallel size: -1 = all ranks (the benchmarked DP + EP=world config), 1 = experts "
                          "replicated (plain data parallelism)")
@@ -164,6 +234,30 @@ def timed_steps(run_step, steps, world, local):
     return max_over_ranks(ms, world), max_over_ranks(wall * 1000.0 / steps, world), clocks
 
 
+def phase_breakdown(engine, run_step, world):
+    """One optimizer step with CUDA events between the engine's phases.
+
+    Returns ``{phase: [max over ranks, min over ranks]}`` in ms, summed over
+    the step's micro-batches and layers (the CUDA graph is off for this step,
+    so the sum also shows host-side gaps as ``between micro-steps``)."""
+    import torch
+    import torch.distributed as dist
+    from ops.engine import PhaseTimer
+    engine.phase_timer = PhaseTimer(engine.device)
+    try:
+        run_step(0)
+        totals = engine.phase_timer.collect()
+    finally:
+        engine.phase_timer = None
+    names = sorted(totals)
+    v = torch.tensor([totals[n] for n in names], dtype=torch.float64, device=engine.device)
+    hi, lo = v.clone(), v.clone()
+    if world > 1:
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    return {n: [round(float(a), 3), round(float(b), 3)] for n, a, b in zip(names, hi.tolist(), lo.tolist())}
+
+
 def make_inputs(vocab, seqs, seq_len, seed, device):
     import torch
     g = torch.Generator(device="cpu").manual_seed(seed)
@@ -231,6 +325,7 @@ def run_ours(args, rank, world, local):
     ms, wall_ms, clocks = timed_steps(step_device, args.steps, world, local)
     launches = _ext.count_launches(False) // max(1, args.steps)
     e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, args.steps, world, local)
+    phases = phase_breakdown(trainer.engine, step_device, world) if args.phases else None
     trainer.engine.check()
     ep_on = trainer.engine.use_ep
     trainer.engine.close()
@@ -250,15 +345,22 @@ def run_ours(args, rank, world, local):
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": int(accum * micro * (S + 1) * 8),
                 "d2h_bytes_per_step": 4, "last_loss": loss_box[-1] if loss_box else None},
         "gpu_launches": int(launches),
+        **({"phases_ms": phases} if phases is not None else {}),
         "impl": "ours",
     }
 
 
 def run_reference(args, rank, world, local):
     import torch
-    ref_root = ROOT / "baseline" / "_ref"
-    if not (ref_root / "training" / "pretrain.py").exists():
-        return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+    ref_root = REF_DIR
+    ok, why = ensure_reference(quiet=True) if rank == 0 or world == 1 else (True, "")
+    if world > 1:
+        import torch.distributed as dist
+        flag = [ok]
+        dist.broadcast_object_list(flag, src=0)
+        ok = flag[0]
+    if not ok or not (ref_root / "training" / "pretrain.py").exists():
+        return {"impl": "reference", "unavailable": f"reference not installed in baseline/_ref: {why}"}
     default_cfg = ROOT / "deepseek-v3-lite_b200" / "configs" / "pretrain_412m.yaml"
     if args.config and Path(args.config).resolve() != default_cfg.resolve():
         # the reference arm runs the reference's own 412M yaml only; it has no
@@ -324,7 +426,13 @@ def run_reference(args, rank, world, local):
         step_device(i)
     torch.cuda.synchronize()
     ms, wall_ms, clocks = timed_steps(step_device, args.steps, world, local)
-    e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, args.steps, world, local)
+    # The reference takes ~25 s per 524K-token step on one GPU; its end-to-end
+    # phase gets the steps that still fit the time budget (at least one), so
+    # the arm ends inside the driver's per-run limit.  The count is reported.
+    budget = float(os.environ.get("DSV3_REF_BUDGET_S", "780"))
+    left = budget - (time.perf_counter() - T_START)
+    e2e_steps = max(1, min(args.steps, int(left // max(wall_ms / 1000.0, 1e-3))))
+    e2e_ms, e2e_wall_ms, _ = timed_steps(step_e2e, e2e_steps, world, local)
     tokens_per_step = args.global_seqs * S
     value = tokens_per_step / (ms / 1000.0)
     return {
@@ -337,7 +445,8 @@ def run_reference(args, rank, world, local):
                    "torch_compile_mode": os.environ.get("TORCH_COMPILE_MODE", "max-autotune")},
         "clocks": clocks,
         "e2e": {"value": round(tokens_per_step / (max(e2e_ms, e2e_wall_ms) / 1000.0), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": int(accum * micro * (S + 1) * 8), "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": int(accum * micro * (S + 1) * 8), "d2h_bytes_per_step": 4,
+                "steps": e2e_steps, "last_loss": loss_box[-1] if loss_box else None},
         "impl": "reference",
     }
 

@@ -14,16 +14,27 @@ engine in ``ops.engine``.
 """
 from __future__ import annotations
 
+import functools
 from typing import Optional, Tuple
 
 import torch
+import torch.utils.checkpoint
 import torch.nn as nn
 import torch.nn.functional as F
 
 from ._native_dispatch import normalize_backend_keys
 from .mla import MultiHeadLatentAttention
 from .moe import DeepSeekMoE
+from .sampling import sample_tokens
 from ops import norm as norm_ops
+
+
+def _direct(block: nn.Module, *args):
+    return block(*args)
+
+
+def _recomputed(block: nn.Module, *args):
+    return torch.utils.checkpoint.checkpoint(block, *args, use_reentrant=False)
 
 
 class SwiGLUFFN(nn.Module):
@@ -93,12 +104,9 @@ class Transformer(nn.Module):
         return self._mask_cache
 
     def _run_layers(self, h: torch.Tensor, start_pos: int, mask: Optional[torch.Tensor], use_cache: bool) -> torch.Tensor:
-        for layer in self.layers:
-            if self.use_checkpoint and self.training:
-                h = torch.utils.checkpoint.checkpoint(layer, h, start_pos, mask, use_cache, use_reentrant=False)
-            else:
-                h = layer(h, start_pos, mask, use_cache)
-        return h
+        """Apply the blocks in order; with activation checkpointing on (training only) each block is recomputed in backward."""
+        call = _recomputed if (self.use_checkpoint and self.training) else _direct
+        return functools.reduce(lambda x, block: call(block, x, start_pos, mask, use_cache), self.layers, h)
 
     def reset_cache(self) -> None:
         """Clear the latent caches of every layer."""
@@ -170,63 +178,63 @@ class Transformer(nn.Module):
 
     # ------------------------------------------------------------- generation
     @torch.inference_mode()
+    @torch.inference_mode()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int = 512, temperature: float = 1.0,
                  top_p: float = 0.9, top_k: int = 0, eos_token_id: Optional[int] = None) -> torch.Tensor:
-        """Prefill ``input_ids`` into the latent cache, then decode token by token.
+        """Prefill ``input_ids`` into the latent cache, then decode one token per step.
 
-        Stops after ``max_new_tokens``, when every row has produced
-        ``eos_token_id``, or when the sequence reaches ``max_seq_len``.
-        Training mode is restored afterwards.
+        Stops after ``max_new_tokens``, once every row has produced
+        ``eos_token_id``, or when the sequence reaches ``max_seq_len`` (at
+        least one token is always produced).  The caches are reset first and
+        the training mode is restored afterwards.  Tokens are written into one
+        preallocated ``[B, prompt + budget]`` buffer; the only per-step host
+        read is the end-of-sequence test when ``eos_token_id`` is given.
         """
         if temperature < 0.0:
             raise ValueError(f"temperature must be >= 0, got {temperature}")
-        was_training = self.training
+        bsz, prompt_len = input_ids.shape
+        budget = min(max_new_tokens, max(1, self.max_seq_len - prompt_len)) if max_new_tokens > 0 else 0
+        out = torch.empty(bsz, prompt_len + budget, dtype=input_ids.dtype, device=input_ids.device)
+        out[:, :prompt_len] = input_ids
+        restore = self.training
         self.reset_cache()
         self.eval()
-        bsz, prompt_len = input_ids.shape
-        out = input_ids.clone()
-        logits = self.forward(out, start_pos=0, use_cache=True)[:, -1, :]
-        done = torch.zeros(bsz, dtype=torch.bool, device=input_ids.device)
-        for step in range(max_new_tokens):
-            nxt = self._sample(logits, temperature, top_p, top_k)
-            out = torch.cat([out, nxt], dim=1)
-            if eos_token_id is not None:
-                done |= nxt.squeeze(-1) == eos_token_id
-                if bool(done.all()):
-                    break
-            if out.size(1) >= self.max_seq_len:
-                break
-            logits = self.forward(nxt, start_pos=prompt_len + step, use_cache=True)[:, -1, :]
-        if was_training:
-            self.train()
-        return out
+        try:
+            written = self._decode_into(out, prompt_len, budget, temperature, top_p, top_k, eos_token_id)
+        finally:
+            self.train(restore)
+        return out[:, :prompt_len + written].clone()
+
+    def _decode_into(self, out: torch.Tensor, prompt_len: int, budget: int, temperature: float, top_p: float,
+                     top_k: int, eos_token_id: Optional[int]) -> int:
+        """Fill ``out[:, prompt_len:prompt_len + budget]``; returns how many columns were written."""
+        if budget == 0:
+            return 0
+        alive = None if eos_token_id is None else torch.ones(out.size(0), dtype=torch.bool, device=out.device)
+        logits = self.forward(out[:, :prompt_len], start_pos=0, use_cache=True)[:, -1]
+        for i in range(budget):
+            tok = self._sample(logits, temperature, top_p, top_k)
+            out[:, prompt_len + i] = tok[:, 0]
+            if alive is not None:
+                alive &= tok[:, 0] != eos_token_id
+                if not bool(alive.any()):
+                    return i + 1
+            if i + 1 < budget:
+                logits = self.forward(tok, start_pos=prompt_len + i, use_cache=True)[:, -1]
+        return budget
 
     @staticmethod
     def _sample(logits: torch.Tensor, temperature: float, top_p: float, top_k: int) -> torch.Tensor:
-        """Sample one token per row; ``temperature == 0`` is greedy."""
-        if temperature == 0.0:
-            return logits.argmax(dim=-1, keepdim=True)
-        logits = logits / temperature
-        if top_k > 0:
-            kth = logits.topk(min(top_k, logits.size(-1)), dim=-1).values[:, -1:]
-            logits = logits.masked_fill(logits < kth, float("-inf"))
-        probs = logits.softmax(dim=-1)
-        if top_p >= 1.0:
-            return torch.multinomial(probs, 1)
-        sp, si = probs.sort(dim=-1, descending=True)
-        # Keep every token whose *exclusive* cumulative mass is within top_p.
-        sp = sp.masked_fill(sp.cumsum(dim=-1) - sp > top_p, 0.0)
-        sp = sp / sp.sum(dim=-1, keepdim=True).clamp(min=1e-10)
-        return si.gather(-1, torch.multinomial(sp, 1))
+        """One token per row (``[B, 1]``); ``temperature == 0`` is greedy (``models/sampling.py``)."""
+        return sample_tokens(logits, temperature, top_p, top_k)
 
 
 def count_parameters(model: nn.Module) -> Tuple[int, int]:
-    """``(total, trainable)`` parameter counts, each tensor counted once."""
-    seen, total, trainable = set(), 0, 0
-    for p in model.parameters():
-        if id(p) in seen:
-            continue
-        seen.add(id(p))
-        total += p.numel()
-        trainable += p.numel() if p.requires_grad else 0
-    return total, trainable
+    """``(total, trainable)`` element counts; a tied tensor counts once.
+
+    ``nn.Module.parameters()`` already yields a shared ``Parameter`` (the tied
+    embedding / head) a single time, which is the deduplication the
+    reference applies by tensor identity.
+    """
+    params = list(model.parameters())
+    return sum(p.numel() for p in params), sum(p.numel() for p in params if p.requires_grad)

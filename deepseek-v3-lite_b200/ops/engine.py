@@ -52,6 +52,33 @@ def _pad(n: int, m: int) -> int:
     return (n + m - 1) // m * m
 
 
+class PhaseTimer:
+    """Device time per named phase of the training step.
+
+    ``mark(name)`` records a CUDA event on the current stream; the time since
+    the previous mark is booked to ``name``.  ``collect()`` synchronises and
+    adds the intervals to ``totals`` (ms).  The engine only marks with the CUDA
+    graph off, so every event is a real launch-order point on the stream.
+    """
+
+    def __init__(self, device):
+        self.device = device
+        self.totals: Dict[str, float] = {}
+        self._events: list = []
+
+    def mark(self, name: str) -> None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self._events.append((name, ev))
+
+    def collect(self) -> Dict[str, float]:
+        torch.cuda.synchronize(self.device)
+        for (_, a), (name, b) in zip(self._events, self._events[1:]):
+            self.totals[name] = self.totals.get(name, 0.0) + a.elapsed_time(b)
+        self._events = []
+        return self.totals
+
+
 class _Ctx(dict):
     """Saved tensors of one layer for its backward."""
     __getattr__ = dict.__getitem__
@@ -130,6 +157,12 @@ class TrainEngine:
         self.use_graphs = os.environ.get("DSV3_CUDA_GRAPH", "1") == "1"
         # NVTX ranges per layer / phase for timeline tools (DSV3_NVTX=1)
         self.nvtx = os.environ.get("DSV3_NVTX", "0") == "1"
+        # per-phase device timing (set by the benchmark's breakdown step)
+        self.phase_timer: Optional[PhaseTimer] = None
+
+    def _mark(self, name: str) -> None:
+        if self.phase_timer is not None:
+            self.phase_timer.mark(name)
 
     # ---------------------------------------------------------------- layout
     def _build_flat(self, groups) -> None:
@@ -308,7 +341,9 @@ class TrainEngine:
         C.mla_pack(q, kvb, kv_a[:, R:], Q, K, Vt, B, S, H, dn, dr, dv, self.cos, self.sin, 0)
         O = torch.empty(T, H * dv, dtype=BF16, device=self.device)
         L = torch.empty(B * H, S, dtype=F32, device=self.device)
+        self._mark("attn proj fwd")
         C.flash_fwd(Q, K, Vt, O, L, 0, attn.softmax_scale, True, H)
+        self._mark("flash fwd")
         ctx.update(kv_a=kv_a, lat=lat, rkv=rkv, Q=Q, K=K, V=Vt, O=O, L=L)
         return ctx
 
@@ -321,7 +356,9 @@ class TrainEngine:
         dK = torch.empty_like(dQ)
         dV = torch.empty(B * H, S, dv, dtype=F32, device=self.device)
         delta = torch.empty(B * H, S, dtype=F32, device=self.device)
+        self._mark("o-proj bwd")
         C.flash_bwd(ctx.Q, ctx.K, ctx.V, ctx.O, dO, ctx.L, delta, dQ, dK, dV, 0, attn.softmax_scale, True, H)
+        self._mark("flash bwd")
         Nq = H * (dn + dr)
         dqkva = torch.empty(T, Nq + R + dr, dtype=BF16, device=self.device)
         dq, dkv_a = dqkva[:, :Nq], dqkva[:, Nq:]
@@ -332,6 +369,7 @@ class TrainEngine:
                       self.g(attn.kv_norm.weight))
         C.linear_wgrad(dqkva, ctx.xn, self.qkva_block(attn, grad=True))
         C.linear_dgrad(dqkva, self.qkva_block(attn), dxn_acc, False)
+        self._mark("attn proj bwd")
 
     # ------------------------------------------------------------------ FFN
     def _swiglu_dense_fwd(self, w1, w2, xn, out, resid_in=None):
@@ -398,8 +436,9 @@ class TrainEngine:
             for i, e in enumerate(moe.shared_experts):
                 shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
         w13, w2, _, _ = self._local_experts(moe, ep)
+        self._mark("router fwd")
         ectx = moe_forward_ep(ep, self._moe_slot[id(moe)], xn, idx, wts, counts, w13, w2, out, I,
-                              overlap=shared_fwd if moe.shared_experts else None)
+                              marks=self._mark, overlap=shared_fwd if moe.shared_experts else None)
         return _Ctx(ep=ectx, idx=idx, wts=wts, ssel=ssel, shared=shared, Ep=Ep, counts=counts), out
 
     def _moe_bwd_ep(self, moe, ctx, xn, dres_bf16, dxn_acc):
@@ -413,9 +452,10 @@ class TrainEngine:
             for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
                 self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
         w13, w2, g13, g2 = self._local_experts(moe, ep)
-        dw = moe_backward_ep(ep, ctx.ep, dres_bf16, w13, w2, g13, g2, dxn_acc, I,
+        dw = moe_backward_ep(ep, ctx.ep, dres_bf16, w13, w2, g13, g2, dxn_acc, I, marks=self._mark,
                              overlap=shared_bwd if moe.shared_experts else None)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
+        self._mark("router bwd")
 
     def _router_bwd(self, moe, ctx, xn, dw, dxn_acc):
         C = self.C
@@ -567,7 +607,7 @@ class TrainEngine:
         ``use_graphs`` the whole micro-step is captured once per input shape
         into a CUDA graph and replayed (no per-kernel host launch cost).
         """
-        if self.use_graphs and torch.cuda.is_current_stream_capturing() is False:
+        if self.use_graphs and self.phase_timer is None and torch.cuda.is_current_stream_capturing() is False:
             return self._graphed(tokens, targets, loss_scale)
         return self._forward_backward(tokens, targets, loss_scale)
 
@@ -625,8 +665,10 @@ class TrainEngine:
         T = B * S
         tok = tokens.reshape(-1).long().contiguous()
         tgt = targets.reshape(-1).long().contiguous()
+        self._mark("between micro-steps")
         x = torch.empty(T, D, dtype=F32, device=self.device)
         C.embedding_fwd(tok, self.f32(m.embed.weight), x)
+        self._mark("embedding fwd")
         saved = []
         for li, layer in enumerate(m.layers):
             self._range(f"fwd layer {li}")
@@ -635,11 +677,14 @@ class TrainEngine:
             x_mid = torch.empty_like(x)
             C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid, True, x)
             xn2, r2 = self._norm(x_mid, layer.ffn_norm.weight)
+            self._mark("o-proj fwd")
             if hasattr(layer.ffn, "experts"):
                 fctx, x_next = self._moe_fwd(layer.ffn, xn2, x_mid)
+                self._mark("moe fwd")
             else:
                 x_next = torch.empty_like(x_mid)
                 fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next, x_mid)
+                self._mark("dense ffn fwd")
             saved.append((x, r1, actx, x_mid, xn2, r2, fctx))
             x = x_next
             self._range(None)
@@ -668,6 +713,7 @@ class TrainEngine:
                 tgts.append(tokens[:, d + 2:d + 2 + Sm].reshape(-1).long().contiguous())
                 seg.append(seg[-1] + B * Sm)
                 prev = hn.float().view(B, Sm, D)  # next depth chains on the normalised hidden
+        self._mark("mtp fwd")
         allx = torch.cat(rows, 0) if len(rows) > 1 else xf
         allt = torch.cat(tgts, 0) if len(tgts) > 1 else tgt
         Tt = allx.shape[0]
@@ -690,6 +736,7 @@ class TrainEngine:
         C.ce_reduce(lrows, allt, seg_t, segw_t, float(loss_scale), losses, rscale)
         self._last_losses = losses
 
+        self._mark("ce fwd")
         # ---------------- backward
         dall = torch.empty(Tt, D, dtype=F32, device=self.device)
         dlog = torch.empty(min(self.ce_chunk, Tt), self.Vp, dtype=BF16, device=self.device)
@@ -700,6 +747,7 @@ class TrainEngine:
             C.linear_wgrad(dl[:, :self.V], allx[a:b], self.g(m.head.weight))
             C.linear_dgrad(dl[:, :self.V], head_w, dall[a:b], False)
         del dlog
+        self._mark("ce bwd")
         dres = torch.zeros(T, D, dtype=F32, device=self.device)
         if mtp_ctx:
             # Depth d+1 consumed the first rows of depth d's normalised hidden,
@@ -720,6 +768,7 @@ class TrainEngine:
                     dres.view(B, S, D)[:, :ctx.Sm].add_(dprev.view(B, ctx.Sm, D))
                 else:
                     carry, carry_rows = dprev, ctx.Sm
+        self._mark("mtp bwd")
         dres_b = torch.empty(T, D, dtype=BF16, device=self.device)
         C.rmsnorm_bwd(dall[:T], hL, self.f32(m.norm.weight), rf, dres, None, dres_b, self.g(m.norm.weight))
         for li, (layer, (x_in, r1, actx, x_mid, xn2, r2, fctx)) in enumerate(zip(reversed(m.layers), reversed(saved))):
@@ -727,9 +776,11 @@ class TrainEngine:
             dxn2 = torch.empty(T, D, dtype=F32, device=self.device)
             if hasattr(layer.ffn, "experts"):
                 self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)
+                self._mark("moe bwd")
             else:
                 self._swiglu_dense_bwd(layer.ffn.w1.weight, layer.ffn.w2.weight, fctx, xn2, dres_b, dxn2,
                                        accumulate=False)
+                self._mark("dense ffn bwd")
             C.rmsnorm_bwd(dxn2, x_mid, self.f32(layer.ffn_norm.weight), r2, dres, None, dres_b,
                           self.g(layer.ffn_norm.weight))
             dxn1 = torch.empty(T, D, dtype=F32, device=self.device)
@@ -738,6 +789,7 @@ class TrainEngine:
                           self.g(layer.attn_norm.weight))
             self._range(None)
         C.embedding_bwd(tok, dres, self.g(m.embed.weight))
+        self._mark("embedding bwd")
 
         balance = torch.zeros((), device=self.device)
         out = {"loss": losses[0], "mtp_loss": losses[1:].mean() if nseg > 1 else None, "balance_loss": balance}
@@ -755,16 +807,18 @@ class TrainEngine:
         return bool(self._finite)
 
     def clip_and_step(self, max_norm: float) -> None:
+        self._mark("between micro-steps")
         if self.dp is not None and hasattr(self.dp, "step"):
             self.dp.step(self.optimizer, max_norm)   # reduce-scatter + sharded AdamW + all-gather
-            return
-        if self.dp is not None:
-            self.dp.reduce_gradients()
-        extra = self.dp.extra_sqsum() if self.dp is not None else None
-        self.optimizer.compute_clip(max_norm, extra)
-        self.optimizer.step()
-        if self.dp is not None:
-            self.dp.after_step()
+        else:
+            if self.dp is not None:
+                self.dp.reduce_gradients()
+            extra = self.dp.extra_sqsum() if self.dp is not None else None
+            self.optimizer.compute_clip(max_norm, extra)
+            self.optimizer.step()
+            if self.dp is not None:
+                self.dp.after_step()
+        self._mark("optimizer step" if self.dp is None else "data-parallel optimizer step")
 
     def zero_grad(self) -> None:
         self.optimizer.zero_grad()

@@ -197,7 +197,7 @@ class ExpertParallel:
         return self._side
 
     def dispatch(self, slot: int, x: torch.Tensor, idx: torch.Tensor, wts: torch.Tensor, counts: torch.Tensor,
-                 overlap=None) -> dict:
+                 overlap=None, marks=None) -> dict:
         """Plan + P2P dispatch of ``x [T, D]`` along ``idx [T, k]``; waits for
         every peer's rows.  Returns the receive-side plan.  ``overlap()``
         (independent work, e.g. the shared experts) runs on a side stream
@@ -217,6 +217,8 @@ class ExpertParallel:
         C.ep_dispatch(self.heap.peers, offs, self.dims, x, idx, wts, plan["send_base"], self.cursor, plan["route"],
                       plan["row_off"], plan["recv_cnt"], self.done[0:1])
         plan["side"] = self._fork(overlap)
+        if marks is not None:
+            marks("ep plan+send")
         C.ep_wait(self.heap.peers, offs, self.dims, PH_DISPATCH, self.expect)
         return plan
 
@@ -227,10 +229,12 @@ class ExpertParallel:
         self.C.ep_wait(self.heap.peers, offs, self.dims, PH_COMBINE, self.expect)
 
     # ------------------------------------------------------------ backward
-    def dispatch_bwd(self, slot: int, g: torch.Tensor, route: torch.Tensor, overlap=None):
+    def dispatch_bwd(self, slot: int, g: torch.Tensor, route: torch.Tensor, overlap=None, marks=None):
         offs = self.offs(slot)
         self.C.ep_dispatch_bwd(self.heap.peers, offs, self.dims, g, route, self.done[2:3])
         side = self._fork(overlap)
+        if marks is not None:
+            marks("ep send bwd")
         self.C.ep_wait(self.heap.peers, offs, self.dims, PH_BWD_DISPATCH, self.expect)
         return side
 
@@ -264,8 +268,8 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     before the combine touches ``out``.
     """
     C = ep.C
-    plan = ep.dispatch(slot, xn, idx, wts, counts, overlap=overlap)
-    marks("dispatch")
+    plan = ep.dispatch(slot, xn, idx, wts, counts, overlap=overlap, marks=marks)
+    marks("ep dispatch wait")
     xs = ep.recv_rows(slot)
     h = torch.empty(ep.cap, inter_dim, dtype=torch.bfloat16, device=xn.device)
     gu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=xn.device)
@@ -286,6 +290,7 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     side = plan.pop("side")
     if side is not None:
         torch.cuda.current_stream(xn.device).wait_stream(side)
+    marks("ep combine wait")
     C.combine_fwd(ep.comb, ep.slot_arange, wts, out)
     marks("combine fwd")
     plan.update(slot=slot, xs=xs, h=h, gu=gu, ys=ys)
@@ -301,8 +306,8 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     on a side stream during the transfers, joined before ``dx_acc`` is read."""
     C = ep.C
     slot = ctx["slot"]
-    side = ep.dispatch_bwd(slot, dout_bf16, ctx["route"], overlap=overlap)
-    marks("dispatch bwd")
+    side = ep.dispatch_bwd(slot, dout_bf16, ctx["route"], overlap=overlap, marks=marks)
+    marks("ep dispatch wait bwd")
     dys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
     dw_rows = torch.empty(ep.cap, dtype=torch.float32, device=dout_bf16.device)
     ep.bwd_prep(slot, ctx["ys"], ctx["row_off"], dys, dw_rows)
@@ -327,6 +332,7 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
         ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])
     if side is not None:
         torch.cuda.current_stream(dx_acc.device).wait_stream(side)
+    marks("ep combine wait bwd")
     C.unpermute_bwd(ep.comb, ep.slot_arange, dx_acc)
     marks("combine bwd")
     return ep.dw_inbox.view(ep.T, ep.k)

@@ -33,6 +33,7 @@ from dataclasses import asdict, dataclass, field
 from pathlib import Path
 from typing import List, Dict, Optional, Tuple
 
+import numpy as np
 import torch
 import torch.nn as nn
 import yaml
@@ -110,54 +111,59 @@ class TrainingConfig:
 
 
 class PretrainDataset(Dataset):
-    """Packed next-token windows over one token file or a directory of shards."""
+    """Next-token training windows packed back to back over a token stream.
+
+    The stream is either one ``torch.save``d 1-D token tensor or the
+    concatenation, in file-name order, of a directory's ``shard_*.bin`` files
+    (the reference's two layouts, ``training/pretrain.py:70-130``).  Window
+    ``i`` is the ``max_seq_len + 1`` tokens starting at ``i * max_seq_len``,
+    returned as ``(inputs, targets)`` shifted by one; a window may span shard
+    files; the trailing partial window is dropped.
+
+    Every file is memory-mapped once and becomes one segment of the stream;
+    ``_ends`` holds each segment's exclusive end offset, so locating a token
+    is one binary search and reading a window walks the segments it overlaps.
+    """
 
     def __init__(self, data_path: str, max_seq_len: int, vocab_size: int):
-        self.max_seq_len = max_seq_len
+        self.max_seq_len = int(max_seq_len)
         self.vocab_size = vocab_size
-        if not os.path.exists(data_path):
+        root = Path(data_path)
+        if not root.exists():
             raise FileNotFoundError(f"Pre-training data not found: {data_path}\n"
-                                    "Prepare token shards first (data/prepare_data.py).")
-        self.layout = "sharded" if os.path.isdir(data_path) else "single"
-        if self.layout == "sharded":
-            self.shard_paths = [str(p) for p in sorted(Path(data_path).glob("shard_*.bin"))]
-            if not self.shard_paths:
-                raise FileNotFoundError(f"No `shard_*.bin` files in {data_path}")
-            self.shards = [torch.load(p, map_location="cpu", weights_only=True, mmap=True) for p in self.shard_paths]
-            self.shard_sizes = [int(s.numel()) for s in self.shards]
-            self.shard_offsets = [0]
-            for n in self.shard_sizes[:-1]:
-                self.shard_offsets.append(self.shard_offsets[-1] + n)
-            self._total_tokens = sum(self.shard_sizes)
-        else:
-            self.data = torch.load(data_path, map_location="cpu", weights_only=True, mmap=True)
-            self._total_tokens = int(self.data.numel())
-        self._n_samples = (self._total_tokens - 1) // self.max_seq_len
+                                    "Build token shards first (data/prepare_data.py or data/build_small_shard.py).")
+        self.layout = "sharded" if root.is_dir() else "single"
+        files = sorted(root.glob("shard_*.bin")) if root.is_dir() else [root]
+        if not files:
+            raise FileNotFoundError(f"{data_path} is a directory without shard_*.bin token files")
+        self.shard_paths = [str(f) for f in files]
+        self._segments = [torch.load(f, map_location="cpu", weights_only=True, mmap=True).reshape(-1) for f in files]
+        self._ends = np.cumsum([seg.numel() for seg in self._segments], dtype=np.int64)
+        self._total_tokens = int(self._ends[-1])
 
     def _locate(self, global_idx: int) -> Tuple[int, int]:
-        """``(shard index, offset in shard)`` of a global token index."""
-        if global_idx < 0 or global_idx >= self._total_tokens:
+        """``(segment, offset)`` of stream position ``global_idx``; ``IndexError`` outside the stream."""
+        if not 0 <= global_idx < self._total_tokens:
             raise IndexError(f"global_idx {global_idx} out of range [0, {self._total_tokens})")
-        import bisect
-        s = bisect.bisect_right(self.shard_offsets, global_idx) - 1
-        return s, global_idx - self.shard_offsets[s]
+        seg = int(np.searchsorted(self._ends, global_idx, side="right"))
+        return seg, global_idx - (int(self._ends[seg - 1]) if seg else 0)
+
+    def _read(self, begin: int, count: int) -> torch.Tensor:
+        seg, off = self._locate(begin)
+        pieces = []
+        while count > 0:
+            piece = self._segments[seg][off:off + count]
+            pieces.append(piece)
+            count -= piece.numel()
+            seg, off = seg + 1, 0
+        return torch.cat(pieces) if len(pieces) > 1 else pieces[0].clone()
 
     def __len__(self) -> int:
-        return self._n_samples
+        return max(0, (self._total_tokens - 1) // self.max_seq_len)
 
     def __getitem__(self, idx: int) -> Tuple[torch.Tensor, torch.Tensor]:
-        start, need = idx * self.max_seq_len, self.max_seq_len + 1
-        if self.layout == "single":
-            chunk = self.data[start:start + need].clone()
-        else:
-            parts, pos = [], start
-            while sum(int(p.numel()) for p in parts) < need:
-                s, off = self._locate(pos)
-                take = min(need - sum(int(p.numel()) for p in parts), self.shard_sizes[s] - off)
-                parts.append(self.shards[s][off:off + take])
-                pos += take
-            chunk = torch.cat(parts) if len(parts) > 1 else parts[0].clone()
-        return chunk[:-1], chunk[1:]
+        window = self._read(idx * self.max_seq_len, self.max_seq_len + 1)
+        return window[:-1], window[1:]
 
 
 class _LazyMetric:
@@ -521,6 +527,21 @@ class Pretrainer:
                 self._log(f"[warn] Could not load checkpoint: {exc}")
         self._log(f"Training from step {step} to {self.config.max_steps}")
         self.raw_model.train()
+        try:
+            step = self._train_loop(loader, step)
+            self.save_checkpoint(step, tag="final")
+        except BaseException:
+            # a background checkpoint write that failed must not go unseen
+            # behind the training error
+            try:
+                self.ckpt_manager.wait()
+            except Exception as exc:
+                self._log(f"[warn] background checkpoint write failed: {exc}")
+            raise
+        self.ckpt_manager.wait()
+        self._log("Training complete.")
+
+    def _train_loop(self, loader, step: int) -> int:
         streak = 0
         while step < self.config.max_steps:
             for tokens, targets in loader:
@@ -541,18 +562,18 @@ class Pretrainer:
                         streak = 0
                     continue
                 streak = 0
+                extras = None
                 if step % self.config.log_every == 0:
                     extras = {"balance_loss": float(metrics["balance_loss"])}
                     if metrics.get("mtp_loss") is not None:
                         extras["mtp_loss"] = float(metrics["mtp_loss"])
                     extras.update(self.step_diagnostics())
-                    self.logger.log(step, float(metrics["loss"]), lr=self.scheduler.get_last_lr()[0], metrics=extras)
+                # the loss stays on the device; the logger reads it once per interval
+                self.logger.log(step, metrics["loss"], lr=self.scheduler.get_last_lr()[0], metrics=extras)
                 if step % self.config.save_every == 0 and step > 0:
                     self.save_checkpoint(step)
                 step += 1
-        self.save_checkpoint(step, tag="final")
-        self.ckpt_manager.wait()
-        self._log("Training complete.")
+        return step
 
 
 def config_from_yaml(yaml_cfg: dict, data_path: Optional[str] = None, checkpoint_dir: Optional[str] = None,
