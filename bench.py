@@ -237,15 +237,19 @@ def timed_steps(run_step, steps, world, local):
 def phase_breakdown(engine, run_step, world):
     """One optimizer step with CUDA events between the engine's phases.
 
-    Returns ``{phase: [max over ranks, min over ranks]}`` in ms, summed over
-    the step's micro-batches and layers (the CUDA graph is off for this step,
-    so the sum also shows host-side gaps as ``between micro-steps``)."""
+    The micro-step is captured once more with event-record nodes between its
+    phases (its own CUDA graph; one untimed step captures it), then one
+    optimizer step is booked.  Returns ``{phase: [max over ranks, min over
+    ranks]}`` in ms, summed over the step's micro-batches and layers."""
     import torch
     import torch.distributed as dist
     from ops.engine import PhaseTimer
     engine.phase_timer = PhaseTimer(engine.device)
     try:
-        run_step(0)
+        run_step(0)                       # capture the marked graph
+        engine.phase_timer.collect()
+        engine.phase_timer.totals = {}
+        run_step(1)
         totals = engine.phase_timer.collect()
     finally:
         engine.phase_timer = None

@@ -634,50 +634,6 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   TORCH_CHECK(false, "flash_bwd: unsupported head dims ", dqk, "/", dvv);
 }
 
-namespace {
-
-template <int R, int DRP, int NW>
-void launch_latent_mma(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv, const at::Tensor& pe,
-                       const at::Tensor& lens, int B, int H, int dr, int qpb, int chunk, int nsplit, double scale,
-                       float* pm, float* pl, float* po, cudaStream_t st) {
-  constexpr int KS = R + DRP + 8;
-  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * NW * 16 * 4;
-  auto kern = latent_decode_mma_kernel<R, DRP, NW>;
-  static bool configured = false;
-  if (!configured) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = true;
-  }
-  dim3 grid(nsplit, (H + 15) / 16, B);
-  kern<<<grid, 32 * NW, smem, st>>>(reinterpret_cast<const bf16*>(q_lat.data_ptr()),
-                                reinterpret_cast<const bf16*>(q_pe.data_ptr()),
-                                reinterpret_cast<const bf16*>(kv.data_ptr()),
-                                reinterpret_cast<const bf16*>(pe.data_ptr()), lens.data_ptr<int>(), H, dr,
-                                kv.stride(0), pe.stride(0), qpb, chunk, nsplit,
-                                (float)(scale * 1.4426950408889634), pm, pl, po);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-// Dispatch onto the instantiated (latent, padded rope) sizes; false if none fits.
-bool run_latent_mma(int R, int dr, const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& kv,
-                    const at::Tensor& pe, const at::Tensor& lens, int B, int H, int qpb, int chunk, int nsplit,
-                    double scale, float* pm, float* pl, float* po, cudaStream_t st) {
-  const int drp = (dr + 15) / 16 * 16;
-#define DSV3_LD_CASE(R_, DRP_, NW_)                                                                           \
-  if (R == R_ && drp == DRP_) {                                                                                \
-    launch_latent_mma<R_, DRP_, NW_>(q_lat, q_pe, kv, pe, lens, B, H, dr, qpb, chunk, nsplit, scale, pm, pl, po, \
-                                     st);                                                                      \
-    return true;                                                                                               \
-  }
-  DSV3_LD_CASE(512, 64, 8)
-  DSV3_LD_CASE(192, 32, 4)
-  DSV3_LD_CASE(128, 32, 8)
-  DSV3_LD_CASE(64, 16, 4)
-#undef DSV3_LD_CASE
-  return false;
-}
-
-}  // namespace
 
 // q_lat [B, H, R], q_pe [B, H, dr], kv [B, S, R] (batch stride kv.stride(0)),
 // pe [B, S, dr], lens [B] int32 -> out [B, H, R] bf16.
@@ -690,36 +646,29 @@ void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   const int B = q_lat.size(0), H = q_lat.size(1), R = q_lat.size(2), dr = q_pe.size(2);
   TORCH_CHECK(R <= 1024 && dr <= 128, "latent_decode: R <= 1024, dr <= 128");
   const at::cuda::CUDAGuard guard(q_lat.device());
-  auto st = at::cuda::getCurrentCUDAStream();
-  const int chunk = 256;
-  const int nsplit = std::max<int>(1, (max_len + chunk - 1) / chunk);
-  const long need = (long)B * H * nsplit * (2 + R);
+  const long long need = latent_decode_scratch_floats(B, H, R, (int)max_len);
   TORCH_CHECK(scratch.numel() >= need && scratch.scalar_type() == at::kFloat, "latent_decode: scratch too small (need ",
               need, " floats)");
-  float* pm = scratch.data_ptr<float>();
-  float* pl = pm + (long)B * H * nsplit;
-  float* po = pl + (long)B * H * nsplit;
   TORCH_CHECK(kv.stride(1) == R && pe.stride(1) == dr && kv.stride(2) == 1 && pe.stride(2) == 1,
               "latent_decode: cache rows must be contiguous");
-  const int qpb_ = (int)std::max<int64_t>(1, qpb);
-  // Tensor-core path: all heads of a query row share each staged cache tile.
-  if (dr % 8 == 0 && dr <= 64 && kv.stride(0) % 8 == 0 && pe.stride(0) % 8 == 0 &&
-      run_latent_mma(R, dr, q_lat, q_pe, kv, pe, lens, B, H, qpb_, chunk, nsplit, scale, pm, pl, po, st)) {
-    latent_decode_merge_kernel<<<B * H, 128, 0, st>>>(pm, pl, po, nsplit, R, B * H,
-                                                      reinterpret_cast<bf16*>(out.data_ptr()));
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    return;
-  }
-  const int warps = B * H * nsplit;
-  latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, st>>>(
-      reinterpret_cast<const bf16*>(q_lat.data_ptr()), reinterpret_cast<const bf16*>(q_pe.data_ptr()),
-      reinterpret_cast<const bf16*>(kv.data_ptr()), reinterpret_cast<const bf16*>(pe.data_ptr()),
-      lens.data_ptr<int>(), H, R, dr, kv.stride(0), pe.stride(0), (int)std::max<int64_t>(1, qpb), chunk, nsplit, B * H,
-      (float)scale, pm, pl, po);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  latent_decode_merge_kernel<<<B * H, 128, 0, st>>>(pm, pl, po, nsplit, R, B * H,
-                                                    reinterpret_cast<bf16*>(out.data_ptr()));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LatentDecodeArgs a{};
+  a.q_lat = reinterpret_cast<const bf16*>(q_lat.data_ptr());
+  a.q_pe = reinterpret_cast<const bf16*>(q_pe.data_ptr());
+  a.kv = reinterpret_cast<const bf16*>(kv.data_ptr());
+  a.pe = reinterpret_cast<const bf16*>(pe.data_ptr());
+  a.lens = lens.data_ptr<int>();
+  a.B = B;
+  a.H = H;
+  a.R = R;
+  a.dr = dr;
+  a.kv_bs = kv.stride(0);
+  a.pe_bs = pe.stride(0);
+  a.qpb = (int)std::max<int64_t>(1, qpb);
+  a.max_len = (int)max_len;
+  a.scale = (float)scale;
+  a.scratch = scratch.data_ptr<float>();
+  a.out = reinterpret_cast<bf16*>(out.data_ptr());
+  C10_CUDA_CHECK(launch_latent_decode(a, at::cuda::getCurrentCUDAStream()));
 }
 
 // The tcgen05 forward (attention_sm100.cuh).  Same contract as flash_fwd.

@@ -13,7 +13,8 @@
 //   dp_norm      all-gather of the per-rank squared norms through peer
 //                stores, then the global clip coefficient (same value on
 //                every rank);
-//   dp_update    AdamW on the shard (fp32 moments of this rank's shard only)
+//   dp_update    AdamW on the shard (fp32 moments of this rank's shard only:
+//                the moment buffers hold [lo, hi) and nothing else)
 //                fused with the all-gather: the updated fp32 master and its
 //                bf16 shadow are stored straight into every peer's buffers.
 //
@@ -160,14 +161,14 @@ __global__ void __launch_bounds__(256) dp_update_kernel(DpArgs a, long long off_
        i += (long long)gridDim.x * blockDim.x) {
     const float4 g = g4[i];
     float4 p = p4[i];
-    float4 mm = reinterpret_cast<float4*>(m)[i], vv = reinterpret_cast<float4*>(v)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i - lo4], vv = reinterpret_cast<float4*>(v)[i - lo4];
     const long long e = 4 * i;
     adamw_elem(p.x, mm.x, vv.x, g.x * coef, e < n_decay, h);
     adamw_elem(p.y, mm.y, vv.y, g.y * coef, e + 1 < n_decay, h);
     adamw_elem(p.z, mm.z, vv.z, g.z * coef, e + 2 < n_decay, h);
     adamw_elem(p.w, mm.w, vv.w, g.w * coef, e + 3 < n_decay, h);
-    reinterpret_cast<float4*>(m)[i] = mm;
-    reinterpret_cast<float4*>(v)[i] = vv;
+    reinterpret_cast<float4*>(m)[i - lo4] = mm;
+    reinterpret_cast<float4*>(v)[i - lo4] = vv;
     const uint2 sh = make_uint2(pack_bf16x2(p.x, p.y), pack_bf16x2(p.z, p.w));
     for (int r = 0; r < a.R; ++r) {
       at_rank<float4>(a, r, off_master)[i] = p;
@@ -241,7 +242,8 @@ void dp_update(const std::vector<int64_t>& peers, const std::vector<int64_t>& of
   const DpArgs a = make_args(peers, offs, me, budget_ns);
   TORCH_CHECK(lo % 4 == 0 && hi % 4 == 0 && off_master % 16 == 0 && off_grad % 16 == 0 && off_shadow % 8 == 0,
               "dp_update: aligned shard");
-  TORCH_CHECK(m.is_contiguous() && v.is_contiguous() && m.numel() >= hi && v.numel() >= hi, "dp_update: moments");
+  TORCH_CHECK(m.is_contiguous() && v.is_contiguous() && m.numel() == hi - lo && v.numel() == hi - lo,
+              "dp_update: moments must hold exactly the shard [lo, hi)");
   if (hi <= lo) return;
   const AdamHyper h{(float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd,
                     1.0f - (float)std::pow(beta1, (double)step), (float)std::sqrt(1.0 - std::pow(beta2, (double)step))};

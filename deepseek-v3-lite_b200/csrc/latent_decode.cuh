@@ -302,3 +302,80 @@ __global__ void __launch_bounds__(32 * NW) latent_decode_mma_kernel(
       *reinterpret_cast<float2*>(po + n * 8 + 2 * tig) = make_float2(o[n][2 * r], o[n][2 * r + 1]);
   }
 }
+
+// ---------------------------------------------------------------------------
+// Host-side launcher shared by both entry points (no torch types): picks the
+// tensor-core kernel when the sizes fit one of its instantiations, else the
+// per-warp kernel, then the merge.  Scratch layout: part_m [B*H*nsplit],
+// part_l [B*H*nsplit], part_o [B*H*nsplit*R] (fp32).  Returns the first
+// launch error (each launch goes through cudaLaunchKernelEx, whose return
+// value is that launch's own status).
+struct LatentDecodeArgs {
+  const bf16* q_lat;
+  const bf16* q_pe;
+  const bf16* kv;
+  const bf16* pe;
+  const int* lens;
+  int B, H, R, dr;
+  long kv_bs, pe_bs;   // batch strides of the caches (elements)
+  int qpb;             // query rows per cache batch row
+  int max_len;
+  float scale;
+  float* scratch;
+  bf16* out;
+};
+
+inline int latent_decode_nsplit(int max_len) { return max_len < 1 ? 1 : (max_len + 255) / 256; }
+
+inline long long latent_decode_scratch_floats(int B, int H, int R, int max_len) {
+  return (long long)B * H * latent_decode_nsplit(max_len) * (2 + R);
+}
+
+template <typename Kern, typename... Args>
+inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <int R, int DRP, int NW>
+inline cudaError_t launch_latent_mma(const LatentDecodeArgs& a, int nsplit, float* pm, float* pl, float* po,
+                                     cudaStream_t st) {
+  constexpr int KS = R + DRP + 8;
+  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * NW * 16 * 4;
+  auto kern = latent_decode_mma_kernel<R, DRP, NW>;
+  // the shared-memory opt-in is per device: set it on every call (cheap, host only)
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_ex(kern, dim3(nsplit, (a.H + 15) / 16, a.B), dim3(32 * NW), smem, st, a.q_lat, a.q_pe, a.kv, a.pe,
+                   a.lens, a.H, a.dr, a.kv_bs, a.pe_bs, a.qpb, 256, nsplit, (float)(a.scale * 1.4426950408889634),
+                   pm, pl, po);
+}
+
+inline cudaError_t launch_latent_decode(const LatentDecodeArgs& a, cudaStream_t st) {
+  const int nsplit = latent_decode_nsplit(a.max_len);
+  float* pm = a.scratch;
+  float* pl = pm + (long long)a.B * a.H * nsplit;
+  float* po = pl + (long long)a.B * a.H * nsplit;
+  cudaError_t e = cudaErrorNotSupported;
+  const int drp = (a.dr + 15) / 16 * 16;
+  const bool mma_ok = a.dr % 8 == 0 && a.dr <= 64 && a.kv_bs % 8 == 0 && a.pe_bs % 8 == 0;
+#define DSV3_LD_CASE(R_, DRP_, NW_) \
+  if (mma_ok && a.R == R_ && drp == DRP_) e = launch_latent_mma<R_, DRP_, NW_>(a, nsplit, pm, pl, po, st);
+  DSV3_LD_CASE(512, 64, 8)
+  DSV3_LD_CASE(192, 32, 4)
+  DSV3_LD_CASE(128, 32, 8)
+  DSV3_LD_CASE(64, 16, 4)
+#undef DSV3_LD_CASE
+  if (e == cudaErrorNotSupported) {
+    const int warps = a.B * a.H * nsplit;
+    e = launch_ex(latent_decode_split_kernel, dim3((warps + 3) / 4), dim3(128), 0, st, a.q_lat, a.q_pe, a.kv, a.pe,
+                  a.lens, a.H, a.R, a.dr, a.kv_bs, a.pe_bs, a.qpb, 256, nsplit, a.B * a.H, a.scale, pm, pl, po);
+  }
+  if (e != cudaSuccess) return e;
+  return launch_ex(latent_decode_merge_kernel, dim3(a.B * a.H), dim3(128), 0, st, (const float*)pm, (const float*)pl,
+                   (const float*)po, nsplit, a.R, a.B * a.H, a.out);
+}

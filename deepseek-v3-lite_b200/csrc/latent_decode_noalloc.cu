@@ -1,6 +1,9 @@
 // Allocation-free absorbed-MLA decode (see latent_decode_noalloc.h for the
-// contract).  Same kernels as the torch entry point; the split-K partials
-// live in a fixed file-scope device array instead of a caller tensor.
+// contract).  It calls the same launcher as the torch entry point
+// `latent_decode` (latent_decode.cuh: the tensor-core kernel where the sizes
+// fit, else the per-warp kernel, then the merge), so both run the same
+// kernels on the same inputs; only the split-K partials live in a fixed
+// file-scope device array instead of a caller tensor.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -22,7 +25,10 @@ typedef __nv_bfloat16 bf16;
 // Split-K partials (max, sum, partial output) of the most recent call.
 static __device__ __align__(256) float g_decode_scratch[DSV3_NOALLOC_SCRATCH_FLOATS];
 
-// Device address of g_decode_scratch per device, looked up once per device.
+// Device address of g_decode_scratch per device, looked up once per device and
+// kept for the life of the process.  A cudaDeviceReset (or any other
+// destruction of the device's primary context) invalidates it; this library
+// does not support calls after such a reset.
 static std::atomic<float*> g_scratch_addr[DSV3_NOALLOC_MAX_DEVICES];
 
 static float* scratch_for_current_device(int* err) {
@@ -49,21 +55,28 @@ extern "C" __attribute__((visibility("default"))) int dsv3_latent_decode_noalloc
   if (!q_lat || !q_pe || !kv || !pe || !lens || !out || B <= 0 || H <= 0 || R <= 0 || R > 1024 || dr < 0 ||
       dr > 128 || max_len <= 0)
     return DSV3_NOALLOC_BAD_ARGS;
-  const int chunk = 256;
-  const int nsplit = (max_len + chunk - 1) / chunk;
-  const long long need = (long long)B * H * nsplit * (2 + R);
-  if (need > DSV3_NOALLOC_SCRATCH_FLOATS) return DSV3_NOALLOC_TOO_LARGE;
+  if (dsv3::latent_decode_scratch_floats(B, H, R, max_len) > DSV3_NOALLOC_SCRATCH_FLOATS) return DSV3_NOALLOC_TOO_LARGE;
   int err = DSV3_NOALLOC_OK;
   float* scratch = scratch_for_current_device(&err);
   if (!scratch) return err;
-  float* pm = scratch;
-  float* pl = pm + (long long)B * H * nsplit;
-  float* po = pl + (long long)B * H * nsplit;
-  const int warps = B * H * nsplit;
-  dsv3::latent_decode_split_kernel<<<(warps + 3) / 4, 128, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(q_lat), static_cast<const __nv_bfloat16*>(q_pe), static_cast<const __nv_bfloat16*>(kv),
-      static_cast<const __nv_bfloat16*>(pe), lens, H, R, dr, (long)kv_batch_stride, (long)pe_batch_stride, 1, chunk, nsplit,
-      B * H, scale, pm, pl, po);
-  dsv3::latent_decode_merge_kernel<<<B * H, 128, 0, stream>>>(pm, pl, po, nsplit, R, B * H, static_cast<__nv_bfloat16*>(out));
-  return cudaGetLastError() == cudaSuccess ? DSV3_NOALLOC_OK : DSV3_NOALLOC_CUDA_ERROR;
+  dsv3::LatentDecodeArgs a{};
+  a.q_lat = static_cast<const __nv_bfloat16*>(q_lat);
+  a.q_pe = static_cast<const __nv_bfloat16*>(q_pe);
+  a.kv = static_cast<const __nv_bfloat16*>(kv);
+  a.pe = static_cast<const __nv_bfloat16*>(pe);
+  a.lens = lens;
+  a.B = B;
+  a.H = H;
+  a.R = R;
+  a.dr = dr;
+  a.kv_bs = (long)kv_batch_stride;
+  a.pe_bs = (long)pe_batch_stride;
+  a.qpb = 1;
+  a.max_len = max_len;
+  a.scale = scale;
+  a.scratch = scratch;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  // the launches' own status (not cudaGetLastError, which would also report,
+  // and clear, an unrelated earlier error of this thread)
+  return dsv3::launch_latent_decode(a, stream) == cudaSuccess ? DSV3_NOALLOC_OK : DSV3_NOALLOC_CUDA_ERROR;
 }

@@ -21,6 +21,15 @@
 //     before any stream capture;
 //   * all calls share the one array, so calls whose kernels overlap on the
 //     GPU (different streams, no ordering between them) race on it;
+//   * the looked-up address is cached per device for the life of the
+//     process; calls after a cudaDeviceReset are not supported;
+//   * lens[b] must not exceed max_len: cache rows past
+//     ceil(max_len / 256) * 256 are not read (the result is then computed
+//     over a truncated cache, silently; no out-of-bounds access occurs);
+//   * a row with lens[b] == 0 yields zeros;
+//   * the return value reports argument errors and the status of this
+//     call's own kernel launches (asynchronous faults surface later, as for
+//     any CUDA launch);
 //   * no cudaMalloc / cudaFree or allocating library routine is called.
 #pragma once
 

@@ -56,9 +56,13 @@ class PhaseTimer:
     """Device time per named phase of the training step.
 
     ``mark(name)`` records a CUDA event on the current stream; the time since
-    the previous mark is booked to ``name``.  ``collect()`` synchronises and
-    adds the intervals to ``totals`` (ms).  The engine only marks with the CUDA
-    graph off, so every event is a real launch-order point on the stream.
+    the previous mark is booked to ``name``.  While a CUDA graph is being
+    captured the events become event-record nodes of the graph
+    (``external=True``), so a replay re-records them and the phases of the
+    graphed micro-step are timed without host launch gaps in between.
+    ``book(events)`` synchronises and adds a list of marks' intervals to
+    ``totals`` (ms); ``collect()`` books the marks recorded since the last
+    ``take()``.
     """
 
     def __init__(self, device):
@@ -67,15 +71,21 @@ class PhaseTimer:
         self._events: list = []
 
     def mark(self, name: str) -> None:
-        ev = torch.cuda.Event(enable_timing=True)
+        ev = torch.cuda.Event(enable_timing=True, external=bool(torch.cuda.is_current_stream_capturing()))
         ev.record()
         self._events.append((name, ev))
 
-    def collect(self) -> Dict[str, float]:
+    def take(self) -> list:
+        ev, self._events = self._events, []
+        return ev
+
+    def book(self, events: list) -> None:
         torch.cuda.synchronize(self.device)
-        for (_, a), (name, b) in zip(self._events, self._events[1:]):
+        for (_, a), (name, b) in zip(events, events[1:]):
             self.totals[name] = self.totals.get(name, 0.0) + a.elapsed_time(b)
-        self._events = []
+
+    def collect(self) -> Dict[str, float]:
+        self.book(self.take())
         return self.totals
 
 
@@ -104,9 +114,10 @@ class TrainEngine:
         self.DP = max(32, _pad(self.dn + self.dr, 16))
         self.V = c["vocab_size"]
         self.Vp = _pad(self.V, 64)
-        self.q_lora = c["q_lora_rank"]
-        if self.q_lora > 0:
-            raise NotImplementedError("q_lora_rank > 0 is not wired into the fused engine yet")
+        # LoRA query path wq_a -> q_norm -> wq_b (reference models/mla.py:43-46, :105-108)
+        self.q_lora = int(c.get("q_lora_rank", 0) or 0)
+        if self.q_lora > 0 and self.q_lora % 8:
+            raise ValueError("q_lora_rank must be a multiple of 8 (16-byte GEMM rows)")
         self.max_seq_len = c["max_seq_len"]
         self.ce_chunk = int(os.environ.get("DSV3_CE_CHUNK_ROWS", "16384"))
         dist_on = torch.distributed.is_available() and torch.distributed.is_initialized()
@@ -187,9 +198,10 @@ class TrainEngine:
         expert_blocks: List[List[torch.nn.Parameter]] = []
         remote: List[torch.nn.Parameter] = []
         for layer in m.layers:
-            # q and kv_a projections share their input: one [wq; wkv_a] block
-            # makes them one GEMM (and one data-gradient, one weight-gradient)
-            add([layer.attn.wq.weight, layer.attn.wkv_a.weight])
+            # q (or LoRA q_a) and kv_a projections share their input: one
+            # [wq; wkv_a] block makes them one GEMM (and one data-gradient, one
+            # weight-gradient)
+            add([self._q_in(layer.attn), layer.attn.wkv_a.weight])
             ffn = layer.ffn
             if hasattr(ffn, "experts") and self.shard_experts:
                 lo, hi = self._exp_range
@@ -291,11 +303,17 @@ class TrainEngine:
         fl = self._fl(w)
         return fl.block_view(fl.grad if grad else fl.shadow, w, (n_groups,) + tuple(w.shape))
 
+    @staticmethod
+    def _q_in(attn):
+        """The query projection applied to the normalised input: ``wq``, or ``wq_a`` of the LoRA chain."""
+        return attn.wq_a.weight if getattr(attn, "q_lora_rank", 0) > 0 else attn.wq.weight
+
     def qkva_block(self, attn, grad: bool = False) -> torch.Tensor:
-        """``[wq; wkv_a]`` as one ``[H*(dn+dr) + R + dr, D]`` operand (shadow or grad)."""
-        fl = self._fl(attn.wq.weight)
-        rows = attn.wq.weight.shape[0] + attn.wkv_a.weight.shape[0]
-        return fl.block_view(fl.grad if grad else fl.shadow, attn.wq.weight, (rows, self.D))
+        """``[wq; wkv_a]`` (``[wq_a; wkv_a]`` with LoRA q) as one ``[Nq_in + R + dr, D]`` operand (shadow or grad)."""
+        first = self._q_in(attn)
+        fl = self._fl(first)
+        rows = first.shape[0] + attn.wkv_a.weight.shape[0]
+        return fl.block_view(fl.grad if grad else fl.shadow, first, (rows, self.D))
 
     # --------------------------------------------------------------- helpers
     def _norm(self, x, weight_param, eps=1e-6):
@@ -327,10 +345,19 @@ class TrainEngine:
         T = B * S
         ctx = _Ctx(xn=xn)
         Nq = H * (dn + dr)
+        nq_in = self.q_lora or Nq
         wqa = self.qkva_block(attn)
         qkva = torch.empty(T, wqa.shape[0], dtype=BF16, device=self.device)
-        C.linear_fwd(xn, wqa, qkva)                                   # [T, H*(dn+dr) + R + dr]
-        q, kv_a = qkva[:, :Nq], qkva[:, Nq:]
+        C.linear_fwd(xn, wqa, qkva)                                   # [T, nq_in + R + dr]
+        kv_a = qkva[:, nq_in:]
+        if self.q_lora:
+            qn = torch.empty(T, self.q_lora, dtype=BF16, device=self.device)
+            rq = torch.empty(T, dtype=F32, device=self.device)
+            C.rmsnorm_fwd(qkva[:, :nq_in], self.f32(attn.q_norm.weight), 1e-6, qn, rq)
+            q = self._linear(qn, attn.wq_b.weight)                    # [T, H*(dn+dr)]
+            ctx.update(qa=qkva[:, :nq_in], qn=qn, rq=rq)
+        else:
+            q = qkva[:, :Nq]
         lat = torch.empty(T, R, dtype=BF16, device=self.device)
         rkv = torch.empty(T, dtype=F32, device=self.device)
         C.rmsnorm_fwd(kv_a[:, :R], self.f32(attn.kv_norm.weight), 1e-6, lat, rkv)
@@ -360,13 +387,19 @@ class TrainEngine:
         C.flash_bwd(ctx.Q, ctx.K, ctx.V, ctx.O, dO, ctx.L, delta, dQ, dK, dV, 0, attn.softmax_scale, True, H)
         self._mark("flash bwd")
         Nq = H * (dn + dr)
-        dqkva = torch.empty(T, Nq + R + dr, dtype=BF16, device=self.device)
-        dq, dkv_a = dqkva[:, :Nq], dqkva[:, Nq:]
+        nq_in = self.q_lora or Nq
+        dqkva = torch.empty(T, nq_in + R + dr, dtype=BF16, device=self.device)
+        dkv_a = dqkva[:, nq_in:]
+        dq = torch.empty(T, Nq, dtype=BF16, device=self.device) if self.q_lora else dqkva[:, :Nq]
         dkvb = torch.empty(T, H * (dn + dv), dtype=BF16, device=self.device)
         C.mla_unpack(dQ, dK, dV, dq, dkvb, dkv_a[:, R:], B, S, H, dn, dr, dv, self.cos, self.sin, 0)
         dlat = self._linear_bwd(dkvb, ctx.lat, attn.wkv_b.weight)
         C.rmsnorm_bwd(dlat, ctx.kv_a[:, :R], self.f32(attn.kv_norm.weight), ctx.rkv, None, dkv_a[:, :R], None,
                       self.g(attn.kv_norm.weight))
+        if self.q_lora:
+            dqn = self._linear_bwd(dq, ctx.qn, attn.wq_b.weight)      # [T, q_lora], dW(wq_b) accumulated
+            C.rmsnorm_bwd(dqn, ctx.qa, self.f32(attn.q_norm.weight), ctx.rq, None, dqkva[:, :nq_in], None,
+                          self.g(attn.q_norm.weight))
         C.linear_wgrad(dqkva, ctx.xn, self.qkva_block(attn, grad=True))
         C.linear_dgrad(dqkva, self.qkva_block(attn), dxn_acc, False)
         self._mark("attn proj bwd")
@@ -607,12 +640,15 @@ class TrainEngine:
         ``use_graphs`` the whole micro-step is captured once per input shape
         into a CUDA graph and replayed (no per-kernel host launch cost).
         """
-        if self.use_graphs and self.phase_timer is None and torch.cuda.is_current_stream_capturing() is False:
+        if self.use_graphs and torch.cuda.is_current_stream_capturing() is False:
             return self._graphed(tokens, targets, loss_scale)
         return self._forward_backward(tokens, targets, loss_scale)
 
     def _graphed(self, tokens, targets, loss_scale):
-        key = (tuple(tokens.shape), float(loss_scale))
+        timer = self.phase_timer
+        if timer is not None:
+            timer.book(timer.take())       # marks issued before this micro-step (host side)
+        key = (tuple(tokens.shape), float(loss_scale), timer is not None)
         entry = self._graphs.get(key)
         if entry is None:
             st_tok = tokens.detach().clone()
@@ -624,19 +660,24 @@ class TrainEngine:
             with torch.cuda.stream(side):
                 self._forward_backward(st_tok, st_tgt, loss_scale)
             torch.cuda.current_stream().wait_stream(side)
+            if timer is not None:
+                timer.take()               # the eager warm-up's marks are not booked
             graph = torch.cuda.CUDAGraph()
             with _ext.launch_scope() as scope, torch.cuda.graph(graph):
                 out = self._forward_backward(st_tok, st_tgt, loss_scale)
+            marks = timer.take() if timer is not None else None
             for f, g in zip(self.flats, saved):
                 f.grad.copy_(g)
             del saved
-            entry = (graph, st_tok, st_tgt, out, self._finite, scope.count)
+            entry = (graph, st_tok, st_tgt, out, self._finite, scope.count, marks)
             self._graphs[key] = entry
-        graph, st_tok, st_tgt, out, finite, n_kernels = entry
+        graph, st_tok, st_tgt, out, finite, n_kernels, marks = entry
         st_tok.copy_(tokens)
         st_tgt.copy_(targets)
         graph.replay()
         _ext.add_launches(n_kernels)
+        if timer is not None:
+            timer.book(marks)              # this replay's event-record nodes
         self._finite = finite
         res = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in out.items()}
         self._last_losses = res["loss"]
@@ -809,7 +850,9 @@ class TrainEngine:
     def clip_and_step(self, max_norm: float) -> None:
         self._mark("between micro-steps")
         if self.dp is not None and hasattr(self.dp, "step"):
-            self.dp.step(self.optimizer, max_norm)   # reduce-scatter + sharded AdamW + all-gather
+            # optimizer.step() runs the reduce-scatter + sharded AdamW + all-gather
+            self.dp.max_norm = float(max_norm)
+            self.optimizer.step()
         else:
             if self.dp is not None:
                 self.dp.reduce_gradients()
@@ -884,13 +927,19 @@ class TrainEngine:
 
     def optimizer_state_for_checkpoint(self) -> dict:
         """torch-AdamW state dict with standalone tensors (reference layout)."""
+        full = None
         if self.dp is not None and hasattr(self.dp, "gather_moments"):
-            self.dp.gather_moments(self.optimizer)   # collective: every rank calls it
-        sd = self.optimizer.state_dict()
-        for st in sd["state"].values():
-            for k in ("exp_avg", "exp_avg_sq"):
-                if k in st:
-                    st[k] = st[k].clone()
-            if "step" in st:
-                st["step"] = st["step"].clone()
+            full = self.dp.gather_moments(self.optimizer)   # collective: every rank calls it
+            self.optimizer._bind_state(full)
+        try:
+            sd = self.optimizer.state_dict()
+            for st in sd["state"].values():
+                for k in ("exp_avg", "exp_avg_sq"):
+                    if k in st:
+                        st[k] = st[k].clone()
+                if "step" in st:
+                    st["step"] = st["step"].clone()
+        finally:
+            if full is not None:
+                self.optimizer._bind_state()
         return sd

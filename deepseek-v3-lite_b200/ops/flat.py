@@ -19,7 +19,9 @@ with no padding (e.g. ``[w1_e0, w3_e0, w1_e1, w3_e1, ...]`` forms the
 ``lr``) whose ``step`` runs the fused kernels over the flat buffers.  Its
 ``state_dict`` is the torch AdamW layout (``step``, ``exp_avg``,
 ``exp_avg_sq`` per parameter, same parameter indices), so optimizer files are
-interchangeable with the reference's.
+interchangeable with the reference's.  Under the peer-memory data-parallel
+step a flat's moments can be sharded (``shard_moments``): the rank keeps only
+its own range and the full moments exist only while a checkpoint is written.
 """
 from __future__ import annotations
 
@@ -141,13 +143,28 @@ class FlatAdamW(torch.optim.Optimizer):
         self.exp_avg = [torch.zeros_like(f.master) for f in self.flats]
         self.exp_avg_sq = [torch.zeros_like(f.master) for f in self.flats]
         self.step_count = 0
+        # flat index -> (lo, hi): the moments of that flat hold only [lo, hi)
+        self.moment_range: Dict[int, tuple] = {}
+        # replaces the local update when set (the data-parallel step); called
+        # from ``step`` so the LR scheduler sees a regular optimizer step
+        self.stepper = None
         self._scratch = torch.empty(1024 * 4, device=dev)
         self.sqsum = torch.zeros(1, device=dev)
         self.grad_norm = torch.zeros(1, device=dev)
         self.clip = torch.ones(1, device=dev)
         self._bind_state()
 
-    def _bind_state(self) -> None:
+    def shard_moments(self, fi: int, lo: int, hi: int) -> None:
+        """Keep only elements ``[lo, hi)`` of flat ``fi``'s AdamW moments (this rank's shard)."""
+        self.exp_avg[fi] = self.exp_avg[fi][lo:hi].clone()
+        self.exp_avg_sq[fi] = self.exp_avg_sq[fi][lo:hi].clone()
+        self.moment_range[fi] = (lo, hi)
+        self._bind_state()
+
+    def _bind_state(self, full: Optional[Dict[int, tuple]] = None) -> None:
+        """Point ``state[p]`` at views of the moment buffers.  A sharded flat
+        binds only ``step`` unless ``full`` supplies its gathered
+        ``(exp_avg, exp_avg_sq)`` full-size buffers (checkpoint writing)."""
         for group in self.param_groups:
             for p in group["params"]:
                 fi = self._flat_of.get(id(p))
@@ -155,11 +172,12 @@ class FlatAdamW(torch.optim.Optimizer):
                     self.state.pop(p, None)
                     continue
                 f = self.flats[fi]
-                self.state[p] = {
-                    "step": torch.tensor(float(self.step_count)),
-                    "exp_avg": f.view(self.exp_avg[fi], p),
-                    "exp_avg_sq": f.view(self.exp_avg_sq[fi], p),
-                }
+                st = {"step": torch.tensor(float(self.step_count))}
+                if fi not in self.moment_range:
+                    st.update(exp_avg=f.view(self.exp_avg[fi], p), exp_avg_sq=f.view(self.exp_avg_sq[fi], p))
+                elif full is not None and fi in full:
+                    st.update(exp_avg=f.view(full[fi][0], p), exp_avg_sq=f.view(full[fi][1], p))
+                self.state[p] = st
 
     def compute_clip(self, max_norm: float, extra_sqsum: Optional[torch.Tensor] = None) -> None:
         """Global grad norm over all flats (plus ``extra_sqsum`` from other
@@ -191,6 +209,9 @@ class FlatAdamW(torch.optim.Optimizer):
 
     @torch.no_grad()
     def step(self, closure=None):
+        if self.stepper is not None:
+            self.stepper(self)
+            return None
         self.step_count += 1
         for fi in range(len(self.flats)):
             self.step_flat(fi)
@@ -211,8 +232,17 @@ class FlatAdamW(torch.optim.Optimizer):
                 fi = self._flat_of.get(id(p))
                 if "exp_avg" in st and fi is not None:
                     f = self.flats[fi]
-                    f.view(self.exp_avg[fi], p).copy_(st["exp_avg"].reshape(p.shape))
-                    f.view(self.exp_avg_sq[fi], p).copy_(st["exp_avg_sq"].reshape(p.shape))
+                    if fi in self.moment_range:
+                        # copy only the part of p inside this rank's shard
+                        lo, hi = self.moment_range[fi]
+                        o = f.offsets[id(p)]
+                        a, b = max(lo, o), min(hi, o + p.numel())
+                        if a < b:
+                            for dst, key in ((self.exp_avg[fi], "exp_avg"), (self.exp_avg_sq[fi], "exp_avg_sq")):
+                                dst[a - lo:b - lo].copy_(st[key].reshape(-1)[a - o:b - o])
+                    else:
+                        f.view(self.exp_avg[fi], p).copy_(st["exp_avg"].reshape(p.shape))
+                        f.view(self.exp_avg_sq[fi], p).copy_(st["exp_avg_sq"].reshape(p.shape))
                     steps.append(int(float(st["step"])))
         if steps:
             self.step_count = max(steps)

@@ -54,8 +54,7 @@ class InferenceEngine:
         self.cos, self.sin = rope_cos_sin(c["max_seq_len"], self.dr, float(c["rope_theta"]), self.device)
         self._cache: Dict[tuple, torch.Tensor] = {}
         self._graphs: Dict[tuple, tuple] = {}
-        if c.get("q_lora_rank", 0) > 0:
-            raise NotImplementedError("q_lora_rank > 0 is not wired into the native inference path yet")
+        self.q_lora = int(c.get("q_lora_rank", 0) or 0)
 
     # ------------------------------------------------------------ weights
     def _key(self, tag, *params):
@@ -74,20 +73,39 @@ class InferenceEngine:
         for k in [k for k in self._cache if k[0] == tag and k[1][0] == id(p)]:
             del self._cache[k]
 
+    @staticmethod
+    def _wq(attn):
+        """The projection that yields q from its input: ``wq`` (input: normalised x)
+        or ``wq_b`` of the LoRA chain (input: ``q_norm(wq_a x)``)."""
+        return attn.wq_b.weight if getattr(attn, "q_lora_rank", 0) > 0 else attn.wq.weight
+
+    def _q_input(self, attn, xn):
+        """What the query projection multiplies: ``xn`` or ``q_norm(wq_a xn)``."""
+        if not self.q_lora:
+            return xn
+        qa = self._lin(xn, self.bf16(attn.wq_a.weight))
+        qn = torch.empty_like(qa)
+        self.C.rmsnorm_fwd(qa, attn.q_norm.weight.detach().float().contiguous(), 1e-6, qn,
+                           torch.empty(0, device=self.device))
+        return qn
+
     def _absorbed(self, attn):
-        """(Wq_lat [H*R, D], Wq_pe [H*dr, D], W_out [D, H*R]) for ``attn`` (bf16)."""
-        k = self._key("abs", attn.wq.weight, attn.wkv_b.weight, attn.wo.weight)
+        """(Wq_lat [H*R, Din], Wq_pe [H*dr, Din], W_out [D, H*R]) for ``attn`` (bf16);
+        ``Din`` is the query projection's input width (D, or q_lora_rank)."""
+        wq_p = self._wq(attn)
+        k = self._key("abs", wq_p, attn.wkv_b.weight, attn.wo.weight)
         got = self._cache.get(k)
         if got is not None:
             return got
-        self._drop("abs", attn.wq.weight)
+        self._drop("abs", wq_p)
         H, dn, dr, dv, R, D = self.H, self.dn, self.dr, self.dv, self.R, self.D
         with torch.no_grad():
-            wq = attn.wq.weight.float().view(H, dn + dr, D)
+            Din = wq_p.shape[1]
+            wq = wq_p.float().view(H, dn + dr, Din)
             wkvb = attn.wkv_b.weight.float().view(H, dn + dv, R)
             w_k, w_v = wkvb[:, :dn], wkvb[:, dn:]
-            q_lat = torch.einsum("hdr,hdk->hrk", w_k, wq[:, :dn]).reshape(H * R, D)   # rows: W_k[h]^T Wq_nope[h]
-            q_pe = wq[:, dn:].reshape(H * dr, D)
+            q_lat = torch.einsum("hdr,hdk->hrk", w_k, wq[:, :dn]).reshape(H * R, Din)   # rows: W_k[h]^T Wq_nope[h]
+            q_pe = wq[:, dn:].reshape(H * dr, Din)
             wo = attn.wo.weight.float().view(D, H, dv)
             w_out = torch.einsum("khd,hdr->khr", wo, w_v).reshape(D, H * R)          # Wo_h W_v[h]
             got = (q_lat.to(BF16).contiguous(), q_pe.to(BF16).contiguous(), w_out.to(BF16).contiguous())
@@ -175,7 +193,7 @@ class InferenceEngine:
         """Materialised causal attention for a prompt starting at position 0."""
         C, H, dn, dr, dv, R = self.C, self.H, self.dn, self.dr, self.dv, self.R
         T = B * S
-        q = self._lin(xn, self.bf16(attn.wq.weight))
+        q = self._lin(self._q_input(attn, xn), self.bf16(self._wq(attn)))
         kv_a = self._lin(xn, self.bf16(attn.wkv_a.weight))
         lat = torch.empty(T, R, dtype=BF16, device=self.device)
         C.rmsnorm_fwd(kv_a[:, :R], attn.kv_norm.weight.detach().float().contiguous(), 1e-6, lat,
@@ -209,8 +227,9 @@ class InferenceEngine:
         rows = torch.arange(B, device=self.device).repeat_interleave(S)
         attn.kv_cache[rows, pos.long()] = lat
         attn.pe_cache[rows, pos.long()] = kpe.view(T, dr)
-        q_lat = self._lin(xn, wq_lat).view(T, H, R)
-        q_pe = self._lin(xn, wq_pe).view(T, H, dr)
+        q_src = self._q_input(attn, xn)
+        q_lat = self._lin(q_src, wq_lat).view(T, H, R)
+        q_pe = self._lin(q_src, wq_pe).view(T, H, dr)
         C.rope_inplace(q_pe, 0, dr // 2, self.cos, self.sin, pos, 1, 0, False)
         max_len = int(self.c["max_seq_len"])
         nsplit = (max_len + 255) // 256
@@ -263,7 +282,7 @@ class InferenceEngine:
     def _graph_key(self, B: int) -> tuple:
         m = self.model
         caches = tuple(layer.attn.kv_cache.data_ptr() for layer in m.layers)
-        probe = (m.embed.weight, m.layers[0].attn.wq.weight, m.layers[-1].attn.wo.weight, m.head.weight)
+        probe = (m.embed.weight, self._wq(m.layers[0].attn), m.layers[-1].attn.wo.weight, m.head.weight)
         return (B, caches, tuple((p.data_ptr(), p._version) for p in probe))
 
     @torch.no_grad()

@@ -85,9 +85,10 @@ class FusedDataParallel(DataParallel):
     buffers and takes its squared norm, an exchange of the norms (same clip
     coefficient everywhere), and AdamW on the shard only, whose new master and
     bf16 shadow values are stored into every rank's buffers (the
-    all-gather), then a closing barrier.  Adam moments are only advanced for
-    the rank's own shard; ``gather_moments`` assembles the full moments (for
-    checkpoints, in the torch AdamW layout).
+    all-gather), then a closing barrier.  Each rank allocates and advances
+    the Adam moments of its own shard only (ZeRO-1: 8 bytes per replicated
+    parameter per rank become 8 / ranks); ``gather_moments`` assembles the
+    full moments for the duration of a checkpoint write.
     """
 
     PH_READY, PH_NORM, PH_GATHERED = 0, 1, 2
@@ -131,6 +132,12 @@ class FusedDataParallel(DataParallel):
         dev = engine.flats[0].master.device
         self.expect = torch.zeros(4 * 8, dtype=torch.int32, device=dev)
         self.sq = torch.zeros(1, dtype=torch.float32, device=dev)
+        opt = engine.optimizer
+        for fi, (lo, hi) in enumerate(self.shards):
+            opt.shard_moments(fi, lo, hi)
+        # optimizer.step() runs this rank's part of the data-parallel step
+        self.max_norm = float(getattr(engine.config, "max_grad_norm", 1.0))
+        opt.stepper = lambda o: self.step(o, self.max_norm)
 
     def _args(self):
         return self.heap.peers, self.offs, self.rank, self.budget_ns
@@ -172,11 +179,20 @@ class FusedDataParallel(DataParallel):
         optimizer.mark_step()
         C.dp_barrier(peers, offs, me, budget, self.PH_GATHERED, self.expect)
 
-    def gather_moments(self, optimizer) -> None:
-        """Every rank's moment shards -> full moments on every rank (collective)."""
-        for gi, f in enumerate(optimizer.flats[:self.n_heap]):
-            for buf in (optimizer.exp_avg[gi], optimizer.exp_avg_sq[gi]):
+    def gather_moments(self, optimizer) -> dict:
+        """Every rank's moment shards -> ``{flat index: (exp_avg, exp_avg_sq)}``
+        full-size buffers on every rank (collective; the caller drops them)."""
+        full = {}
+        for fi, f in enumerate(optimizer.flats[:self.n_heap]):
+            bufs = []
+            for shard in (optimizer.exp_avg[fi], optimizer.exp_avg_sq[fi]):
+                buf = torch.empty(f.numel, dtype=shard.dtype, device=shard.device)
                 for r in range(self.world_size):
                     lo, hi = _shard(f.numel, r, self.world_size)
                     if hi > lo:
+                        if r == self.rank:
+                            buf[lo:hi].copy_(shard)
                         dist.broadcast(buf[lo:hi], src=r, group=self.group)
+                bufs.append(buf)
+            full[fi] = tuple(bufs)
+        return full

@@ -6,7 +6,10 @@ tiny model's optimizer through three steps with the same rank-specific
 synthetic gradients, once with the NCCL all-reduce step and once with the
 fused reduce-scatter / sharded AdamW / all-gather step over peer memory, and
 checks that both give the same weights, gradient norm (one step clips) and
-second moments; then trains two real steps with the fused step and checks
+second moments; checks that the fused step keeps only this rank's shard of
+the AdamW moments (ZeRO-1) and that the learning rate it applies at optimizer
+steps 1..N is the single-process ``LambdaLR`` schedule, with no scheduler
+ordering warning; then trains two real steps with the fused step and checks
 that every rank holds bit-identical weights.  Exits non-zero on mismatch.
 """
 from __future__ import annotations
@@ -75,7 +78,49 @@ def run(verbose: bool = True) -> bool:
     if not mdiff < 1e-5:
         ok = False
 
-    # (b) real training steps: finite losses, identical weights on every rank
+    # (b) ZeRO-1 moments and the learning-rate schedule under the fused step
+    import warnings
+    from torch.optim.lr_scheduler import LambdaLR
+    from training.pretrain import make_warmup_cosine_lambda
+    eng = engine("fused")
+    opt = eng.optimizer
+    replicated = sum(f.numel for f in eng.flats[:eng.dp.n_heap])
+    held = sum(m.numel() for m in opt.exp_avg[:eng.dp.n_heap])
+    expect = sum(hi - lo for lo, hi in eng.dp.shards)
+    if verbose:
+        print(f"[rank {rank}] AdamW moments held for replicated parameters: {8 * held:,} bytes "
+              f"(unsharded: {8 * replicated:,})", flush=True)
+    if held != expect or (world > 1 and held >= replicated):
+        ok = False
+        print(f"[rank {rank}] moment shard holds {held} elements, expected {expect}", flush=True)
+    lam = make_warmup_cosine_lambda(3, 10, 0.1)
+    sched = LambdaLR(opt, lam)
+    applied = []
+    inner = opt.stepper
+
+    def recording(o):
+        applied.append([float(g["lr"]) for g in o.param_groups])
+        inner(o)
+    opt.stepper = recording
+    with warnings.catch_warnings(record=True) as caught:
+        warnings.simplefilter("always")
+        for _ in range(6):
+            for f in eng.flats:
+                f.grad.normal_(0, 1e-2)
+            eng.clip_and_step(1.0)
+            sched.step()
+    expected = [[1e-3 * lam(k)] * len(opt.param_groups) for k in range(6)]
+    if any(abs(a - b) > 1e-12 for ra, rb in zip(applied, expected) for a, b in zip(ra, rb)) or len(applied) != 6:
+        ok = False
+        print(f"[rank {rank}] learning rates applied {applied} != schedule {expected}", flush=True)
+    if any("lr_scheduler.step()" in str(w.message) for w in caught):
+        ok = False
+        print(f"[rank {rank}] scheduler ordering warning raised", flush=True)
+    torch.cuda.synchronize()
+    eng.check()
+    eng.close()
+
+    # (c) real training steps: finite losses, identical weights on every rank
     eng = engine("fused")
     g = torch.Generator(device="cpu").manual_seed(7 + rank)
     for _ in range(2):

@@ -21,14 +21,16 @@ def _cos(a, b):
     return F.cosine_similarity(a.flatten().double(), b.flatten().double(), dim=0).item()
 
 
-def test_engine_matches_eager():
+@pytest.mark.parametrize("q_lora", [0, 64], ids=["direct_q", "lora_q"])
+def test_engine_matches_eager(q_lora):
     from models.mtp import MultiTokenPrediction
     from models.transformer import Transformer
     from ops.engine import TrainEngine
     from training.pretrain import TrainingConfig, _unique_params
 
+    cfg = dict(CFG, q_lora_rank=q_lora)
     torch.manual_seed(0)
-    ref = Transformer(dict(CFG)).cuda()
+    ref = Transformer(dict(cfg)).cuda()
     # Spread the router scores (the 0.006-std init leaves every sigmoid score
     # within ~0.03 of 0.5, so bf16 operand rounding flips near-tied top-k picks
     # and the comparison would test tie-breaking instead of the kernels), and
@@ -36,9 +38,9 @@ def test_engine_matches_eager():
     for moe in ref.moe_layers():
         moe.gate.weight.data.mul_(40.0)
         moe.gate.bias.uniform_(-0.05, 0.05)
-    ref_mtp = MultiTokenPrediction(dict(CFG), ref).cuda()
+    ref_mtp = MultiTokenPrediction(dict(cfg), ref).cuda()
     model = copy.deepcopy(ref)
-    mtp = MultiTokenPrediction(dict(CFG), model).cuda()
+    mtp = MultiTokenPrediction(dict(cfg), model).cuda()
     mtp.load_state_dict(ref_mtp.state_dict())
 
     B, S = 4, 128
@@ -101,12 +103,14 @@ def test_engine_matches_eager():
     assert _cos(torch.cat(ours_all), torch.cat(ref_all)) > 0.99
 
     # one optimizer step moves the weights like torch AdamW would
-    before = model.layers[0].attn.wq.weight.detach().clone()
+    attn0 = model.layers[0].attn
+    q_w = attn0.wq_b.weight if q_lora else attn0.wq.weight
+    before = q_w.detach().clone()
     eng.clip_and_step(1.0)
     eng.zero_grad()
     torch.cuda.synchronize()
-    assert not torch.equal(before, model.layers[0].attn.wq.weight)
-    assert torch.isfinite(model.layers[0].attn.wq.weight).all()
+    assert not torch.equal(before, q_w)
+    assert torch.isfinite(q_w).all()
     eng.check()
 
 

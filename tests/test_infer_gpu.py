@@ -26,11 +26,11 @@ def _close(a, b, tol, what=""):
     assert rel.max().item() < 8 * tol, f"{what}: worst position rel err {rel.max().item():.3f}"
 
 
-@pytest.fixture(scope="module")
-def model():
+@pytest.fixture(scope="module", params=[0, 64], ids=["direct_q", "lora_q"])
+def model(request):
     from models.transformer import Transformer
     torch.manual_seed(0)
-    m = Transformer(dict(CFG)).cuda().eval()
+    m = Transformer(dict(CFG, q_lora_rank=request.param)).cuda().eval()
     for moe in m.moe_layers():   # spread router scores so bf16 rounding does not flip top-k picks
         moe.gate.weight.data.mul_(10.0)
     return m
