@@ -378,6 +378,13 @@ def run_reference(args, rank, world, local):
     # calls.  Its own TORCH_COMPILE_MODE hook selects the same autotuning
     # without CUDA graphs.
     os.environ.setdefault("TORCH_COMPILE_MODE", "max-autotune-no-cudagraphs")
+    # A compile cache from an earlier run of this same arm on this kind of box
+    # (inductor's FX-graph / autotuning / kernel cache, kept untracked next to
+    # the reference install) shortens its ~3-minute compile; the compiled
+    # kernels are the same ones a cold compile produces.
+    cache = REF_DIR.parent / "_ref_inductor_cache"
+    if cache.is_dir():
+        os.environ.setdefault("TORCHINDUCTOR_CACHE_DIR", str(cache))
     from training.pretrain import Pretrainer, TrainingConfig  # the reference's own modules
     y = load_yaml(str(ref_root / "configs" / "pretrain_a100_422m.yaml"))
     t, m = y["training"], y["model"]

@@ -1,9 +1,22 @@
 // Expert-parallel MoE token movement over NVLink / NVSwitch peer memory.
 //
 // Ranks of one box share a symmetric heap (csrc/comm.cu): the same offsets in
-// every rank's region, every region mapped into every peer.  Routed experts
-// are split into contiguous ranges, rank d owning [d*E/R, (d+1)*E/R).  Per
-// MoE layer and micro-batch:
+// every rank's region, every region mapped into every peer.  Two receive
+// layouts:
+//
+//   owner     routed experts are split into contiguous ranges, rank d owning
+//             [d*E/R, (d+1)*E/R), and receives every row routed to them (the
+//             layout when each rank holds only its own experts' weights);
+//   balanced  (expert weights replicated) the rows of all ranks, in expert
+//             order with each expert's range padded to 256, form one global
+//             sequence of P rows; rank d receives the contiguous share
+//             [d*chunk, (d+1)*chunk), chunk = P / R rounded up to 256.  Every
+//             rank then runs the same number of expert rows whatever the
+//             routing, an expert's rows may be split between two ranks, and
+//             each rank adds its rows' part of the expert weight gradients
+//             (the data-parallel gradient sum completes them).
+//
+// Per MoE layer and micro-batch:
 //
 //   ep_plan        (1 CTA) all-gathers the per-expert routing counts by P2P
 //                  stores + a signal, waits for every rank's counts and
@@ -65,6 +78,7 @@ struct EpArgs {
   long long off_origin;                // int32  [cap]     source rank * T*k + slot, -1 on padding
   long long off_w;                     // f32    [cap]     gate weight of the row
   int me, R, E, k, T, D, cap;
+  int bal;                             // 1: balanced layout, 0: owner layout
   unsigned long long budget_ns;
 };
 
@@ -143,9 +157,13 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpArgs a, const int* __re
                                                        uint32_t* sendcnt, int* __restrict__ cnt_all,
                                                        int* __restrict__ send_base, int* __restrict__ row_off,
                                                        int* __restrict__ recv_cnt, int* __restrict__ tile_group,
-                                                       int max_tiles, int* __restrict__ cursor, unsigned int* status) {
+                                                       int max_tiles, int* __restrict__ cursor,
+                                                       int* __restrict__ bal_info, unsigned int* status) {
   __shared__ int s_cnt[kMaxRanks * kMaxExperts];
   __shared__ int s_off[kMaxExperts + 1];
+  __shared__ int s_start[kMaxExperts + 1];
+  __shared__ int s_tot[kMaxExperts];
+  __shared__ int s_chunk;
   __shared__ int s_abort;
   const int tid = threadIdx.x, R = a.R, E = a.E;
   if (tid == 0) s_abort = 0;
@@ -178,6 +196,57 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpArgs a, const int* __re
   }
   __syncthreads();
   // 3. layout of every rank's receive slot (each rank computes all of them)
+  if (a.bal) {
+    // balanced: global expert-ordered sequence cut into R equal shares
+    for (int e = tid; e < E; e += blockDim.x) {
+      int tot = 0;
+      for (int s = 0; s < R; ++s) tot += s_cnt[s * E + e];
+      s_tot[e] = tot;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int e = 0; e < E; ++e) {
+        s_start[e] = acc;
+        acc += (s_tot[e] + 255) / 256 * 256;
+      }
+      s_start[E] = acc;
+      s_chunk = max(256, ((acc + R - 1) / R + 255) / 256 * 256);
+    }
+    __syncthreads();
+    const int chunk = s_chunk, lo = a.me * chunk;
+    const int used = max(0, min(chunk, s_start[E] - lo));
+    for (int e = tid; e < E; e += blockDim.x) {
+      int pre = 0;
+      for (int s = 0; s < a.me; ++s) pre += s_cnt[s * E + e];
+      send_base[e] = s_start[e] + pre;                       // global position of my first row of e
+      s_off[e] = min(max(s_start[e] - lo, 0), used);
+      recv_cnt[e] = min(max(s_start[e] + s_tot[e] - lo, 0), used) - s_off[e];   // real rows of e in my share
+    }
+    if (tid == 0) {
+      s_off[E] = used;
+      bal_info[0] = chunk;
+      bal_info[1] = used;
+      if (chunk > a.cap) record_error(status, DSV3_ERR_BOUNDS);   // receive capacity exceeded
+    }
+    __syncthreads();
+    for (int i = tid; i <= E; i += blockDim.x) row_off[i] = s_off[i];
+    for (int i = tid; i < max_tiles; i += blockDim.x) {
+      const int row = i * 128;
+      int g = -1;
+      if (row < used) {
+        int l = 0, h = E - 1;  // last e with s_off[e] <= row: the expert whose rows hold `row`
+        while (l < h) {
+          const int mid = (l + h + 1) >> 1;
+          if (s_off[mid] <= row) l = mid;
+          else h = mid - 1;
+        }
+        g = l;
+      }
+      tile_group[i] = g;
+    }
+    return;
+  }
   const int e_lo = first_expert(a.me, E, R), Eloc = first_expert(a.me + 1, E, R) - e_lo;
   if (tid < R) {
     const int d = tid, e0 = first_expert(d, E, R), e1 = first_expert(d + 1, E, R);
@@ -225,16 +294,29 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpArgs a, const __nv_b
                                                           const int* __restrict__ send_base, int* cursor,
                                                           int* __restrict__ route, const int* __restrict__ row_off,
                                                           const int* __restrict__ recv_cnt, int Eloc,
-                                                          unsigned int* done, unsigned int* status) {
+                                                          const int* __restrict__ bal_info, unsigned int* done,
+                                                          unsigned int* status) {
   const int lane = threadIdx.x & 31;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nwarps = (gridDim.x * blockDim.x) >> 5;
   const int TK = a.T * a.k, D8 = a.D / 8;
+  const int chunk = a.bal ? bal_info[0] : 0;
   for (int i = warp; i < TK; i += nwarps) {
     int row = 0, d = 0;
     if (lane == 0) {
       const int e = idx[i];
-      d = owner_of(e, a.E, a.R);
-      row = send_base[e] + atomicAdd(&cursor[e], 1);
+      if (a.bal) {
+        const int gp = send_base[e] + atomicAdd(&cursor[e], 1);   // global position in expert order
+        d = gp / chunk;
+        row = gp - d * chunk;
+        if (d >= a.R) {
+          record_error(status, DSV3_ERR_BOUNDS);
+          d = 0;
+          row = a.cap;
+        }
+      } else {
+        d = owner_of(e, a.E, a.R);
+        row = send_base[e] + atomicAdd(&cursor[e], 1);
+      }
       if (row >= a.cap) {
         record_error(status, DSV3_ERR_BOUNDS);
         row = -1;
@@ -366,9 +448,9 @@ int sm_count() {
 }
 
 // peers: heap base per rank; offs: [flags, counts, comb, dw, bwd, xs, origin, w];
-// dims: [me, R, E, k, T, D, cap, budget_ns]
+// dims: [me, R, E, k, T, D, cap, budget_ns(, balanced)]
 EpArgs make_args(const std::vector<int64_t>& peers, const std::vector<int64_t>& offs, const std::vector<int64_t>& dims) {
-  TORCH_CHECK(offs.size() == 8 && dims.size() == 8, "ep: offs has 8 entries, dims has 8 entries");
+  TORCH_CHECK(offs.size() == 8 && (dims.size() == 8 || dims.size() == 9), "ep: offs has 8 entries, dims 8 or 9");
   EpArgs a{};
   const int R = (int)dims[1];
   TORCH_CHECK(R >= 1 && R <= kMaxRanks && (int)peers.size() == R, "ep: 1..8 ranks, one heap base per rank");
@@ -390,6 +472,7 @@ EpArgs make_args(const std::vector<int64_t>& peers, const std::vector<int64_t>& 
   a.D = (int)dims[5];
   a.cap = (int)dims[6];
   a.budget_ns = (unsigned long long)dims[7];
+  a.bal = dims.size() == 9 ? (int)(dims[8] != 0) : 0;
   TORCH_CHECK(a.me >= 0 && a.me < R, "ep: rank out of range");
   TORCH_CHECK(a.E >= R && a.E <= kMaxExperts, "ep: R <= E <= 256");
   TORCH_CHECK(a.D % 8 == 0 && a.cap % 256 == 0, "ep: D % 8 == 0, capacity a multiple of 256");
@@ -397,7 +480,17 @@ EpArgs make_args(const std::vector<int64_t>& peers, const std::vector<int64_t>& 
   return a;
 }
 
-int local_experts(const EpArgs& a) { return first_expert(a.me + 1, a.E, a.R) - first_expert(a.me, a.E, a.R); }
+// weight groups of the receive layout: this rank's experts (owner) or all experts (balanced)
+int local_experts(const EpArgs& a) {
+  return a.bal ? a.E : first_expert(a.me + 1, a.E, a.R) - first_expert(a.me, a.E, a.R);
+}
+
+const int* bal_ptr(const EpArgs& a, const c10::optional<at::Tensor>& bal_info) {
+  if (!a.bal) return nullptr;
+  TORCH_CHECK(bal_info.has_value() && bal_info->scalar_type() == at::kInt && bal_info->numel() >= 2,
+              "ep: the balanced layout needs bal_info (int32 [>= 2])");
+  return bal_info->data_ptr<int>();
+}
 
 const __nv_bfloat16* cbf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
 __nv_bfloat16* bf(at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
@@ -413,8 +506,9 @@ int copy_grid(long rows) {
 void ep_plan(const std::vector<int64_t>& peers, const std::vector<int64_t>& offs, const std::vector<int64_t>& dims,
              const at::Tensor& counts, at::Tensor& expect, at::Tensor& sendcnt, at::Tensor& cnt_all,
              at::Tensor& send_base, at::Tensor& row_off, at::Tensor& recv_cnt, at::Tensor& tile_group,
-             at::Tensor& cursor) {
+             at::Tensor& cursor, const c10::optional<at::Tensor>& bal_info) {
   const EpArgs a = make_args(peers, offs, dims);
+  const int* bal = bal_ptr(a, bal_info);
   const int Eloc = local_experts(a);
   TORCH_CHECK(counts.numel() == a.E && cnt_all.numel() == a.R * a.E && send_base.numel() == a.E &&
                   row_off.numel() == Eloc + 1 && recv_cnt.numel() == Eloc && cursor.numel() == a.E,
@@ -424,15 +518,16 @@ void ep_plan(const std::vector<int64_t>& peers, const std::vector<int64_t>& offs
   ep_plan_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(a, counts.data_ptr<int>(), u32(expect),
       u32(sendcnt), cnt_all.data_ptr<int>(), send_base.data_ptr<int>(), row_off.data_ptr<int>(),
       recv_cnt.data_ptr<int>(), tile_group.data_ptr<int>(), (int)tile_group.numel(), cursor.data_ptr<int>(),
-      status_ptr());
+      const_cast<int*>(bal), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void ep_dispatch(const std::vector<int64_t>& peers, const std::vector<int64_t>& offs, const std::vector<int64_t>& dims,
                  const at::Tensor& x, const at::Tensor& idx, const at::Tensor& w, const at::Tensor& send_base,
                  at::Tensor& cursor, at::Tensor& route, const at::Tensor& row_off, const at::Tensor& recv_cnt,
-                 at::Tensor& done) {
+                 at::Tensor& done, const c10::optional<at::Tensor>& bal_info) {
   const EpArgs a = make_args(peers, offs, dims);
+  const int* bal = bal_ptr(a, bal_info);
   TORCH_CHECK(x.size(0) == a.T && x.size(1) == a.D && x.stride(1) == 1 && x.stride(0) % 8 == 0,
               "ep_dispatch: x [T, D] with 16-byte rows");
   TORCH_CHECK(idx.numel() == (long)a.T * a.k && w.numel() == idx.numel() && route.numel() == 2 * idx.numel(),
@@ -440,7 +535,7 @@ void ep_dispatch(const std::vector<int64_t>& peers, const std::vector<int64_t>& 
   const at::cuda::CUDAGuard guard(x.device());
   ep_dispatch_kernel<<<copy_grid((long)a.T * a.k), 256, 0, at::cuda::getCurrentCUDAStream()>>>(a, cbf(x), x.stride(0),
       idx.data_ptr<int>(), w.data_ptr<float>(), send_base.data_ptr<int>(), cursor.data_ptr<int>(),
-      route.data_ptr<int>(), row_off.data_ptr<int>(), recv_cnt.data_ptr<int>(), local_experts(a), u32(done),
+      route.data_ptr<int>(), row_off.data_ptr<int>(), recv_cnt.data_ptr<int>(), local_experts(a), bal, u32(done),
       status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -491,8 +586,16 @@ void ep_bwd_prep(const std::vector<int64_t>& peers, const std::vector<int64_t>& 
 }
 
 void register_ep(pybind11::module_& m) {
-  m.def("ep_plan", &ep_plan, "all-gather routing counts over peer memory and build the receive layout");
-  m.def("ep_dispatch", &ep_dispatch, "store routed token rows into the owners' receive slots (P2P)");
+  m.def("ep_plan", &ep_plan, "all-gather routing counts over peer memory and build the receive layout",
+        pybind11::arg("peers"), pybind11::arg("offs"), pybind11::arg("dims"), pybind11::arg("counts"),
+        pybind11::arg("expect"), pybind11::arg("sendcnt"), pybind11::arg("cnt_all"), pybind11::arg("send_base"),
+        pybind11::arg("row_off"), pybind11::arg("recv_cnt"), pybind11::arg("tile_group"), pybind11::arg("cursor"),
+        pybind11::arg("bal_info") = pybind11::none());
+  m.def("ep_dispatch", &ep_dispatch, "store routed token rows into their receive slots (P2P)",
+        pybind11::arg("peers"), pybind11::arg("offs"), pybind11::arg("dims"), pybind11::arg("x"), pybind11::arg("idx"),
+        pybind11::arg("w"), pybind11::arg("send_base"), pybind11::arg("cursor"), pybind11::arg("route"),
+        pybind11::arg("row_off"), pybind11::arg("recv_cnt"), pybind11::arg("done"),
+        pybind11::arg("bal_info") = pybind11::none());
   m.def("ep_dispatch_bwd", &ep_dispatch_bwd, "send output-gradient rows along the forward routes (P2P)");
   m.def("ep_wait", &ep_wait, "bounded wait for every peer's signal of a phase");
   m.def("ep_send_back", &ep_send_back, "store per-row results into the home ranks' combine inbox (P2P)");

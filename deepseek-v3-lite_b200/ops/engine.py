@@ -170,6 +170,13 @@ class TrainEngine:
         self.nvtx = os.environ.get("DSV3_NVTX", "0") == "1"
         # per-phase device timing (set by the benchmark's breakdown step)
         self.phase_timer: Optional[PhaseTimer] = None
+        # Activation recomputation: keep only each layer's input and rerun the
+        # layer's forward in the backward pass (config.activation_recompute or
+        # DSV3_RECOMPUTE=1).  Off by default: on 180 GB the memory is better
+        # spent on larger micro-batches; it lets long sequences or the scaled
+        # model fit.
+        self.recompute = bool(getattr(config, "activation_recompute", False)) or \
+            os.environ.get("DSV3_RECOMPUTE", "0") == "1"
 
     def _mark(self, name: str) -> None:
         if self.phase_timer is not None:
@@ -266,9 +273,14 @@ class TrainEngine:
         return self.flat_nodecay
 
     def _local_experts(self, moe, ep):
-        """bf16 weights and fp32 gradient views of this rank's routed experts:
-        (w13 [Eloc, 2, I, D], w2 [Eloc, D, I], g13 [Eloc, 2I, D], g2 [Eloc, D, I])."""
+        """bf16 weights and fp32 gradient views of the expert-parallel layout's
+        weight groups: (w13 [G, 2, I, D], w2 [G, D, I], g13 [G, 2I, D],
+        g2 [G, D, I]); every expert in the balanced layout, this rank's own
+        in the owner layout."""
         E = moe.n_routed_experts
+        if ep.balanced:
+            w1, w2 = moe.experts[0].w1.weight, moe.experts[0].w2.weight
+            return (self.swiglu_w13(w1, E), self.stacked(w2, E), self.swiglu_g13(w1, E), self.stacked(w2, E, grad=True))
         if self.shard_experts:
             first = moe.experts[ep.lo]
             n = ep.hi - ep.lo
@@ -425,15 +437,33 @@ class TrainEngine:
         self.C.linear_dgrad(dgu, w13, dxn_acc, accumulate)
         self.C.linear_wgrad(dgu, xn, self.swiglu_g13(w1, 1).view(2 * I, -1))
 
+    def _fork(self, work):
+        """Run ``work()`` on the engine's side stream, ordered after everything
+        issued so far on the current stream; returns the stream to join."""
+        if not hasattr(self, "_side_stream"):
+            self._side_stream = torch.cuda.Stream(device=self.device)
+        cur = torch.cuda.current_stream(self.device)
+        self._side_stream.wait_stream(cur)
+        with torch.cuda.stream(self._side_stream):
+            work()
+        return self._side_stream
+
+    def _join(self, side) -> None:
+        if side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(side)
+
     def _ep_group(self, tokens: int):
         """The expert-parallel buffers, created on first use (a collective:
         every rank reaches it at the same MoE layer)."""
         if self.ep is None:
             from parallel.ep import ExpertParallel
             c = self.cfg
+            # balanced layout while expert weights are replicated (DSV3_EP_BALANCED=0: owner layout)
+            balanced = not self.shard_experts and os.environ.get("DSV3_EP_BALANCED", "1") != "0"
             self.ep = ExpertParallel(c["n_routed_experts"], c["n_activated_experts"], self.D, tokens,
                                      n_slots=len(self._moe_slot), group=self.dp.group,
-                                     capacity_factor=float(getattr(self.config, "ep_capacity_factor", 0.0)))
+                                     capacity_factor=float(getattr(self.config, "ep_capacity_factor", 0.0)),
+                                     balanced=balanced)
         if self.ep.T != tokens:
             raise RuntimeError(f"expert-parallel buffers are sized for {self.ep.T} tokens per micro-batch, got "
                                f"{tokens}; keep the micro-batch shape fixed")
@@ -521,12 +551,18 @@ class TrainEngine:
         h = torch.empty(P, I, dtype=BF16, device=self.device)
         gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
         C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu, group_rows=256)
-        ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys, group_rows=256)
         out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
         shared = []
-        for i, e in enumerate(moe.shared_experts):
-            shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
+
+        def shared_fwd():
+            for i, e in enumerate(moe.shared_experts):
+                shared.append(self._swiglu_dense_fwd(e.w1.weight, e.w2.weight, xn, out, resid_in if i == 0 else None))
+        # the shared experts run on a side stream beside the routed experts'
+        # permutation and grouped GEMMs (joined before the combine adds into out)
+        side = self._fork(shared_fwd) if moe.shared_experts else None
+        ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
+        C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys, group_rows=256)
+        self._join(side)
         C.combine_fwd(ys, dst, wts, out)
         return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
                     h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts), out
@@ -539,8 +575,13 @@ class TrainEngine:
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
         if not moe.shared_experts:
             dxn_acc.zero_()
-        for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
-            self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
+
+        def shared_bwd():
+            for i, (e, sctx) in enumerate(zip(moe.shared_experts, ctx.shared)):
+                self._swiglu_dense_bwd(e.w1.weight, e.w2.weight, sctx, xn, dres_bf16, dxn_acc, accumulate=i > 0)
+        # shared experts on a side stream beside the routed backward; joined
+        # before the un-permute adds the routed input gradients into dxn_acc
+        side = self._fork(shared_bwd) if moe.shared_experts else None
         P = ctx.xs.shape[0]
         dys = torch.empty(P, self.D, dtype=BF16, device=self.device)
         dw = torch.empty(T, k, dtype=F32, device=self.device)
@@ -553,6 +594,7 @@ class TrainEngine:
         dxs = torch.empty(P, self.D, dtype=BF16, device=self.device)
         C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs, group_rows=256)
         C.grouped_wgrad(dgu, ctx.xs, ctx.row_off, self.swiglu_g13(w1, E))
+        self._join(side)
         C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
 
@@ -626,6 +668,24 @@ class TrainEngine:
                       self.g(blk.norm_e.weight))
 
     # ------------------------------------------------------------ full step
+    def _layer_fwd(self, layer, x, B, S):
+        """One transformer block on the fp32 residual ``x``: returns (saved tensors, next residual)."""
+        C = self.C
+        xn1, r1 = self._norm(x, layer.attn_norm.weight)
+        actx = self._mla_fwd(layer.attn, xn1, B, S)
+        x_mid = torch.empty_like(x)
+        C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid, True, x)
+        xn2, r2 = self._norm(x_mid, layer.ffn_norm.weight)
+        self._mark("o-proj fwd")
+        if hasattr(layer.ffn, "experts"):
+            fctx, x_next = self._moe_fwd(layer.ffn, xn2, x_mid)
+            self._mark("moe fwd")
+        else:
+            x_next = torch.empty_like(x_mid)
+            fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next, x_mid)
+            self._mark("dense ffn fwd")
+        return (x, r1, actx, x_mid, xn2, r2, fctx), x_next
+
     @property
     def _empty_i32(self):
         if not hasattr(self, "_e_i32"):
@@ -713,20 +773,9 @@ class TrainEngine:
         saved = []
         for li, layer in enumerate(m.layers):
             self._range(f"fwd layer {li}")
-            xn1, r1 = self._norm(x, layer.attn_norm.weight)
-            actx = self._mla_fwd(layer.attn, xn1, B, S)
-            x_mid = torch.empty_like(x)
-            C.linear_fwd(actx.O, self.w(layer.attn.wo.weight), x_mid, True, x)
-            xn2, r2 = self._norm(x_mid, layer.ffn_norm.weight)
-            self._mark("o-proj fwd")
-            if hasattr(layer.ffn, "experts"):
-                fctx, x_next = self._moe_fwd(layer.ffn, xn2, x_mid)
-                self._mark("moe fwd")
-            else:
-                x_next = torch.empty_like(x_mid)
-                fctx = self._swiglu_dense_fwd(layer.ffn.w1.weight, layer.ffn.w2.weight, xn2, x_next, x_mid)
-                self._mark("dense ffn fwd")
-            saved.append((x, r1, actx, x_mid, xn2, r2, fctx))
+            ctx, x_next = self._layer_fwd(layer, x, B, S)
+            # with recomputation only the layer input survives the forward pass
+            saved.append(x if self.recompute else ctx)
             x = x_next
             self._range(None)
         hL = x
@@ -812,8 +861,12 @@ class TrainEngine:
         self._mark("mtp bwd")
         dres_b = torch.empty(T, D, dtype=BF16, device=self.device)
         C.rmsnorm_bwd(dall[:T], hL, self.f32(m.norm.weight), rf, dres, None, dres_b, self.g(m.norm.weight))
-        for li, (layer, (x_in, r1, actx, x_mid, xn2, r2, fctx)) in enumerate(zip(reversed(m.layers), reversed(saved))):
+        for li, (layer, kept) in enumerate(zip(reversed(m.layers), reversed(saved))):
             self._range(f"bwd layer {len(saved) - 1 - li}")
+            if self.recompute:
+                kept, _ = self._layer_fwd(layer, kept, B, S)
+                self._mark("recompute fwd")
+            x_in, r1, actx, x_mid, xn2, r2, fctx = kept
             dxn2 = torch.empty(T, D, dtype=F32, device=self.device)
             if hasattr(layer.ffn, "experts"):
                 self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)

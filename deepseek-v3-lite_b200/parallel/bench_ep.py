@@ -92,8 +92,10 @@ class OursLayer:
         bf = dict(device=device, dtype=torch.bfloat16)
         self.gate = (torch.randn(E, D, generator=g) * 0.02).to(**bf)
         self.bias = torch.zeros(E, device=device)
-        self.ep = ExpertParallel(E, TOPK, D, T, n_slots=1)
-        lo, hi = self.ep.lo, self.ep.hi
+        self.ep = ExpertParallel(E, TOPK, D, T, n_slots=1,
+                                 balanced=os.environ.get("DSV3_EP_BALANCED", "1") != "0")
+        # weight groups of the layout: all experts (balanced) or the owned ones
+        lo, hi = self.ep.g_lo, self.ep.g_lo + self.ep.G
         std = 1.0 / D ** 0.5
         self.w13 = (torch.randn(hi - lo, 2, INTER, D, generator=g) * std).to(**bf)
         self.w2 = (torch.randn(hi - lo, D, INTER, generator=g) * (1.0 / INTER ** 0.5)).to(**bf)

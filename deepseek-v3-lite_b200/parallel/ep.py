@@ -1,8 +1,20 @@
 """Expert parallelism for DeepSeekMoE over the GPUs of one NVSwitch box.
 
 Routed experts are split into contiguous ranges, rank ``d`` of ``R`` owning
-``[d*E//R, (d+1)*E//R)`` (uneven when ``R`` does not divide ``E``).  A MoE
-layer on every rank then runs
+``[d*E//R, (d+1)*E//R)`` (uneven when ``R`` does not divide ``E``).  Where
+the rows go depends on the layout:
+
+* ``balanced`` (the default while expert weights are replicated): all ranks'
+  rows in expert order, each expert's range padded to 256 rows, form one
+  sequence that is cut into ``R`` equal contiguous shares; rank ``d``
+  computes share ``d``.  Every rank runs the same number of expert rows
+  whatever the routing (at random init some experts get several times the
+  mean), an expert's rows may be split over two ranks, and each rank adds its
+  rows' part of every touched expert's weight gradient;
+* ``owner`` (sharded expert weights): rank ``d`` receives every row routed to
+  the experts it owns and computes their weight gradients.
+
+A MoE layer on every rank then runs
 
 forward
   router GEMM + top-k (local) -> ``ep_plan``: all-gather of the per-expert
@@ -61,8 +73,35 @@ def owner_of(expert: int, n_experts: int, world: int) -> int:
     return d
 
 
+def balanced_capacity(tokens: int, topk: int, n_experts: int, world: int) -> int:
+    """Rows of one rank's receive slot in the balanced layout: its share of
+    the largest possible padded sequence (every rank's ``tokens * topk`` rows
+    plus up to 255 padding rows per expert), rounded up to 256."""
+    total = world * tokens * topk + n_experts * 255
+    return max(256, _pad(-(-total // world), 256))
+
+
+def plan_reference_balanced(cnt_all: torch.Tensor, rank: int):
+    """What ``ep_plan`` computes in the balanced layout, in plain PyTorch (CPU oracle).
+
+    Returns ``(send_base [E] (global positions), row_off [E+1], recv_cnt [E],
+    chunk, used)`` for ``rank``."""
+    R, E = cnt_all.shape
+    tot = cnt_all.sum(0)
+    start = torch.zeros(E + 1, dtype=torch.int64)
+    start[1:] = torch.cumsum((tot + 255) // 256 * 256, 0)
+    chunk = max(256, _pad(-(-int(start[-1]) // R), 256))
+    lo = rank * chunk
+    used = max(0, min(chunk, int(start[-1]) - lo))
+    send_base = (start[:E] + cnt_all[:rank].sum(0)).to(torch.int32)
+    row_off = (start - lo).clamp(0, used).to(torch.int32)
+    row_off[E] = used
+    recv_cnt = ((start[:E] + tot - lo).clamp(0, used) - row_off[:E]).to(torch.int32)
+    return send_base, row_off, recv_cnt, chunk, used
+
+
 def receive_capacity(tokens: int, topk: int, n_experts: int, world: int, capacity_factor: float = 0.0) -> int:
-    """Rows of one rank's receive slot.
+    """Rows of one rank's receive slot (owner layout).
 
     Exact worst case by default: every token of every rank can send
     ``min(k, local experts)`` rows to one rank, plus up to 255 padding rows
@@ -120,7 +159,7 @@ class ExpertParallel:
     """
 
     def __init__(self, n_experts: int, topk: int, dim: int, tokens: int, n_slots: int, group=None,
-                 capacity_factor: float = 0.0, timeout_s: Optional[float] = None):
+                 capacity_factor: float = 0.0, timeout_s: Optional[float] = None, balanced: bool = True):
         from .symm import SymmetricHeap, heap_layout
         import torch.distributed as dist
         self.C = native()
@@ -136,7 +175,12 @@ class ExpertParallel:
         self.E, self.k, self.D, self.T = n_experts, topk, dim, tokens
         self.lo, self.hi = expert_range(self.rank, n_experts, self.world)
         self.Eloc = self.hi - self.lo
-        self.cap = receive_capacity(tokens, topk, n_experts, self.world, capacity_factor)
+        self.balanced = bool(balanced)
+        # weight groups the grouped GEMMs see: all experts (balanced) or the owned ones
+        self.G = n_experts if self.balanced else self.Eloc
+        self.g_lo = 0 if self.balanced else self.lo
+        self.cap = (balanced_capacity(tokens, topk, n_experts, self.world) if self.balanced else
+                    receive_capacity(tokens, topk, n_experts, self.world, capacity_factor))
         TK = tokens * topk
         if timeout_s is None:
             timeout_s = float(os.environ.get("DSV3_EP_TIMEOUT_S", "30"))
@@ -160,7 +204,7 @@ class ExpertParallel:
         # DSV3_EP_FUSED_COMBINE=0 uses the separate send-back kernel instead
         self.fused_combine = os.environ.get("DSV3_EP_FUSED_COMBINE", "1") != "0"
         self.cursor = torch.zeros(n_experts, dtype=torch.int32, device=dev)
-        self.dims = [self.rank, self.world, n_experts, topk, tokens, dim, self.cap, self.budget_ns]
+        self.dims = [self.rank, self.world, n_experts, topk, tokens, dim, self.cap, self.budget_ns, int(self.balanced)]
         self.comb = self.heap.tensor(self.off_comb, (TK, dim), torch.bfloat16)
         self.dw_inbox = self.heap.tensor(self.off_dw, (TK,), torch.float32)
         self.slot_arange = torch.arange(TK, dtype=torch.int32, device=dev).view(tokens, topk)
@@ -206,16 +250,18 @@ class ExpertParallel:
         plan = {
             "cnt_all": torch.empty(self.world, self.E, dtype=torch.int32, device=dev),
             "send_base": torch.empty(self.E, dtype=torch.int32, device=dev),
-            "row_off": torch.empty(self.Eloc + 1, dtype=torch.int32, device=dev),
-            "recv_cnt": torch.empty(self.Eloc, dtype=torch.int32, device=dev),
+            "row_off": torch.empty(self.G + 1, dtype=torch.int32, device=dev),
+            "recv_cnt": torch.empty(self.G, dtype=torch.int32, device=dev),
             "tile_group": torch.empty(self.cap // 128, dtype=torch.int32, device=dev),
             "route": torch.empty(2, self.T * self.k, dtype=torch.int32, device=dev),
+            "bal_info": torch.zeros(4, dtype=torch.int32, device=dev),
         }
         offs = self.offs(slot)
+        bal = plan["bal_info"] if self.balanced else None
         C.ep_plan(self.heap.peers, offs, self.dims, counts, self.expect, self.sendcnt, plan["cnt_all"],
-                  plan["send_base"], plan["row_off"], plan["recv_cnt"], plan["tile_group"], self.cursor)
+                  plan["send_base"], plan["row_off"], plan["recv_cnt"], plan["tile_group"], self.cursor, bal)
         C.ep_dispatch(self.heap.peers, offs, self.dims, x, idx, wts, plan["send_base"], self.cursor, plan["route"],
-                      plan["row_off"], plan["recv_cnt"], self.done[0:1])
+                      plan["row_off"], plan["recv_cnt"], self.done[0:1], bal)
         plan["side"] = self._fork(overlap)
         if marks is not None:
             marks("ep plan+send")
@@ -260,8 +306,9 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
                    out: torch.Tensor, inter_dim: int, marks=_no_mark, overlap=None) -> dict:
     """Routed-expert part of a MoE layer under expert parallelism.
 
-    ``w13_local [Eloc, 2, I, D]`` / ``w2_local [Eloc, D, I]``: the owned
-    experts' bf16 weights.  Adds ``sum_j w[t, j] * expert_j(x[t])`` into the
+    ``w13_local [G, 2, I, D]`` / ``w2_local [G, D, I]``: the bf16 weights of
+    the layout's weight groups (``ep.G``: every expert in the balanced
+    layout, the owned ones in the owner layout).  Adds ``sum_j w[t, j] * expert_j(x[t])`` into the
     fp32 ``out``.  Returns the context the backward needs.  ``marks(name)``
     is called after each phase (the microbenchmark records events there);
     ``overlap()`` runs on a side stream during the transfers and is joined
@@ -315,7 +362,7 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     C.swiglu_dgrad(dys, w2_local, ctx["tile_group"], ctx["gu"], dgu, group_rows=256)
     C.grouped_wgrad(dys, ctx["h"], ctx["row_off"], g2_local)
     dxs = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
-    w13_2d = w13_local.reshape(ep.Eloc, 2 * inter_dim, ep.D)
+    w13_2d = w13_local.reshape(ep.G, 2 * inter_dim, ep.D)
     if ep.fused_combine:
         # input-gradient GEMM whose epilogue sends each row (and its gate-weight
         # gradient) to the home rank; the weight gradient runs meanwhile

@@ -5,8 +5,9 @@
 routed-expert layer forward + backward through the peer-memory dispatch /
 combine kernels on every rank, twice (so the signal counters advance across
 calls), and compares each rank's outputs, token gradients, gate-weight
-gradients and owned-expert weight gradients with an fp32 PyTorch evaluation
-of the same layer over the tokens of all ranks.  Exits non-zero on mismatch.
+gradients and expert weight gradients with an fp32 PyTorch evaluation of the
+same layer over the tokens of all ranks, in both receive layouts (balanced:
+the ranks' partial expert gradients summed; owner: each rank's own experts).  Exits non-zero on mismatch.
 Run without torchrun it checks the single-rank path (the rank stores into its
 own heap through the same kernels).  ``--engine`` instead trains the same tiny
 model with experts spread over the ranks and with experts replicated and
@@ -59,7 +60,10 @@ def reference_layer(x, idx, wts, dout, w1, w3, w2):
     return y.detach(), xs.grad, ws.grad, p1.grad, p3.grad, p2.grad
 
 
-def run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=True) -> bool:
+def run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=True, balanced=True) -> bool:
+    """Layer check in one receive layout (``balanced`` or owner).  In the
+    balanced layout each rank holds partial weight gradients of every expert
+    its share touches; their sum over ranks is compared with the reference."""
     sys.path.insert(0, __file__.rsplit("/parallel/", 1)[0])
     import torch.distributed as dist
     from ops._ext import native
@@ -80,8 +84,8 @@ def run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=True) -> bool:
     counts = torch.zeros(E, dtype=torch.int32, device=device)
     C.router_topk(logits, torch.zeros(E, device=device), E, k, 1.0, idx, wts, ssel, counts)
 
-    ep = ExpertParallel(E, k, D, T, n_slots=2, timeout_s=20)
-    lo, hi = ep.lo, ep.hi
+    ep = ExpertParallel(E, k, D, T, n_slots=2, timeout_s=20, balanced=balanced)
+    lo, hi = ep.g_lo, ep.g_lo + ep.G          # weight groups of the layout
     ok = True
     # every rank's tokens for the owned-expert weight-gradient reference
     if world > 1:
@@ -115,17 +119,21 @@ def run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=True) -> bool:
         g2 = torch.zeros(hi - lo, D, I, device=device)
         dw = moe_backward_ep(ep, ctx, dout, w13[lo:hi], w2b[lo:hi], g13, g2, dx, I).clone()
         torch.cuda.synchronize()
+        if balanced and world > 1:
+            for gbuf in (g13, g2):               # partial per rank; the sum is the gradient
+                dist.all_reduce(gbuf)
         cnt_global = ctx["cnt_all"].sum(0)
         expect_global = torch.bincount(idx_all.long().flatten(), minlength=E).to(cnt_global)
         if not torch.equal(cnt_global, expect_global):
             ok = False
             print(f"[rank {rank}] exchanged counts differ from the all-gathered routing", flush=True)
-        close(f"it{it} y", out, y_ref, 2e-2)
-        close(f"it{it} dx", dx, dx_ref, 3e-2)
-        close(f"it{it} dw", dw, dw_ref, 3e-2)
-        close(f"it{it} dW1", g13[:, :I], g1_ref[lo:hi], 3e-2)
-        close(f"it{it} dW3", g13[:, I:], g3_ref[lo:hi], 3e-2)
-        close(f"it{it} dW2", g2, g2_ref[lo:hi], 3e-2)
+        tag = f"{'balanced' if balanced else 'owner'} it{it}"
+        close(f"{tag} y", out, y_ref, 2e-2)
+        close(f"{tag} dx", dx, dx_ref, 3e-2)
+        close(f"{tag} dw", dw, dw_ref, 3e-2)
+        close(f"{tag} dW1", g13[:, :I], g1_ref[lo:hi], 3e-2)
+        close(f"{tag} dW3", g13[:, I:], g3_ref[lo:hi], 3e-2)
+        close(f"{tag} dW2", g2, g2_ref[lo:hi], 3e-2)
     code = C.status_read()
     if code:
         ok = False
@@ -358,7 +366,7 @@ def main() -> None:
     elif a.engine:
         ok = run_engine()
     else:
-        ok = run(a.experts, a.topk, a.dim, a.inter, a.tokens)
+        ok = all([run(a.experts, a.topk, a.dim, a.inter, a.tokens, balanced=b) for b in (True, False)])
     import torch.distributed as dist
     if dist.is_initialized():
         flag = torch.tensor([1 if ok else 0], device="cuda")

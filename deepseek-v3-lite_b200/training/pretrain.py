@@ -108,6 +108,10 @@ class TrainingConfig:
     # Write checkpoints from a background thread after a host snapshot (new;
     # the reference saves synchronously).
     async_checkpoint: bool = False
+    # Recompute each layer's forward in the fused engine's backward instead of
+    # keeping its activations (new; `grad_checkpoint` keeps its reference
+    # meaning for the eager module path).
+    activation_recompute: bool = False
 
 
 class PretrainDataset(Dataset):
@@ -613,6 +617,7 @@ def config_from_yaml(yaml_cfg: dict, data_path: Optional[str] = None, checkpoint
         ep_capacity_factor=float(yaml_cfg.get("parallel", {}).get("ep_capacity_factor", 0.0)),
         ep_shard_experts=bool(yaml_cfg.get("parallel", {}).get("shard_experts", False)),
         async_checkpoint=bool(t.get("async_checkpoint", False)),
+        activation_recompute=bool(t.get("activation_recompute", False)),
     )
 
 

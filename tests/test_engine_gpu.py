@@ -135,3 +135,39 @@ def test_pretrainer_uses_engine_and_learns(tmp_path):
         assert torch.equal(a, b), n
     out2 = tr2.train_step(data[:, :-1], data[:, 1:], 0)
     assert torch.isfinite(out2["loss"])
+
+
+def test_engine_recompute_matches_stored_activations():
+    """Activation recomputation (layer inputs kept, forward rerun in backward)
+    gives the same loss and gradients as keeping every activation."""
+    from models.mtp import MultiTokenPrediction
+    from models.transformer import Transformer
+    from ops.engine import TrainEngine
+    from training.pretrain import TrainingConfig, _unique_params
+
+    torch.manual_seed(0)
+    base = Transformer(dict(CFG)).cuda()
+    for moe in base.moe_layers():
+        moe.gate.weight.data.mul_(40.0)
+    base_mtp = MultiTokenPrediction(dict(CFG), base).cuda()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    tokens = torch.randint(0, CFG["vocab_size"], (4, 128), device="cuda", generator=g)
+    targets = torch.randint(0, CFG["vocab_size"], (4, 128), device="cuda", generator=g)
+    results = []
+    for recompute in (False, True):
+        mtp = copy.deepcopy(base_mtp)
+        params = _unique_params(mtp)
+        groups = [{"params": [p for p in params if p.dim() >= 2], "weight_decay": 0.1},
+                  {"params": [p for p in params if p.dim() < 2], "weight_decay": 0.0}]
+        eng = TrainEngine(mtp.main_model, mtp, TrainingConfig(lr=1e-3, activation_recompute=recompute), groups)
+        assert eng.recompute == recompute
+        for _ in range(2):            # second call replays the captured graph
+            eng.zero_grad()
+            out = eng.forward_backward(tokens, targets, loss_scale=1.0)
+        torch.cuda.synchronize()
+        eng.check()
+        results.append((out["loss"].item(), out["mtp_loss"].item(), [f.grad.clone() for f in eng.flats]))
+    (l0, m0, g0), (l1, m1, g1) = results
+    assert abs(l0 - l1) < 1e-4 * max(1.0, abs(l0)) and abs(m0 - m1) < 1e-4 * max(1.0, abs(m0))
+    for a, b in zip(g0, g1):
+        assert ((a - b).norm() / a.norm().clamp_min(1e-12)).item() < 1e-3

@@ -86,3 +86,41 @@ def test_plan_skips_empty_experts():
     sb1, _, _, _ = plan_reference(cnt, 1, cap)
     assert row_off1.tolist() == [0, 256, 512]
     assert sb1[3] == 256 + 3 and send_base[3] == 256
+
+
+@pytest.mark.parametrize("R,E,k", [(2, 8, 2), (8, 20, 4), (8, 64, 6), (3, 5, 3), (8, 8, 1)])
+def test_balanced_plan_covers_every_row_once(R, E, k):
+    from parallel.ep import balanced_capacity, plan_reference_balanced
+    T = 333
+    g = torch.Generator().manual_seed(R * 100 + E)
+    # skewed routing: a few experts take most rows (as at random init)
+    logits = torch.randn(R, T, E, generator=g) + torch.linspace(0, 3, E)
+    idx = logits.topk(k, dim=-1).indices
+    cnt = torch.stack([torch.bincount(idx[s].flatten(), minlength=E) for s in range(R)]).to(torch.int32)
+    cap = balanced_capacity(T, k, E, R)
+    plans = [plan_reference_balanced(cnt, r) for r in range(R)]
+    chunk = plans[0][3]
+    assert all(p[3] == chunk for p in plans) and chunk % 256 == 0 and chunk <= cap
+    tot = cnt.sum(0)
+    # every rank computes at most one share; shares differ only at the tail
+    used = [p[4] for p in plans]
+    assert sum(used) == int(((tot + 255) // 256 * 256).sum())
+    assert max(used) <= chunk
+    # simulate the dispatch: every (source, expert) row lands in a real-row slot of its expert
+    seen = {d: set() for d in range(R)}
+    for s in range(R):
+        send_base = plans[s][0]
+        for e in range(E):
+            for j in range(int(cnt[s, e])):
+                gp = int(send_base[e]) + j
+                d, row = gp // chunk, gp % chunk
+                _, row_off, recv_cnt, _, _ = plans[d]
+                assert int(row_off[e]) <= row < int(row_off[e]) + int(recv_cnt[e])
+                assert row not in seen[d]
+                seen[d].add(row)
+    for d in range(R):
+        _, row_off, recv_cnt, _, u = plans[d]
+        assert len(seen[d]) == int(recv_cnt.sum())
+        assert torch.all(row_off[1:] >= row_off[:-1]) and int(row_off[-1]) == u
+        # 256-row alignment of every expert boundary inside a share (CTA-pair tiles stay in one expert)
+        assert all(int(v) % 256 == 0 for v in row_off)

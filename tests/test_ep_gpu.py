@@ -22,14 +22,16 @@ pytestmark = pytest.mark.gpu
 PKG = Path(__file__).resolve().parent.parent / "deepseek-v3-lite_b200"
 
 
-def test_ep_single_rank_layer_matches_fp32():
+@pytest.mark.parametrize("balanced", [True, False], ids=["balanced", "owner"])
+def test_ep_single_rank_layer_matches_fp32(balanced):
     from parallel.ep_selftest import run
-    assert run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=False)
+    assert run(E=8, k=2, D=256, I=128, T=512, iters=2, verbose=False, balanced=balanced)
 
 
-def test_ep_single_rank_uneven_experts():
+@pytest.mark.parametrize("balanced", [True, False], ids=["balanced", "owner"])
+def test_ep_single_rank_uneven_experts(balanced):
     from parallel.ep_selftest import run
-    assert run(E=5, k=3, D=128, I=128, T=300, iters=2, verbose=False)
+    assert run(E=5, k=3, D=128, I=128, T=300, iters=2, verbose=False, balanced=balanced)
 
 
 def test_ep_wait_times_out_without_peer_signal():
