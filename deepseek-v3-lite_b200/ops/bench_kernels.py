@@ -85,12 +85,42 @@ def attention_cases(C, wide_bwd=False):
     return out
 
 
+def decode_cases(C):
+    """Absorbed latent decode (the MLA microbenchmark's decode: 64 rows x 16
+    heads over a 4096-row cache of R 512 + rope 64): cache bytes read per
+    step over the kernel time (split + merge)."""
+    out = []
+    for (B, H, R, dr, S) in [(64, 16, 512, 64, 4096), (64, 12, 192, 24, 2048)]:
+        q_lat, q_pe = torch.randn(B, H, R, device="cuda").bfloat16(), torch.randn(B, H, dr, device="cuda").bfloat16()
+        kv, pe = torch.randn(B, S, R, device="cuda").bfloat16(), torch.randn(B, S, dr, device="cuda").bfloat16()
+        lens = torch.full((B,), S, dtype=torch.int32, device="cuda")
+        scratch = torch.empty(B * H * ((S + 255) // 256) * (2 + R), device="cuda")
+        o = torch.empty(B, H, R, device="cuda", dtype=torch.bfloat16)
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+
+        def step():
+            flush.zero_()             # the cache does not stay in L2 between steps
+            C.latent_decode(q_lat, q_pe, kv, pe, lens, 0.07, S, scratch, o)
+        t_all = _time(step, 20)
+        t_flush = _time(lambda: flush.zero_(), 20)
+        t = max(t_all - t_flush, 1e-6)
+        nbytes = B * S * (R + dr) * 2
+        out.append({"case": f"latent decode B{B} H{H} R{R} rope{dr} ctx{S}", "us": round(t * 1e3, 1),
+                    "cache_GBps": round(nbytes / t / 1e6, 1)})
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--wide-bwd", action="store_true", help="also time the two-kernel tcgen05 attention backward")
     ap.add_argument("--attention-only", action="store_true")
+    ap.add_argument("--decode-only", action="store_true")
     a = ap.parse_args()
     C = native()
+    if a.decode_only:
+        for r in decode_cases(C):
+            print(json.dumps(r), flush=True)
+        return
     for pairs in (() if a.attention_only else (1, 0)):
         C.gemm_pairs(pairs)
         for r in gemm_cases(C):

@@ -163,6 +163,96 @@ def case_ep_dispatch():
     ep.close()
 
 
+def case_small_kernels():
+    """Every memory-bound kernel of the 412M micro-step once more, on its real
+    shapes (32K tokens, D 768, 20 experts top-4, vocab 100,018): router top-k,
+    permutation, gather, combine forward / backward, un-permute, router
+    backward, RMSNorm forward / backward, embedding forward / backward, MLA
+    pack / unpack, CE row / reduce, gradient norm, fused AdamW over a 64M
+    flat buffer, and the data-parallel step's kernels on a one-rank
+    symmetric heap (barrier, reduce-scatter, norm exchange, update +
+    all-gather).  Each runs twice; capture the second."""
+    from parallel.dp import FusedDataParallel
+    from .rope import rope_cos_sin
+    C = native()
+    T, D, E, k, V = 32768, 768, 20, 4, 100018
+    Ep = 24
+    H, dn, dr, dv, R, S, B = 12, 48, 24, 64, 192, 2048, 16
+    dev = "cuda"
+    f32 = dict(device=dev, dtype=torch.float32)
+    i32 = dict(device=dev, dtype=torch.int32)
+    logits = torch.randn(T, Ep, **f32)
+    bias = torch.zeros(E, **f32)
+    idx, wts, ssel = torch.empty(T, k, **i32), torch.empty(T, k, **f32), torch.empty(T, k, **f32)
+    P = (T * k + E * 255 + 255) // 256 * 256
+    row_off, tg = torch.empty(E + 1, **i32), torch.empty(P // 128, **i32)
+    cursor, src, dst = torch.empty(E, **i32), torch.empty(P, **i32), torch.empty(T, k, **i32)
+    xn, xs, ys = _bf(T, D), torch.empty(P, D, device=dev, dtype=torch.bfloat16), _bf(P, D)
+    out, dacc = torch.zeros(T, D, **f32), torch.zeros(T, D, **f32)
+    dres_b, dys, dw = _bf(T, D), torch.empty(P, D, device=dev, dtype=torch.bfloat16), torch.empty(T, k, **f32)
+    dlog = torch.empty(T, Ep, device=dev, dtype=torch.bfloat16)
+    x, dy = torch.randn(T, D, **f32), torch.randn(T, D, **f32)
+    wn, gwn = torch.ones(D, **f32), torch.zeros(D, **f32)
+    yb, rs = torch.empty(T, D, device=dev, dtype=torch.bfloat16), torch.empty(T, **f32)
+    tok = torch.randint(0, V, (T,), device=dev)
+    emb, gemb = torch.randn(V, D, **f32) * 0.01, torch.zeros(V, D, **f32)
+    cos, sin = rope_cos_sin(S, dr, 10000.0, torch.device(dev))
+    q, kvb, kva = _bf(T, H * (dn + dr)), _bf(T, H * (dn + dv)), _bf(T, R + dr)
+    DP = 80
+    Qp, Kp = torch.empty(B * H, S, DP, device=dev, dtype=torch.bfloat16), torch.empty(B * H, S, DP, device=dev,
+                                                                                    dtype=torch.bfloat16)
+    Vt = torch.empty(B * H, S, dv, device=dev, dtype=torch.bfloat16)
+    dQ, dK, dV = torch.randn(B * H, S, DP, **f32), torch.randn(B * H, S, DP, **f32), torch.randn(B * H, S, dv, **f32)
+    dq, dkvb = torch.empty_like(q), torch.empty_like(kvb)
+    dkva = torch.empty(T, R + dr, device=dev, dtype=torch.bfloat16)
+    Tt, nt = 2 * T, (V + 255) // 256
+    pmax, psum = torch.randn(Tt, 2 * nt, **f32), torch.rand(Tt, 2 * nt, **f32) + 1
+    tl, allt = torch.randn(Tt, **f32), torch.randint(0, V, (Tt,), device=dev)
+    lse, lrows, rsc = torch.empty(Tt, **f32), torch.empty(Tt, **f32), torch.empty(Tt, **f32)
+    seg, segw, losses = torch.tensor([0, T, Tt], **i32), torch.tensor([1.0, 0.3], **f32), torch.empty(2, **f32)
+    n = 64 * 1024 * 1024
+    master, grad = torch.randn(n, **f32), torch.randn(n, **f32) * 1e-3
+    m1, v1, shadow = torch.zeros(n, **f32), torch.zeros(n, **f32), torch.empty(n, device=dev, dtype=torch.bfloat16)
+    coef, sq, nrm, scr = torch.ones(1, **f32), torch.zeros(1, **f32), torch.zeros(1, **f32), torch.empty(4096, **f32)
+    heap, alloc = FusedDataParallel.make_heap([n])
+    hm, hg, hs = alloc("master", n, torch.float32), alloc("grad", n, torch.float32), alloc("shadow", n, torch.bfloat16)
+    hm.copy_(master)
+    hg.copy_(grad)
+    offs = [heap.dp_offs[0], heap.dp_offs[1]]
+    om, og, osd = heap.dp_offs[2], heap.dp_offs[3], heap.dp_offs[4]
+    expect = torch.zeros(32, **i32)
+    budget = int(5e9)
+    for it in range(2):
+        counts = torch.zeros(E, **i32)
+        C.router_topk(logits, bias, E, k, 1.0, idx, wts, ssel, counts)
+        C.permute_plan(counts, row_off, tg, cursor, src)
+        C.permute_scatter(idx, row_off, cursor, src, dst)
+        C.gather_rows(xn, src, k, xs)
+        C.combine_fwd(ys, dst, wts, out)
+        C.combine_bwd(dres_b, ys, src, wts, k, dys, dw)
+        C.unpermute_bwd(dys, dst, dacc)
+        C.router_bwd(dw, ssel, idx, 1.0, dlog)
+        C.rmsnorm_fwd(x, wn, 1e-6, yb, rs)
+        C.rmsnorm_bwd(dy, x, wn, rs, dacc, None, yb, gwn)
+        C.embedding_fwd(tok, emb, x)
+        C.embedding_bwd(tok, dy, gemb)
+        C.mla_pack(q, kvb, kva[:, R:], Qp, Kp, Vt, B, S, H, dn, dr, dv, cos, sin, 0)
+        C.mla_unpack(dQ, dK, dV, dq, dkvb, dkva[:, R:], B, S, H, dn, dr, dv, cos, sin, 0)
+        C.ce_rows(pmax, psum, tl, allt, lse, lrows)
+        C.ce_reduce(lrows, allt, seg, segw, 1.0 / 16, losses, rsc)
+        C.grad_sqsum([grad], scr, sq)
+        C.adamw_flat(master, grad, m1, v1, shadow, n, 1e-4, 0.9, 0.95, 1e-8, 0.1, it + 1, coef)
+        sq.zero_()
+        C.dp_barrier(heap.peers, offs, 0, budget, FusedDataParallel.PH_READY, expect)
+        C.dp_reduce(heap.peers, offs, 0, budget, og, 0, n, 1.0, sq)
+        C.dp_norm(heap.peers, offs, 0, budget, sq, expect, 1.0, nrm, coef)
+        C.dp_update(heap.peers, offs, 0, budget, om, og, osd, m1, v1, 0, n, n, 1e-4, 0.9, 0.95, 1e-8, 0.1, it + 1,
+                    coef)
+        C.dp_barrier(heap.peers, offs, 0, budget, FusedDataParallel.PH_GATHERED, expect)
+    torch.cuda.synchronize()
+    heap.close()
+
+
 def case_train_step():
     import os
     import yaml

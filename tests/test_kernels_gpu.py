@@ -351,9 +351,6 @@ def test_flash_bwd_tcgen05(C, B, H, S, DP, DV):
         close(got[0], Qr.grad, rtol=3e-2, atol=3e-2)
 
 
-@pytest.mark.skipif(os.environ.get("DSV3_TEST_WIDE_BWD") != "1",
-                    reason="the two-kernel tcgen05 backward for qk 128/192 is opt-in until validated on a B200 "
-                           "(DSV3_TEST_WIDE_BWD=1 runs this test)")
 @pytest.mark.parametrize("B,H,S,DP,DV", [(1, 2, 1000, 192, 128), (2, 2, 512, 128, 128), (1, 1, 300, 192, 128),
                                          (2, 3, 700, 80, 64)])
 def test_flash_bwd_wide(C, B, H, S, DP, DV):
