@@ -47,8 +47,11 @@ struct FaCfg {
   static constexpr int OFF_V = OFF_K + ST * K_B;
   static constexpr int OFF_P = OFF_V + ST * V_B;
   static constexpr int OFF_BAR = OFF_P + 2 * P_B;
-  static constexpr int OFF_XR = OFF_BAR + 256;            // row-max / row-sum exchange [2][2][128] f32
-  static constexpr int SMEM = OFF_XR + 2048 + 1024;
+  // row-max / row-sum exchange [2][2][128] f32 of the two-warpgroup softmax,
+  // where it fits next to the rings (not at qk 128 / v 128)
+  static constexpr int XR_B = OFF_BAR + 256 + 2048 + 1024 <= 232448 ? 2048 : 0;
+  static constexpr int OFF_XR = OFF_BAR + 256;
+  static constexpr int SMEM = OFF_XR + XR_B + 1024;
 };
 
 template <int NA, int NB, int DV, int WG = 1>
@@ -60,6 +63,7 @@ __global__ void __launch_bounds__(64 + 128 * WG, 1)
                         unsigned int* status) {
   using C = FaCfg<NA, NB, DV>;
   static_assert(DV % 64 == 0 && DV <= 128, "DV must be 64 or 128");
+  static_assert(WG == 1 || C::XR_B > 0, "two softmax warpgroups need the exchange buffer");
   extern __shared__ __align__(1024) uint8_t fa_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -378,8 +382,11 @@ namespace dsv3 {
 //   P^T  = exp2(S^T c - L[q]),  dS^T = P^T (dP^T - delta[q])   (softmax warps,
 //          one key row per thread, written to smem as bf16 K-major tiles)
 //   dV  += P^T dO_i     dK += dS^T Q_i                   (TMEM accumulators)
-//   dQ_i = dS K          -> TMEM, drained by four more warps with fp32
-//                           vector reductions into the global dQ
+//   dQ_i = dS K          -> TMEM, drained with fp32 vector reductions into
+//                           the global dQ: by the softmax warps after they
+//                           hand tile i+1 to the MMA warp (DRAIN = 0), or by
+//                           four dedicated drain warps that run beside the
+//                           softmax of the next tile (DRAIN = 1)
 //
 // Q_i / K are used both K-major (for S^T) and MN-major (for dK / dQ): a
 // 128-row tile of 64 (or 16) head-dim columns in 128B (32B) swizzle is the
@@ -405,8 +412,8 @@ struct FabCfg {
   static_assert(C_DQ + DQKP <= 512, "TMEM budget");
 };
 
-template <int NA, int NB, int DV>
-__global__ void __launch_bounds__(320, 1)
+template <int NA, int NB, int DV, int DRAIN = 0>
+__global__ void __launch_bounds__(320 + 128 * DRAIN, 1)
     fa_bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
                         const __grid_constant__ CUtensorMap tmKa, const __grid_constant__ CUtensorMap tmKb,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -451,7 +458,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(p_full, 256);
     mbar_init(p_free, 1);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 256);
+    mbar_init(dq_free, DRAIN ? 128 : 256);
     mbar_init(acc_done, 1);
     mbar_init(ld_ready, 128);
     *abort_flag = 0;
@@ -594,12 +601,41 @@ __global__ void __launch_bounds__(320, 1)
         mbar_wait_bounded(acc_done, 0, nullptr, status, DSV3_ERR_WAIT_TMEM);
       }
     }
+  } else if (DRAIN && warp >= 10) {
+    // ------------------------------------------- dQ drain (warps 10-13)
+    // One query row of dQ_i per thread (TMEM lane = query row), all DQK
+    // columns, fp32 vector reductions into the global dQ; then dq_free lets
+    // the MMA warp write dQ_{i+1}.
+    const int quarter = warp & 3;
+    const int qr = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    for (int it = 0; it < iters; ++it) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(dq_full, it & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) break;
+      tc_fence_after();
+      const int q = (qstart + it) * 128 + qr;
+      float* dqr = dQ + ((size_t)bh * Sq + q) * DQK;
+#pragma unroll
+      for (int c = 0; c < DQK / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld16(tmem + lane_base + C::C_DQ + c * 16, r);
+        tmem_ld_wait();
+        if (q < Sq)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dqr + c * 16 + e),
+                         "f"(__uint_as_float(r[e]) * scale), "f"(__uint_as_float(r[e + 1]) * scale),
+                         "f"(__uint_as_float(r[e + 2]) * scale), "f"(__uint_as_float(r[e + 3]) * scale)
+                         : "memory");
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
   } else {
     // ---------------------------------------------- compute (key rows)
     // Warps 2-5 and 6-9 share each key row (same TMEM lane quarter): the
     // first group takes query columns 0-63 of S^T / dP^T, the second 64-127.
-    // After handing tile i to the MMA warp they drain dQ_{i-1} (each group
-    // half of its columns) with fp32 vector reductions.
+    // Without drain warps they drain dQ_{i-1} (each group half of its
+    // columns) with fp32 vector reductions after handing tile i over.
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int kr = quarter * 32 + lane;
@@ -655,20 +691,6 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[4][16], dr[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld16(tmem + lane_base + C::C_S + half * 64 + c * 16, sr[c]);
-        tmem_ld16(tmem + lane_base + C::C_DP + half * 64 + c * 16, dr[c]);
-      }
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(s_free);
-      // P^T / dS^T of tile it-1 must have been consumed before they are overwritten
-      if (it > 0 && !__all_sync(0xffffffffu, mbar_wait_bounded(p_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
-        ok = false;
-        break;
-      }
       // keys >= lim[q] are masked: key <= q_off + q  <=>  q >= key - q_off
       const int qmin = causal ? key - q_off : -0x7fffffff;
       // tiles fully inside the sequences and the causal band skip the per-element mask
@@ -677,38 +699,67 @@ __global__ void __launch_bounds__(320, 1)
       uint8_t* dsrow = smem + C::OFF_DS + half * 16384 + kr * 128;
       const float4* L4 = reinterpret_cast<const float4*>(Lb + half * 64);
       const float4* D4 = reinterpret_cast<const float4*>(Db + half * 64);
+      // The half's 64 query columns are read from TMEM in NP passes (two
+      // passes of 32 with the drain warps, whose threads have fewer registers).
+      constexpr int NP = DRAIN ? 2 : 1, PC = 64 / NP;
+      bool pass_ok = true;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t pk[4], dk[4];
-        const float4 la = L4[2 * c], lb = L4[2 * c + 1], da = D4[2 * c], db = D4[2 * c + 1];
-        const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
-        const float dl[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+      for (int pass = 0; pass < NP; ++pass) {
+        uint32_t sr[PC / 16][16], dr[PC / 16][16];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float pv[2], dv2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = c * 8 + 2 * e + u;           // within this half
-            const int q = q0 + half * 64 + col;
-            const float s = __uint_as_float(sr[col >> 4][col & 15]);
-            const float dp = __uint_as_float(dr[col >> 4][col & 15]);
-            float p = ex2_approx(s * scale_log2 - lv[2 * e + u]);
-            if (!all_valid && !(q < Sq && key < Sk && q >= qmin)) p = 0.f;
-            pv[u] = p;
-            dv2[u] = p * (dp - dl[2 * e + u]);
-          }
-          pk[e] = pack_bf16x2(pv[0], pv[1]);
-          dk[e] = pack_bf16x2(dv2[0], dv2[1]);
+        for (int c = 0; c < PC / 16; ++c) {
+          tmem_ld16(tmem + lane_base + C::C_S + half * 64 + pass * PC + c * 16, sr[c]);
+          tmem_ld16(tmem + lane_base + C::C_DP + half * 64 + pass * PC + c * 16, dr[c]);
         }
-        const int sw = (c ^ (kr & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + sw) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(dsrow + sw) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+        tmem_ld_wait();
+        if (pass == NP - 1) {
+          tc_fence_before();
+          mbar_arrive(s_free);
+        }
+        // P^T / dS^T of tile it-1 must have been consumed before they are overwritten
+        if (pass == 0 && it > 0 &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(p_free, ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+          pass_ok = false;
+          break;
+        }
+#pragma unroll
+        for (int cc = 0; cc < PC / 8; ++cc) {
+          const int c = pass * (PC / 8) + cc;              // 8-column chunk within the half
+          uint32_t pk[4], dk[4];
+          const float4 la = L4[2 * c], lb = L4[2 * c + 1], da = D4[2 * c], db = D4[2 * c + 1];
+          const float lv[8] = {la.x, la.y, la.z, la.w, lb.x, lb.y, lb.z, lb.w};
+          const float dl[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float pv[2], dv2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int col = cc * 8 + 2 * e + u;            // within this pass
+              const int q = q0 + half * 64 + pass * PC + col;
+              const float s = __uint_as_float(sr[col >> 4][col & 15]);
+              const float dp = __uint_as_float(dr[col >> 4][col & 15]);
+              float p = ex2_approx(s * scale_log2 - lv[2 * e + u]);
+              if (!all_valid && !(q < Sq && key < Sk && q >= qmin)) p = 0.f;
+              pv[u] = p;
+              dv2[u] = p * (dp - dl[2 * e + u]);
+            }
+            pk[e] = pack_bf16x2(pv[0], pv[1]);
+            dk[e] = pack_bf16x2(dv2[0], dv2[1]);
+          }
+          const int sw = (c ^ (kr & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + sw) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(dsrow + sw) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+        }
+      }
+      if (!pass_ok) {
+        ok = false;
+        break;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
       // dQ_{it-1} finished with the MMAs that released P^T / dS^T above
-      if (it > 0) {
+      if (!DRAIN && it > 0) {
         tc_fence_after();
         drain_dq(it - 1);
       }
@@ -717,7 +768,7 @@ __global__ void __launch_bounds__(320, 1)
     if (ok && iters > 0 &&
         __all_sync(0xffffffffu, mbar_wait_bounded(acc_done, 0, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
       tc_fence_after();
-      drain_dq(iters - 1);
+      if (!DRAIN) drain_dq(iters - 1);
       float* dkr = dK + ((size_t)bh * Sk + key) * DQK;
       float* dvr = dVo + ((size_t)bh * Sk + key) * DV;
       for (int c = dq_c0; c < dq_c1; ++c) {

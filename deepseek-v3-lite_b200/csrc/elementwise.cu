@@ -483,56 +483,80 @@ __global__ void mla_pack_v(const __nv_bfloat16* __restrict__ q, long ldq, const 
   }
 }
 
-// Gradient of mla_pack_v.  dQ, dK fp32 [B,H,S,DP], dV fp32 [B,H,S,dv].
-__global__ void mla_unpack_v(const float* __restrict__ dQ, const float* __restrict__ dK, const float* __restrict__ dV,
-                             __nv_bfloat16* __restrict__ dq, long lddq, __nv_bfloat16* __restrict__ dkvb,
-                             __nv_bfloat16* __restrict__ dkpe, long ldk, int S, int H, int dn, int dr, int dv, int DP,
-                             const float* __restrict__ cosv, const float* __restrict__ sinv, int start) {
-  extern __shared__ float pe_acc[];  // [dr]
-  const int t = blockIdx.x, b = t / S, s = t % S, p = s + start;
-  for (int c = threadIdx.x; c < dr; c += blockDim.x) pe_acc[c] = 0.f;
-  __syncthreads();
-  const int qk_chunks = (dn + dr) / 8, v_chunks = dv / 8;
-  const int per_head = qk_chunks + v_chunks;
-  for (int idx = threadIdx.x; idx < H * per_head; idx += blockDim.x) {
-    const int h = idx / per_head, j = idx % per_head;
-    if (j >= qk_chunks) {
-      const int c = (j - qk_chunks) * 8;
-      const float4* src = reinterpret_cast<const float4*>(dV + (((size_t)b * H + h) * S + s) * dv + c);
-      const float4 a = src[0], bb = src[1];
-      *reinterpret_cast<uint4*>(dkvb + ((size_t)t * H + h) * (dn + dv) + dn + c) =
-          make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(bb.x, bb.y), pack_bf16x2(bb.z, bb.w));
-      continue;
-    }
-    const int c = j * 8;
-    const size_t o = (((size_t)b * H + h) * S + s) * DP + c;
-    float qv[8], kv[8];
-    *reinterpret_cast<float4*>(qv) = reinterpret_cast<const float4*>(dQ + o)[0];
-    *reinterpret_cast<float4*>(qv + 4) = reinterpret_cast<const float4*>(dQ + o)[1];
-    *reinterpret_cast<float4*>(kv) = reinterpret_cast<const float4*>(dK + o)[0];
-    *reinterpret_cast<float4*>(kv + 4) = reinterpret_cast<const float4*>(dK + o)[1];
-    uint32_t qo[4], ko[4];
-    if (c + 8 <= dn) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        qo[e] = pack_bf16x2(qv[2 * e], qv[2 * e + 1]);
-        ko[e] = pack_bf16x2(kv[2 * e], kv[2 * e + 1]);
+// Attention gradients back to the projection outputs (inverse of mla_pack),
+// one CTA per (batch row, TB consecutive positions).  For each head the TB
+// positions' rows of dQ / dK / dV are adjacent in memory, so consecutive
+// threads read consecutive 32-byte chunks: nope / v chunks go to dq and dkvb
+// as bf16; each decoupled-RoPE chunk of a position is handled by one thread
+// that walks the heads, applies the inverse rotation to dq and sums the
+// rotated dK over heads into the shared k_pe gradient in registers.
+template <int TB>
+__global__ void __launch_bounds__(256) mla_unpack_blk(const float* __restrict__ dQ, const float* __restrict__ dK,
+                                                      const float* __restrict__ dV, __nv_bfloat16* __restrict__ dq,
+                                                      long lddq, __nv_bfloat16* __restrict__ dkvb,
+                                                      __nv_bfloat16* __restrict__ dkpe, long ldk, int S, int H, int dn,
+                                                      int dr, int dv, int DP, const float* __restrict__ cosv,
+                                                      const float* __restrict__ sinv, int start) {
+  const int b = blockIdx.y, s0 = blockIdx.x * TB;
+  const int nn = dn / 8, nv = dv / 8, nr = dr / 8, per = nn + nv;
+  const int main_items = H * TB * per, rope_items = TB * nr;
+  for (int idx = threadIdx.x; idx < main_items + rope_items; idx += blockDim.x) {
+    if (idx < main_items) {
+      const int h = idx / (TB * per), rem = idx - h * (TB * per), i = rem / per, j = rem - i * per;
+      const int s = s0 + i;
+      if (s >= S) continue;
+      const size_t t = (size_t)b * S + s, row = ((size_t)b * H + h) * S + s;
+      if (j < nn) {
+        const int c = j * 8;
+        const float4* q4 = reinterpret_cast<const float4*>(dQ + row * DP + c);
+        const float4* k4 = reinterpret_cast<const float4*>(dK + row * DP + c);
+        const float4 qa = q4[0], qb = q4[1], ka = k4[0], kb = k4[1];
+        *reinterpret_cast<uint4*>(dq + t * lddq + (size_t)h * (dn + dr) + c) =
+            make_uint4(pack_bf16x2(qa.x, qa.y), pack_bf16x2(qa.z, qa.w), pack_bf16x2(qb.x, qb.y), pack_bf16x2(qb.z, qb.w));
+        *reinterpret_cast<uint4*>(dkvb + (t * H + h) * (dn + dv) + c) =
+            make_uint4(pack_bf16x2(ka.x, ka.y), pack_bf16x2(ka.z, ka.w), pack_bf16x2(kb.x, kb.y), pack_bf16x2(kb.z, kb.w));
+      } else {
+        const int c = (j - nn) * 8;
+        const float4* v4 = reinterpret_cast<const float4*>(dV + row * dv + c);
+        const float4 a = v4[0], bb = v4[1];
+        *reinterpret_cast<uint4*>(dkvb + (t * H + h) * (dn + dv) + dn + c) =
+            make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(bb.x, bb.y), pack_bf16x2(bb.z, bb.w));
       }
-      *reinterpret_cast<uint4*>(dkvb + ((size_t)t * H + h) * (dn + dv) + c) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
     } else {
+      const int r = idx - main_items, i = r / nr, k = r - i * nr;
+      const int s = s0 + i;
+      if (s >= S) continue;
+      const size_t t = (size_t)b * S + s;
+      const int p = s + start, c = dn + k * 8;
+      float cs[4], sn[4], acc[8];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = (c - dn) / 2 + e;
-        const float cs = cosv[(size_t)p * (dr / 2) + i], sn = sinv[(size_t)p * (dr / 2) + i];
-        qo[e] = pack_bf16x2(qv[2 * e] * cs + qv[2 * e + 1] * sn, -qv[2 * e] * sn + qv[2 * e + 1] * cs);
-        atomicAdd(&pe_acc[2 * i], kv[2 * e] * cs + kv[2 * e + 1] * sn);
-        atomicAdd(&pe_acc[2 * i + 1], -kv[2 * e] * sn + kv[2 * e + 1] * cs);
+        cs[e] = cosv[(size_t)p * (dr / 2) + k * 4 + e];
+        sn[e] = sinv[(size_t)p * (dr / 2) + k * 4 + e];
       }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int h = 0; h < H; ++h) {
+        const size_t row = ((size_t)b * H + h) * S + s;
+        float qv[8], kv[8];
+        *reinterpret_cast<float4*>(qv) = reinterpret_cast<const float4*>(dQ + row * DP + c)[0];
+        *reinterpret_cast<float4*>(qv + 4) = reinterpret_cast<const float4*>(dQ + row * DP + c)[1];
+        *reinterpret_cast<float4*>(kv) = reinterpret_cast<const float4*>(dK + row * DP + c)[0];
+        *reinterpret_cast<float4*>(kv + 4) = reinterpret_cast<const float4*>(dK + row * DP + c)[1];
+        uint32_t qo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qo[e] = pack_bf16x2(qv[2 * e] * cs[e] + qv[2 * e + 1] * sn[e], -qv[2 * e] * sn[e] + qv[2 * e + 1] * cs[e]);
+          acc[2 * e] += kv[2 * e] * cs[e] + kv[2 * e + 1] * sn[e];
+          acc[2 * e + 1] += -kv[2 * e] * sn[e] + kv[2 * e + 1] * cs[e];
+        }
+        *reinterpret_cast<uint4*>(dq + t * lddq + (size_t)h * (dn + dr) + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+      }
+      *reinterpret_cast<uint4*>(dkpe + t * ldk + k * 8) =
+          make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                     pack_bf16x2(acc[6], acc[7]));
     }
-    *reinterpret_cast<uint4*>(dq + (size_t)t * lddq + (size_t)h * (dn + dr) + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
   }
-  __syncthreads();
-  for (int c = threadIdx.x; c < dr; c += blockDim.x) dkpe[(size_t)t * ldk + c] = __float2bfloat16(pe_acc[c]);
 }
 
 int blocks_for(long n, int per) { return (int)((n + per - 1) / per); }
@@ -675,7 +699,8 @@ void mla_unpack(const at::Tensor& dQ, const at::Tensor& dK, const at::Tensor& dV
   auto* dpe = reinterpret_cast<__nv_bfloat16*>(dkpe.data_ptr());
   if (dV.scalar_type() == at::kFloat && dn % 8 == 0 && dr % 8 == 0 && dv % 8 == 0 && DP % 8 == 0 &&
       dkpe.stride(0) % 8 == 0 && dq.stride(0) % 8 == 0) {
-    mla_unpack_v<<<B * S, 256, dr * sizeof(float), st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
+    constexpr int TB = 16;
+    mla_unpack_blk<TB><<<dim3((S + TB - 1) / TB, B), 256, 0, st>>>(dQ.data_ptr<float>(), dK.data_ptr<float>(),
         dV.data_ptr<float>(), dqp, dq.stride(0), dkp, dpe, dkpe.stride(0), S, H, dn, dr, dv, DP, cosv.data_ptr<float>(),
         sinv.data_ptr<float>(), start);
     C10_CUDA_KERNEL_LAUNCH_CHECK();

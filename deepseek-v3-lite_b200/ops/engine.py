@@ -537,6 +537,7 @@ class TrainEngine:
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
         idx, wts, ssel, counts, Ep = self._router(moe, xn)
+        self._mark("router fwd")
         P = _pad(T * k + E * 255, 256)       # expert ranges are 256-row aligned (CTA-pair tiles)
         row_off = torch.empty(E + 1, dtype=torch.int32, device=self.device)
         tile_group = torch.empty(P // 128, dtype=torch.int32, device=self.device)
@@ -547,10 +548,12 @@ class TrainEngine:
         C.permute_scatter(idx, row_off, cursor, src, dst)
         xs = torch.empty(P, self.D, dtype=BF16, device=self.device)
         C.gather_rows(xn, src, k, xs)
+        self._mark("moe permute fwd")
         w1 = moe.experts[0].w1.weight
         h = torch.empty(P, I, dtype=BF16, device=self.device)
         gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
         C.swiglu_fwd(xs, self.swiglu_w13(w1, E), tile_group, h, gu, group_rows=256)
+        self._mark("experts gate/up fwd")
         out = torch.empty_like(resid_in) if moe.shared_experts else resid_in.clone()
         shared = []
 
@@ -562,7 +565,9 @@ class TrainEngine:
         side = self._fork(shared_fwd) if moe.shared_experts else None
         ys = torch.empty(P, self.D, dtype=BF16, device=self.device)
         C.grouped_fwd(h, self.stacked(moe.experts[0].w2.weight, E), tile_group, ys, group_rows=256)
+        self._mark("experts down fwd")
         self._join(side)
+        self._mark("shared experts join")
         C.combine_fwd(ys, dst, wts, out)
         return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
                     h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts), out
@@ -586,17 +591,24 @@ class TrainEngine:
         dys = torch.empty(P, self.D, dtype=BF16, device=self.device)
         dw = torch.empty(T, k, dtype=F32, device=self.device)
         C.combine_bwd(dres_bf16, ctx.ys, ctx.src, ctx.wts, k, dys, dw)
+        self._mark("combine bwd")
         w1 = moe.experts[0].w1.weight
         w2 = moe.experts[0].w2.weight
         dgu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
         C.swiglu_dgrad(dys, self.stacked(w2, E), ctx.tile_group, ctx.gu, dgu, group_rows=256)
+        self._mark("experts swiglu dgrad")
         C.grouped_wgrad(dys, ctx.h, ctx.row_off, self.stacked(w2, E, grad=True))
+        self._mark("experts down wgrad")
         dxs = torch.empty(P, self.D, dtype=BF16, device=self.device)
         C.grouped_dgrad(dgu, self.swiglu_w13(w1, E).view(E, 2 * I, self.D), ctx.tile_group, dxs, group_rows=256)
+        self._mark("experts dgrad")
         C.grouped_wgrad(dgu, ctx.xs, ctx.row_off, self.swiglu_g13(w1, E))
+        self._mark("experts up wgrad")
         self._join(side)
+        self._mark("shared experts join")
         C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
+        self._mark("router bwd")
 
     # ------------------------------------------------------------------ MTP
     def _mtp_fwd(self, mod, h_prev, emb, Bm, Sm):

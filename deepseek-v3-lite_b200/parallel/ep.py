@@ -321,6 +321,7 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
     h = torch.empty(ep.cap, inter_dim, dtype=torch.bfloat16, device=xn.device)
     gu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=xn.device)
     C.swiglu_fwd(xs, w13_local, plan["tile_group"], h, gu, group_rows=256)
+    marks("experts gate/up fwd")
     ys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=xn.device)
     if ep.fused_combine:
         # down projection whose epilogue stores every row into its home rank's
@@ -334,10 +335,11 @@ def moe_forward_ep(ep: ExpertParallel, slot: int, xn: torch.Tensor, idx, wts, co
         C.grouped_fwd(h, w2_local, plan["tile_group"], ys, group_rows=256)
         marks("experts fwd")
         ep.combine_send(slot, ys, plan["row_off"])
+    marks("ep combine wait")
     side = plan.pop("side")
     if side is not None:
         torch.cuda.current_stream(xn.device).wait_stream(side)
-    marks("ep combine wait")
+    marks("shared experts join")
     C.combine_fwd(ep.comb, ep.slot_arange, wts, out)
     marks("combine fwd")
     plan.update(slot=slot, xs=xs, h=h, gu=gu, ys=ys)
@@ -358,9 +360,12 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
     dys = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
     dw_rows = torch.empty(ep.cap, dtype=torch.float32, device=dout_bf16.device)
     ep.bwd_prep(slot, ctx["ys"], ctx["row_off"], dys, dw_rows)
+    marks("ep bwd prep")
     dgu = torch.empty(ep.cap, 2 * inter_dim, dtype=torch.bfloat16, device=dout_bf16.device)
     C.swiglu_dgrad(dys, w2_local, ctx["tile_group"], ctx["gu"], dgu, group_rows=256)
+    marks("experts swiglu dgrad")
     C.grouped_wgrad(dys, ctx["h"], ctx["row_off"], g2_local)
+    marks("experts down wgrad")
     dxs = torch.empty(ep.cap, ep.D, dtype=torch.bfloat16, device=dout_bf16.device)
     w13_2d = w13_local.reshape(ep.G, 2 * inter_dim, ep.D)
     if ep.fused_combine:
@@ -369,6 +374,7 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
         origin, _ = ep.recv_meta(slot)
         C.grouped_scatter(dgu, w13_2d, True, ctx["tile_group"], dxs, 256, ep.peers_dev, ep.off_comb, origin, dw_rows,
                           ep.off_dw, ep.T * ep.k, ep.off_flags, ep.rank, PH_BWD_COMBINE, ep.done[4:5])
+        marks("experts dgrad+send")
         C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
         marks("experts bwd")
         C.ep_wait(ep.heap.peers, ep.offs(slot), ep.dims, PH_BWD_COMBINE, ep.expect)
@@ -377,9 +383,10 @@ def moe_backward_ep(ep: ExpertParallel, ctx: dict, dout_bf16: torch.Tensor, w13_
         C.grouped_wgrad(dgu, ctx["xs"], ctx["row_off"], g13_local)
         marks("experts bwd")
         ep.combine_send_bwd(slot, dxs, dw_rows, ctx["row_off"])
+    marks("ep combine wait bwd")
     if side is not None:
         torch.cuda.current_stream(dx_acc.device).wait_stream(side)
-    marks("ep combine wait bwd")
+    marks("shared experts join")
     C.unpermute_bwd(ep.comb, ep.slot_arange, dx_acc)
     marks("combine bwd")
     return ep.dw_inbox.view(ep.T, ep.k)
