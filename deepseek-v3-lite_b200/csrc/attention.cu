@@ -465,6 +465,28 @@ void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   CUtensorMap qb = NB ? mk(q, Sq, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : qa;
   CUtensorMap kb = NB ? mk(k, Sk, DP, 16, CU_TENSOR_MAP_SWIZZLE_32B) : ka;
   CUtensorMap vm = mk(v, Sk, DV, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  // two query tiles per CTA (independent softmax chains) for qk <= 80, v 64;
+  // DSV3_FA_FWD_2Q=0 selects the one-tile kernel
+  if constexpr (Fa2Cfg<NA, NB, DV>::FITS) {
+    static const bool two_q = [] {
+      const char* e = getenv("DSV3_FA_FWD_2Q");
+      return !(e != nullptr && e[0] == '0');
+    }();
+    if (two_q) {
+      using C2 = Fa2Cfg<NA, NB, DV>;
+      auto k2 = fa_fwd2q_sm100_kernel<NA, NB, DV>;
+      static bool cfg2 = false;
+      if (!cfg2) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, C2::SMEM));
+        cfg2 = true;
+      }
+      k2<<<dim3((Sq + 255) / 256, BH), 320, C2::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
+          reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq, Sk, H, q_off,
+          (float)(scale * 1.4426950408889634), causal ? 1 : 0, status_ptr());
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      return;
+    }
+  }
   // two softmax warpgroups per CTA where the exchange buffer fits
   // (DSV3_FA_FWD_WG=1: one)
   constexpr int WG2 = Cfg::XR_B > 0 ? 2 : 1;

@@ -374,6 +374,327 @@ __global__ void __launch_bounds__(64 + 128 * WG, 1)
 namespace dsv3 {
 
 // ----------------------------------------------------------------------------
+// Forward with two query tiles per CTA (qk up to 80, v 64).  Tiles A (rows
+// m0..m0+127) and B (m0+128..m0+255) of the same head share every K / V tile
+// brought in by TMA; warps 2-5 run tile A's softmax and warps 6-9 tile B's,
+// two independent chains, so while one waits on its TMEM loads or barriers
+// the other issues.  TMEM: S_A, S_B (128 columns each, one buffer per tile:
+// S_t(j+1) is written once the tile's softmax holds S_t(j) in registers),
+// O_A, O_B (DV each).  P_A, P_B: one 32 KB shared tile each (P_t(j) is
+// written once PV_t(j-1) has read P_t(j-1)).  The MMA thread issues, per KV
+// tile j, S_A(j) and S_B(j), then PV_A(j-1) and PV_B(j-1).  Under the causal
+// mask tile B sees one more KV tile than A.
+// ----------------------------------------------------------------------------
+template <int NA, int NB, int DV>
+struct Fa2Cfg {
+  static constexpr int Q_B = NA * 16384 + NB * 4096;
+  static constexpr int K_B = Q_B;
+  static constexpr int V_B = (DV / 64) * 16384;
+  static constexpr int P_B = 32768;
+  static constexpr int OFF_K = 2 * Q_B;
+  static constexpr int OFF_V = OFF_K + 2 * K_B;
+  static constexpr int OFF_P = OFF_V + 2 * V_B;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_B;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr bool FITS = SMEM <= 232448 && DV == 64 && NA == 1;
+};
+
+template <int NA, int NB, int DV>
+__global__ void __launch_bounds__(320, 1)
+    fa_fwd2q_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
+                          const __grid_constant__ CUtensorMap tmKa, const __grid_constant__ CUtensorMap tmKb,
+                          const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
+                          float* __restrict__ L, int Sq, int Sk, int H, int q_off, float scale_log2, int causal,
+                          unsigned int* status) {
+  using C = Fa2Cfg<NA, NB, DV>;
+  static_assert(C::FITS, "two-tile forward: qk <= 80, v 64");
+  extern __shared__ __align__(1024) uint8_t fa2_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa2_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem + C::OFF_K;
+  uint8_t* sV = smem + C::OFF_V;
+  uint8_t* sP = smem + C::OFF_P;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bar;
+  uint64_t* k_full = bar + 1;    // [2]
+  uint64_t* k_empty = bar + 3;   // [2]
+  uint64_t* v_full = bar + 5;    // [2]
+  uint64_t* v_empty = bar + 7;   // [2]
+  uint64_t* s_full = bar + 9;    // [tile]
+  uint64_t* s_free = bar + 11;   // [tile]
+  uint64_t* p_full = bar + 13;   // [tile]
+  uint64_t* pv_done = bar + 15;  // [tile]
+  uint64_t* drain = bar + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 18);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, m0 = blockIdx.x * 256;
+  const int nk = (Sk + 127) / 128;
+  // KV tiles each query tile attends to (0 when the tile lies past Sq)
+  int nt[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int mt = m0 + 128 * t;
+    nt[t] = mt >= Sq ? 0 : (causal ? min(nk, (q_off + mt + 128 + 127) / 128) : nk);
+  }
+  const int n_all = max(nt[0], nt[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------- producer: Q_A, Q_B, then K
+      const int nq = nt[1] > 0 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nq * C::Q_B);
+      for (int t = 0; t < nq; ++t) {
+#pragma unroll
+        for (int a = 0; a < NA; ++a) tma_load_3d(smem + t * C::Q_B + a * 16384, &tmQa, q_full, a * 64, m0 + 128 * t, bh);
+        if (NB) tma_load_3d(smem + t * C::Q_B + NA * 16384, &tmQb, q_full, NA * 64, m0 + 128 * t, bh);
+      }
+      uint32_t issued = 0, last_phase = 0;
+      for (int j = 0; j < n_all; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(&k_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::K_B);
+        uint8_t* k = sK + st * C::K_B;
+#pragma unroll
+        for (int a = 0; a < NA; ++a) tma_load_3d(k + a * 16384, &tmKa, &k_full[st], a * 64, j * 128, bh);
+        if (NB) tma_load_3d(k + NA * 16384, &tmKb, &k_full[st], NA * 64, j * 128, bh);
+        issued |= 1u << st;
+        last_phase = (last_phase & ~(1u << st)) | (ph << st);
+      }
+      mbar_wait_bounded(q_full, 0, nullptr, status, DSV3_ERR_WAIT_FULL);
+      for (int st = 0; st < 2; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(&k_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+    } else if (lane == 1) {
+      // -------------------------------------------------------- producer: V
+      uint32_t issued = 0, last_phase = 0;
+      for (int j = 0; j < n_all; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait_bounded(&v_empty[st], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::V_B);
+        uint8_t* v = sV + st * C::V_B;
+#pragma unroll
+        for (int d = 0; d < DV / 64; ++d) tma_load_3d(v + d * 16384, &tmV, &v_full[st], d * 64, j * 128, bh);
+        issued |= 1u << st;
+        last_phase = (last_phase & ~(1u << st)) | (ph << st);
+      }
+      for (int st = 0; st < 2; ++st)
+        if (issued & (1u << st)) mbar_wait_bounded(&v_full[st], (last_phase >> st) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------ MMA issuer
+      constexpr uint32_t IDS = idesc_bf16_f32(128, 128, 0, 0);
+      constexpr uint32_t IDO = idesc_bf16_f32(128, DV, 0, 1);
+      bool ok = n_all > 0 && mbar_wait_bounded(q_full, 0, abort_flag, status, DSV3_ERR_WAIT_FULL);
+      bool any = false;
+      for (int j = 0; ok && j <= n_all; ++j) {
+        if (j < n_all) {
+          const int st = j & 1;
+          if (!mbar_wait_bounded(&k_full[st], (j >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+          const uint32_t k = smem_u32(sK + st * C::K_B);
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j >= nt[t]) continue;
+            // the tile's only S buffer is free once its softmax loaded S_t(j-1)
+            if (j >= 1 && !mbar_wait_bounded(&s_free[t], (j - 1) & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t q = smem_u32(smem + t * C::Q_B);
+            uint32_t acc = 0;
+#pragma unroll
+            for (int a = 0; a < NA; ++a)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                umma_bf16(tmem + t * 128, smem_desc_sw128(q + a * 16384 + kk * 32, 16, 1024),
+                          smem_desc_sw128(k + a * 16384 + kk * 32, 16, 1024), IDS, acc);
+                acc = 1;
+              }
+            if (NB) umma_bf16(tmem + t * 128, smem_desc_sw32(q + NA * 16384, 256), smem_desc_sw32(k + NA * 16384, 256),
+                              IDS, acc);
+            umma_commit(&s_full[t]);
+            any = true;
+          }
+          if (!ok) break;
+          umma_commit(&k_empty[st]);   // K_j is free once every S of tile j is computed
+        }
+        if (j >= 1) {
+          const int pj = j - 1, vs = pj & 1;
+          if (!mbar_wait_bounded(&v_full[vs], (pj >> 1) & 1, abort_flag, status, DSV3_ERR_WAIT_FULL)) break;
+          const uint32_t v = smem_u32(sV + vs * C::V_B);
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (pj >= nt[t]) continue;
+            if (!mbar_wait_bounded(&p_full[t], pj & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t pp = smem_u32(sP + t * C::P_B);
+            const uint32_t tO = tmem + 256 + t * DV;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              umma_bf16(tO, smem_desc_sw128(pp + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                        smem_desc_sw128(v + kk * 2048, 16384, 1024), IDO, (pj > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&pv_done[t]);
+          }
+          if (!ok) break;
+          umma_commit(&v_empty[vs]);
+        }
+      }
+      if (any) {
+        umma_commit(drain);
+        mbar_wait_bounded(drain, 0, nullptr, status, DSV3_ERR_WAIT_TMEM);
+      }
+    }
+  } else {
+    // ---------------------------------------- softmax / epilogue of tile t
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = m0 + 128 * t + row;
+    const int qpos = q_off + qrow;
+    const int n_blocks = nt[t];
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_base + t * 128;
+    const uint32_t tO = tmem + lane_base + 256 + t * DV;
+    uint8_t* prow = sP + t * C::P_B + row * 128;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_blocks && ok; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[t], j & 1, abort_flag, status, DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t raw[8][16];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tmem_ld16(tS + c * 16, raw[c]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) s[c * 16 + e] = __uint_as_float(raw[c][e]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[t]);
+      const int n0 = j * 128;
+      const int lim = causal ? min(Sk, qpos + 1) - n0 : Sk - n0;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float v = c < lim ? s[c] * scale_log2 : -INFINITY;
+        s[c] = v;
+        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+      }
+      const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float m_new = fmaxf(m_used, rmax);
+      // PV_t(j-1) must have read P_t(j-1) (single buffer) and written O_t
+      // before this tile rescales O_t or overwrites P_t.
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[t], (j - 1) & 1, abort_flag, status,
+                                                                DSV3_ERR_WAIT_TMEM))) {
+        ok = false;
+        break;
+      }
+      if (j == 0) {
+        m_used = m_new;
+      } else if (__any_sync(0xffffffffu, m_new > m_used + 8.0f)) {
+        tc_fence_after();
+        const float corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_new);
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < DV / 16; ++d) {
+          uint32_t r[16];
+          tmem_ld16(tO + d * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+          tmem_st16(tO + d * 16, r);
+        }
+        tmem_st_wait();
+        m_used = m_new;
+      }
+      const float msub = m_used == -INFINITY ? 0.f : m_used;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2_approx(s[c * 8 + 2 * e] - msub);
+          const float p1 = ex2_approx(s[c * 8 + 2 * e + 1] - msub);
+          rs4[e] += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        const int blk = c >> 3, cc = c & 7;
+        *reinterpret_cast<uint4*>(prow + blk * 16384 + ((cc ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && n_blocks > 0 &&
+        __all_sync(0xffffffffu, mbar_wait_bounded(&pv_done[t], (n_blocks - 1) & 1, abort_flag, status,
+                                                  DSV3_ERR_WAIT_TMEM))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int b = bh / H, h = bh % H;
+      __nv_bfloat16* orow = O + (((size_t)b * Sq + qrow) * H + h) * DV;
+#pragma unroll
+      for (int d = 0; d < DV / 16; ++d) {
+        uint32_t r[16];
+        tmem_ld16(tO + d * 16, r);
+        tmem_ld_wait();
+        if (qrow < Sq) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) pk[e] = pack_bf16x2(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+          reinterpret_cast<uint4*>(orow + d * 16)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4*>(orow + d * 16)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+      }
+      if (qrow < Sq) L[(size_t)bh * Sq + qrow] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------
 // Flash-attention backward on tcgen05.  One CTA per (128-key tile, b*h); it
 // walks the query tiles that can see its keys (causal) and keeps dK / dV for
 // its keys in TMEM:

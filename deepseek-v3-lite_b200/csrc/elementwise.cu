@@ -271,20 +271,26 @@ __global__ void ce_rows_kernel(const float* __restrict__ pmax, const float* __re
 // Deterministic per-segment mean of the row losses (rows [seg_start[i],
 // seg_start[i+1]) with targets != -100).  Writes loss[i] = mean and the
 // backward row scale  weight[i] * grad_scale / count_i  (0 for ignored rows).
-__global__ void ce_reduce_kernel(const float* __restrict__ loss_rows, const long* __restrict__ tgt,
-                                 const int* __restrict__ seg_start, const float* __restrict__ seg_weight, int nseg,
-                                 float grad_scale, float* __restrict__ loss_out, float* __restrict__ row_scale) {
-  __shared__ float ssum[32];
-  __shared__ float scnt[32];
+// Segment means of the row losses (main, MTP depths) in two grid-wide
+// passes: ce_seg_sum_kernel adds every row block's per-segment (sum, count)
+// into acc[nseg][2]; ce_seg_scale_kernel writes each row's gradient scale
+// (segment weight * grad_scale / count for rows with a target) and block 0
+// the segment losses.
+__global__ void ce_seg_sum_kernel(const float* __restrict__ loss_rows, const long* __restrict__ tgt,
+                                  const int* __restrict__ seg_start, int nseg, int rows,
+                                  float* __restrict__ acc) {
+  __shared__ float ssum[32], scnt[32];
+  const int r0 = blockIdx.x * blockDim.x * 4;
+  const int r1 = min(rows, r0 + (int)blockDim.x * 4);
   for (int sgi = 0; sgi < nseg; ++sgi) {
-    const int a = seg_start[sgi], b = seg_start[sgi + 1];
+    const int a = max(seg_start[sgi], r0), b = min(seg_start[sgi + 1], r1);
+    if (a >= b) continue;                       // uniform across the block
     float sum = 0.f, cnt = 0.f;
-    for (int r = a + threadIdx.x; r < b; r += blockDim.x) {
+    for (int r = a + threadIdx.x; r < b; r += blockDim.x)
       if (tgt[r] >= 0) {
         sum += loss_rows[r];
         cnt += 1.f;
       }
-    }
     sum = warp_sum(sum);
     cnt = warp_sum(cnt);
     if ((threadIdx.x & 31) == 0) {
@@ -298,15 +304,27 @@ __global__ void ce_reduce_kernel(const float* __restrict__ loss_rows, const long
       s2 = warp_sum(s2);
       c2 = warp_sum(c2);
       if (threadIdx.x == 0) {
-        loss_out[sgi] = c2 > 0 ? s2 / c2 : 0.f;
-        scnt[0] = c2;
+        atomicAdd(&acc[2 * sgi], s2);
+        atomicAdd(&acc[2 * sgi + 1], c2);
       }
     }
     __syncthreads();
-    const float c = scnt[0];
-    const float sc = c > 0 ? seg_weight[sgi] * grad_scale / c : 0.f;
-    for (int r = a + threadIdx.x; r < b; r += blockDim.x) row_scale[r] = tgt[r] >= 0 ? sc : 0.f;
-    __syncthreads();
+  }
+}
+
+__global__ void ce_seg_scale_kernel(const long* __restrict__ tgt, const int* __restrict__ seg_start,
+                                    const float* __restrict__ seg_weight, int nseg, int rows, float grad_scale,
+                                    const float* __restrict__ acc, float* __restrict__ loss_out,
+                                    float* __restrict__ row_scale) {
+  if (blockIdx.x == 0 && threadIdx.x < nseg) {
+    const float c = acc[2 * threadIdx.x + 1];
+    loss_out[threadIdx.x] = c > 0.f ? acc[2 * threadIdx.x] / c : 0.f;
+  }
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    int sgi = 0;
+    while (sgi + 1 < nseg && r >= seg_start[sgi + 1]) ++sgi;
+    const float c = acc[2 * sgi + 1];
+    row_scale[r] = (tgt[r] >= 0 && c > 0.f) ? seg_weight[sgi] * grad_scale / c : 0.f;
   }
 }
 
@@ -760,9 +778,15 @@ void ce_rows(const at::Tensor& pmax, const at::Tensor& psum, const at::Tensor& t
 void ce_reduce(const at::Tensor& loss_rows, const at::Tensor& tgt, const at::Tensor& seg_start,
                const at::Tensor& seg_weight, double grad_scale, at::Tensor& loss_out, at::Tensor& row_scale) {
   const at::cuda::CUDAGuard guard(loss_rows.device());
-  ce_reduce_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(loss_rows.data_ptr<float>(),
-      tgt.data_ptr<int64_t>(), seg_start.data_ptr<int>(), seg_weight.data_ptr<float>(), seg_start.numel() - 1,
-      (float)grad_scale, loss_out.data_ptr<float>(), row_scale.data_ptr<float>());
+  const int nseg = seg_start.numel() - 1, rows = loss_rows.numel();
+  auto st = at::cuda::getCurrentCUDAStream();
+  at::Tensor acc = at::zeros({2 * nseg}, loss_rows.options());
+  ce_seg_sum_kernel<<<std::max(1, (rows + 1023) / 1024), 256, 0, st>>>(loss_rows.data_ptr<float>(),
+      tgt.data_ptr<int64_t>(), seg_start.data_ptr<int>(), nseg, rows, acc.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  ce_seg_scale_kernel<<<std::max(1, std::min(1024, (rows + 255) / 256)), 256, 0, st>>>(tgt.data_ptr<int64_t>(),
+      seg_start.data_ptr<int>(), seg_weight.data_ptr<float>(), nseg, rows, (float)grad_scale, acc.data_ptr<float>(),
+      loss_out.data_ptr<float>(), row_scale.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

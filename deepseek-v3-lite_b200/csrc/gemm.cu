@@ -84,11 +84,13 @@ template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW, int CG>
 void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
   using C = GemmCfg<BN, CG>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW, CG>;
+  constexpr int kSmem = C::SMEM_BYTES + epi_smem_bytes<E>();
+  static_assert(kSmem <= 232448, "GEMM shared memory budget");
   static int max_units = 0;   // resident CTAs (CG = 1) or clusters (CG = 2)
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.dynamicSmemBytes = kSmem;
   cfg.stream = at::cuda::getCurrentCUDAStream();
   if constexpr (CG == 2) {
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -99,7 +101,7 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
     cfg.numAttrs = 1;
   }
   if (max_units == 0) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
     if constexpr (CG == 2) {
       cfg.gridDim = dim3(2 * (num_sms() / 2));
       int clusters = 0;

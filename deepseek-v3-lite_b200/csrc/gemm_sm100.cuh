@@ -44,6 +44,12 @@ enum class Epi : int {
 
 constexpr int kEpiWarps = 8;                 // two warpgroups drain TMEM
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+// ScatterBF16 stages each warp's 32 rows x 64 columns (bf16) in shared memory
+// so its stores to other ranks go out as 128-byte row segments
+constexpr int kScatterStageBytes = kEpiWarps * 32 * 128;
+
+template <Epi E>
+constexpr int epi_smem_bytes() { return E == Epi::ScatterBF16 ? kScatterStageBytes : 0; }
 
 struct GemmArgs {
   int M;                 // valid output rows (per group for GroupedK)
@@ -163,6 +169,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint4* scatter_stage = reinterpret_cast<uint4*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -361,6 +368,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if constexpr (S == Sched::GroupedK)
           base += (size_t)ti.g * args.out_group_stride * (E == Epi::StoreBF16 ? 2 : 4);
         static_assert(HALF % 32 == 0, "epilogue drains 32 columns per TMEM wait");
+        // ScatterBF16 with N a multiple of 64: this warp's rows are staged 64
+        // columns at a time and stored to the home ranks as 128-byte row
+        // segments (a warp instruction covers 8 rows x 64 bytes, two
+        // instructions a row's 128 bytes) instead of 16-byte pieces per row.
+        uint4* stage = scatter_stage + (warp - 2) * 256;   // [32 rows][8 x 16 B]
+        const bool staged = E == Epi::ScatterBF16 && (args.N % 64) == 0;
 #pragma unroll 1
         for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
           uint32_t rr[2][16];   // two TMEM loads in flight per wait
@@ -390,7 +403,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               reinterpret_cast<uint4*>(o)[0] = v0;
               reinterpret_cast<uint4*>(o)[1] = v1;
               if constexpr (E == Epi::ScatterBF16) {
-                if (remote != nullptr) {
+                if (staged) {
+                  const int slot = ((c2 & 63) >> 3) + 2 * q;          // 16-byte unit of the row's 64 columns
+                  stage[lane * 8 + slot] = v0;
+                  stage[lane * 8 + slot + 1] = v1;
+                } else if (remote != nullptr) {
                   reinterpret_cast<uint4*>(remote + col)[0] = v0;
                   reinterpret_cast<uint4*>(remote + col)[1] = v1;
                 }
@@ -444,6 +461,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (col + j < args.N) atomicAdd(o + j, __uint_as_float(r[j]));
             }
           }
+          }
+          if constexpr (E == Epi::ScatterBF16) {
+            // after every second 32-column step: 64 staged columns of 32 rows
+            // go out, lanes 4i..4i+3 covering one row's 64 bytes per instruction
+            const int cbase = ti.n0 + (c2 & ~63);
+            if (staged && (c2 & 63) == 32 && cbase < args.N) {
+              __syncwarp();
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int u = i * 32 + lane, rr = u >> 3, qq = u & 7;
+                const unsigned long long rp =
+                    __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(remote), rr);
+                if (rp != 0ull) reinterpret_cast<uint4*>(rp)[(cbase >> 3) + qq] = stage[u];
+              }
+              __syncwarp();
+            }
           }
         }
       } else if constexpr (E == Epi::SwigluFwd) {

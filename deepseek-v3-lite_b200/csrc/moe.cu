@@ -25,75 +25,87 @@ namespace {
 constexpr int kMaxExpertsPerLane = 8;  // E <= 256
 constexpr int kGroupRows = 256;        // expert row ranges: multiples of one CTA-pair GEMM tile
 
-__global__ void router_topk_kernel(const float* __restrict__ logits, long ldl, const float* __restrict__ bias, int T,
-                                   int E, int k, float route_scale, int* __restrict__ idx, float* __restrict__ w,
-                                   float* __restrict__ s_sel, int* __restrict__ counts) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+// Sigmoid + bias top-k routing, one warp per token (TPW tokens per warp in
+// turn).  NL experts per lane (E <= 32 * NL) keeps the arg-max loops fully
+// unrolled over live registers only.  Per-expert counts are histogrammed in
+// shared memory and added to the global counts once per CTA.
+template <int NL>
+__global__ void __launch_bounds__(256) router_topk_kernel(const float* __restrict__ logits, long ldl,
+                                                          const float* __restrict__ bias, int T, int E, int k,
+                                                          float route_scale, int* __restrict__ idx,
+                                                          float* __restrict__ w, float* __restrict__ s_sel,
+                                                          int* __restrict__ counts, int tpw) {
+  __shared__ int hist[32 * NL];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  float sc[kMaxExpertsPerLane], bsc[kMaxExpertsPerLane];
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  float bias_l[NL];
 #pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    const int e = lane + 32 * i;
-    if (e < E) {
-      const float s = 1.0f / (1.0f + __expf(-logits[(size_t)t * ldl + e]));
-      sc[i] = s;
-      bsc[i] = s + bias[e];
-    } else {
-      sc[i] = 0.f;
-      bsc[i] = -INFINITY;
-    }
-  }
-  float chosen_s[8];
-  int chosen_e[8];
-  float total = 0.f;
-  for (int j = 0; j < k; ++j) {
-    // warp arg-max over the biased scores; ties go to the lower expert id
-    float bv = -INFINITY;
-    int be = 0x7fffffff;
+  for (int i = 0; i < NL; ++i) bias_l[i] = lane + 32 * i < E ? bias[lane + 32 * i] : 0.f;
+  for (int tt = 0; tt < tpw; ++tt) {
+    const int t = warp_global * tpw + tt;
+    if (t >= T) break;
+    float sc[NL], bsc[NL];
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    for (int i = 0; i < NL; ++i) {
       const int e = lane + 32 * i;
-      if (e < E && (bsc[i] > bv || (bsc[i] == bv && e < be))) {
-        bv = bsc[i];
-        be = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i)
-      if (lane + 32 * i == be) {
-        s = sc[i];
+      if (e < E) {
+        const float s = 1.0f / (1.0f + __expf(-logits[(size_t)t * ldl + e]));
+        sc[i] = s;
+        bsc[i] = s + bias_l[i];
+      } else {
+        sc[i] = 0.f;
         bsc[i] = -INFINITY;
       }
-    s = __shfl_sync(0xffffffffu, s, be & 31);
-    chosen_s[j] = s;
-    chosen_e[j] = be;
-    total += s;
-  }
-  if (lane < k) {
-    float s = 0.f;
-    int e = 0;
+    }
+    float total = 0.f, my_s = 0.f;
+    int my_e = 0;
+    for (int j = 0; j < k; ++j) {
+      // warp arg-max over the biased scores; ties go to the lower expert id
+      float bv = -INFINITY;
+      int be = 0x7fffffff;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j == lane) {
-        s = chosen_s[j];
-        e = chosen_e[j];
+      for (int i = 0; i < NL; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && (bsc[i] > bv || (bsc[i] == bv && e < be))) {
+          bv = bsc[i];
+          be = e;
+        }
       }
-    idx[(size_t)t * k + lane] = e;
-    s_sel[(size_t)t * k + lane] = s;
-    w[(size_t)t * k + lane] = s / fmaxf(total, 1e-10f) * route_scale;
-    atomicAdd(&counts[e], 1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+        if (ov > bv || (ov == bv && oe < be)) {
+          bv = ov;
+          be = oe;
+        }
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < NL; ++i)
+        if (lane + 32 * i == be) {
+          s = sc[i];
+          bsc[i] = -INFINITY;
+        }
+      s = __shfl_sync(0xffffffffu, s, be & 31);
+      if (lane == j) {
+        my_s = s;
+        my_e = be;
+      }
+      total += s;
+    }
+    if (lane < k) {
+      idx[(size_t)t * k + lane] = my_e;
+      s_sel[(size_t)t * k + lane] = my_s;
+      w[(size_t)t * k + lane] = my_s / fmaxf(total, 1e-10f) * route_scale;
+      atomicAdd(&hist[my_e], 1);
+    }
   }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (hist[e]) atomicAdd(&counts[e], hist[e]);
 }
 
 // Single block.  row_off[e] = sum_{e'<e} pad256(counts[e']); tile_group[i] =
@@ -294,9 +306,18 @@ void router_topk(const at::Tensor& logits, const at::Tensor& bias, int64_t E, in
   const int T = logits.size(0);
   TORCH_CHECK(E <= 32 * kMaxExpertsPerLane && k <= 8 && k <= E, "router_topk: E <= 256, k <= 8");
   const at::cuda::CUDAGuard guard(logits.device());
-  router_topk_kernel<<<nblk(T, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(logits.data_ptr<float>(),
-      logits.stride(0), bias.data_ptr<float>(), T, E, k, (float)route_scale, idx.data_ptr<int>(), w.data_ptr<float>(),
-      s_sel.data_ptr<float>(), counts.data_ptr<int>());
+  constexpr int kTpw = 8;   // tokens per warp: 64 per CTA of 8 warps
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int grid = nblk(T, 8 * kTpw);
+#define DSV3_ROUTER(NL_)                                                                                     \
+  router_topk_kernel<NL_><<<grid, 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0),                \
+      bias.data_ptr<float>(), T, E, k, (float)route_scale, idx.data_ptr<int>(), w.data_ptr<float>(),       \
+      s_sel.data_ptr<float>(), counts.data_ptr<int>(), kTpw)
+  if (E <= 32) DSV3_ROUTER(1);
+  else if (E <= 64) DSV3_ROUTER(2);
+  else if (E <= 128) DSV3_ROUTER(4);
+  else DSV3_ROUTER(8);
+#undef DSV3_ROUTER
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

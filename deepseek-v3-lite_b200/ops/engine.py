@@ -735,7 +735,10 @@ class TrainEngine:
             if timer is not None:
                 timer.take()               # the eager warm-up's marks are not booked
             graph = torch.cuda.CUDAGraph()
-            with _ext.launch_scope() as scope, torch.cuda.graph(graph):
+            # thread-local capture: a CUDA call from another thread (the data
+            # loader's pin-memory thread allocating pinned buffers) must not
+            # invalidate this capture
+            with _ext.launch_scope() as scope, torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 out = self._forward_backward(st_tok, st_tgt, loss_scale)
             marks = timer.take() if timer is not None else None
             for f, g in zip(self.flats, saved):

@@ -306,7 +306,10 @@ class InferenceEngine:
                 self.forward(st, pos=sp, want_hidden=True)
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
-            with _ext.launch_scope() as scope, torch.cuda.graph(graph):
+            # thread-local capture: a CUDA call from another thread (the data
+            # loader's pin-memory thread allocating pinned buffers) must not
+            # invalidate this capture
+            with _ext.launch_scope() as scope, torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 out = self.forward(st, pos=sp, want_hidden=True)
             entry = (graph, st, sp, out, scope.count)
             self._graphs[key] = entry
