@@ -55,16 +55,25 @@ class _Timer:
         return out, (time.perf_counter() - t0) * 1e3
 
 
+def _positive(v: str) -> int:
+    n = int(v)
+    if n < 1:
+        raise argparse.ArgumentTypeError("--steps must be at least 1")
+    return n
+
+
 def _measure(trainer, model, vocab, steps, new, device):
     timer = _Timer(device)
     g = torch.Generator().manual_seed(0)
     tok = torch.randint(0, vocab, (4, 129), generator=g).to(device)
     trainer.train_step(tok[:, :-1], tok[:, 1:], 0)                       # warm-up
-    times = []
+    times, last = [], None
     for i in range(steps):
         out, ms = timer(lambda: trainer.train_step(tok[:, :-1], tok[:, 1:], i + 1))
         times.append(ms)
-    loss = float(out["loss"])
+        if out is not None:          # None: the NaN guard skipped this micro-batch
+            last = out
+    loss = float(last["loss"]) if last is not None else None
     step_ms = statistics.median(times)
     prompt = torch.randint(0, vocab, (1, 16), generator=g).to(device)
     model.eval()
@@ -73,7 +82,7 @@ def _measure(trainer, model, vocab, steps, new, device):
         gen, dec_ms = timer(lambda: model.generate(prompt, max_new_tokens=new, temperature=0.0))
     produced = int(gen.shape[1] - prompt.shape[1])
     return {"step_ms": round(step_ms, 3), "train_tokens_per_s": round(4 * 128 / (step_ms / 1e3), 1),
-            "last_loss": round(loss, 4), "decode_ms": round(dec_ms, 3), "decode_tokens": produced,
+            "last_loss": round(loss, 4) if loss is not None else None, "decode_ms": round(dec_ms, 3), "decode_tokens": produced,
             "decode_tokens_per_s": round(produced / (dec_ms / 1e3), 1)}
 
 
@@ -112,7 +121,7 @@ def run_reference(steps, new, device):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=_positive, default=5)
     ap.add_argument("--new", type=int, default=16)
     a = ap.parse_args(argv)
     device = torch.device("cuda" if torch.cuda.is_available() else "cpu")
