@@ -120,7 +120,7 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
 
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
-  if constexpr (BN == 256) {
+  if constexpr (BN == 256 || (BN == 128 && B_MN)) {
     // row-grouped tiles may pair only when every expert range is 256-aligned
     const bool grouping_ok = S != Sched::GroupedM || a.tile_rows == 256;
     if (use_pairs() && grouping_ok && a.m_tiles > 0 && a.M >= 256) {
@@ -286,16 +286,21 @@ void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& 
   g.M = P; g.N = I; g.K = D; g.inter = I;
   g.out = dgu.data_ptr(); g.ldo = dgu.stride(0);
   g.aux = gu.data_ptr(); g.ld_aux = gu.stride(0);
-  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(I, 256); g.kb_per_split = cdiv(D, 64);
+  // I a multiple of 128 but not of 256 (the 412M experts' 384): 128-wide
+  // column tiles (still CTA pairs) leave no half-empty tile
+  const int bn = (I % 256 != 0 && I % 128 == 0) ? 128 : 256;
+  g.m_tiles = cdiv(P, 128); g.n_tiles = cdiv(I, bn); g.kb_per_split = cdiv(D, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(dy, P, D, dy.stride(0));
   CUtensorMap tb = map_b_mnmajor(w2, G, D, I, I, D * I);
   if (tile_group.numel() > 0) {
     g.tile_group = tile_group.data_ptr<int>();
     g.tile_rows = (int)group_rows;
-    launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+    if (bn == 128) launch<128, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+    else launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
   } else {
-    launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+    if (bn == 128) launch<128, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+    else launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
   }
 }
 

@@ -154,7 +154,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using C = GemmCfg<BN, CG>;
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
-  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs: BN=256");
+  // CTA pairs: BN 256, or BN 128 with an MN-major B (each CTA then loads one
+  // 64-column box of B)
+  static_assert(CG == 1 || (CG == 2 && (BN == 256 || (BN == 128 && B_MN))), "CTA pairs: BN=256, or BN=128 with MN-major B");
   constexpr int BMT = 128 * CG;                   // rows of one (pair) tile
   const uint32_t cta = CG == 2 ? cluster_ctarank() : 0u;
   const bool leader = cta == 0;
@@ -236,8 +238,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if constexpr (B_SWIGLU) {
               tma_load_4d_pair(sB, &tmB, fb, k0, ti.n0, (int)cta, bg);   // CTA 0: gate rows, CTA 1: up rows
             } else if constexpr (B_MN) {
-              tma_load_3d_pair(sB, &tmB, fb, ti.n0 + (int)cta * 128, k0, bg);
-              tma_load_3d_pair(sB + 8192, &tmB, fb, ti.n0 + (int)cta * 128 + 64, k0, bg);
+              tma_load_3d_pair(sB, &tmB, fb, ti.n0 + (int)cta * (BN / 2), k0, bg);
+              if constexpr (BN / 2 > 64) tma_load_3d_pair(sB + 8192, &tmB, fb, ti.n0 + (int)cta * (BN / 2) + 64, k0, bg);
             } else {
               tma_load_3d_pair(sB, &tmB, fb, k0, ti.n0 + (int)cta * 128, bg);
             }
