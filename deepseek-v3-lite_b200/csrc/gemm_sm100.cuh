@@ -42,6 +42,7 @@ enum class Epi : int {
                      // combine inbox over peer memory (expert-parallel combine)
 };
 
+constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
 constexpr int kEpiWarps = 8;                 // two warpgroups drain TMEM
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 // ScatterBF16 stages each warp's 32 rows x 64 columns (bf16) in shared memory
@@ -618,16 +619,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int q = 0; q < 2; ++q) {
           const uint32_t (&r)[16] = rr[q];
           const int col = ti.n0 + c2 + 16 * q;
+          // exp(x - m) = 2^(x log2(e) - m log2(e)): one FFMA and one ex2 per
+          // element; column bounds are only checked in the vocabulary's last tile
+          const bool full = col + 16 <= args.N;
           float cmax = -INFINITY;
+          if (full) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (col + j < args.N) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+            for (int j = 0; j < 16; ++j) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < args.N) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+          }
           if (cmax == -INFINITY) continue;
           const float nm = fmaxf(run_max, cmax);
-          float s = run_sum * __expf(run_max - nm);
+          const float nml = nm * kLog2e;
+          float s = run_sum * ex2_approx((run_max - nm) * kLog2e);
+          if (full) {
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (col + j < args.N) s += __expf(__uint_as_float(r[j]) - nm);
+            for (int j = 0; j < 16; ++j) s4[j & 3] += ex2_approx(fmaf(__uint_as_float(r[j]), kLog2e, -nml));
+            s += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < args.N) s += ex2_approx(fmaf(__uint_as_float(r[j]), kLog2e, -nml));
+          }
           run_sum = s;
           run_max = nm;
           if (tgt >= col && tgt < col + 16 && tgt < args.N) {
@@ -645,6 +662,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const long tgt = row_ok ? args.targets[row] : -1;
         const float l = row_ok ? args.lse[row] : 0.0f;
         const float sc = row_ok ? args.row_scale[row] : 0.0f;
+        const float ll = l * kLog2e;
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo;
 #pragma unroll 1
         for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
@@ -658,13 +676,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t (&r)[16] = rr[q];
           const int col = ti.n0 + c2 + 16 * q;
           if (!row_ok || col >= args.N) continue;
+          // softmax row (2^(x log2(e) - lse log2(e))) times the row scale; the
+          // target column's "- 1" is applied to the one chunk that holds it
+          float pv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pv[j] = ex2_approx(fmaf(__uint_as_float(r[j]), kLog2e, -ll)) * sc;
+          if (tgt >= col && tgt < col + 16) {
+            const int tj = (int)(tgt - col);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (j == tj) pv[j] -= sc;
+          }
           uint32_t pk[8];
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const float p0 = (__expf(__uint_as_float(r[j]) - l) - (col + j == tgt ? 1.0f : 0.0f)) * sc;
-            const float p1 = (__expf(__uint_as_float(r[j + 1]) - l) - (col + j + 1 == tgt ? 1.0f : 0.0f)) * sc;
-            pk[j / 2] = pack_bf16x2(p0, p1);
-          }
+          for (int j = 0; j < 16; j += 2) pk[j / 2] = pack_bf16x2(pv[j], pv[j + 1]);
           if (col + 16 <= args.N) {
             reinterpret_cast<uint4*>(o + col)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             reinterpret_cast<uint4*>(o + col)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
 // expert owning 128-row tile i (or -1); cursor zeroed; src[0..P) = -1.
 __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* __restrict__ row_off,
                                     int* __restrict__ tile_group, int max_tiles, int* __restrict__ cursor,
-                                    int* __restrict__ src, int P) {
+                                    int* __restrict__ src, int P, int src_tail_only) {
   extern __shared__ int off_s[];  // E + 1
   if (threadIdx.x == 0) {
     int acc = 0;
@@ -139,7 +139,55 @@ __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* 
     }
     tile_group[i] = g;
   }
-  for (int i = threadIdx.x; i < P; i += blockDim.x) src[i] = -1;
+  // src = -1 everywhere, or (permute_gather writes the expert ranges) only
+  // past the last expert's range
+  for (int i = (src_tail_only ? off_s[E] : 0) + threadIdx.x; i < P; i += blockDim.x) src[i] = -1;
+}
+
+// Permutation fused with the gather: one warp per (token, slot) takes the
+// next row of its expert's range, records src / dst, and copies the token's
+// activation row there; the warps past the T * k assignments zero the
+// padding rows of each expert's 256-row range (src = -1).  Replaces
+// permute_scatter + gather_rows (and permute_plan's src initialisation).
+__global__ void __launch_bounds__(256) permute_gather_kernel(const int* __restrict__ idx, int n_assign, int k,
+                                                             const int* __restrict__ counts,
+                                                             const int* __restrict__ row_off, int* cursor,
+                                                             const __nv_bfloat16* __restrict__ x, long ldx, int D,
+                                                             int* __restrict__ src, int* __restrict__ dst,
+                                                             __nv_bfloat16* __restrict__ out, long ldo, int E, int P,
+                                                             unsigned int* status) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int D8 = D / 8;
+  if (w < n_assign) {
+    int pos = 0;
+    if (lane == 0) {
+      const int e = idx[w];
+      pos = -1;
+      if (e >= 0 && e < E) pos = row_off[e] + atomicAdd(&cursor[e], 1);
+      if (pos < 0 || pos >= P) {
+        record_error(status, DSV3_ERR_BOUNDS);
+        pos = -1;
+      } else {
+        src[pos] = w;
+        dst[w] = pos;
+      }
+    }
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    if (pos < 0) return;
+    const uint4* sr = reinterpret_cast<const uint4*>(x + (size_t)(w / k) * ldx);
+    uint4* o = reinterpret_cast<uint4*>(out + (size_t)pos * ldo);
+    for (int c = lane; c < D8; c += 32) o[c] = sr[c];
+    return;
+  }
+  const int p = w - n_assign;                 // padding slot: expert p / 256, row p % 256 past its count
+  if (p >= E * 256) return;
+  const int e = p >> 8, j = p & 255;
+  const int r = row_off[e] + counts[e] + j;
+  if (r >= row_off[e + 1] || r >= P) return;
+  uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * ldo);
+  for (int c = lane; c < D8; c += 32) o[c] = make_uint4(0, 0, 0, 0);
+  if (lane == 0) src[r] = -1;
 }
 
 __global__ void permute_scatter_kernel(const int* __restrict__ idx, int n_assign, const int* __restrict__ row_off,
@@ -322,12 +370,12 @@ void router_topk(const at::Tensor& logits, const at::Tensor& bias, int64_t E, in
 }
 
 void permute_plan(const at::Tensor& counts, at::Tensor& row_off, at::Tensor& tile_group, at::Tensor& cursor,
-                  at::Tensor& src) {
+                  at::Tensor& src, bool src_tail_only) {
   const int E = counts.numel();
   const at::cuda::CUDAGuard guard(counts.device());
   permute_plan_kernel<<<1, 1024, (E + 1) * sizeof(int), at::cuda::getCurrentCUDAStream()>>>(counts.data_ptr<int>(),
       E, row_off.data_ptr<int>(), tile_group.data_ptr<int>(), tile_group.numel(), cursor.data_ptr<int>(),
-      src.data_ptr<int>(), src.numel());
+      src.data_ptr<int>(), src.numel(), src_tail_only ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -338,6 +386,21 @@ void permute_scatter(const at::Tensor& idx, const at::Tensor& row_off, at::Tenso
   permute_scatter_kernel<<<nblk(n, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(idx.data_ptr<int>(), n,
       row_off.data_ptr<int>(), cursor.data_ptr<int>(), src.data_ptr<int>(), dst.data_ptr<int>(),
       (int)cursor.numel(), (int)src.numel(), status_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void permute_gather(const at::Tensor& idx, const at::Tensor& counts, const at::Tensor& row_off, at::Tensor& cursor,
+                    const at::Tensor& x, at::Tensor& src, at::Tensor& dst, at::Tensor& out) {
+  const int n = idx.numel(), E = counts.numel(), P = out.size(0), D = x.size(1);
+  const int k = n / std::max<int64_t>(1, x.size(0));
+  TORCH_CHECK(n == x.size(0) * k && dst.numel() == n && src.numel() >= P, "permute_gather: idx [T, k], src [P]");
+  TORCH_CHECK(D % 8 == 0 && x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0 && out.size(1) == D,
+              "permute_gather: 16-byte rows");
+  const at::cuda::CUDAGuard guard(x.device());
+  const long warps = (long)n + (long)E * 256;
+  permute_gather_kernel<<<nblk(warps, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(idx.data_ptr<int>(), n, k,
+      counts.data_ptr<int>(), row_off.data_ptr<int>(), cursor.data_ptr<int>(), cbf(x), x.stride(0), D,
+      src.data_ptr<int>(), dst.data_ptr<int>(), bf(out), out.stride(0), E, P, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -388,8 +451,12 @@ void router_bwd(const at::Tensor& dw, const at::Tensor& s_sel, const at::Tensor&
 
 void register_moe(pybind11::module_& m) {
   m.def("router_topk", &router_topk, "sigmoid + bias top-k routing with per-expert counts");
-  m.def("permute_plan", &permute_plan, "128-row padded expert ranges and the tile->expert map");
+  m.def("permute_plan", &permute_plan, "256-row padded expert ranges and the tile->expert map",
+        pybind11::arg("counts"), pybind11::arg("row_off"), pybind11::arg("tile_group"), pybind11::arg("cursor"),
+        pybind11::arg("src"), pybind11::arg("src_tail_only") = false);
   m.def("permute_scatter", &permute_scatter, "destination row of each (token, slot)");
+  m.def("permute_gather", &permute_gather,
+        "expert-sorted slots of every (token, slot) fused with the copy of its row; padding rows zeroed");
   m.def("gather_rows", &gather_rows, "expert-sorted activation rows (padding rows zeroed)");
   m.def("combine_fwd", &combine_fwd, "weighted sum of expert outputs into the fp32 residual");
   m.def("combine_bwd", &combine_bwd, "gradients of the weighted combine");

@@ -544,10 +544,9 @@ class TrainEngine:
         cursor = torch.empty(E, dtype=torch.int32, device=self.device)
         src = torch.empty(P, dtype=torch.int32, device=self.device)
         dst = torch.empty(T, k, dtype=torch.int32, device=self.device)
-        C.permute_plan(counts, row_off, tile_group, cursor, src)
-        C.permute_scatter(idx, row_off, cursor, src, dst)
+        C.permute_plan(counts, row_off, tile_group, cursor, src, src_tail_only=True)
         xs = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.gather_rows(xn, src, k, xs)
+        C.permute_gather(idx, counts, row_off, cursor, xn, src, dst, xs)   # expert-sorted rows in one pass
         self._mark("moe permute fwd")
         w1 = moe.experts[0].w1.weight
         h = torch.empty(P, I, dtype=BF16, device=self.device)

@@ -174,10 +174,9 @@ class InferenceEngine:
         cursor = torch.empty(E, dtype=torch.int32, device=self.device)
         src = torch.empty(P, dtype=torch.int32, device=self.device)
         dst = torch.empty(T, k, dtype=torch.int32, device=self.device)
-        C.permute_plan(counts, row_off, tg, cursor, src)
-        C.permute_scatter(idx, row_off, cursor, src, dst)
+        C.permute_plan(counts, row_off, tg, cursor, src, src_tail_only=True)
         xs = torch.empty(P, self.D, dtype=BF16, device=self.device)
-        C.gather_rows(xn, src, k, xs)
+        C.permute_gather(idx, counts, row_off, cursor, xn, src, dst, xs)
         w13, w2 = self._experts(moe)
         h = torch.empty(P, I, dtype=BF16, device=self.device)
         gu = torch.empty(P, 2 * I, dtype=BF16, device=self.device)
