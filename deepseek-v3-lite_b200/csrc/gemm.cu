@@ -80,9 +80,10 @@ bool use_pairs() {
   return g_pairs == 1;
 }
 
+// tc: the output's tensor map for the TMA-store epilogues (unused otherwise)
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW, int CG>
-void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
-  using C = GemmCfg<BN, CG>;
+void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr) {
+  using C = GemmCfg<BN, CG, E>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW, CG>;
   constexpr int kSmem = C::SMEM_BYTES + epi_smem_bytes<E>();
   static_assert(kSmem <= 232448, "GEMM shared memory budget");
@@ -115,11 +116,14 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
   a.status = status_ptr();
   const int units = std::min(a.num_tiles, max_units);
   cfg.gridDim = dim3(units * CG);
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+  CUtensorMap none;
+  memset(&none, 0, sizeof(none));
+  TORCH_CHECK(tc != nullptr || E != Epi::CeBwdTma, "TMA-store epilogue without an output map");
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc != nullptr ? *tc : none, a));
 }
 
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr) {
   if constexpr (BN == 256 || (BN == 128 && B_MN)) {
     // row-grouped tiles may pair only when every expert range is 256-aligned
     const bool grouping_ok = S != Sched::GroupedM || a.tile_rows == 256;
@@ -127,11 +131,35 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a) {
       GemmArgs b = a;                      // re-tile the rows in 256-row pair tiles
       b.m_tiles = cdiv(a.M, 256);
       b.num_tiles = a.num_tiles / a.m_tiles * b.m_tiles;
-      launch_cg<BN, A_MN, B_MN, S, E, SW, 2>(ta, tb, b);
+      launch_cg<BN, A_MN, B_MN, S, E, SW, 2>(ta, tb, b, tc);
       return;
     }
   }
-  launch_cg<BN, A_MN, B_MN, S, E, SW, 1>(ta, tb, a);
+  launch_cg<BN, A_MN, B_MN, S, E, SW, 1>(ta, tb, a, tc);
+}
+
+// LM-head tiles walk 16,384-row panels, rows fastest: the panel's hidden rows
+// (25 MB at D 768) stay in L2 while the vocabulary weight (154 MB at V 100K,
+// more than the 126 MB L2) streams through once per panel instead of once
+// per 256-row tile.  DSV3_CE_PANEL_ROWS overrides (0: columns fastest).
+int ce_panel_rows() {
+  static int rows = -1;
+  if (rows < 0) {
+    const char* e = getenv("DSV3_CE_PANEL_ROWS");
+    rows = e != nullptr ? std::max(0, atoi(e)) : 16384;
+  }
+  return rows;
+}
+
+// CE-gradient epilogue: bf16 dlogits staged in shared memory and written by
+// TMA stores (default) or stored row by row from registers (DSV3_CE_TMA_STORE=0).
+bool ce_tma_store() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("DSV3_CE_TMA_STORE");
+    on = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 GemmArgs blank_args() {
@@ -451,6 +479,7 @@ void ce_fwd_partials(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   g.part_sum = part_sum.data_ptr<float>();
   g.tgt_logit = tgt_logit.data_ptr<float>();
   g.m_tiles = cdiv(T, 128); g.n_tiles = nt; g.kb_per_split = cdiv(D, 64);
+  g.panel_rows = ce_panel_rows();
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(x, T, D, x.stride(0));
   CUtensorMap tb = map_b_kmajor(w, 1, V, D, w.stride(0), V * w.stride(0));
@@ -458,6 +487,8 @@ void ce_fwd_partials(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
 }
 
 // Backward half: dlogits[T, :V] = (softmax(x w^T) - onehot(target)) * row_scale.
+// When dlogits has at least V rounded up to 8 columns, its columns V .. that
+// bound are set to zero as well (the TMA-store epilogue writes 16-byte units).
 void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& targets, const at::Tensor& lse,
                    const at::Tensor& row_scale, at::Tensor& dlogits) {
   check_bf16_rows(x, "x");
@@ -474,10 +505,21 @@ void ce_bwd_logits(const at::Tensor& x, const at::Tensor& w, const at::Tensor& t
   g.row_scale = row_scale.data_ptr<float>();
   g.out = dlogits.data_ptr(); g.ldo = dlogits.stride(0);
   g.m_tiles = cdiv(T, 128); g.n_tiles = cdiv(V, 256); g.kb_per_split = cdiv(D, 64);
+  g.panel_rows = ce_panel_rows();
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(x, T, D, x.stride(0));
   CUtensorMap tb = map_b_kmajor(w, 1, V, D, w.stride(0), V * w.stride(0));
-  launch<256, 0, 0, Sched::Dense, Epi::CeBwd, false>(ta, tb, g);
+  if (ce_tma_store() && dlogits.size(1) >= (V + 7) / 8 * 8) {
+    // dlogits written in 32-row x 64-column boxes; the store clips rows >= T
+    // and columns past V rounded up to 8 (columns V .. that bound get zeros)
+    uint64_t dims[2] = {(uint64_t)V, (uint64_t)T};
+    uint64_t st[1] = {(uint64_t)dlogits.stride(0) * 2};
+    uint32_t box[2] = {64, 32};
+    CUtensorMap tc = make_map(dlogits.data_ptr(), 2, dims, st, box);
+    launch<256, 0, 0, Sched::Dense, Epi::CeBwdTma, false>(ta, tb, g, &tc);
+  } else {
+    launch<256, 0, 0, Sched::Dense, Epi::CeBwd, false>(ta, tb, g);
+  }
 }
 
 }  // namespace dsv3

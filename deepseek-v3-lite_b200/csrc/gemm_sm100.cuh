@@ -38,8 +38,11 @@ enum class Epi : int {
   CeBwd = 6,         // (softmax - onehot) * scale, bf16
   StoreF32 = 7,      // out (fp32) = acc
   ResidF32 = 8,      // out (fp32) = aux (fp32) + acc   (out-of-place residual add)
-  ScatterBF16 = 9    // out (bf16) = acc, and each row also stored into its home rank's
+  ScatterBF16 = 9,   // out (bf16) = acc, and each row also stored into its home rank's
                      // combine inbox over peer memory (expert-parallel combine)
+  CeBwdTma = 10      // CeBwd, each warp's 32 x 64 output boxes staged in shared memory
+                     // (128-byte swizzle) and written by TMA stores; columns N .. N rounded
+                     // up to 8 receive zeros
 };
 
 constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
@@ -49,8 +52,15 @@ constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
 // so its stores to other ranks go out as 128-byte row segments
 constexpr int kScatterStageBytes = kEpiWarps * 32 * 128;
 
+// CeBwdTma: two 32 x 64 bf16 boxes (4 KB each) per epilogue warp, 1024-byte
+// aligned after the barrier block
+constexpr int kTmaBoxBytes = 32 * 128;
+constexpr int kTmaStageBytes = kEpiWarps * 2 * kTmaBoxBytes;
+
 template <Epi E>
-constexpr int epi_smem_bytes() { return E == Epi::ScatterBF16 ? kScatterStageBytes : 0; }
+constexpr int epi_smem_bytes() {
+  return E == Epi::ScatterBF16 ? kScatterStageBytes : (E == Epi::CeBwdTma ? 1024 + kTmaStageBytes : 0);
+}
 
 struct GemmArgs {
   int M;                 // valid output rows (per group for GroupedK)
@@ -59,6 +69,9 @@ struct GemmArgs {
   int m_tiles, n_tiles, k_splits, groups;
   int num_tiles;
   int kb_per_split;      // Dense: K-blocks per split
+  int panel_rows;        // Dense: > 0 walks the tiles in panels of this many rows, rows fastest
+                         // inside a panel (a B operand larger than L2 is then streamed once per
+                         // panel while the panel's A rows stay in L2); 0: columns fastest
   const int* tile_group;     // GroupedM: expert of each 128-row tile (< 0: unused tile)
   int tile_rows;             // GroupedM: expert ranges are multiples of this (128 or 256; 256 allows CTA pairs)
   const int* group_row_off;  // GroupedK: [groups + 1] padded row offsets (multiples of 128)
@@ -93,14 +106,15 @@ struct GemmArgs {
 // CG = 2: a CTA pair shares one 256-row tile (each CTA: 128 rows of A and
 // BN/2 rows of B in its own shared memory), which halves the B traffic per
 // MMA and leaves room for more pipeline stages.
-template <int BN, int CG = 1>
+template <int BN, int CG = 1, Epi E = Epi::StoreBF16>
 struct GemmCfg {
   static constexpr int BM = 128;            // accumulator rows per CTA
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = CG == 2 ? 6 : (BN >= 256 ? 4 : 6);
+  // the TMA-store staging (64 KB) takes one (pair) or one more (single) stage
+  static constexpr int STAGES = E == Epi::CeBwdTma ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : (BN >= 256 ? 4 : 6));
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
@@ -114,10 +128,23 @@ struct TileInfo {
 template <Sched S>
 __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN_, int BM_ = 128) {
   TileInfo ti;
-  int n = t % a.n_tiles;
-  int rest = t / a.n_tiles;
-  int m = rest % a.m_tiles;
-  int outer = rest / a.m_tiles;
+  int n, m, outer;
+  if (S == Sched::Dense && a.panel_rows > 0) {
+    const int mn = a.m_tiles * a.n_tiles;
+    outer = t / mn;
+    int r = t - outer * mn;
+    const int pt = max(1, a.panel_rows / BM_);           // m-tiles per panel
+    const int p = r / (pt * a.n_tiles);
+    r -= p * pt * a.n_tiles;
+    const int pm = min(pt, a.m_tiles - p * pt);           // the last panel may be shorter
+    n = r / pm;
+    m = p * pt + (r - n * pm);
+  } else {
+    n = t % a.n_tiles;
+    const int rest = t / a.n_tiles;
+    m = rest % a.m_tiles;
+    outer = rest / a.m_tiles;
+  }
   ti.n_tile = n;
   ti.n0 = n * BN_;
   ti.m0 = m * BM_;
@@ -152,8 +179,10 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
 // the gate half with column c of the up half.
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using C = GemmCfg<BN, CG>;
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+  using C = GemmCfg<BN, CG, E>;
+  constexpr bool kTmaOut = E == Epi::CeBwdTma;
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
   // CTA pairs: BN 256, or BN 128 with an MN-major B (each CTA then loads one
   // 64-column box of B)
@@ -173,6 +202,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   uint4* scatter_stage = reinterpret_cast<uint4*>(smem + C::STAGES * C::STAGE_BYTES + C::BAR_BYTES);
+  uint8_t* tma_stage = smem + C::STAGES * C::STAGE_BYTES + 1024;   // CeBwdTma boxes (1024-byte aligned)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -192,6 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (kTmaOut) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     if constexpr (CG == 2) {
@@ -340,6 +371,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r_in_tile = quarter * 32 + lane;
     constexpr int HALF = BN / 2;
     int local = 0;
+    int tma_box = 0;                           // CeBwdTma: boxes this warp has stored (buffer = parity)
+    (void)tma_box;
     for (int t = tile0; t < args.num_tiles && !*abort_flag; t += tstep) {
       TileInfo ti = decode_tile<S>(t, args, B_SWIGLU ? 128 : BN, BMT);
       if (!ti.run) continue;
@@ -658,14 +691,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           args.part_max[(size_t)row * 2 * args.n_tiles + 2 * ti.n_tile + half] = run_max;
           args.part_sum[(size_t)row * 2 * args.n_tiles + 2 * ti.n_tile + half] = run_sum;
         }
-      } else if constexpr (E == Epi::CeBwd) {
+      } else if constexpr (E == Epi::CeBwd || E == Epi::CeBwdTma) {
         const long tgt = row_ok ? args.targets[row] : -1;
         const float l = row_ok ? args.lse[row] : 0.0f;
         const float sc = row_ok ? args.row_scale[row] : 0.0f;
         const float ll = l * kLog2e;
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo;
+        // CeBwdTma: lane = row of this warp's 32-row box; the 16-byte chunk j
+        // of a 64-column box row sits at chunk j ^ (row & 7) (128-byte swizzle)
+        uint8_t* box_row = tma_stage + (warp - 2) * 2 * kTmaBoxBytes + lane * 128;
+        const int box_y = ti.m0 + quarter * 32;
 #pragma unroll 1
-        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+        for (int c4 = half * HALF; c4 < (half + 1) * HALF; c4 += 64) {
+          uint8_t* brow = box_row + (tma_box & 1) * kTmaBoxBytes;
+          if constexpr (kTmaOut) {
+            if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int c2 = c4; c2 < c4 + 64; c2 += 32) {
           uint32_t rr[2][16];
           __syncwarp();
           tmem_ld16(tbase + c2, rr[0]);
@@ -675,7 +719,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int q = 0; q < 2; ++q) {
           const uint32_t (&r)[16] = rr[q];
           const int col = ti.n0 + c2 + 16 * q;
-          if (!row_ok || col >= args.N) continue;
+          // out-of-range rows / columns of a TMA box are clipped by the store
+          if (!kTmaOut && (!row_ok || col >= args.N)) continue;
           // softmax row (2^(x log2(e) - lse log2(e))) times the row scale; the
           // target column's "- 1" is applied to the one chunk that holds it
           float pv[16];
@@ -687,16 +732,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < 16; ++j)
               if (j == tj) pv[j] -= sc;
           }
+          if (kTmaOut && col + 16 > args.N) {
+            // the store clips the box at 16-byte granularity: columns N .. N
+            // rounded up to 8 are written too, as zeros
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j >= args.N) pv[j] = 0.0f;
+          }
           uint32_t pk[8];
 #pragma unroll
           for (int j = 0; j < 16; j += 2) pk[j / 2] = pack_bf16x2(pv[j], pv[j + 1]);
-          if (col + 16 <= args.N) {
+          if constexpr (kTmaOut) {
+            const int ch = ((c2 - c4) + 16 * q) >> 3;   // first of this group's two 16-byte chunks
+            *reinterpret_cast<uint4*>(brow + ((ch ^ (lane & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(brow + (((ch + 1) ^ (lane & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else if (col + 16 <= args.N) {
             reinterpret_cast<uint4*>(o + col)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             reinterpret_cast<uint4*>(o + col)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           } else {
             const uint16_t* ps = reinterpret_cast<const uint16_t*>(pk);
             for (int j = 0; col + j < args.N; ++j) reinterpret_cast<uint16_t*>(o + col)[j] = ps[j];
           }
+          }
+          }
+          if constexpr (kTmaOut) {
+            fence_proxy_async_smem();   // this lane's box row is visible to the TMA engine
+            __syncwarp();
+            if (lane == 0) {
+              if (ti.n0 + c4 < args.N && box_y < args.M)
+                tma_store_2d(&tmC, box_row + (tma_box & 1) * kTmaBoxBytes, ti.n0 + c4, box_y);
+              bulk_commit_group();
+            }
+            ++tma_box;
           }
         }
       }
@@ -707,6 +774,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         else mbar_arrive(&tempty[buf]);
       }
       ++local;
+    }
+    if constexpr (kTmaOut) {
+      if (lane == 0) bulk_wait_group_all();   // this warp's stores are done before the CTA's shared memory goes
     }
   }
 

@@ -144,50 +144,95 @@ __global__ void permute_plan_kernel(const int* __restrict__ counts, int E, int* 
   for (int i = (src_tail_only ? off_s[E] : 0) + threadIdx.x; i < P; i += blockDim.x) src[i] = -1;
 }
 
-// Permutation fused with the gather: one warp per (token, slot) takes the
-// next row of its expert's range, records src / dst, and copies the token's
-// activation row there; the warps past the T * k assignments zero the
-// padding rows of each expert's 256-row range (src = -1).  Replaces
-// permute_scatter + gather_rows (and permute_plan's src initialisation).
-__global__ void __launch_bounds__(256) permute_gather_kernel(const int* __restrict__ idx, int n_assign, int k,
-                                                             const int* __restrict__ counts,
-                                                             const int* __restrict__ row_off, int* cursor,
-                                                             const __nv_bfloat16* __restrict__ x, long ldx, int D,
-                                                             int* __restrict__ src, int* __restrict__ dst,
-                                                             __nv_bfloat16* __restrict__ out, long ldo, int E, int P,
-                                                             unsigned int* status) {
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int D8 = D / 8;
-  if (w < n_assign) {
-    int pos = 0;
-    if (lane == 0) {
-      const int e = idx[w];
-      pos = -1;
-      if (e >= 0 && e < E) pos = row_off[e] + atomicAdd(&cursor[e], 1);
-      if (pos < 0 || pos >= P) {
+// Permutation fused with the gather.  A chunk CTA takes kPgThreads / k
+// consecutive tokens: each (token, slot) counts itself into its expert in
+// shared memory, one thread per expert reserves the chunk's rows of that
+// expert with a single global atomicAdd on the cursor, and each token row is
+// then read once and stored to its k destination rows.  The first E CTAs zero
+// the padding rows [row_off[e] + counts[e], row_off[e + 1]) of expert e and set
+// their src to -1.  Replaces permute_scatter + gather_rows (and permute_plan's
+// src initialisation).  Row order inside an expert's range depends on the
+// order in which chunks reserve; src / dst describe whichever order results.
+constexpr int kPgThreads = 256;
+constexpr int kPgUnroll = 4;  // 16-byte loads in flight per lane
+
+__global__ void __launch_bounds__(kPgThreads) permute_gather_kernel(const int* __restrict__ idx, int n_assign,
+                                                                    int k, const int* __restrict__ counts,
+                                                                    const int* __restrict__ row_off, int* cursor,
+                                                                    const __nv_bfloat16* __restrict__ x, long ldx,
+                                                                    int D, int* __restrict__ src,
+                                                                    int* __restrict__ dst,
+                                                                    __nv_bfloat16* __restrict__ out, long ldo, int E,
+                                                                    int P, unsigned int* status) {
+  __shared__ int s_cnt[kMaxExpertsPerLane * 32];
+  __shared__ int s_pos[kPgThreads];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int D8 = D >> 3;
+  if ((int)blockIdx.x < E) {  // padding rows of expert blockIdx.x
+    const int e = blockIdx.x;
+    const int r0 = row_off[e] + counts[e], r1 = min(row_off[e + 1], P);
+    for (int r = r0 + warp; r < r1; r += kPgThreads / 32) {
+      uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * ldo);
+      for (int c = lane; c < D8; c += 32) o[c] = make_uint4(0, 0, 0, 0);
+      if (lane == 0) src[r] = -1;
+    }
+    return;
+  }
+  const int tpb = kPgThreads / k;
+  const int tok0 = (blockIdx.x - E) * tpb;
+  const int a0 = tok0 * k;
+  const int na = min(tpb * k, n_assign - a0);
+  for (int e = t; e < E; e += kPgThreads) s_cnt[e] = 0;
+  __syncthreads();
+  int e = -1, rank = 0;
+  if (t < na) {
+    e = idx[a0 + t];
+    if (e >= 0 && e < E) {
+      rank = atomicAdd(&s_cnt[e], 1);
+    } else {
+      record_error(status, DSV3_ERR_BOUNDS);
+      e = -1;
+    }
+  }
+  __syncthreads();
+  for (int j = t; j < E; j += kPgThreads) {
+    const int c = s_cnt[j];
+    s_cnt[j] = c ? atomicAdd(&cursor[j], c) : 0;  // this chunk's first row of expert j
+  }
+  __syncthreads();
+  if (t < na) {
+    int pos = -1;
+    if (e >= 0) {
+      pos = row_off[e] + s_cnt[e] + rank;
+      if (pos >= row_off[e + 1] || pos >= P) {
         record_error(status, DSV3_ERR_BOUNDS);
         pos = -1;
       } else {
-        src[pos] = w;
-        dst[w] = pos;
+        src[pos] = a0 + t;
+        dst[a0 + t] = pos;
       }
     }
-    pos = __shfl_sync(0xffffffffu, pos, 0);
-    if (pos < 0) return;
-    const uint4* sr = reinterpret_cast<const uint4*>(x + (size_t)(w / k) * ldx);
-    uint4* o = reinterpret_cast<uint4*>(out + (size_t)pos * ldo);
-    for (int c = lane; c < D8; c += 32) o[c] = sr[c];
-    return;
+    s_pos[t] = pos;
   }
-  const int p = w - n_assign;                 // padding slot: expert p / 256, row p % 256 past its count
-  if (p >= E * 256) return;
-  const int e = p >> 8, j = p & 255;
-  const int r = row_off[e] + counts[e] + j;
-  if (r >= row_off[e + 1] || r >= P) return;
-  uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * ldo);
-  for (int c = lane; c < D8; c += 32) o[c] = make_uint4(0, 0, 0, 0);
-  if (lane == 0) src[r] = -1;
+  __syncthreads();
+  const int ntok = na / k;
+  for (int i = warp; i < ntok; i += kPgThreads / 32) {
+    const uint4* sr = reinterpret_cast<const uint4*>(x + (size_t)(tok0 + i) * ldx);
+    for (int c0 = lane; c0 < D8; c0 += 32 * kPgUnroll) {
+      uint4 v[kPgUnroll];
+#pragma unroll
+      for (int u = 0; u < kPgUnroll; ++u)
+        if (c0 + 32 * u < D8) v[u] = __ldg(sr + c0 + 32 * u);
+      for (int j = 0; j < k; ++j) {
+        const int pos = s_pos[i * k + j];
+        if (pos < 0) continue;
+        uint4* o = reinterpret_cast<uint4*>(out + (size_t)pos * ldo);
+#pragma unroll
+        for (int u = 0; u < kPgUnroll; ++u)
+          if (c0 + 32 * u < D8) o[c0 + 32 * u] = v[u];
+      }
+    }
+  }
 }
 
 __global__ void permute_scatter_kernel(const int* __restrict__ idx, int n_assign, const int* __restrict__ row_off,
@@ -397,8 +442,10 @@ void permute_gather(const at::Tensor& idx, const at::Tensor& counts, const at::T
   TORCH_CHECK(D % 8 == 0 && x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0 && out.size(1) == D,
               "permute_gather: 16-byte rows");
   const at::cuda::CUDAGuard guard(x.device());
-  const long warps = (long)n + (long)E * 256;
-  permute_gather_kernel<<<nblk(warps, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(idx.data_ptr<int>(), n, k,
+  TORCH_CHECK(k >= 1 && k <= kPgThreads && E <= kMaxExpertsPerLane * 32, "permute_gather: k <= 256, E <= 256");
+  const int tpb = kPgThreads / k;
+  const int grid = E + nblk(x.size(0), tpb);
+  permute_gather_kernel<<<grid, kPgThreads, 0, at::cuda::getCurrentCUDAStream()>>>(idx.data_ptr<int>(), n, k,
       counts.data_ptr<int>(), row_off.data_ptr<int>(), cursor.data_ptr<int>(), cbf(x), x.stride(0), D,
       src.data_ptr<int>(), dst.data_ptr<int>(), bf(out), out.stride(0), E, P, status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

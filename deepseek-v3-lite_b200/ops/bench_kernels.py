@@ -6,7 +6,8 @@ shapes (forward, data gradient, weight gradient; cuBLAS via ``torch.matmul``
 on the same forward shape for reference; with and without CTA-pair tiles)
 and the attention kernels (tcgen05
 vs warp-level mma.sync) on the 412M, MTP and MLA-microbenchmark head dims.
-``--wide-bwd`` adds the two-kernel tcgen05 backward (``flash_bwd_wide``).
+``--wide-bwd`` adds the two-kernel tcgen05 backward (``flash_bwd_wide``);
+``--lm-head-only`` times the fused LM head + cross-entropy GEMMs alone.
 """
 from __future__ import annotations
 
@@ -85,6 +86,35 @@ def attention_cases(C, wide_bwd=False):
     return out
 
 
+def lm_head_cases(C, rows=65520, chunk=16380, V=100018, D=768):
+    """Fused LM head + cross-entropy on the 412M step's shapes: the forward
+    partials over all main + MTP rows, then per row chunk the dlogits epilogue
+    GEMM and the two gradient GEMMs that read it.  The 154 MB vocabulary
+    weight exceeds L2, so the tile order decides how often it is re-read."""
+    x = torch.randn(rows, D, device="cuda").bfloat16()
+    w = (torch.randn(V, D, device="cuda") * 0.05).bfloat16()
+    tgt = torch.randint(0, V, (rows,), device="cuda")
+    nt = (V + 255) // 256
+    pm, ps = torch.empty(rows, 2 * nt, device="cuda"), torch.empty(rows, 2 * nt, device="cuda")
+    tl = torch.zeros(rows, device="cuda")
+    lse = torch.full((rows,), 12.0, device="cuda")
+    scale = torch.full((rows,), 1.0 / rows, device="cuda")
+    dl = torch.empty(chunk, (V + 63) // 64 * 64, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(V, D, device="cuda")
+    dx = torch.empty(chunk, D, device="cuda")
+    fl_fwd = 2.0 * rows * V * D
+    fl_chunk = 2.0 * chunk * V * D
+    t_fwd = _time(lambda: C.ce_fwd_partials(x, w, tgt, pm, ps, tl), 5)
+    xc, tc, lc, sc = x[:chunk], tgt[:chunk], lse[:chunk], scale[:chunk]
+    t_bwd = _time(lambda: C.ce_bwd_logits(xc, w, tc, lc, sc, dl), 5)
+    t_wg = _time(lambda: C.linear_wgrad(dl[:, :V], xc, dw), 5)
+    t_dg = _time(lambda: C.linear_dgrad(dl[:, :V], w, dx, False), 5)
+    return [{"case": f"lm head + CE, {rows} rows x V {V} x D {D} (bwd chunks of {chunk})",
+             "fwd_partials_ms": round(t_fwd, 3), "fwd_tflops": round(fl_fwd / t_fwd / 1e9, 1),
+             "bwd_dlogits_ms_per_chunk": round(t_bwd, 3), "bwd_dlogits_tflops": round(fl_chunk / t_bwd / 1e9, 1),
+             "wgrad_ms_per_chunk": round(t_wg, 3), "dgrad_ms_per_chunk": round(t_dg, 3)}]
+
+
 def decode_cases(C):
     """Absorbed latent decode (the MLA microbenchmark's decode: 64 rows x 16
     heads over a 4096-row cache of R 512 + rope 64): cache bytes read per
@@ -115,8 +145,13 @@ def main():
     ap.add_argument("--wide-bwd", action="store_true", help="also time the two-kernel tcgen05 attention backward")
     ap.add_argument("--attention-only", action="store_true")
     ap.add_argument("--decode-only", action="store_true")
+    ap.add_argument("--lm-head-only", action="store_true")
     a = ap.parse_args()
     C = native()
+    if a.lm_head_only:
+        for r in lm_head_cases(C):
+            print(json.dumps(r), flush=True)
+        return
     if a.decode_only:
         for r in decode_cases(C):
             print(json.dumps(r), flush=True)

@@ -142,8 +142,8 @@ def test_swiglu_dense(C):
     close(h, torch.nn.functional.silu(g) * u)
 
 
-def test_ce_partials_and_grad(C):
-    T, D, V = 300, 256, 1000
+@pytest.mark.parametrize("T,D,V", [(300, 256, 1000), (1000, 768, 5003), (200, 128, 777)])
+def test_ce_partials_and_grad(C, T, D, V):
     x, w = bf(T, D, seed=13), bf(V, D, scale=0.1, seed=14)
     tgt = torch.randint(0, V, (T,), device="cuda")
     tgt[5] = -100
@@ -160,8 +160,16 @@ def test_ce_partials_and_grad(C):
     ok = tgt >= 0
     close(tl[ok], logits[ok, tgt[ok]], rtol=1e-4, atol=1e-3)
     scale = torch.full((T,), 0.5, device="cuda")
-    dl = torch.empty(T, V + 8, device="cuda", dtype=torch.bfloat16)
+    # a view of a larger buffer: the rows past T and the columns past V rounded
+    # up to 8 keep their sentinel; columns V .. V rounded up to 8 may be zeroed
+    ldo = (V + 8 + 7) // 8 * 8
+    v8 = (V + 7) // 8 * 8
+    buf = torch.full((T + 40, ldo), 7.0, device="cuda", dtype=torch.bfloat16)
+    dl = buf[:T]
     C.ce_bwd_logits(x, w, tgt, lse.contiguous(), scale, dl)
     ref = torch.softmax(logits, -1)
     ref[ok, tgt[ok]] -= 1.0
     close(dl[:, :V], ref * 0.5, rtol=1e-2, atol=2e-3)
+    assert (buf[:, v8:] == 7.0).all() and (buf[T:] == 7.0).all()
+    pad = buf[:T, V:v8]
+    assert ((pad == 0.0) | (pad == 7.0)).all()
