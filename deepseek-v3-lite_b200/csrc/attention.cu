@@ -203,17 +203,35 @@ __global__ void __launch_bounds__(128) fa_fwd_kernel(const bf16* __restrict__ Q,
 
 // delta[row] = sum_d dO[row, d] * O[row, d]
 // O / dO token-major [B, S, H, DV]; row r = (b*S + s)*H + h; delta is [B*H, S].
+// DV / 8 lanes share a row (one 16-byte load of each tensor per lane), so a
+// warp's loads cover 32 * 16 consecutive bytes; the partial dots are summed
+// over the row's lanes by shuffles.
 template <int DV>
-__global__ void fa_bwd_pre_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO, float* __restrict__ delta,
-                                  long rows, int S, int H) {
-  const long r = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
+__global__ void __launch_bounds__(256) fa_bwd_pre_kernel(const bf16* __restrict__ O, const bf16* __restrict__ dO,
+                                                         float* __restrict__ delta, long rows, int S, int H) {
+  constexpr int LPR = DV / 8;                       // lanes per row
+  static_assert(DV % 8 == 0 && LPR <= 32 && (32 % LPR) == 0, "fa_bwd_pre: DV / 8 divides 32");
+  const long t = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long r = t / LPR;
+  const int j = (int)(t % LPR);
   float acc = 0.f;
-  for (int c = lane; c < DV; c += 32) acc += __bfloat162float(O[r * DV + c]) * __bfloat162float(dO[r * DV + c]);
-  acc = warp_sum(acc);
-  const long h = r % H, bs = r / H, b = bs / S, s = bs % S;
-  if (lane == 0) delta[(b * H + h) * S + s] = acc;
+  if (r < rows) {
+    const uint4 a = reinterpret_cast<const uint4*>(O + r * DV)[j];
+    const uint4 d = reinterpret_cast<const uint4*>(dO + r * DV)[j];
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(d2[i]);
+      acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+    }
+  }
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (r < rows && j == 0) {
+    const long h = r % H, bs = r / H, b = bs / S, s = bs % S;
+    delta[(b * H + h) * S + s] = acc;
+  }
 }
 
 template <int DQK, int DV>
@@ -423,6 +441,17 @@ void run_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int DV>
+void launch_bwd_pre(const at::Tensor& o, const at::Tensor& dout, at::Tensor& delta, long rows, int Sq, int H,
+                    cudaStream_t st) {
+  TORCH_CHECK(((reinterpret_cast<uintptr_t>(o.data_ptr()) | reinterpret_cast<uintptr_t>(dout.data_ptr())) & 15) == 0,
+              "flash_bwd: O and dO must be 16-byte aligned");
+  fa_bwd_pre_kernel<DV><<<(int)((rows * (DV / 8) + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const bf16*>(o.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+      delta.data_ptr<float>(), rows, Sq, H);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 template <int DQK, int DV>
 void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
@@ -430,9 +459,7 @@ void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, cons
   const int BH = q.size(0), Sq = q.size(1), Sk = k.size(1);
   auto st = at::cuda::getCurrentCUDAStream();
   const long rows = (long)BH * Sq;
-  fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
-      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_bwd_pre<DV>(o, dout, delta, rows, Sq, H, st);
   auto kern = fa_bwd_kernel<DQK, DV>;
   const size_t smem = bwd_smem<DQK, DV>();
   static bool cfg = false;
@@ -518,9 +545,7 @@ void run_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   const int B = BH / H;
   auto st = at::cuda::getCurrentCUDAStream();
   const long rows = (long)BH * Sq;
-  fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
-      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_bwd_pre<DV>(o, dout, delta, rows, Sq, H, st);
   using Cfg = FabCfg<NA, NB, DV>;
   auto mk = [](const at::Tensor& t, int S, int D, uint32_t box0, CUtensorMapSwizzle swz) {
     uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)t.size(0)};
@@ -572,9 +597,7 @@ void run_bwd_sm100_wide(const at::Tensor& q, const at::Tensor& k, const at::Tens
   const int B = BH / H;
   auto st = at::cuda::getCurrentCUDAStream();
   const long rows = (long)BH * Sq;
-  fa_bwd_pre_kernel<DV><<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const bf16*>(o.data_ptr()),
-      reinterpret_cast<const bf16*>(dout.data_ptr()), delta.data_ptr<float>(), rows, Sq, H);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_bwd_pre<DV>(o, dout, delta, rows, Sq, H, st);
   // [b*h, S, D] bf16 with `box_rows`-row boxes: 64 columns in 128B swizzle
   // (or the 16-column block in 32B swizzle)
   auto mk = [](const at::Tensor& t, int S, int D, uint32_t box_rows, bool narrow = false) {
@@ -713,7 +736,18 @@ void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
   a.scale = (float)scale;
   a.scratch = scratch.data_ptr<float>();
   a.out = reinterpret_cast<bf16*>(out.data_ptr());
+  a.cache_rows = std::min(kv.size(1), pe.size(1));
+  a.cache_batches = (int)std::min(kv.size(0), pe.size(0));
+  a.status = status_ptr();
   C10_CUDA_CHECK(launch_latent_decode(a, at::cuda::getCurrentCUDAStream()));
+}
+
+// Query (mode < 0) or set which kernel latent_decode runs where the sizes
+// fit: 1 = tcgen05, 0 = warp-level mma.sync.  Returns the previous mode.
+int64_t decode_tc(int64_t mode) {
+  const int prev = latent_tc_enabled() ? 1 : 0;
+  if (mode >= 0) latent_tc_mode() = mode ? 1 : 0;
+  return prev;
 }
 
 // The tcgen05 forward (attention_sm100.cuh).  Same contract as flash_fwd.
@@ -781,6 +815,7 @@ void register_attention(pybind11::module_& m) {
   m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)", pybind11::arg("q_lat"),
         pybind11::arg("q_pe"), pybind11::arg("kv"), pybind11::arg("pe"), pybind11::arg("lens"), pybind11::arg("scale"),
         pybind11::arg("max_len"), pybind11::arg("scratch"), pybind11::arg("out"), pybind11::arg("qpb") = 1);
+  m.def("decode_tc", &decode_tc, "query (-1) or set (0/1) the tcgen05 latent-decode kernel; returns the previous mode");
 }
 
 }  // namespace dsv3

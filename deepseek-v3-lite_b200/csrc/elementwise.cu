@@ -452,6 +452,123 @@ __global__ void rmsnorm_bwd_v(const TDy* __restrict__ dy, long lddy, const TIn* 
   for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], dw_s[c]);
 }
 
+// ------------------------------------- MoE input gradient + RMSNorm backward
+// The gradient at a MoE layer's normalised input has three parts: the shared
+// experts' (fp32, optional), the routed experts' rows un-permuted from the
+// expert-sorted buffer (bf16, one row per (token, slot)), and the router
+// logits' (dlog[t, :E] @ W_gate, K = E).  One warp per token row sums them in
+// registers and runs the RMSNorm backward on the sum:
+//   g = dsh[t] + sum_j dxs[dst[t, j]] + sum_e dlog[t, e] W_gate[e]
+//   dres[t] += rstd (g w - x_hat <x_hat, g w> / D),  dres_b[t] = bf16(dres[t]),
+//   dw += g * x_hat.
+// Replaces unpermute_bwd, the router data-gradient GEMM and rmsnorm_bwd (three
+// fp32 round trips of the [T, D] gradient).  W_gate (as fp32) and the norm
+// weight sit in shared memory; lanes broadcast the row's router-logit
+// gradients by shuffle.  All of a row's loads are issued before the first use.
+constexpr int kMoeNormMaxK = 8;   // routed slots per token the fused kernel unrolls
+
+template <int PAIRS>
+__global__ void __launch_bounds__(256, 1) moe_norm_bwd_v(
+    const __nv_bfloat16* __restrict__ dxs, long ldxs, const int* __restrict__ dst, int k, int P,
+    const float* __restrict__ dsh, long ldsh, const __nv_bfloat16* __restrict__ dlog, long ldl,
+    const __nv_bfloat16* __restrict__ wg, int E, const float* __restrict__ x, long ldx, const float* __restrict__ w,
+    const float* __restrict__ rstd, float* __restrict__ dres, long ldr, __nv_bfloat16* __restrict__ dres_b, long ldb,
+    float* __restrict__ dw, int T, int rows_per_block, unsigned int* status) {
+  constexpr int D = 64 * PAIRS;
+  extern __shared__ __align__(16) uint8_t moe_norm_smem[];
+  float* dw_s = reinterpret_cast<float*>(moe_norm_smem);                                           // [D]
+  float* w_s = dw_s + D;                                                                            // [D]
+  float2* wg_s = reinterpret_cast<float2*>(moe_norm_smem + 2 * D * sizeof(float));                  // [E][D / 2]
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    dw_s[c] = 0.f;
+    w_s[c] = w[c];
+  }
+  for (int i = threadIdx.x; i < E * (D / 2); i += blockDim.x)
+    wg_s[i] = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(wg)[i]);
+  __syncthreads();
+  const int warps = blockDim.x >> 5;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(T, r0 + rows_per_block);
+  float2 dwl[PAIRS];
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) dwl[i] = make_float2(0.f, 0.f);
+  for (int row = r0 + wid; row < r1; row += warps) {
+    // every load of the row is issued before any is consumed: the k slot
+    // indices (lane j holds slot j), the router gradients (lane e holds e),
+    // the shared part, x, the accumulated residual gradient, then the k rows
+    const int myp = (k > 0 && lane < k) ? dst[(size_t)row * k + lane] : 0;
+    const float al0 = lane < E ? __bfloat162float(dlog[(size_t)row * ldl + lane]) : 0.f;
+    float2 g[PAIRS], xv[PAIRS], av[PAIRS];
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      const int c = 2 * (lane + 32 * i);
+      g[i] = dsh ? *reinterpret_cast<const float2*>(dsh + (size_t)row * ldsh + c) : make_float2(0.f, 0.f);
+      xv[i] = *reinterpret_cast<const float2*>(x + (size_t)row * ldx + c);
+      av[i] = *reinterpret_cast<const float2*>(dres + (size_t)row * ldr + c);
+    }
+#pragma unroll
+    for (int j = 0; j < kMoeNormMaxK; ++j) {
+      if (j < k) {
+        const int p = __shfl_sync(0xffffffffu, myp, j);
+        if (p >= 0 && p < P) {
+#pragma unroll
+          for (int i = 0; i < PAIRS; ++i) {
+            const float2 v = ld2(dxs + (size_t)p * ldxs + 2 * (lane + 32 * i));
+            g[i].x += v.x;
+            g[i].y += v.y;
+          }
+        } else if (lane == 0) {
+          record_error(status, DSV3_ERR_BOUNDS);
+        }
+      }
+    }
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const float al = e0 == 0 ? al0 : (e0 + lane < E ? __bfloat162float(dlog[(size_t)row * ldl + e0 + lane]) : 0.f);
+      const int ne = min(32, E - e0);
+      for (int e = 0; e < ne; ++e) {
+        const float a = __shfl_sync(0xffffffffu, al, e);
+        const float2* wr = wg_s + (size_t)(e0 + e) * (D / 2);
+#pragma unroll
+        for (int i = 0; i < PAIRS; ++i) {
+          const float2 f = wr[lane + 32 * i];
+          g[i].x = fmaf(a, f.x, g[i].x);
+          g[i].y = fmaf(a, f.y, g[i].y);
+        }
+      }
+    }
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      xv[i].x *= r;   // x_hat
+      xv[i].y *= r;
+      const float2 wv = *reinterpret_cast<const float2*>(w_s + 2 * (lane + 32 * i));
+      dot += xv[i].x * g[i].x * wv.x + xv[i].y * g[i].y * wv.y;
+      dwl[i].x += g[i].x * xv[i].x;
+      dwl[i].y += g[i].y * xv[i].y;
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      const int c = 2 * (lane + 32 * i);
+      const float2 wv = *reinterpret_cast<const float2*>(w_s + c);
+      float2 sv = av[i];
+      sv.x += r * (g[i].x * wv.x - xv[i].x * dot);
+      sv.y += r * (g[i].y * wv.y - xv[i].y * dot);
+      *reinterpret_cast<float2*>(dres + (size_t)row * ldr + c) = sv;
+      *reinterpret_cast<uint32_t*>(dres_b + (size_t)row * ldb + c) = pack_bf16x2(sv.x, sv.y);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    atomicAdd(&dw_s[2 * (lane + 32 * i)], dwl[i].x);
+    atomicAdd(&dw_s[2 * (lane + 32 * i) + 1], dwl[i].y);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dw[c], dw_s[c]);
+}
+
 // -------------------------------------------------- vectorised MLA packing
 // One block per token; each thread moves one 8-element (16-byte) chunk of Q,
 // K or V for one head.  Requires dn, dr, dv, DP to be multiples of 8.
@@ -665,6 +782,67 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Shared memory the fused MoE-gradient + norm backward needs (W_gate staged as bf16).
+int64_t moe_norm_bwd_smem(int64_t E, int64_t D) { return D * 8 + E * D * 4; }
+
+void moe_norm_bwd(c10::optional<at::Tensor> dxs, c10::optional<at::Tensor> dst, c10::optional<at::Tensor> dsh,
+                  const at::Tensor& dlog, const at::Tensor& wg, const at::Tensor& x, const at::Tensor& w,
+                  const at::Tensor& rstd, at::Tensor& dres, at::Tensor& dres_b, at::Tensor& dw) {
+  const int T = x.size(0), D = x.size(1), E = wg.size(0);
+  TORCH_CHECK(x.scalar_type() == at::kFloat && dres.scalar_type() == at::kFloat && w.scalar_type() == at::kFloat &&
+              dw.scalar_type() == at::kFloat && rstd.scalar_type() == at::kFloat, "moe_norm_bwd: fp32 x / dres / w / dw");
+  TORCH_CHECK(dres_b.scalar_type() == at::kBFloat16 && dlog.scalar_type() == at::kBFloat16 &&
+              wg.scalar_type() == at::kBFloat16 && wg.is_contiguous() && wg.size(1) == D,
+              "moe_norm_bwd: bf16 dres_b / dlog, contiguous bf16 W_gate [E, D]");
+  TORCH_CHECK(dlog.size(0) == T && dlog.size(1) >= E && dlog.stride(1) == 1, "moe_norm_bwd: dlog [T, >= E]");
+  TORCH_CHECK(dxs.has_value() == dst.has_value(), "moe_norm_bwd: dxs and dst together");
+  const int k = dst ? (int)dst->size(1) : 0;
+  TORCH_CHECK(k <= kMoeNormMaxK, "moe_norm_bwd: at most ", kMoeNormMaxK, " routed slots per token");
+  const int P = dxs ? (int)dxs->size(0) : 0;
+  if (dxs) {
+    TORCH_CHECK(dxs->scalar_type() == at::kBFloat16 && dxs->size(1) == D && dxs->stride(1) == 1 &&
+                dxs->stride(0) % 2 == 0, "moe_norm_bwd: bf16 dxs [P, D]");
+    TORCH_CHECK(dst->scalar_type() == at::kInt && dst->is_contiguous() && dst->size(0) == T, "moe_norm_bwd: dst [T, k]");
+  }
+  if (dsh) TORCH_CHECK(dsh->scalar_type() == at::kFloat && dsh->size(0) == T && dsh->size(1) == D &&
+                       dsh->stride(1) == 1 && dsh->stride(0) % 2 == 0, "moe_norm_bwd: fp32 dsh [T, D]");
+  TORCH_CHECK(x.stride(1) == 1 && dres.stride(1) == 1 && dres_b.stride(1) == 1 && x.stride(0) % 2 == 0 &&
+              dres.stride(0) % 2 == 0 && dres_b.stride(0) % 2 == 0, "moe_norm_bwd: row-major, even row strides");
+  const size_t smem = (size_t)moe_norm_bwd_smem(E, D);
+  TORCH_CHECK(smem <= 200 * 1024, "moe_norm_bwd: W_gate too large for shared memory");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (T == 0) return;
+  // one CTA per SM (W_gate is staged once per SM), 8 rows per CTA at least
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int rows_per_block = std::max(8, blocks_for(T, sms));
+  const int grid = blocks_for(T, rows_per_block);
+#define DSV3_MNB(P_)                                                                                               \
+  if (D == 64 * P_) {                                                                                              \
+    auto kern = moe_norm_bwd_v<P_>;                                                                                \
+    if (smem > 48 * 1024) C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                                              (int)smem));                                         \
+    kern<<<grid, 256, smem, st>>>(dxs ? reinterpret_cast<const __nv_bfloat16*>(dxs->data_ptr()) : nullptr,       \
+        dxs ? dxs->stride(0) : 0, dst ? dst->data_ptr<int>() : nullptr, k, P,                                      \
+        dsh ? dsh->data_ptr<float>() : nullptr, dsh ? dsh->stride(0) : 0,                                          \
+        reinterpret_cast<const __nv_bfloat16*>(dlog.data_ptr()), dlog.stride(0),                                   \
+        reinterpret_cast<const __nv_bfloat16*>(wg.data_ptr()), E, x.data_ptr<float>(), x.stride(0),                \
+        w.data_ptr<float>(), rstd.data_ptr<float>(), dres.data_ptr<float>(), dres.stride(0),                       \
+        reinterpret_cast<__nv_bfloat16*>(dres_b.data_ptr()), dres_b.stride(0), dw.data_ptr<float>(), T,           \
+        rows_per_block, status_ptr());                                                                             \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();                                                                                \
+    return;                                                                                                        \
+  }
+  DSV3_PAIRS_LIST(DSV3_MNB)
+#undef DSV3_MNB
+  TORCH_CHECK(false, "moe_norm_bwd: D must be 64 x one of 1, 2, 3, 4, 6, 8, 12, 16, 24, 32");
+}
+
 void rope_inplace(at::Tensor& x, int64_t off, int64_t half, const at::Tensor& cosv, const at::Tensor& sinv,
                   c10::optional<at::Tensor> pos, int64_t seqlen, int64_t start, bool inverse) {
   // x: [T, H, W] bf16 view (any strides on T / H, unit on W)
@@ -812,6 +990,9 @@ void register_elementwise(pybind11::module_& m) {
   m.def("heads_unpack", &heads_unpack, "gradient of heads_pack (fp32 -> bf16 strided)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd, "y(bf16) = rmsnorm(x) * w; stores 1/rms per row");
   m.def("rmsnorm_bwd", &rmsnorm_bwd, "RMSNorm backward (dx accumulate or store, dw +=)");
+  m.def("moe_norm_bwd", &moe_norm_bwd,
+        "MoE input gradient (shared + un-permuted routed + router rows) fused with the RMSNorm backward");
+  m.def("moe_norm_bwd_smem", &moe_norm_bwd_smem, "shared memory bytes moe_norm_bwd needs for E experts of width D");
   m.def("rope_inplace", &rope_inplace, "rotate interleaved pairs in place (optionally inverse)");
   m.def("mla_pack", &mla_pack, "MLA Q/K/V packing with RoPE for the attention kernels");
   m.def("mla_unpack", &mla_unpack, "gradient of mla_pack");

@@ -5,6 +5,7 @@
 #pragma once
 #include "common.cuh"
 #include "mma_sync.cuh"
+#include "latent_decode_tc.cuh"
 
 // Absorbed decode: per (batch row b, head h): scores over cache rows
 // [0, len_b) = q_lat . kv + q_pe . pe, softmax, out = sum p * kv (latent R).
@@ -323,6 +324,9 @@ struct LatentDecodeArgs {
   float scale;
   float* scratch;
   bf16* out;
+  long cache_rows;          // rows per cache batch (0: kv_bs / R)
+  int cache_batches;        // cache batch rows (0: ceil(B / qpb))
+  unsigned int* status;     // device status word for bounded-wait failures (may be null)
 };
 
 // DSV3_DECODE_TILE=64 selects the one-CTA-per-SM 64-row tiles for R 512.
@@ -351,6 +355,49 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// DSV3_DECODE_TC=1 selects the tcgen05 kernel (latent_decode_tc.cuh) where
+// the sizes fit; by default the warp-level (mma.sync) kernel runs, which is
+// faster while the tcgen05 kernel cannot overlap a tile's loads with the
+// previous tile's products (measured on the B5 decode case: 158 us tcgen05,
+// 148 us mma.sync).
+inline int& latent_tc_mode() {
+  static int v = -1;
+  return v;
+}
+
+inline bool latent_tc_enabled() {
+  int& v = latent_tc_mode();
+  if (v < 0) {
+    const char* e = getenv("DSV3_DECODE_TC");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// tcgen05 kernel for NCL latent chunks of 64 columns (NCL / 2 output blocks
+// of 128).  Sets *done = false (and launches nothing) when a tensor map
+// cannot describe the caches.
+template <int NCL>
+inline cudaError_t launch_latent_tc(const LatentDecodeArgs& a, int nsplit, float* pm, float* pl, float* po,
+                                    cudaStream_t st, bool* done) {
+  *done = false;
+  const long rows = a.cache_rows > 0 ? a.cache_rows : a.kv_bs / a.R;
+  const long prow = a.cache_rows > 0 ? a.cache_rows : a.pe_bs / a.dr;
+  const long nb = a.cache_batches > 0 ? a.cache_batches : (a.B + a.qpb - 1) / a.qpb;
+  CUtensorMap tkv, tpe;
+  if (rows < 1 || prow < 1 || !ltc_map(&tkv, a.kv, a.R, rows, nb, a.kv_bs) || !ltc_map(&tpe, a.pe, a.dr, prow, nb, a.pe_bs))
+    return cudaSuccess;
+  auto kern = latent_decode_tc_kernel<NCL>;
+  constexpr int smem = LtcCfg<NCL>::SMEM;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const int items = a.B * ((a.H + 15) / 16) * nsplit;
+  const int grid = items < ltc_num_sms() ? items : ltc_num_sms();
+  *done = true;
+  return launch_ex(kern, dim3(grid), dim3(kLtcThreads), (size_t)smem, st, tkv, tpe, a.q_lat, a.q_pe, a.lens, a.B,
+                   a.H, a.R, a.dr, a.qpb, nsplit, (float)(a.scale * 1.4426950408889634), pm, pl, po, a.status);
+}
+
 template <int R, int DRP, int NW, int TK = 64>
 inline cudaError_t launch_latent_mma(const LatentDecodeArgs& a, int nsplit, float* pm, float* pl, float* po,
                                      cudaStream_t st) {
@@ -371,8 +418,25 @@ inline cudaError_t launch_latent_decode(const LatentDecodeArgs& a, cudaStream_t 
   float* pl = pm + (long long)a.B * a.H * nsplit;
   float* po = pl + (long long)a.B * a.H * nsplit;
   cudaError_t e = cudaErrorNotSupported;
+  // tcgen05 kernel: R a multiple of 64 up to 512, rope width a multiple of 8
+  // up to 64, 16-byte aligned rows and batches
+  const bool tc_ok = latent_tc_enabled() && a.R % 64 == 0 && a.R <= 512 && a.dr % 8 == 0 && a.dr > 0 &&
+                     a.dr <= 64 && a.kv_bs % 8 == 0 && a.pe_bs % 8 == 0 && a.B > 0 &&
+                     (reinterpret_cast<uintptr_t>(a.q_lat) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.q_pe) & 15) == 0;
+  if (tc_ok) {
+    bool done = false;
+    const int ncl = (a.R + 127) / 128 * 2;
+    if (ncl == 2) e = launch_latent_tc<2>(a, nsplit, pm, pl, po, st, &done);
+    else if (ncl == 4) e = launch_latent_tc<4>(a, nsplit, pm, pl, po, st, &done);
+    else if (ncl == 6) e = launch_latent_tc<6>(a, nsplit, pm, pl, po, st, &done);
+    else e = launch_latent_tc<8>(a, nsplit, pm, pl, po, st, &done);
+    if (e != cudaSuccess) return e;
+    if (!done) e = cudaErrorNotSupported;
+  }
   const int drp = (a.dr + 15) / 16 * 16;
-  const bool mma_ok = a.dr % 8 == 0 && a.dr <= 64 && a.kv_bs % 8 == 0 && a.pe_bs % 8 == 0;
+  // warp-level tensor-core kernel where the tcgen05 one did not launch
+  const bool mma_ok = e == cudaErrorNotSupported && a.dr % 8 == 0 && a.dr <= 64 && a.kv_bs % 8 == 0 &&
+                      a.pe_bs % 8 == 0;
 #define DSV3_LD_CASE(R_, DRP_, NW_) \
   if (mma_ok && a.R == R_ && drp == DRP_) e = launch_latent_mma<R_, DRP_, NW_>(a, nsplit, pm, pl, po, st);
   // R 512: 32-row cache tiles and 4 warps keep shared memory at ~95 KB, so two

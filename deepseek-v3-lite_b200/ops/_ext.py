@@ -14,7 +14,9 @@ _mod = None
 _err = None
 
 # Kernels launched per entry point (entries not listed launch one kernel).
-_LAUNCHES_PER_CALL = {"ce_reduce": 2, "flash_bwd": 2, "flash_bwd_wide": 3, "latent_decode": 2, "grad_sqsum": 3, "status_read": 0, "status_reset": 0}
+_LAUNCHES_PER_CALL = {"ce_reduce": 2, "flash_bwd": 2, "flash_bwd_wide": 3, "latent_decode": 2, "grad_sqsum": 3,
+                      "status_read": 0, "status_reset": 0, "moe_norm_bwd_smem": 0,
+                      "decode_tc": 0, "gemm_pairs": 0}
 _counting = [False, 0]
 
 

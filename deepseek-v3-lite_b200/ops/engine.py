@@ -177,6 +177,10 @@ class TrainEngine:
         # model fit.
         self.recompute = bool(getattr(config, "activation_recompute", False)) or \
             os.environ.get("DSV3_RECOMPUTE", "0") == "1"
+        # MoE layers: the FFN norm's backward runs fused with the sum of the
+        # shared, routed and router input gradients (DSV3_MOE_NORM_FUSED=0: the
+        # separate un-permute, router data-gradient GEMM and norm backward)
+        self.fuse_moe_norm = os.environ.get("DSV3_MOE_NORM_FUSED", "1") != "0"
 
     def _mark(self, name: str) -> None:
         if self.phase_timer is not None:
@@ -504,7 +508,7 @@ class TrainEngine:
                               marks=self._mark, overlap=shared_fwd if moe.shared_experts else None)
         return _Ctx(ep=ectx, idx=idx, wts=wts, ssel=ssel, shared=shared, Ep=Ep, counts=counts), out
 
-    def _moe_bwd_ep(self, moe, ctx, xn, dres_bf16, dxn_acc):
+    def _moe_bwd_ep(self, moe, ctx, xn, dres_bf16, dxn_acc, norm=None):
         from parallel.ep import moe_backward_ep
         C, ep = self.C, self.ep
         E, I = moe.n_routed_experts, moe.moe_inter_dim
@@ -517,17 +521,42 @@ class TrainEngine:
         w13, w2, g13, g2 = self._local_experts(moe, ep)
         dw = moe_backward_ep(ep, ctx.ep, dres_bf16, w13, w2, g13, g2, dxn_acc, I, marks=self._mark,
                              overlap=shared_bwd if moe.shared_experts else None)
+        if self._norm_fusable(moe, norm):
+            dlog = self._router_dlog(moe, ctx, xn, dw)
+            self._moe_norm_bwd(moe, None, None, dxn_acc, dlog, norm)
+            self._mark("router bwd + norm bwd")
+            return True
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
         self._mark("router bwd")
+        return False
 
-    def _router_bwd(self, moe, ctx, xn, dw, dxn_acc):
+    def _router_dlog(self, moe, ctx, xn, dw):
+        """Router logit gradients [T, Ep] (bf16) and the gate weight gradient."""
         C = self.C
         T, E = xn.shape[0], moe.n_routed_experts
         dlog = torch.empty(T, ctx.Ep, dtype=BF16, device=self.device)
         C.router_bwd(dw, ctx.ssel, ctx.idx, float(moe.gate.route_scale), dlog)
-        gw = moe.gate.weight
-        C.linear_wgrad(dlog[:, :E], xn, self.g(gw))
-        C.linear_dgrad(dlog[:, :E], self.w(gw), dxn_acc)
+        C.linear_wgrad(dlog[:, :E], xn, self.g(moe.gate.weight))
+        return dlog
+
+    def _router_bwd(self, moe, ctx, xn, dw, dxn_acc):
+        dlog = self._router_dlog(moe, ctx, xn, dw)
+        self.C.linear_dgrad(dlog[:, :moe.n_routed_experts], self.w(moe.gate.weight), dxn_acc)
+
+    def _norm_fusable(self, moe, norm):
+        """Whether the FFN norm's backward can run fused with the MoE input-gradient sum."""
+        if norm is None or not self.fuse_moe_norm:
+            return False
+        D = self.D
+        return D % 64 == 0 and D // 64 in (1, 2, 3, 4, 6, 8, 12, 16, 24, 32) and \
+            self.C.moe_norm_bwd_smem(moe.n_routed_experts, D) <= 200 * 1024
+
+    def _moe_norm_bwd(self, moe, dxs, dst, dsh, dlog, norm):
+        """g = dsh + un-permuted dxs + dlog @ W_gate, then the RMSNorm backward of g
+        (norm = (x, weight param, rstd, dres fp32 accumulated, dres bf16 copy))."""
+        x, nw, rstd, dres, dres_b = norm
+        self.C.moe_norm_bwd(dxs, dst, dsh, dlog, self.w(moe.gate.weight), x, self.f32(nw), rstd, dres, dres_b,
+                            self.g(nw))
 
     def _moe_fwd(self, moe, xn, resid_in):
         """Returns (ctx, resid_in + MoE(xn)) as a new fp32 tensor."""
@@ -571,13 +600,18 @@ class TrainEngine:
         return _Ctx(idx=idx, wts=wts, ssel=ssel, row_off=row_off, tile_group=tile_group, src=src, dst=dst, xs=xs,
                     h=h, gu=gu, ys=ys, shared=shared, Ep=Ep, counts=counts), out
 
-    def _moe_bwd(self, moe, ctx, xn, dres_bf16, dxn_acc):
+    def _moe_bwd(self, moe, ctx, xn, dres_bf16, dxn_acc, norm=None):
+        """MoE backward into dxn_acc (fp32).  With norm = (x, weight, rstd, dres,
+        dres_b) and a fusable shape, the FFN norm's backward runs fused with the
+        input-gradient sum instead (dxn_acc then holds only the shared experts'
+        part) and True is returned."""
         if self.use_ep:
-            return self._moe_bwd_ep(moe, ctx, xn, dres_bf16, dxn_acc)
+            return self._moe_bwd_ep(moe, ctx, xn, dres_bf16, dxn_acc, norm)
         C = self.C
         T = xn.shape[0]
         E, k, I = moe.n_routed_experts, moe.topk, moe.moe_inter_dim
-        if not moe.shared_experts:
+        fused = self._norm_fusable(moe, norm)
+        if not moe.shared_experts and not fused:
             dxn_acc.zero_()
 
         def shared_bwd():
@@ -605,9 +639,15 @@ class TrainEngine:
         self._mark("experts up wgrad")
         self._join(side)
         self._mark("shared experts join")
+        if fused:
+            dlog = self._router_dlog(moe, ctx, xn, dw)
+            self._moe_norm_bwd(moe, dxs, ctx.dst, dxn_acc if moe.shared_experts else None, dlog, norm)
+            self._mark("router bwd + norm bwd")
+            return True
         C.unpermute_bwd(dxs, ctx.dst, dxn_acc)
         self._router_bwd(moe, ctx, xn, dw, dxn_acc)
         self._mark("router bwd")
+        return False
 
     # ------------------------------------------------------------------ MTP
     def _mtp_fwd(self, mod, h_prev, emb, Bm, Sm):
@@ -882,15 +922,18 @@ class TrainEngine:
                 self._mark("recompute fwd")
             x_in, r1, actx, x_mid, xn2, r2, fctx = kept
             dxn2 = torch.empty(T, D, dtype=F32, device=self.device)
+            normed = False
             if hasattr(layer.ffn, "experts"):
-                self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2)
+                normed = self._moe_bwd(layer.ffn, fctx, xn2, dres_b, dxn2,
+                                       norm=(x_mid, layer.ffn_norm.weight, r2, dres, dres_b))
                 self._mark("moe bwd")
             else:
                 self._swiglu_dense_bwd(layer.ffn.w1.weight, layer.ffn.w2.weight, fctx, xn2, dres_b, dxn2,
                                        accumulate=False)
                 self._mark("dense ffn bwd")
-            C.rmsnorm_bwd(dxn2, x_mid, self.f32(layer.ffn_norm.weight), r2, dres, None, dres_b,
-                          self.g(layer.ffn_norm.weight))
+            if not normed:
+                C.rmsnorm_bwd(dxn2, x_mid, self.f32(layer.ffn_norm.weight), r2, dres, None, dres_b,
+                              self.g(layer.ffn_norm.weight))
             dxn1 = torch.empty(T, D, dtype=F32, device=self.device)
             self._mla_bwd(layer.attn, actx, dres_b, dxn1, B, S)
             C.rmsnorm_bwd(dxn1, x_in, self.f32(layer.attn_norm.weight), r1, dres, None, dres_b,

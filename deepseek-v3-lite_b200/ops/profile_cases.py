@@ -143,6 +143,37 @@ def case_latent_decode():
         C.latent_decode(q_lat, q_pe, kv, pe, lens, 0.07, S, scratch, out)
 
 
+def case_latent_decode_tc():
+    """The same decode case on the tcgen05 kernel (latent_decode_tc.cuh)."""
+    C = native()
+    prev = C.decode_tc(1)
+    try:
+        case_latent_decode()
+    finally:
+        C.decode_tc(prev)
+
+
+def case_moe_norm_bwd():
+    """MoE input gradient fused with the FFN norm backward on the 412M step's
+    shapes: 32K tokens, D 768, top-4 of 20 experts, shared-expert part."""
+    C = native()
+    T, D, E, k = 32768, 768, 20, 4
+    P = (T * k + E * 255 + 255) // 256 * 256
+    dxs = _bf(P, D)
+    dst = torch.randperm(P, device="cuda")[:T * k].view(T, k).int().contiguous()
+    dsh = torch.randn(T, D, device="cuda")
+    dlog = _bf(T, 24)
+    wg = _bf(E, D)
+    x = torch.randn(T, D, device="cuda")
+    w = torch.ones(D, device="cuda")
+    rstd = torch.ones(T, device="cuda")
+    dres = torch.zeros(T, D, device="cuda")
+    dres_b = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(D, device="cuda")
+    for _ in range(2):
+        C.moe_norm_bwd(dxs, dst, dsh, dlog, wg, x, w, rstd, dres, dres_b, dw)
+
+
 def case_ep_dispatch():
     """Expert-parallel dispatch kernel on one rank (the rank stores into its own
     heap): 32K tokens x top-4 of 20 experts, D 768."""

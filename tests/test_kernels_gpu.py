@@ -143,6 +143,84 @@ def test_latent_decode(C):
     close(out.cpu(), ref)
 
 
+def _check_permutation(idx, counts, row_off, src, dst, xs, x, k):
+    """Every (token, slot) owns one row of its expert's range holding the token's
+    row; the rest of each range is zero with src = -1; src and dst invert."""
+    E = counts.numel()
+    ro, cnt = row_off.cpu(), counts.cpu()
+    flat = idx.flatten().long().cpu()
+    d = dst.flatten().long().cpu()
+    s = src.cpu()
+    assert torch.equal(s[d], torch.arange(flat.numel(), dtype=torch.int32))
+    for e in range(E):
+        mine = d[flat == e]
+        assert mine.numel() == cnt[e] and ((mine >= ro[e]) & (mine < ro[e] + cnt[e])).all()
+        assert (s[ro[e] + cnt[e]:ro[e + 1]] == -1).all()
+        assert (xs[ro[e] + cnt[e]:ro[e + 1]] == 0).all()
+    assert torch.equal(xs[dst.flatten().long()], x.repeat_interleave(k, 0))
+
+
+@pytest.mark.parametrize("T,E,k", [(1000, 20, 4), (777, 40, 6), (300, 8, 1)])
+def test_permute_gather_shapes(C, T, E, k):
+    D = 384
+    idx = torch.stack([torch.randperm(E, device="cuda")[:k] for _ in range(T)]).int()
+    counts = torch.bincount(idx.flatten().long(), minlength=E).int()
+    P = ((T * k + E * 255 + 255) // 256) * 256
+    row_off = torch.empty(E + 1, device="cuda", dtype=torch.int32)
+    tg = torch.empty(P // 128, device="cuda", dtype=torch.int32)
+    cursor = torch.empty(E, device="cuda", dtype=torch.int32)
+    src = torch.empty(P, device="cuda", dtype=torch.int32)
+    dst = torch.empty(T, k, device="cuda", dtype=torch.int32)
+    x = torch.randn(T, D, device="cuda").bfloat16()
+    xs = torch.full((P, D), 3.0, device="cuda", dtype=torch.bfloat16)
+    C.permute_plan(counts, row_off, tg, cursor, src, src_tail_only=True)
+    C.permute_gather(idx, counts, row_off, cursor, x, src, dst, xs)
+    torch.cuda.synchronize()
+    _check_permutation(idx, counts, row_off, src, dst, xs, x, k)
+    assert (src[row_off[E].item():] == -1).all()
+
+
+
+@pytest.mark.parametrize("B,H,R,dr,S,cache_rows,qpb", [
+    (64, 16, 512, 64, 700, 700, 1),     # MLA microbenchmark dims (tcgen05 kernel, R 512)
+    (5, 12, 192, 24, 1000, 1024, 1),    # 412M dims: 12 heads, rope 24, a cache longer than max_len
+    (3, 20, 128, 32, 300, 300, 1),      # two head groups, the second partly empty
+    (6, 16, 64, 16, 129, 129, 3),       # three query rows per cache row (speculative verification)
+])
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
+def test_latent_decode_shapes(C, B, H, R, dr, S, cache_rows, qpb, tc):
+    """Absorbed decode against fp32 over each row's own cache length (0, 1,
+    tile-straddling and full lengths), on the tcgen05 and the mma.sync kernels."""
+    prev = C.decode_tc(tc)
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + R)
+    rnd = lambda *sh: torch.randn(*sh, device="cuda", generator=g)
+    Bc = B // qpb
+    q_lat, q_pe = rnd(B, H, R).bfloat16(), rnd(B, H, dr).bfloat16()
+    kv, pe = rnd(Bc, cache_rows, R).bfloat16(), rnd(Bc, cache_rows, dr).bfloat16()
+    lens = torch.randint(1, S + 1, (B,), device="cuda", generator=g).int()
+    lens[0] = S
+    if B > 2:
+        lens[1] = 0
+        lens[2] = min(S, 129)
+    scale = 0.08
+    nsplit = (S + 255) // 256
+    scratch = torch.empty(B * H * nsplit * (2 + R), device="cuda")
+    out = torch.full((B, H, R), float("nan"), device="cuda", dtype=torch.bfloat16)
+    try:
+        C.latent_decode(q_lat, q_pe, kv, pe, lens, scale, S, scratch, out, qpb)
+        torch.cuda.synchronize()
+    finally:
+        C.decode_tc(prev)
+    assert C.status_read() == 0
+    ref = torch.zeros(B, H, R, device="cuda")
+    for b in range(B):
+        n = int(lens[b])
+        if n:
+            k, p = kv[b // qpb, :n].float(), pe[b // qpb, :n].float()
+            ref[b] = torch.softmax((q_lat[b].float() @ k.T + q_pe[b].float() @ p.T) * scale, -1) @ k
+    close(out, ref)
+
+
 def test_router_and_permutation(C):
     T, E, k, D = 1000, 20, 4, 256
     logits = torch.randn(T, 24, device="cuda")
@@ -176,6 +254,13 @@ def test_router_and_permutation(C):
     xs = torch.empty(P, D, device="cuda", dtype=torch.bfloat16)
     C.gather_rows(x, src, k, xs)
     assert torch.equal(xs[dst.flatten().long()], x.repeat_interleave(k, 0))
+    # the fused permutation + gather gives the same ranges, rows and padding
+    xs2 = torch.full((P, D), 7.0, device="cuda", dtype=torch.bfloat16)
+    src2 = torch.empty(P, device="cuda", dtype=torch.int32)
+    dst2 = torch.empty(T, k, device="cuda", dtype=torch.int32)
+    C.permute_plan(counts, row_off, tg, cursor, src2, src_tail_only=True)
+    C.permute_gather(idx, counts, row_off, cursor, x, src2, dst2, xs2)
+    _check_permutation(idx, counts, row_off, src2, dst2, xs2, x, k)
     # combine forward / backward
     y = torch.randn(P, D, device="cuda").bfloat16()
     out = torch.zeros(T, D, device="cuda")
@@ -385,3 +470,41 @@ def test_flash_bwd_wide(C, B, H, S, DP, DV):
         close(got[2], Vr.grad, rtol=3e-2, atol=3e-2)
         close(got[1], Kr.grad, rtol=3e-2, atol=3e-2)
         close(got[0], Qr.grad, rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("D,E,with_shared,with_routed", [(256, 20, True, True), (768, 20, False, True),
+                                                        (768, 40, True, False), (128, 6, True, True)])
+def test_moe_norm_bwd_fused(C, D, E, with_shared, with_routed):
+    """Shared + un-permuted routed + router-logit input gradient, then the
+    RMSNorm backward, against an fp32 reference of the same sum."""
+    T, k = 333, 4
+    P = T * k + 64
+    g = torch.Generator(device="cuda").manual_seed(5)
+    rnd = lambda *s: torch.randn(*s, device="cuda", generator=g)
+    dxs = rnd(P, D).bfloat16()
+    dst = torch.randperm(P, device="cuda", generator=g)[:T * k].view(T, k).int().contiguous()
+    dsh = rnd(T, D)
+    Ep = (E + 7) // 8 * 8
+    dlog = rnd(T, Ep).bfloat16()
+    wg = (rnd(E, D) * 0.2).bfloat16()
+    x = rnd(T, D)
+    w = 1.0 + 0.1 * rnd(D)
+    rstd = torch.rsqrt(x.pow(2).mean(-1) + 1e-6)
+    dres0 = rnd(T, D)
+    dres = dres0.clone()
+    dres_b = torch.empty(T, D, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(D, device="cuda")
+    C.moe_norm_bwd(dxs if with_routed else None, dst if with_routed else None, dsh if with_shared else None,
+                   dlog, wg, x, w, rstd, dres, dres_b, dw)
+    gsum = dlog[:, :E].float() @ wg.float()
+    if with_shared:
+        gsum = gsum + dsh
+    if with_routed:
+        gsum = gsum + dxs.float()[dst.long()].sum(1)
+    xh = x * rstd[:, None]
+    gw = gsum * w
+    d = rstd[:, None] * (gw - xh * (gw * xh).mean(-1, keepdim=True))
+    close(dres, dres0 + d, rtol=1e-4, atol=1e-4)
+    close(dres_b, dres0 + d, rtol=1e-2, atol=1e-2)
+    close(dw, (gsum * xh).sum(0), rtol=1e-4, atol=1e-3)
+    assert C.status_read() == 0

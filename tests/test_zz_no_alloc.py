@@ -71,8 +71,8 @@ def test_noalloc_matches_entry_point():
     from ops._ext import native
     C = native()
     fn = _lib()
-    # two calls in a row through the C symbol: the tensor-core path (R 512, rope 64)
-    # and the per-warp path (R 192, rope 24)
+    # two calls in a row through the C symbol: R 512 / rope 64 and R 192 / rope 24
+    # (both sizes run on the tcgen05 kernel)
     for seed, (B, H, R, dr, S) in enumerate([(4, 8, 512, 64, 1000), (2, 16, 192, 24, 300)]):
         q_lat, q_pe, kv, pe, lens = _case(seed, B, H, R, dr, S)
         scale = 0.07
