@@ -743,10 +743,11 @@ void latent_decode(const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Te
 }
 
 // Query (mode < 0) or set which kernel latent_decode runs where the sizes
-// fit: 1 = tcgen05, 0 = warp-level mma.sync.  Returns the previous mode.
+// fit: 1 = tcgen05, 0 = warp-level mma.sync, 2 = by latent rank (default).
+// Returns the previous mode.
 int64_t decode_tc(int64_t mode) {
-  const int prev = latent_tc_enabled() ? 1 : 0;
-  if (mode >= 0) latent_tc_mode() = mode ? 1 : 0;
+  const int prev = latent_tc_mode();
+  if (mode >= 0) latent_tc_mode() = mode > 2 ? 2 : (int)mode;
   return prev;
 }
 
@@ -815,7 +816,7 @@ void register_attention(pybind11::module_& m) {
   m.def("latent_decode", &latent_decode, "absorbed MLA decode over the latent cache (split-K)", pybind11::arg("q_lat"),
         pybind11::arg("q_pe"), pybind11::arg("kv"), pybind11::arg("pe"), pybind11::arg("lens"), pybind11::arg("scale"),
         pybind11::arg("max_len"), pybind11::arg("scratch"), pybind11::arg("out"), pybind11::arg("qpb") = 1);
-  m.def("decode_tc", &decode_tc, "query (-1) or set (0/1) the tcgen05 latent-decode kernel; returns the previous mode");
+  m.def("decode_tc", &decode_tc, "query (-1) or set the latent-decode kernel (0 mma.sync, 1 tcgen05, 2 by rank); returns the previous mode");
 }
 
 }  // namespace dsv3

@@ -355,23 +355,24 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// DSV3_DECODE_TC=1 selects the tcgen05 kernel (latent_decode_tc.cuh) where
-// the sizes fit; by default the warp-level (mma.sync) kernel runs, which is
-// faster while the tcgen05 kernel cannot overlap a tile's loads with the
-// previous tile's products (measured on the B5 decode case: 158 us tcgen05,
-// 148 us mma.sync).
+// Which kernel latent_decode runs where the tcgen05 one fits: mode 1 =
+// tcgen05 (latent_decode_tc.cuh), 0 = the warp-level mma.sync kernel, 2 =
+// automatic (the default): tcgen05 for a latent rank of 384 or more, where it
+// is faster (measured on the MLA decode case, R 512: 120 us against 149 us),
+// mma.sync below (R 192: 41 us against 39 us).  DSV3_DECODE_TC=0/1 sets the
+// initial mode.
 inline int& latent_tc_mode() {
   static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("DSV3_DECODE_TC");
+    v = e == nullptr ? 2 : (e[0] == '1' ? 1 : (e[0] == '0' ? 0 : 2));
+  }
   return v;
 }
 
-inline bool latent_tc_enabled() {
-  int& v = latent_tc_mode();
-  if (v < 0) {
-    const char* e = getenv("DSV3_DECODE_TC");
-    v = (e != nullptr && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
+inline bool latent_tc_enabled(int R) {
+  const int v = latent_tc_mode();
+  return v == 1 || (v == 2 && R >= 384);
 }
 
 // tcgen05 kernel for NCL latent chunks of 64 columns (NCL / 2 output blocks
@@ -392,7 +393,8 @@ inline cudaError_t launch_latent_tc(const LatentDecodeArgs& a, int nsplit, float
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int items = a.B * ((a.H + 15) / 16) * nsplit;
-  const int grid = items < ltc_num_sms() ? items : ltc_num_sms();
+  const int ctas = 2 * ltc_num_sms();   // two persistent CTAs per SM
+  const int grid = items < ctas ? items : ctas;
   *done = true;
   return launch_ex(kern, dim3(grid), dim3(kLtcThreads), (size_t)smem, st, tkv, tpe, a.q_lat, a.q_pe, a.lens, a.B,
                    a.H, a.R, a.dr, a.qpb, nsplit, (float)(a.scale * 1.4426950408889634), pm, pl, po, a.status);
@@ -420,7 +422,7 @@ inline cudaError_t launch_latent_decode(const LatentDecodeArgs& a, cudaStream_t 
   cudaError_t e = cudaErrorNotSupported;
   // tcgen05 kernel: R a multiple of 64 up to 512, rope width a multiple of 8
   // up to 64, 16-byte aligned rows and batches
-  const bool tc_ok = latent_tc_enabled() && a.R % 64 == 0 && a.R <= 512 && a.dr % 8 == 0 && a.dr > 0 &&
+  const bool tc_ok = latent_tc_enabled(a.R) && a.R % 64 == 0 && a.R <= 512 && a.dr % 8 == 0 && a.dr > 0 &&
                      a.dr <= 64 && a.kv_bs % 8 == 0 && a.pe_bs % 8 == 0 && a.B > 0 &&
                      (reinterpret_cast<uintptr_t>(a.q_lat) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.q_pe) & 15) == 0;
   if (tc_ok) {

@@ -1,22 +1,25 @@
 // tcgen05 absorbed-MLA decode over the latent cache (sm_100a).  Included by
 // latent_decode.cuh inside each user's anonymous namespace.
 //
-// Work item = (query row b, group of 16 heads, split of 256 cache rows); a
-// persistent CTA (one per SM) walks items.  Per 128-row tile of the cache
+// Work item = (query row b, group of 16 heads, split of 256 cache rows);
+// persistent CTAs (two per SM) walk items.  Per 128-row tile of the cache
 // (latent R columns + rope columns, cache batch b / qpb):
 //
 //   S^T [128 rows x 16 heads]  = K [128 x (R + 64)] . Q^T           (TMEM cols 0..15)
 //   softmax over the 128 rows of each head column (4 warps, one row each)
 //   O^T [R x 16] += V^T [R x 128] . P^T [128 x 16]                  (TMEM, 16 cols per 128 latent)
 //
-// V is the latent part of the same tile, so the cache is read once for all
-// 16 heads.  The tile is staged by TMA as 64-column chunks of 128 rows
-// (16 KB, 128-byte swizzle) in fixed slots: latent chunks 0 .. NCL-1, rope
-// chunk NCL (zero-filled past dr).  S^T uses every chunk K-major; the PV
-// product reads latent chunks 2m, 2m+1 MN-major as the A operand of output
-// block m.  A slot is refilled with the next tile's chunk as soon as the MMA
-// that last reads it completes (tcgen05.commit on the slot's empty barrier),
-// so the next tile's loads overlap this tile's softmax and PV.
+// The tile is staged by TMA as 64-column chunks of 128 rows (16 KB, 128-byte
+// swizzle) through a ring of kLtcSlots slots.  Per tile the ring carries the
+// S pass (latent chunks 0 .. NCL-1, the rope chunk zero-filled past dr, and
+// one empty use so the next pass starts on an even slot), then the PV pass
+// (latent chunks 0 .. NCL-1 again, read MN-major in adjacent slot pairs 2m,
+// 2m+1 as the A operand of output block m).  The PV pass re-reads the tile's
+// latent part a few microseconds after the S pass brought it in, so it comes
+// from L2, not DRAM; in exchange the ring is small enough for two CTAs per SM,
+// and loads run ahead of the tensor core through both passes and across
+// tiles.  Chunks wholly past R are empty uses (no copy, no S MMA; the PV rows
+// they feed are latent dims past R, which are discarded).
 //
 // Warp roles: 0 = TMA producer, 1 = MMA issuer (owns TMEM), 2..5 = softmax /
 // epilogue (warp w reads TMEM lanes 32 * (w % 4) ..; the four warps meet at a
@@ -29,15 +32,17 @@
 constexpr int kLtcThreads = 192;          // producer, MMA, 4 softmax warps
 constexpr int kLtcChunk = 128 * 128;      // one 64-column x 128-row bf16 chunk (bytes)
 constexpr int kLtcQChunk = 16 * 128;      // 16 heads x 64 columns (bytes)
+constexpr int kLtcSlots = 4;              // ring slots (even: PV pairs sit in slots 2i, 2i+1)
 
 template <int NCL>
 struct LtcCfg {
   static constexpr int NCH = NCL + 1;                    // + the rope chunk
-  static constexpr int OFF_Q = NCH * kLtcChunk;
+  static constexpr int USES = 2 * NCL + 2;               // ring uses per tile: S pass (NCL + 2), PV pass (NCL)
+  static constexpr int OFF_Q = kLtcSlots * kLtcChunk;
   static constexpr int OFF_P = OFF_Q + NCH * kLtcQChunk;  // P: two [16][64] K-major chunks
   static constexpr int OFF_RED = OFF_P + 2 * kLtcQChunk;  // [2][4][16] floats + [4][16] floats
   static constexpr int OFF_BAR = OFF_RED + (2 * 4 * 16 + 4 * 16) * 4;
-  static constexpr int NBAR = 2 * NCH + 6;
+  static constexpr int NBAR = 2 * kLtcSlots + 6;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;   // + TMEM slot, abort flag, sync counter; slack
   static constexpr int TMEM_COLS = 128;                  // S^T at 0, O^T block m at 32 + 16 m
 };
@@ -73,7 +78,7 @@ __device__ __forceinline__ bool ltc_sync(unsigned int* ctr, unsigned int& epoch,
 }
 
 template <int NCL>
-__global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
+__global__ void __launch_bounds__(kLtcThreads, 2) latent_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_pe,
     const bf16* __restrict__ q_lat, const bf16* __restrict__ q_pe, const int* __restrict__ lens, int B, int H, int R,
     int dr, int qpb, int nsplit, float scale_log2, float* __restrict__ part_m, float* __restrict__ part_l,
@@ -86,8 +91,8 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
   float* red = reinterpret_cast<float*>(smem + C::OFF_RED);       // [2][4][16] tile maxima
   float* red_l = red + 2 * 4 * 16;                                // [4][16] row sums
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* empty = full + NCH;
-  uint64_t* s_full = empty + NCH;
+  uint64_t* empty = full + kLtcSlots;
+  uint64_t* s_full = empty + kLtcSlots;
   uint64_t* p_full = s_full + 1;
   uint64_t* pv_done = p_full + 1;
   uint64_t* q_ready = pv_done + 1;
@@ -102,7 +107,7 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
   const int items = B * HG * nsplit;
 
   if (threadIdx.x == 0) {
-    for (int c = 0; c < NCH; ++c) {
+    for (int c = 0; c < kLtcSlots; ++c) {
       mbar_init(&full[c], 1);
       mbar_init(&empty[c], 1);
     }
@@ -139,39 +144,50 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
     nt = r1 > r0 ? (r1 - r0 + 127) / 128 : 0;
   };
 
+  // ring use v of a tile: 0 .. NCL-1 S-pass latent chunk v, NCL the rope
+  // chunk, NCL + 1 empty, NCL + 2 .. 2 NCL + 1 PV-pass latent chunk
+  // v - NCL - 2; a latent chunk wholly past R is an empty use
+  auto use_chunk = [&](int v) { return v < NCL ? v : (v == NCL ? NCL : (v == NCL + 1 ? -1 : v - NCL - 2)); };
+  auto use_loads = [&](int v) {
+    const int c = use_chunk(v);
+    return c == NCL || (c >= 0 && 64 * c < R);
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t tiles = 0;   // tiles loaded so far: slot phase parity
-      uint32_t last_phase = 0;
-      bool issued_any = false;
+      uint32_t g = 0;           // ring uses so far: slot g % kLtcSlots, phase (g / kLtcSlots) & 1
+      uint32_t last_phase = 0;  // per slot: phase its latest use completes
       bool ok = true;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         int b, hg, split, r0, r1, nt;
         decode_item(it, b, hg, split, r0, r1, nt);
         const int cb = b / qpb;
-        for (int t = 0; t < nt && ok; ++t, ++tiles) {
+        for (int t = 0; t < nt && ok; ++t) {
           const int row = r0 + 128 * t;
-          for (int c = 0; c < NCH; ++c) {
-            if (!mbar_wait_bounded(&empty[c], (tiles & 1u) ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) {
+          for (int v = 0; v < C::USES; ++v, ++g) {
+            const int slot = g % kLtcSlots;
+            const uint32_t ph = (g / kLtcSlots) & 1u;
+            if (!mbar_wait_bounded(&empty[slot], ph ^ 1u, abort_flag, status, DSV3_ERR_WAIT_EMPTY)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full[c], kLtcChunk);
-            if (c < NCL) tma_load_3d(smem + c * kLtcChunk, &tm_kv, &full[c], 64 * c, row, cb);
-            else tma_load_3d(smem + c * kLtcChunk, &tm_pe, &full[c], 0, row, cb);
-            // slot c's latest copy completes phase `tiles` of full[c]
-            last_phase = (last_phase & ~(1u << c)) | ((tiles & 1u) << c);
-            issued_any = true;
+            const int c = use_chunk(v);
+            if (use_loads(v)) {
+              mbar_arrive_expect_tx(&full[slot], kLtcChunk);
+              if (c < NCL) tma_load_3d(smem + slot * kLtcChunk, &tm_kv, &full[slot], 64 * c, row, cb);
+              else tma_load_3d(smem + slot * kLtcChunk, &tm_pe, &full[slot], 0, row, cb);
+            } else {
+              mbar_arrive(&full[slot]);   // an empty use completes its phase at once
+            }
+            last_phase = (last_phase & ~(1u << slot)) | (ph << slot);
           }
         }
       }
-      // every issued copy lands before the CTA may exit (chunks go out in
-      // slot order, so slots past the first unissued one hold the previous tile)
-      if (issued_any) {
-        for (int c = 0; c < NCH; ++c)
-          mbar_wait_bounded(&full[c], (last_phase >> c) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
-      }
+      // every issued copy lands before the CTA may exit
+      const uint32_t used = g < (uint32_t)kLtcSlots ? g : (uint32_t)kLtcSlots;
+      for (uint32_t sl = 0; sl < used; ++sl)
+        mbar_wait_bounded(&full[sl], (last_phase >> sl) & 1u, nullptr, status, DSV3_ERR_WAIT_FULL);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -180,7 +196,7 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
       constexpr uint32_t I_O = idesc_bf16_f32(128, 16, 1, 0);    // O^T += V^T P^T (V^T read MN-major)
       const uint32_t base = smem_u32(smem);
       const uint32_t q_s = base + C::OFF_Q, p_s = base + C::OFF_P;
-      uint32_t tiles = 0, items_done = 0;
+      uint32_t g = 0, tiles = 0, items_done = 0;
       bool ok = true, issued_any = false;
       for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
         int b, hg, split, r0, r1, nt;
@@ -190,23 +206,28 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
         tc_fence_after();
         for (int t = 0; t < nt; ++t, ++tiles) {
           const uint32_t ph = tiles & 1u;
+          // S pass: S^T += chunk . Q^T(chunk), each slot released by the commit after its MMAs
           uint32_t acc = 0;
-          for (int c = 0; c < NCH; ++c) {
-            if (!mbar_wait_bounded(&full[c], ph, abort_flag, status, DSV3_ERR_WAIT_FULL)) {
+          for (int v = 0; v < NCL + 2; ++v, ++g) {
+            const int slot = g % kLtcSlots;
+            if (!mbar_wait_bounded(&full[slot], (g / kLtcSlots) & 1u, abort_flag, status, DSV3_ERR_WAIT_FULL)) {
               ok = false;
               break;
             }
             tc_fence_after();
+            const int c = use_chunk(v);
+            if (use_loads(v)) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              umma_bf16(tmem, smem_desc_sw128(base + c * kLtcChunk + kk * 32, 16, 1024),
-                        smem_desc_sw128(q_s + c * kLtcQChunk + kk * 32, 16, 1024), I_S, acc);
-              acc = 1;
+              for (int kk = 0; kk < 4; ++kk) {
+                umma_bf16(tmem, smem_desc_sw128(base + slot * kLtcChunk + kk * 32, 16, 1024),
+                          smem_desc_sw128(q_s + c * kLtcQChunk + kk * 32, 16, 1024), I_S, acc);
+                acc = 1;
+              }
+              issued_any = true;
             }
-            issued_any = true;
+            umma_commit(&empty[slot]);
           }
           if (!ok) break;
-          umma_commit(&empty[NCL]);   // the rope chunk is free once S^T is done
           umma_commit(s_full);
           if (!mbar_wait_bounded(p_full, ph, abort_flag, status, DSV3_ERR_WAIT_FULL)) {
             ok = false;
@@ -219,18 +240,29 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
             }
           }
           tc_fence_after();
+          // PV pass: output block m reads latent chunks 2m, 2m+1 from slots s, s+1
 #pragma unroll 1
-          for (int m = 0; m < NMB; ++m) {
+          for (int m = 0; m < NMB && ok; ++m, g += 2) {
+            const int slot = g % kLtcSlots;   // even
+            const uint32_t sph = (g / kLtcSlots) & 1u;
+            if (!mbar_wait_bounded(&full[slot], sph, abort_flag, status, DSV3_ERR_WAIT_FULL) ||
+                !mbar_wait_bounded(&full[slot + 1], sph, abort_flag, status, DSV3_ERR_WAIT_FULL)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
               umma_bf16(tmem + 32 + 16 * m,
-                        smem_desc_sw128(base + 2 * m * kLtcChunk + kk * 2048, kLtcChunk, 1024),
+                        smem_desc_sw128(base + slot * kLtcChunk + kk * 2048, kLtcChunk, 1024),
                         smem_desc_sw128(p_s + (kk >> 2) * kLtcQChunk + (kk & 3) * 32, 16, 1024), I_O,
                         (t > 0 || kk > 0) ? 1u : 0u);
             }
-            umma_commit(&empty[2 * m]);
-            umma_commit(&empty[2 * m + 1]);
+            issued_any = true;
+            umma_commit(&empty[slot]);
+            umma_commit(&empty[slot + 1]);
           }
+          if (!ok) break;
           umma_commit(pv_done);
         }
         ++items_done;
@@ -257,11 +289,7 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
       int b, hg, split, r0, r1, nt;
       decode_item(it, b, hg, split, r0, r1, nt);
       const int h0 = hg * 16;
-      if (nt == 0) {   // nothing of this row's cache in this split
-        for (int i = tid; i < 16 * R; i += 128) {
-          const int h = h0 + i / R;
-          if (h < H) part_o[((size_t)(b * H + h) * nsplit + split) * R + i % R] = 0.f;
-        }
+      if (nt == 0) {   // nothing of this row's cache in this split (the merge skips its O)
         if (tid < 16 && h0 + tid < H) {
           part_m[(size_t)(b * H + h0 + tid) * nsplit + split] = -INFINITY;
           part_l[(size_t)(b * H + h0 + tid) * nsplit + split] = 0.f;
@@ -269,19 +297,28 @@ __global__ void __launch_bounds__(kLtcThreads, 1) latent_decode_tc_kernel(
         continue;
       }
       // queries of the 16 heads as NCH chunks of [16][64] (128-byte swizzle;
-      // zeros past H, past R and past dr)
-      for (int u = tid; u < 16 * NCH * 8; u += 128) {
-        const int c = u / 128, h = (u / 8) % 16, j = u % 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (h0 + h < H) {
-          const size_t qrow = (size_t)b * H + h0 + h;
-          if (c < NCL) {
-            if (64 * c + 8 * j < R) v = *reinterpret_cast<const uint4*>(q_lat + qrow * R + 64 * c + 8 * j);
-          } else if (8 * j < dr) {
-            v = *reinterpret_cast<const uint4*>(q_pe + qrow * dr + 8 * j);
+      // zeros past H, past R and past dr): thread tid moves 16-byte unit
+      // tid % 8 of head tid / 8 in every chunk, all loads issued before the
+      // first store
+      {
+        const int h = tid >> 3, j = tid & 7;
+        const bool hv = h0 + h < H;
+        const size_t qrow = (size_t)b * H + h0 + h;
+        uint4 v[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          v[c] = make_uint4(0, 0, 0, 0);
+          if (hv) {
+            if (c < NCL) {
+              if (64 * c + 8 * j < R) v[c] = *reinterpret_cast<const uint4*>(q_lat + qrow * R + 64 * c + 8 * j);
+            } else if (8 * j < dr) {
+              v[c] = *reinterpret_cast<const uint4*>(q_pe + qrow * dr + 8 * j);
+            }
           }
         }
-        *reinterpret_cast<uint4*>(q_sm + c * kLtcQChunk + h * 128 + ((j ^ (h & 7)) << 4)) = v;
+#pragma unroll
+        for (int c = 0; c < NCH; ++c)
+          *reinterpret_cast<uint4*>(q_sm + c * kLtcQChunk + h * 128 + ((j ^ (h & 7)) << 4)) = v[c];
       }
       fence_proxy_async_smem();
       __syncwarp();

@@ -131,8 +131,16 @@ def case_ce_bwd():
 
 
 def case_latent_decode():
-    """Tensor-core absorbed decode: 64 rows x 16 heads over a 4096-row latent cache (R 512 + rope 64)."""
+    """Warp-level (mma.sync) absorbed decode: 64 rows x 16 heads over a 4096-row latent cache (R 512 + rope 64)."""
     C = native()
+    prev = C.decode_tc(0)
+    try:
+        _decode_case(C)
+    finally:
+        C.decode_tc(prev)
+
+
+def _decode_case(C):
     B, H, R, dr, S = 64, 16, 512, 64, 4096
     q_lat, q_pe = _bf(B, H, R), _bf(B, H, dr)
     kv, pe = _bf(B, S, R), _bf(B, S, dr)
@@ -148,7 +156,7 @@ def case_latent_decode_tc():
     C = native()
     prev = C.decode_tc(1)
     try:
-        case_latent_decode()
+        _decode_case(C)
     finally:
         C.decode_tc(prev)
 
