@@ -476,6 +476,17 @@ void run_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, cons
 }
 
 
+// Causal tcgen05 kernels take, instead of a plain 1, the number of (batch,
+// head) rows per tile-order group: tiles run heaviest first within a group,
+// and a group's K/V (or Q/dO) rows, about 64 MB at most, stay in L2 while
+// its CTAs run.  0 = not causal.
+inline int causal_groups(bool causal, int BH, long rows, int dqk, int dv) {
+  if (!causal) return 0;
+  const long per_bh = std::max(1L, rows * (long)(dqk + dv) * 2);
+  const long g = (64L << 20) / per_bh;
+  return (int)std::max(1L, std::min((long)BH, g));
+}
+
 template <int NA, int NB, int DV>
 void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                    int q_off, double scale, bool causal, int H) {
@@ -509,7 +520,7 @@ void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
       }
       k2<<<dim3((Sq + 255) / 256, BH), 320, C2::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
           reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq, Sk, H, q_off,
-          (float)(scale * 1.4426950408889634), causal ? 1 : 0, status_ptr());
+          (float)(scale * 1.4426950408889634), causal_groups(causal, BH, Sk, (int)q.size(2), DV), status_ptr());
       C10_CUDA_KERNEL_LAUNCH_CHECK();
       return;
     }
@@ -533,7 +544,7 @@ void run_fwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   dim3 grid((Sq + 127) / 128, BH);
   kern<<<grid, 64 + 128 * wg, Cfg::SMEM, at::cuda::getCurrentCUDAStream()>>>(qa, qb, ka, kb, vm,
       reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Sq, Sk, H, q_off,
-      (float)(scale * 1.4426950408889634), causal ? 1 : 0, status_ptr());
+      (float)(scale * 1.4426950408889634), causal_groups(causal, BH, Sk, (int)q.size(2), DV), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -582,7 +593,7 @@ void run_bwd_sm100(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   dim3 grid((Sk + 127) / 128, BH);
   kern<<<grid, 320 + 128 * drain, Cfg::SMEM, st>>>(qa, qb, ka, kb, vm, dom, lse.data_ptr<float>(), delta.data_ptr<float>(),
       dq.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(), Sq, Sk, H, q_off,
-      (float)(scale * 1.4426950408889634), (float)scale, causal ? 1 : 0, status_ptr());
+      (float)(scale * 1.4426950408889634), (float)scale, causal_groups(causal, BH, Sq, (int)q.size(2), DV), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -631,10 +642,10 @@ void run_bwd_sm100_wide(const at::Tensor& q, const at::Tensor& k, const at::Tens
   }
   kkv<<<dim3((Sk + 127) / 128, BH), 320, Ckv::SMEM, st>>>(q64, q64b, k128, k128b, v128, do64, lse.data_ptr<float>(),
       delta.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(), Sq, Sk, H, q_off, sl2, sc,
-      causal ? 1 : 0, status_ptr());
+      causal_groups(causal, BH, Sq, (int)q.size(2), DV), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   kq<<<dim3((Sq + 127) / 128, BH), 320, Cq::SMEM, st>>>(q128, q128b, k128, k128b, v128, do128, lse.data_ptr<float>(),
-      delta.data_ptr<float>(), dq.data_ptr<float>(), Sq, Sk, H, q_off, sl2, sc, causal ? 1 : 0, status_ptr());
+      delta.data_ptr<float>(), dq.data_ptr<float>(), Sq, Sk, H, q_off, sl2, sc, causal_groups(causal, BH, Sk, (int)q.size(2), DV), status_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

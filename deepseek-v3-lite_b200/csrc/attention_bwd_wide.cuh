@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(320, 1)
   float* sLD = reinterpret_cast<float*>(smem + C::OFF_LD);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, n0 = blockIdx.x * 128;
+  int k_tile, bh;
+  fa_tile_order(causal, false, k_tile, bh);  // earlier key tiles are seen by more queries
+  const int n0 = k_tile * 128;
   const int b = bh / H, h = bh % H;
   // first 64-query sub-tile with a query that sees key n0 (key <= q + q_off)
   const int qstart = causal ? max(0, (n0 - q_off) / 64) : 0;
@@ -418,7 +420,9 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, m0 = blockIdx.x * 128;
+  int q_tile, bh;
+  fa_tile_order(causal, true, q_tile, bh);   // later query tiles see more keys
+  const int m0 = q_tile * 128;
   const int b = bh / H, h = bh % H;
   int n_blocks = (Sk + 127) / 128;
   if (causal) n_blocks = min(n_blocks, (q_off + m0 + 128 + 127) / 128);

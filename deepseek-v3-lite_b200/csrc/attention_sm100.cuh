@@ -54,6 +54,27 @@ struct FaCfg {
   static constexpr int SMEM = OFF_XR + XR_B + 1024;
 };
 
+// Causal grids: `causal` (nonzero) is the number of (batch, head) rows per
+// group.  Groups run one after another; inside a group tiles run heaviest
+// first across its rows (longest-processing-time order, so each group ends
+// on its shortest CTAs) while the group's K/V (or Q/dO) rows stay in L2.
+// Linear block L: group g = L / (G * T), then tile rank r / rows_g (0 =
+// heaviest) and row g * G + r % rows_g.  Non-causal grids keep
+// (blockIdx.x, blockIdx.y).
+__device__ __forceinline__ void fa_tile_order(int causal, bool heavy_last_index, int& tile, int& bh) {
+  tile = blockIdx.x;
+  bh = blockIdx.y;
+  if (causal > 0) {
+    const int T = gridDim.x, BH = gridDim.y, G = causal;
+    const int L = blockIdx.x + blockIdx.y * T;
+    const int g = L / (G * T), r = L - g * G * T;
+    const int rows = min(G, BH - g * G);
+    const int rank = r / rows;
+    tile = heavy_last_index ? T - 1 - rank : rank;
+    bh = g * G + r % rows;
+  }
+}
+
 template <int NA, int NB, int DV, int WG = 1>
 __global__ void __launch_bounds__(64 + 128 * WG, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQa, const __grid_constant__ CUtensorMap tmQb,
@@ -87,7 +108,9 @@ __global__ void __launch_bounds__(64 + 128 * WG, 1)
   float* xr = reinterpret_cast<float*>(smem + C::OFF_XR);   // [2 parities][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, m0 = blockIdx.x * 128;
+  int q_tile, bh;
+  fa_tile_order(causal, true, q_tile, bh);   // later query tiles see more keys
+  const int m0 = q_tile * 128;
   int n_blocks = (Sk + 127) / 128;
   if (causal) n_blocks = min(n_blocks, (q_off + m0 + 128 + 127) / 128);
 
@@ -428,7 +451,9 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, m0 = blockIdx.x * 256;
+  int q_tile, bh;
+  fa_tile_order(causal, true, q_tile, bh);   // later query tiles see more keys
+  const int m0 = q_tile * 256;
   const int nk = (Sk + 127) / 128;
   // KV tiles each query tile attends to (0 when the tile lies past Sq)
   int nt[2];
@@ -762,7 +787,9 @@ __global__ void __launch_bounds__(320 + 128 * DRAIN, 1)
   float* sLD = reinterpret_cast<float*>(smem + C::OFF_LD);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, n0 = blockIdx.x * 128;
+  int k_tile, bh;
+  fa_tile_order(causal, false, k_tile, bh);  // earlier key tiles are seen by more queries
+  const int n0 = k_tile * 128;
   const int b = bh / H, h = bh % H;
   const int qstart = causal ? max(0, (n0 - q_off) / 128) : 0;
   const int nq = (Sq + 127) / 128;
