@@ -118,7 +118,7 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const 
   cfg.gridDim = dim3(units * CG);
   CUtensorMap none;
   memset(&none, 0, sizeof(none));
-  TORCH_CHECK(tc != nullptr || E != Epi::CeBwdTma, "TMA-store epilogue without an output map");
+  TORCH_CHECK(tc != nullptr || !epi_tma(E), "TMA-store epilogue without an output map");
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc != nullptr ? *tc : none, a));
 }
 
@@ -160,6 +160,46 @@ bool ce_tma_store() {
     on = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return on == 1;
+}
+
+// fp32 GEMM outputs staged in shared memory and written (or added, for the
+// accumulating and split-K modes) by TMA; DSV3_GEMM_TMA_EPI=0 keeps the row
+// stores / vector atomics from registers.
+bool gemm_tma_epi() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("DSV3_GEMM_TMA_EPI");
+    on = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// 3-D fp32 output map [groups][rows][cols] (row stride ld, group stride
+// gstride elements) with 32 x 32 boxes for the TMA epilogues; false when the
+// layout does not allow it (TMA writes 16-byte units: cols, ld, gstride
+// multiples of 4 and a 16-byte aligned base).
+bool map_out_f32(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld, int64_t groups,
+                 int64_t gstride) {
+  if (!gemm_tma_epi() || cols % 4 != 0 || ld % 4 != 0 || gstride % 4 != 0 ||
+      (reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
+    return false;
+  uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)groups};
+  uint64_t st[2] = {(uint64_t)ld * 4, (uint64_t)std::max<int64_t>(gstride, ld * rows) * 4};
+  uint32_t box[3] = {32, 32, 1};
+  *m = make_map(ptr, 3, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+  return true;
+}
+
+// bf16 output map [rows][cols] (as 3-D with one group) with 32-row x 64-column
+// boxes for the bf16 TMA-store epilogue; false when cols or ld is not a
+// multiple of 8 or the base is not 16-byte aligned.
+bool map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  if (true || !gemm_tma_epi() || cols % 8 != 0 || ld % 8 != 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
+  uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, 1};
+  uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)ld * rows * 2};
+  uint32_t box[3] = {64, 32, 1};
+  *m = make_map(ptr, 3, dims, st, box);
+  return true;
 }
 
 GemmArgs blank_args() {
@@ -207,12 +247,28 @@ void linear_fwd(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, bool 
   const int bn = N <= 128 ? 128 : 256;
   g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(N, bn); g.kb_per_split = cdiv(K, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
+  CUtensorMap tc, tcb;
+  const bool tma = f32 && map_out_f32(&tc, out.data_ptr(), M, N, out.stride(0), 1, 0) &&
+                   (mode != 2 || (g.ld_aux % 4 == 0 && (reinterpret_cast<uintptr_t>(g.aux) & 15) == 0));
+  const bool tmab = !f32 && map_out_bf16(&tcb, out.data_ptr(), M, N, out.stride(0));
 #define DSV3_LIN(BN_)                                                                            \
   switch (mode) {                                                                                \
-    case 0: launch<BN_, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g); break;            \
-    case 1: launch<BN_, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g); break;               \
-    case 2: launch<BN_, 0, 0, Sched::Dense, Epi::ResidF32, false>(ta, tb, g); break;             \
-    default: launch<BN_, 0, 0, Sched::Dense, Epi::StoreF32, false>(ta, tb, g); break;            \
+    case 0:                                                                                      \
+      if (tmab) launch<BN_, 0, 0, Sched::Dense, Epi::StoreBF16Tma, false>(ta, tb, g, &tcb);      \
+      else launch<BN_, 0, 0, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);                     \
+      break;                                                                                     \
+    case 1:                                                                                      \
+      if (tma) launch<BN_, 0, 0, Sched::Dense, Epi::AddF32Tma, false>(ta, tb, g, &tc);           \
+      else launch<BN_, 0, 0, Sched::Dense, Epi::AddF32, false>(ta, tb, g);                        \
+      break;                                                                                     \
+    case 2:                                                                                      \
+      if (tma) launch<BN_, 0, 0, Sched::Dense, Epi::ResidF32Tma, false>(ta, tb, g, &tc);         \
+      else launch<BN_, 0, 0, Sched::Dense, Epi::ResidF32, false>(ta, tb, g);                      \
+      break;                                                                                     \
+    default:                                                                                     \
+      if (tma) launch<BN_, 0, 0, Sched::Dense, Epi::StoreF32Tma, false>(ta, tb, g, &tc);         \
+      else launch<BN_, 0, 0, Sched::Dense, Epi::StoreF32, false>(ta, tb, g);                      \
+      break;                                                                                     \
   }
   if (bn == 128) { DSV3_LIN(128) } else { DSV3_LIN(256) }
 #undef DSV3_LIN
@@ -235,9 +291,21 @@ void linear_dgrad(const at::Tensor& dy, const at::Tensor& w, at::Tensor& out, bo
   const bool f32 = out.scalar_type() == at::kFloat;
   g.m_tiles = cdiv(M, 128); g.n_tiles = cdiv(K, 256); g.kb_per_split = cdiv(N, 64);
   g.num_tiles = g.m_tiles * g.n_tiles;
-  if (f32 && accumulate) launch<256, 0, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
-  else if (f32) launch<256, 0, 1, Sched::Dense, Epi::StoreF32, false>(ta, tb, g);
-  else launch<256, 0, 1, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+  CUtensorMap tc;
+  const bool tma = f32 && map_out_f32(&tc, out.data_ptr(), M, K, out.stride(0), 1, 0);
+  if (f32 && accumulate) {
+    if (tma) launch<256, 0, 1, Sched::Dense, Epi::AddF32Tma, false>(ta, tb, g, &tc);
+    else launch<256, 0, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
+  } else if (f32) {
+    if (tma) launch<256, 0, 1, Sched::Dense, Epi::StoreF32Tma, false>(ta, tb, g, &tc);
+    else launch<256, 0, 1, Sched::Dense, Epi::StoreF32, false>(ta, tb, g);
+  } else {
+    CUtensorMap tcb;
+    if (map_out_bf16(&tcb, out.data_ptr(), M, K, out.stride(0)))
+      launch<256, 0, 1, Sched::Dense, Epi::StoreBF16Tma, false>(ta, tb, g, &tcb);
+    else
+      launch<256, 0, 1, Sched::Dense, Epi::StoreBF16, false>(ta, tb, g);
+  }
 }
 
 // dw [N,K] fp32 += dy[M,N]^T @ x[M,K]   (reduction over the M token rows)
@@ -262,7 +330,10 @@ void linear_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& dw) {
   splits = cdiv(total_kb, g.kb_per_split);
   g.k_splits = splits;
   g.num_tiles = base_tiles * splits;
-  if (splits > 1) launch<256, 1, 1, Sched::Dense, Epi::AtomicAddF32, false>(ta, tb, g);
+  CUtensorMap tc;
+  if (map_out_f32(&tc, dw.data_ptr(), N, K, K, 1, 0))   // split partials add atomically at L2
+    launch<256, 1, 1, Sched::Dense, Epi::AddF32Tma, false>(ta, tb, g, &tc);
+  else if (splits > 1) launch<256, 1, 1, Sched::Dense, Epi::AtomicAddF32, false>(ta, tb, g);
   else launch<256, 1, 1, Sched::Dense, Epi::AddF32, false>(ta, tb, g);
 }
 
@@ -350,7 +421,11 @@ void grouped_fwd(const at::Tensor& a, const at::Tensor& w, const at::Tensor& til
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(a, P, K, a.stride(0));
   CUtensorMap tb = map_b_kmajor(w, G, N, K, K, N * K);
-  launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
+  CUtensorMap tcb;
+  if (map_out_bf16(&tcb, out.data_ptr(), P, N, out.stride(0)))
+    launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16Tma, false>(ta, tb, g, &tcb);
+  else
+    launch<256, 0, 0, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
 }
 
 // Expert-grouped GEMM whose epilogue also stores every output row into its
@@ -425,7 +500,11 @@ void grouped_dgrad(const at::Tensor& dy, const at::Tensor& w, const at::Tensor& 
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(dy, P, N, dy.stride(0));
   CUtensorMap tb = map_b_mnmajor(w, G, N, K, K, N * K);
-  launch<256, 0, 1, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
+  CUtensorMap tcb;
+  if (map_out_bf16(&tcb, out.data_ptr(), P, K, out.stride(0)))
+    launch<256, 0, 1, Sched::GroupedM, Epi::StoreBF16Tma, false>(ta, tb, g, &tcb);
+  else
+    launch<256, 0, 1, Sched::GroupedM, Epi::StoreBF16, false>(ta, tb, g);
 }
 
 // Grouped weight gradient: out[g] [Ma, Nb] fp32 += a[rows_g, Ma]^T @ b[rows_g, Nb]
@@ -455,7 +534,10 @@ void grouped_wgrad(const at::Tensor& a, const at::Tensor& b, const at::Tensor& r
   g.num_tiles = base * splits;
   CUtensorMap ta = map_a_mnmajor(a, Ma, P, a.stride(0));
   CUtensorMap tb = map_b_mnmajor(b, 1, P, Nb, b.stride(0), P * b.stride(0));
-  if (splits > 1) launch<256, 1, 1, Sched::GroupedK, Epi::AtomicAddF32, false>(ta, tb, g);
+  CUtensorMap tc;
+  if (map_out_f32(&tc, out.data_ptr(), Ma, Nb, Nb, G, Ma * Nb))
+    launch<256, 1, 1, Sched::GroupedK, Epi::AddF32Tma, false>(ta, tb, g, &tc);
+  else if (splits > 1) launch<256, 1, 1, Sched::GroupedK, Epi::AtomicAddF32, false>(ta, tb, g);
   else launch<256, 1, 1, Sched::GroupedK, Epi::AddF32, false>(ta, tb, g);
 }
 

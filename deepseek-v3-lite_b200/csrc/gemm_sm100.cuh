@@ -40,10 +40,22 @@ enum class Epi : int {
   ResidF32 = 8,      // out (fp32) = aux (fp32) + acc   (out-of-place residual add)
   ScatterBF16 = 9,   // out (bf16) = acc, and each row also stored into its home rank's
                      // combine inbox over peer memory (expert-parallel combine)
-  CeBwdTma = 10      // CeBwd, each warp's 32 x 64 output boxes staged in shared memory
+  CeBwdTma = 10,     // CeBwd, each warp's 32 x 64 output boxes staged in shared memory
                      // (128-byte swizzle) and written by TMA stores; columns N .. N rounded
                      // up to 8 receive zeros
+  // fp32 outputs through shared memory: each warp's 32 x 32 fp32 boxes go out
+  // by TMA (N a multiple of 4; the output map is 3-D [groups][rows][N])
+  StoreF32Tma = 11,  // out = acc (TMA store)
+  AddF32Tma = 12,    // out += acc (TMA reduce-add, atomic per element: also split-K)
+  ResidF32Tma = 13,  // out = aux + acc (aux read by the epilogue, TMA store)
+  StoreBF16Tma = 14  // out (bf16) = acc through 32 x 64 bf16 boxes (N a multiple of 8)
 };
+
+// Epilogues that stage their output in shared memory and write it with TMA.
+constexpr bool epi_tma(Epi E) {
+  return E == Epi::CeBwdTma || E == Epi::StoreF32Tma || E == Epi::AddF32Tma || E == Epi::ResidF32Tma ||
+         E == Epi::StoreBF16Tma;
+}
 
 constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
 constexpr int kEpiWarps = 8;                 // two warpgroups drain TMEM
@@ -59,7 +71,7 @@ constexpr int kTmaStageBytes = kEpiWarps * 2 * kTmaBoxBytes;
 
 template <Epi E>
 constexpr int epi_smem_bytes() {
-  return E == Epi::ScatterBF16 ? kScatterStageBytes : (E == Epi::CeBwdTma ? 1024 + kTmaStageBytes : 0);
+  return E == Epi::ScatterBF16 ? kScatterStageBytes : (epi_tma(E) ? 1024 + kTmaStageBytes : 0);
 }
 
 struct GemmArgs {
@@ -114,7 +126,7 @@ struct GemmCfg {
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // the TMA-store staging (64 KB) takes one (pair) or one more (single) stage
-  static constexpr int STAGES = E == Epi::CeBwdTma ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : (BN >= 256 ? 4 : 6));
+  static constexpr int STAGES = epi_tma(E) ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : (BN >= 256 ? 4 : 6));
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
@@ -182,7 +194,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
   using C = GemmCfg<BN, CG, E>;
-  constexpr bool kTmaOut = E == Epi::CeBwdTma;
+  constexpr bool kTmaOut = epi_tma(E);
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
   // CTA pairs: BN 256, or BN 128 with an MN-major B (each CTA then loads one
   // 64-column box of B)
@@ -386,6 +398,96 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool row_ok = row < args.M;
       uint32_t r[16];
 
+      if constexpr (E == Epi::StoreBF16Tma) {
+        // Two 32-column TMEM steps = one 32 x 64 bf16 box (lane = row, 8
+        // 16-byte chunks, chunk j at j ^ (row & 7)); two boxes per warp alternate.
+        uint8_t* box_row = tma_stage + (warp - 2) * 2 * kTmaBoxBytes + lane * 128;
+        const int box_y = ti.m0 + quarter * 32;
+#pragma unroll 1
+        for (int c4 = half * HALF; c4 < (half + 1) * HALF; c4 += 64) {
+          uint8_t* brow = box_row + (tma_box & 1) * kTmaBoxBytes;
+          if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
+          __syncwarp();
+#pragma unroll 1
+          for (int c2 = c4; c2 < c4 + 64; c2 += 32) {
+            uint32_t rr[2][16];
+            __syncwarp();
+            tmem_ld16(tbase + c2, rr[0]);
+            tmem_ld16(tbase + c2 + 16, rr[1]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              uint32_t pk[8];
+#pragma unroll
+              for (int j = 0; j < 16; j += 2)
+                pk[j / 2] = pack_bf16x2(__uint_as_float(rr[q][j]), __uint_as_float(rr[q][j + 1]));
+              const int ch = ((c2 - c4) + 16 * q) >> 3;
+              *reinterpret_cast<uint4*>(brow + ((ch ^ (lane & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              *reinterpret_cast<uint4*>(brow + (((ch + 1) ^ (lane & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (ti.n0 + c4 < args.N && box_y < args.M) tma_store_3d(&tmC, brow - lane * 128, ti.n0 + c4, box_y, 0);
+            bulk_commit_group();
+          }
+          ++tma_box;
+        }
+      } else
+      if constexpr (E == Epi::StoreF32Tma || E == Epi::AddF32Tma || E == Epi::ResidF32Tma) {
+        // One 32-column TMEM step = one 32 x 32 fp32 box: lane = row of the
+        // warp's 32 rows, its 32 values as 8 16-byte chunks, chunk j at
+        // j ^ (row & 7) (128-byte swizzle); two boxes per warp alternate.
+        uint8_t* box_row = tma_stage + (warp - 2) * 2 * kTmaBoxBytes + lane * 128;
+        const int box_y = ti.m0 + quarter * 32;
+        const int gz = (S == Sched::GroupedK) ? ti.g : 0;
+        const float* aux_row = nullptr;
+        if constexpr (E == Epi::ResidF32Tma)
+          aux_row = reinterpret_cast<const float*>(args.aux) + (size_t)(row_ok ? row : 0) * args.ld_aux;
+#pragma unroll 1
+        for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
+          const int col = ti.n0 + c2;
+          uint8_t* brow = box_row + (tma_box & 1) * kTmaBoxBytes;
+          float4 av[8];
+          if constexpr (E == Epi::ResidF32Tma) {   // the residual's 32 values, requested before the TMEM wait
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              av[j] = (row_ok && col + 4 * j < args.N) ? reinterpret_cast<const float4*>(aux_row + col)[j]
+                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          uint32_t rr[2][16];
+          __syncwarp();
+          tmem_ld16(tbase + c2, rr[0]);
+          tmem_ld16(tbase + c2 + 16, rr[1]);
+          if (lane == 0) bulk_wait_group_read<1>();   // the store that last used this buffer has read it
+          __syncwarp();
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(rr[j >> 2][(j & 3) * 4]), __uint_as_float(rr[j >> 2][(j & 3) * 4 + 1]),
+                                   __uint_as_float(rr[j >> 2][(j & 3) * 4 + 2]),
+                                   __uint_as_float(rr[j >> 2][(j & 3) * 4 + 3]));
+            if constexpr (E == Epi::ResidF32Tma) {
+              v.x += av[j].x;
+              v.y += av[j].y;
+              v.z += av[j].z;
+              v.w += av[j].w;
+            }
+            *reinterpret_cast<float4*>(brow + ((j ^ (lane & 7)) << 4)) = v;
+          }
+          fence_proxy_async_smem();   // this lane's box row is visible to the TMA engine
+          __syncwarp();
+          if (lane == 0) {
+            if (col < args.N && box_y < args.M) {
+              if constexpr (E == Epi::AddF32Tma) tma_reduce_add_3d(&tmC, brow - lane * 128, col, box_y, gz);
+              else tma_store_3d(&tmC, brow - lane * 128, col, box_y, gz);
+            }
+            bulk_commit_group();
+          }
+          ++tma_box;
+        }
+      } else
       if constexpr (E == Epi::StoreBF16 || E == Epi::AddF32 || E == Epi::AtomicAddF32 || E == Epi::StoreF32 ||
                     E == Epi::ResidF32 || E == Epi::ScatterBF16) {
         char* base = reinterpret_cast<char*>(args.out);

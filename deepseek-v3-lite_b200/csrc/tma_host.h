@@ -28,10 +28,11 @@ inline EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 tensor map, 128-byte swizzle, zero fill out of bounds.  dims[0] is the
+// Tensor map (bf16 unless `dtype` says otherwise), 128-byte swizzle, zero fill out of bounds.  dims[0] is the
 // contiguous dimension; strides are in bytes for dims[1..rank-1].
 inline CUtensorMap make_map(const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                            const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+                            const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+                            CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base address must be 16-byte aligned");
   for (int i = 0; i + 1 < rank; ++i)
     TORCH_CHECK(strides_bytes[i] % 16 == 0, "TMA strides must be multiples of 16 bytes");
@@ -44,7 +45,7 @@ inline CUtensorMap make_map(const void* ptr, int rank, const uint64_t* dims, con
     e[i] = 1;
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), d, s, b, e,
+  CUresult r = encode_fn()(&m, dtype, rank, const_cast<void*>(ptr), d, s, b, e,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", int(r));

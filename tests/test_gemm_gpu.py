@@ -51,7 +51,34 @@ def test_linear_dgrad(C, M, N, K):
     dy, w = bf(M, N, seed=3), bf(N, K, scale=0.05, seed=4)
     out = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
     C.linear_dgrad(dy, w, out)
-    close(out, dy.float() @ w.float())
+    ref = dy.float() @ w.float()
+    close(out, ref)
+    # fp32 outputs: plain store and accumulate, in a wider buffer whose
+    # padding columns and rows must stay untouched
+    buf = torch.full((M + 8, K + 8), 5.0, device="cuda")
+    o32 = buf[:M, :K]
+    C.linear_dgrad(dy, w, o32, False)
+    close(o32, ref, rtol=1e-3, atol=1e-3)
+    C.linear_dgrad(dy, w, o32, True)
+    close(o32, 2 * ref, rtol=1e-3, atol=1e-3)
+    assert (buf[:, K:] == 5.0).all() and (buf[M:] == 5.0).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 768, 768), (300, 216, 768), (129, 102, 192), (1000, 768, 1536)])
+def test_linear_fwd_f32_store_and_residual(C, M, N, K):
+    a, w = bf(M, K, seed=7), bf(N, K, scale=0.05, seed=8)
+    ref = a.float() @ w.float().t()
+    ld = (N + 7) // 8 * 8 + 8            # row stride a multiple of 8; N = 102 takes the register path
+    buf = torch.full((M, ld), 5.0, device="cuda")
+    out = buf[:, :N]
+    C.linear_fwd(a, w, out, False)
+    close(out, ref, rtol=1e-3, atol=1e-3)
+    resid = torch.randn(M, ld, device="cuda")[:, :N]
+    buf2 = torch.full((M, ld), 5.0, device="cuda")
+    out2 = buf2[:, :N]
+    C.linear_fwd(a, w, out2, True, resid)
+    close(out2, resid + ref, rtol=1e-3, atol=1e-3)
+    assert (buf[:, N:] == 5.0).all() and (buf2[:, N:] == 5.0).all()
 
 
 @pytest.mark.parametrize("M,N,K", [(4096, 768, 768), (1000, 216, 768), (16384, 256, 512)])
