@@ -194,7 +194,7 @@ bool map_out_f32(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t 
 // boxes for the bf16 TMA-store epilogue; false when cols or ld is not a
 // multiple of 8 or the base is not 16-byte aligned.
 bool map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t ld) {
-  if (true || !gemm_tma_epi() || cols % 8 != 0 || ld % 8 != 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
+  if (!gemm_tma_epi() || cols % 8 != 0 || ld % 8 != 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
   uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, 1};
   uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)ld * rows * 2};
   uint32_t box[3] = {64, 32, 1};
