@@ -82,7 +82,8 @@ bool use_pairs() {
 
 // tc: the output's tensor map for the TMA-store epilogues (unused otherwise)
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW, int CG>
-void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr) {
+void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr,
+               const CUtensorMap* td = nullptr) {
   using C = GemmCfg<BN, CG, E>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, S, E, SW, CG>;
   constexpr int kSmem = C::SMEM_BYTES + epi_smem_bytes<E>();
@@ -119,11 +120,13 @@ void launch_cg(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const 
   CUtensorMap none;
   memset(&none, 0, sizeof(none));
   TORCH_CHECK(tc != nullptr || !epi_tma(E), "TMA-store epilogue without an output map");
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc != nullptr ? *tc : none, a));
+  TORCH_CHECK(td != nullptr || E != Epi::SwigluFwdTma, "SwiGLU TMA epilogue without the gate / up map");
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc != nullptr ? *tc : none, td != nullptr ? *td : none, a));
 }
 
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool SW>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr) {
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUtensorMap* tc = nullptr,
+            const CUtensorMap* td = nullptr) {
   if constexpr (BN == 256 || (BN == 128 && B_MN)) {
     // row-grouped tiles may pair only when every expert range is 256-aligned
     const bool grouping_ok = S != Sched::GroupedM || a.tile_rows == 256;
@@ -131,11 +134,11 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& a, const CUt
       GemmArgs b = a;                      // re-tile the rows in 256-row pair tiles
       b.m_tiles = cdiv(a.M, 256);
       b.num_tiles = a.num_tiles / a.m_tiles * b.m_tiles;
-      launch_cg<BN, A_MN, B_MN, S, E, SW, 2>(ta, tb, b, tc);
+      launch_cg<BN, A_MN, B_MN, S, E, SW, 2>(ta, tb, b, tc, td);
       return;
     }
   }
-  launch_cg<BN, A_MN, B_MN, S, E, SW, 1>(ta, tb, a, tc);
+  launch_cg<BN, A_MN, B_MN, S, E, SW, 1>(ta, tb, a, tc, td);
 }
 
 // LM-head tiles walk 16,384-row panels, rows fastest: the panel's hidden rows
@@ -198,6 +201,17 @@ bool map_out_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t cols, int64_t
   uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, 1};
   uint64_t st[2] = {(uint64_t)ld * 2, (uint64_t)ld * rows * 2};
   uint32_t box[3] = {64, 32, 1};
+  *m = make_map(ptr, 3, dims, st, box);
+  return true;
+}
+
+// bf16 [rows][2][I] map of a gate / up pair buffer (row stride ld, the up half
+// I columns after the gate half) with 32-row x 64-column boxes.
+bool map_pair_bf16(CUtensorMap* m, void* ptr, int64_t rows, int64_t I, int64_t ld) {
+  if (!gemm_tma_epi() || I % 64 != 0 || ld % 8 != 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return false;
+  uint64_t dims[3] = {(uint64_t)I, 2, (uint64_t)rows};
+  uint64_t st[2] = {(uint64_t)I * 2, (uint64_t)ld * 2};
+  uint32_t box[3] = {64, 1, 32};
   *m = make_map(ptr, 3, dims, st, box);
   return true;
 }
@@ -359,14 +373,20 @@ void swiglu_fwd(const at::Tensor& x, const at::Tensor& w13, const at::Tensor& ti
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(x, P, D, x.stride(0));
   CUtensorMap tb = map_b_swiglu(w13, G, I, D);
+  // h and the gate / up pair leave through shared memory and TMA where the maps fit
+  CUtensorMap tc, td;
+  const bool tma = map_out_bf16(&tc, h.data_ptr(), P, I, h.stride(0)) &&
+                   map_pair_bf16(&td, gu.data_ptr(), P, I, gu.stride(0));
   if (tile_group.numel() > 0) {
     TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.numel() >= g.m_tiles, "tile_group: int32 [tiles]");
     g.tile_group = tile_group.data_ptr<int>();
     g.tile_rows = (int)group_rows;
-    launch<256, 0, 0, Sched::GroupedM, Epi::SwigluFwd, true>(ta, tb, g);
+    if (tma) launch<256, 0, 0, Sched::GroupedM, Epi::SwigluFwdTma, true>(ta, tb, g, &tc, &td);
+    else launch<256, 0, 0, Sched::GroupedM, Epi::SwigluFwd, true>(ta, tb, g);
   } else {
     TORCH_CHECK(G == 1, "dense SwiGLU expects one weight group");
-    launch<256, 0, 0, Sched::Dense, Epi::SwigluFwd, true>(ta, tb, g);
+    if (tma) launch<256, 0, 0, Sched::Dense, Epi::SwigluFwdTma, true>(ta, tb, g, &tc, &td);
+    else launch<256, 0, 0, Sched::Dense, Epi::SwigluFwd, true>(ta, tb, g);
   }
 }
 
@@ -392,14 +412,26 @@ void swiglu_dgrad(const at::Tensor& dy, const at::Tensor& w2, const at::Tensor& 
   g.num_tiles = g.m_tiles * g.n_tiles;
   CUtensorMap ta = map_a_kmajor(dy, P, D, dy.stride(0));
   CUtensorMap tb = map_b_mnmajor(w2, G, D, I, I, D * I);
+  CUtensorMap tc;   // dg / du through shared memory and TMA where the map fits
+  const bool tma = map_pair_bf16(&tc, dgu.data_ptr(), P, I, dgu.stride(0));
   if (tile_group.numel() > 0) {
     g.tile_group = tile_group.data_ptr<int>();
     g.tile_rows = (int)group_rows;
-    if (bn == 128) launch<128, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
-    else launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+    if (tma) {
+      if (bn == 128) launch<128, 0, 1, Sched::GroupedM, Epi::SwigluBwdTma, false>(ta, tb, g, &tc);
+      else launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwdTma, false>(ta, tb, g, &tc);
+    } else {
+      if (bn == 128) launch<128, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+      else launch<256, 0, 1, Sched::GroupedM, Epi::SwigluBwd, false>(ta, tb, g);
+    }
   } else {
-    if (bn == 128) launch<128, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
-    else launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+    if (tma) {
+      if (bn == 128) launch<128, 0, 1, Sched::Dense, Epi::SwigluBwdTma, false>(ta, tb, g, &tc);
+      else launch<256, 0, 1, Sched::Dense, Epi::SwigluBwdTma, false>(ta, tb, g, &tc);
+    } else {
+      if (bn == 128) launch<128, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+      else launch<256, 0, 1, Sched::Dense, Epi::SwigluBwd, false>(ta, tb, g);
+    }
   }
 }
 

@@ -48,13 +48,15 @@ enum class Epi : int {
   StoreF32Tma = 11,  // out = acc (TMA store)
   AddF32Tma = 12,    // out += acc (TMA reduce-add, atomic per element: also split-K)
   ResidF32Tma = 13,  // out = aux + acc (aux read by the epilogue, TMA store)
-  StoreBF16Tma = 14  // out (bf16) = acc through 32 x 64 bf16 boxes (N a multiple of 8)
+  StoreBF16Tma = 14, // out (bf16) = acc through 32 x 64 bf16 boxes (N a multiple of 8)
+  SwigluFwdTma = 15, // SwigluFwd with h (map C) and the gate / up pair (map D, [rows][2][I]) by TMA
+  SwigluBwdTma = 16  // SwigluBwd with dg / du (map C, [rows][2][I]) by TMA
 };
 
 // Epilogues that stage their output in shared memory and write it with TMA.
 constexpr bool epi_tma(Epi E) {
   return E == Epi::CeBwdTma || E == Epi::StoreF32Tma || E == Epi::AddF32Tma || E == Epi::ResidF32Tma ||
-         E == Epi::StoreBF16Tma;
+         E == Epi::StoreBF16Tma || E == Epi::SwigluFwdTma || E == Epi::SwigluBwdTma;
 }
 
 constexpr float kLog2e = 1.4426950408889634f;   // log2(e)
@@ -69,9 +71,14 @@ constexpr int kScatterStageBytes = kEpiWarps * 32 * 128;
 constexpr int kTmaBoxBytes = 32 * 128;
 constexpr int kTmaStageBytes = kEpiWarps * 2 * kTmaBoxBytes;
 
+// SwigluFwdTma: three boxes per warp (h, g, u of one 64-column half tile)
+constexpr int kSwigluStageBytes = kEpiWarps * 3 * kTmaBoxBytes;
+
 template <Epi E>
 constexpr int epi_smem_bytes() {
-  return E == Epi::ScatterBF16 ? kScatterStageBytes : (epi_tma(E) ? 1024 + kTmaStageBytes : 0);
+  return E == Epi::ScatterBF16 ? kScatterStageBytes
+                               : (E == Epi::SwigluFwdTma ? 1024 + kSwigluStageBytes
+                                                         : (epi_tma(E) ? 1024 + kTmaStageBytes : 0));
 }
 
 struct GemmArgs {
@@ -126,7 +133,8 @@ struct GemmCfg {
   static constexpr int B_BYTES = (BN / CG) * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   // the TMA-store staging (64 KB) takes one (pair) or one more (single) stage
-  static constexpr int STAGES = epi_tma(E) ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : (BN >= 256 ? 4 : 6));
+  static constexpr int STAGES = E == Epi::SwigluFwdTma ? (CG == 2 ? 4 : 2)
+                                : (epi_tma(E) ? (CG == 2 ? 5 : 3) : (CG == 2 ? 6 : (BN >= 256 ? 4 : 6)));
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + BAR_BYTES;
@@ -192,7 +200,8 @@ __device__ __forceinline__ TileInfo decode_tile(int t, const GemmArgs& a, int BN
 template <int BN, int A_MN, int B_MN, Sched S, Epi E, bool B_SWIGLU, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                      GemmArgs args) {
   using C = GemmCfg<BN, CG, E>;
   constexpr bool kTmaOut = epi_tma(E);
   static_assert(!B_SWIGLU || (BN == 256 && !B_MN), "SwiGLU B layout needs BN=256, K-major");
@@ -235,6 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if constexpr (kTmaOut) tma_prefetch_desc(&tmC);
+    if constexpr (E == Epi::SwigluFwdTma) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     if constexpr (CG == 2) {
@@ -617,10 +627,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-      } else if constexpr (E == Epi::SwigluFwd) {
+      } else if constexpr (E == Epi::SwigluFwd || E == Epi::SwigluFwdTma) {
         // TMEM columns [0,128): gate, [128,256): up, for I-columns n0 .. n0+127.
+        // SwigluFwdTma: this warp's 64 columns of h, g and u go to three
+        // 32 x 64 boxes (lane = row, chunk j at j ^ (row & 7)), then TMA.
+        constexpr bool kT = E == Epi::SwigluFwdTma;
         __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(args.out);
         __nv_bfloat16* gu = reinterpret_cast<__nv_bfloat16*>(args.out2);
+        uint8_t* hbox = tma_stage + (warp - 2) * 3 * kTmaBoxBytes + lane * 128;
+        if constexpr (kT) {
+          if (lane == 0) bulk_wait_group_read<0>();   // the previous tile's stores have read the boxes
+          __syncwarp();
+        }
         uint32_t u[16];
 #pragma unroll 1
         for (int c = half * 64; c < half * 64 + 64; c += 16) {
@@ -629,7 +647,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld16(tbase + 128 + c, u);
           tmem_ld_wait();
           const int col = ti.n0 + c;
-          if (!row_ok || col >= args.N) continue;
+          if (!kT && (!row_ok || col >= args.N)) continue;
           const int nv = min(16, args.N - col);
           uint32_t hp[8], gp[8], up[8];
 #pragma unroll
@@ -643,6 +661,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             hp[j / 2] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
             gp[j / 2] = pack_bf16x2(g0, g1);
             up[j / 2] = pack_bf16x2(u0, u1);
+          }
+          if constexpr (kT) {
+            const int ch = (c - half * 64) >> 3;
+            const int o0 = (ch ^ (lane & 7)) << 4, o1 = ((ch + 1) ^ (lane & 7)) << 4;
+            *reinterpret_cast<uint4*>(hbox + o0) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+            *reinterpret_cast<uint4*>(hbox + o1) = make_uint4(hp[4], hp[5], hp[6], hp[7]);
+            *reinterpret_cast<uint4*>(hbox + kTmaBoxBytes + o0) = make_uint4(gp[0], gp[1], gp[2], gp[3]);
+            *reinterpret_cast<uint4*>(hbox + kTmaBoxBytes + o1) = make_uint4(gp[4], gp[5], gp[6], gp[7]);
+            *reinterpret_cast<uint4*>(hbox + 2 * kTmaBoxBytes + o0) = make_uint4(up[0], up[1], up[2], up[3]);
+            *reinterpret_cast<uint4*>(hbox + 2 * kTmaBoxBytes + o1) = make_uint4(up[4], up[5], up[6], up[7]);
+            continue;
           }
           __nv_bfloat16* ho = h + (size_t)row * args.ldo + col;
           __nv_bfloat16* go = gu + (size_t)row * args.ldo2 + col;
@@ -665,14 +694,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-      } else if constexpr (E == Epi::SwigluBwd) {
+        if constexpr (kT) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int col = ti.n0 + half * 64, y = ti.m0 + quarter * 32;
+            if (col < args.N && y < args.M) {
+              tma_store_3d(&tmC, hbox, col, y, 0);                        // h [rows][I]
+              tma_store_3d(&tmD, hbox + kTmaBoxBytes, col, 0, y);         // gate half of [rows][2][I]
+              tma_store_3d(&tmD, hbox + 2 * kTmaBoxBytes, col, 1, y);     // up half
+            }
+            bulk_commit_group();
+          }
+        }
+      } else if constexpr (E == Epi::SwigluBwd || E == Epi::SwigluBwdTma) {
         // Accumulator = dh for I-columns n0 .. n0+BN-1.  out = dgu [M, 2I].
+        // SwigluBwdTma: each 64 columns of dg and du go to two 32 x 64 boxes
+        // of this warp (lane = row, chunk j at j ^ (row & 7)), then TMA.
+        constexpr bool kT = E == Epi::SwigluBwdTma;
         const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(args.aux);
         __nv_bfloat16* dgu = reinterpret_cast<__nv_bfloat16*>(args.out);
+        uint8_t* gbox = tma_stage + (warp - 2) * 2 * kTmaBoxBytes + lane * 128;
 #pragma unroll 1
         for (int c2 = half * HALF; c2 < (half + 1) * HALF; c2 += 32) {
           uint32_t rr[2][16];
           uint16_t gvv[2][16], uvv[2][16];
+          if constexpr (kT) {
+            if (((c2 - half * HALF) & 63) == 0) {
+              if (lane == 0) bulk_wait_group_read<0>();   // the boxes' previous stores have read them
+            }
+          }
           __syncwarp();
           tmem_ld16(tbase + c2, rr[0]);
           tmem_ld16(tbase + c2 + 16, rr[1]);
@@ -723,6 +774,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             dg[j / 2] = pack_bf16x2(o[0][0], o[0][1]);
             du[j / 2] = pack_bf16x2(o[1][0], o[1][1]);
           }
+          if constexpr (kT) {
+            const int ch = ((c - half * HALF) & 63) >> 3;
+            const int o0 = (ch ^ (lane & 7)) << 4, o1 = ((ch + 1) ^ (lane & 7)) << 4;
+            *reinterpret_cast<uint4*>(gbox + o0) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
+            *reinterpret_cast<uint4*>(gbox + o1) = make_uint4(dg[4], dg[5], dg[6], dg[7]);
+            *reinterpret_cast<uint4*>(gbox + kTmaBoxBytes + o0) = make_uint4(du[0], du[1], du[2], du[3]);
+            *reinterpret_cast<uint4*>(gbox + kTmaBoxBytes + o1) = make_uint4(du[4], du[5], du[6], du[7]);
+            continue;
+          }
           __nv_bfloat16* go = dgu + (size_t)row * args.ldo + col;
           __nv_bfloat16* uo = dgu + (size_t)row * args.ldo + args.inter + col;
           if (nv == 16) {
@@ -738,6 +798,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               reinterpret_cast<uint16_t*>(uo)[j] = us[j];
             }
           }
+          }
+          if constexpr (kT) {
+            if (((c2 + 32 - half * HALF) & 63) == 0) {   // a 64-column pair of boxes is complete
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                const int col = ti.n0 + (c2 & ~63), y = ti.m0 + quarter * 32;
+                if (col < args.N && y < args.M) {
+                  tma_store_3d(&tmC, gbox, col, 0, y);                  // dg half of [rows][2][I]
+                  tma_store_3d(&tmC, gbox + kTmaBoxBytes, col, 1, y);   // du half
+                }
+                bulk_commit_group();
+              }
+            }
           }
         }
       } else if constexpr (E == Epi::CeFwd) {
