@@ -1119,26 +1119,32 @@ __global__ void __launch_bounds__(320 + 128 * DRAIN, 1)
       if (!DRAIN) drain_dq(iters - 1);
       float* dkr = dK + ((size_t)bh * Sk + key) * DQK;
       float* dvr = dVo + ((size_t)bh * Sk + key) * DV;
-      for (int c = dq_c0; c < dq_c1; ++c) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + C::C_DK + c * 16, r);
-        tmem_ld_wait();
-        if (key < Sk)
+      // every TMEM read of this thread's dK / dV columns is issued before the
+      // one wait (the CTA's last work: no serial load-wait-store chain)
+      constexpr int KC = (NDQ + 1) / 2, VC = DV / 32;
+      uint32_t rk[KC][16], rv[VC][16];
+#pragma unroll
+      for (int j = 0; j < KC; ++j)
+        if (dq_c0 + j < dq_c1) tmem_ld16(tmem + lane_base + C::C_DK + (dq_c0 + j) * 16, rk[j]);
+#pragma unroll
+      for (int j = 0; j < VC; ++j) tmem_ld16(tmem + lane_base + C::C_DV + (half * VC + j) * 16, rv[j]);
+      tmem_ld_wait();
+      if (key < Sk) {
+#pragma unroll
+        for (int j = 0; j < KC; ++j)
+          if (dq_c0 + j < dq_c1)
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4*>(dkr + (dq_c0 + j) * 16 + e) =
+                  make_float4(__uint_as_float(rk[j][e]) * scale, __uint_as_float(rk[j][e + 1]) * scale,
+                              __uint_as_float(rk[j][e + 2]) * scale, __uint_as_float(rk[j][e + 3]) * scale);
+#pragma unroll
+        for (int j = 0; j < VC; ++j)
 #pragma unroll
           for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(dkr + c * 16 + e) =
-                make_float4(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale,
-                            __uint_as_float(r[e + 2]) * scale, __uint_as_float(r[e + 3]) * scale);
-      }
-      for (int c = half * (DV / 32); c < (half + 1) * (DV / 32); ++c) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + C::C_DV + c * 16, r);
-        tmem_ld_wait();
-        if (key < Sk)
-#pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4*>(dvr + c * 16 + e) = make_float4(
-                __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+            *reinterpret_cast<float4*>(dvr + (half * VC + j) * 16 + e) =
+                make_float4(__uint_as_float(rv[j][e]), __uint_as_float(rv[j][e + 1]), __uint_as_float(rv[j][e + 2]),
+                            __uint_as_float(rv[j][e + 3]));
       }
     }
   }
