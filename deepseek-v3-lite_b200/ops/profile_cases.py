@@ -55,6 +55,16 @@ def case_dense_dgrad_f32():
         C.linear_dgrad(dy, w, out, False)
 
 
+def case_resid_fwd():
+    """Dense forward with the fp32 residual add (the o-projection shape: 32K x 768 x 768)."""
+    C = native()
+    a, w = _bf(32768, 768), _bf(768, 768)
+    resid = torch.randn(32768, 768, device="cuda")
+    out = torch.empty(32768, 768, device="cuda")
+    for _ in range(2):
+        C.linear_fwd(a, w, out, True, resid)
+
+
 def _attn_inputs(B=2, H=12, S=2048, DP=80, DV=64):
     Q, K, V = _bf(B * H, S, DP), _bf(B * H, S, DP), _bf(B * H, S, DV)
     O = torch.empty(B, S, H, DV, device="cuda", dtype=torch.bfloat16)
