@@ -349,6 +349,39 @@ __global__ void heads_unpack_kernel(const float* __restrict__ src, int H, int hd
   for (int c = threadIdx.x; c < hd; c += blockDim.x) d[c] = __float2bfloat16(r[c]);
 }
 
+// 16-byte versions: one thread per 8-element chunk; consecutive threads take
+// consecutive chunks of a head row, then consecutive tokens of the same head,
+// so a warp reads 128-byte row pieces and writes contiguous [S, DP] rows.
+// Need hd, DP, ld and col0 multiples of 8 and 16-byte aligned bases.
+__global__ void heads_pack_v(const __nv_bfloat16* __restrict__ src, long ld, int col0, int H, int hd, int S, int DP,
+                             __nv_bfloat16* __restrict__ dst, long T) {
+  const int chunks = DP / 8;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * H * chunks) return;
+  const int j = (int)(idx % chunks);
+  const long t = (idx / chunks) % T;
+  const int h = (int)(idx / (chunks * T));
+  const long b = t / S, s = t % S;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (8 * j < hd) v = *reinterpret_cast<const uint4*>(src + t * ld + col0 + (size_t)h * hd + 8 * j);
+  *reinterpret_cast<uint4*>(dst + ((b * H + h) * S + s) * DP + 8 * j) = v;
+}
+
+__global__ void heads_unpack_v(const float* __restrict__ src, int H, int hd, int S, int DP,
+                               __nv_bfloat16* __restrict__ dst, long ld, int col0, long T) {
+  const int chunks = hd / 8;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * H * chunks) return;
+  const int j = (int)(idx % chunks);
+  const long t = (idx / chunks) % T;
+  const int h = (int)(idx / (chunks * T));
+  const long b = t / S, s = t % S;
+  const float4* r = reinterpret_cast<const float4*>(src + ((b * H + h) * S + s) * DP + 8 * j);
+  const float4 x = r[0], y = r[1];
+  *reinterpret_cast<uint4*>(dst + t * ld + col0 + (size_t)h * hd + 8 * j) =
+      make_uint4(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w), pack_bf16x2(y.x, y.y), pack_bf16x2(y.z, y.w));
+}
+
 // ---------------------------------------------- RMSNorm, width-specialised
 // PAIRS = D / 64: each lane owns PAIRS column pairs (2 * (lane + 32 i)), so a
 // warp reads 256 contiguous bytes of fp32 (128 of bf16) per step.
@@ -971,6 +1004,17 @@ void ce_reduce(const at::Tensor& loss_rows, const at::Tensor& tgt, const at::Ten
 void heads_pack(const at::Tensor& src, int64_t col0, int64_t H, int64_t hd, int64_t S, at::Tensor& dst) {
   const int T = src.size(0), DP = dst.size(-1);
   const at::cuda::CUDAGuard guard(src.device());
+  const bool vec = hd % 8 == 0 && DP % 8 == 0 && src.stride(0) % 8 == 0 && col0 % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(src.data_ptr()) | reinterpret_cast<uintptr_t>(dst.data_ptr())) & 15) == 0;
+  if (vec) {
+    const long total = (long)T * H * (DP / 8);
+    if (total == 0) return;
+    heads_pack_v<<<(int)((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), (int)col0, (int)H, (int)hd, (int)S, DP,
+        reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), (long)T);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   heads_pack_kernel<<<dim3(T, H), 64, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), col0, H, hd, S, DP,
       reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()));
@@ -980,6 +1024,17 @@ void heads_pack(const at::Tensor& src, int64_t col0, int64_t H, int64_t hd, int6
 void heads_unpack(const at::Tensor& src, int64_t H, int64_t hd, int64_t S, at::Tensor& dst, int64_t col0) {
   const int T = dst.size(0), DP = src.size(-1);
   const at::cuda::CUDAGuard guard(src.device());
+  const bool vec = hd % 8 == 0 && DP % 4 == 0 && dst.stride(0) % 8 == 0 && col0 % 8 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(src.data_ptr()) | reinterpret_cast<uintptr_t>(dst.data_ptr())) & 15) == 0;
+  if (vec) {
+    const long total = (long)T * H * (hd / 8);
+    if (total == 0) return;
+    heads_unpack_v<<<(int)((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        src.data_ptr<float>(), (int)H, (int)hd, (int)S, DP, reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()),
+        dst.stride(0), (int)col0, (long)T);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   heads_unpack_kernel<<<dim3(T, H), 64, 0, at::cuda::getCurrentCUDAStream()>>>(src.data_ptr<float>(), H, hd, S, DP,
       reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), dst.stride(0), col0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -508,3 +508,23 @@ def test_moe_norm_bwd_fused(C, D, E, with_shared, with_routed):
     close(dres_b, dres0 + d, rtol=1e-2, atol=1e-2)
     close(dw, (gsum * xh).sum(0), rtol=1e-4, atol=1e-3)
     assert C.status_read() == 0
+
+
+@pytest.mark.parametrize("B,S,H,hd,DP,col0", [(2, 150, 3, 64, 64, 0), (2, 150, 3, 64, 80, 192), (1, 77, 2, 20, 32, 48)])
+def test_heads_pack_unpack(C, B, S, H, hd, DP, col0):
+    """[T, ld] head slices <-> [B*H, S, DP] (zero padded), on the 16-byte path
+    and (hd 20) the scalar one."""
+    T = B * S
+    ld = col0 + H * hd + 8
+    src = torch.randn(T, ld, device="cuda").bfloat16()
+    dst = torch.full((B * H, S, DP), 3.0, device="cuda", dtype=torch.bfloat16)
+    C.heads_pack(src, col0, H, hd, S, dst)
+    ref = torch.zeros(B * H, S, DP, device="cuda", dtype=torch.bfloat16)
+    ref[:, :, :hd] = src[:, col0:col0 + H * hd].view(B, S, H, hd).permute(0, 2, 1, 3).reshape(B * H, S, hd)
+    assert torch.equal(dst, ref)
+    g = torch.randn(B * H, S, DP, device="cuda")
+    out = torch.full((T, ld), 5.0, device="cuda", dtype=torch.bfloat16)
+    C.heads_unpack(g, H, hd, S, out, col0)
+    want = g[:, :, :hd].view(B, H, S, hd).permute(0, 2, 1, 3).reshape(T, H * hd).bfloat16()
+    assert torch.equal(out[:, col0:col0 + H * hd], want)
+    assert (out[:, :col0] == 5.0).all() and (out[:, col0 + H * hd:] == 5.0).all()
